@@ -1,0 +1,495 @@
+#!/usr/bin/env python3
+"""Benchmark of the pn_fir_tau attention operator (forward + backward).
+
+Headline (BASELINE metric): flash_pn_fir_tau_attention fwd+bwd TFLOP/s at
+N=4096 (config 3: B=8, H=8, N=4096, d=64, bf16, half of the 64-row query
+blocks scaled by 0.05), algorithmic FLOPs 7*B*H*N^2*d per step (causal = half
+of dense QK^T + PV forward and the five backward products; skipped silent
+tiles still count). Alongside: the 6-layer pn_fir_tau LM training step in
+tokens/s (config 4), the end-to-end number through the public API with host
+buffers, the dominant kernel's roofline, a bounded CPU-oracle baseline and
+the SM clocks seen during the timed region.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+    torchrun --nproc-per-node N bench.py --gpus N ...     (one rank per GPU)
+
+Multi-GPU: every rank runs its own config-3-sized shard of batch x heads
+(weak scaling, no collective on the operator's data path); the shared tau
+gradient is summed across ranks with one fp32 all-reduce per step, and the LM
+uses DDP over NCCL. ``--impl reference`` times the CPU oracle (the reference's
+eager algorithm restated in oracle/) on rank 0 only.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import re
+import statistics
+import sys
+import threading
+import time
+from datetime import timedelta
+from pathlib import Path
+
+import torch
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+METRIC = "pn_fir_tau attn fwd+bwd TFLOP/s (% tensor peak) at N=4096; 6-layer LM tokens/s"
+WORKLOADS = {
+    "c3": dict(B=8, H=8, N=4096, D=64, quiet_frac=0.5,
+               desc="flash_pn_fir_tau_attention fwd+bwd, B8 H8 N4096 d64 bf16, 50% of 64-row q blocks x0.05"),
+    "c2": dict(B=16, H=4, N=512, D=64, quiet_frac=0.0, desc="flash_pn_fir_tau_attention fwd+bwd, B16 H4 N512 d64 bf16"),
+    "c5": dict(B=8, H=16, N=16384, D=128, quiet_frac=0.0,
+               desc="flash_pn_fir_tau_attention fwd+bwd, B8 H16 N16384 d128 bf16"),
+}
+L2_BYTES = 126 * 2**20
+FALLBACK_PEAK_TFLOPS = 1590.0
+FALLBACK_HBM_GBS = 6650.0
+
+
+def parse_args():
+    ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=30)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--workload", choices=sorted(WORKLOADS), default="c3")
+    ap.add_argument("--tau", type=float, default=0.0)
+    ap.add_argument("--seed", type=int, default=0)
+    ap.add_argument("--lm-steps", type=int, default=10)
+    ap.add_argument("--no-lm", action="store_true")
+    ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--no-cpu", action="store_true")
+    ap.add_argument("--cpu-seconds", type=float, default=12.0)
+    ap.add_argument("--generic", action="store_true", help="force the generic SIMT kernels")
+    return ap.parse_args()
+
+
+# ---------------------------------------------------------------------------
+# distributed plumbing
+# ---------------------------------------------------------------------------
+
+
+class Dist:
+    def __init__(self):
+        self.world = int(os.environ.get("WORLD_SIZE", "1"))
+        self.rank = int(os.environ.get("RANK", "0"))
+        self.local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+        self.active = self.world > 1
+
+    def init(self, backend: str):
+        if self.active:
+            import torch.distributed as dist
+
+            dist.init_process_group(backend, timeout=timedelta(seconds=180))
+
+    def barrier(self):
+        if self.active:
+            import torch.distributed as dist
+
+            dist.barrier()
+
+    def max(self, x: float, device) -> float:
+        if not self.active:
+            return x
+        import torch.distributed as dist
+
+        t = torch.tensor([x], dtype=torch.float64, device=device)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    def close(self):
+        if self.active:
+            import torch.distributed as dist
+
+            dist.destroy_process_group()
+
+
+# ---------------------------------------------------------------------------
+# clocks (NVML reads only; nothing is ever set)
+# ---------------------------------------------------------------------------
+
+
+class ClockSampler:
+    """Samples SM clock and clock-event reasons of one GPU every `period` s."""
+
+    REASONS = {
+        0x0000000000000008: "hw_slowdown",
+        0x0000000000000040: "hw_thermal_slowdown",
+        0x0000000000000020: "sw_thermal_slowdown",
+        0x0000000000000004: "sw_power_cap",
+        0x0000000000000080: "hw_power_brake_slowdown",
+        0x0000000000000001: "gpu_idle",
+        0x0000000000000002: "applications_clocks_setting",
+        0x0000000000000100: "display_clock_setting",
+    }
+
+    def __init__(self, device: torch.device, period: float = 0.02):
+        self.period = period
+        self.samples: list[tuple[float, int]] = []
+        self.max_mhz = None
+        self.error = None
+        self._stop = threading.Event()
+        self._thread = None
+        self.handle = None
+        try:
+            import pynvml
+
+            pynvml.nvmlInit()
+            self.nvml = pynvml
+            uuid = str(torch.cuda.get_device_properties(device).uuid)
+            for i in range(pynvml.nvmlDeviceGetCount()):
+                h = pynvml.nvmlDeviceGetHandleByIndex(i)
+                u = pynvml.nvmlDeviceGetUUID(h)
+                u = u.decode() if isinstance(u, bytes) else u
+                if u.replace("GPU-", "") == uuid.replace("GPU-", ""):
+                    self.handle = h
+                    break
+            if self.handle is None:
+                self.handle = pynvml.nvmlDeviceGetHandleByIndex(device.index or 0)
+            self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(self.handle, pynvml.NVML_CLOCK_SM)
+        except Exception as e:  # noqa: BLE001 - clocks are reported as unavailable
+            self.error = f"{type(e).__name__}: {e}"
+
+    def _run(self):
+        nv = self.nvml
+        while not self._stop.is_set():
+            try:
+                mhz = nv.nvmlDeviceGetClockInfo(self.handle, nv.NVML_CLOCK_SM)
+                try:
+                    reasons = nv.nvmlDeviceGetCurrentClocksEventReasons(self.handle)
+                except AttributeError:
+                    reasons = nv.nvmlDeviceGetCurrentClocksThrottleReasons(self.handle)
+                self.samples.append((mhz, int(reasons)))
+            except Exception as e:  # noqa: BLE001
+                self.error = f"{type(e).__name__}: {e}"
+                return
+            self._stop.wait(self.period)
+
+    def __enter__(self):
+        if self.handle is not None:
+            self._thread = threading.Thread(target=self._run, daemon=True)
+            self._thread.start()
+        return self
+
+    def __exit__(self, *exc):
+        self._stop.set()
+        if self._thread is not None:
+            self._thread.join()
+
+    def summary(self) -> dict:
+        if not self.samples:
+            return {"sm_mhz": None, "sm_max_mhz": self.max_mhz, "reasons": [], "samples": 0,
+                    "error": self.error or "no samples"}
+        mhz = [m for m, _ in self.samples]
+        seen = 0
+        for _, r in self.samples:
+            seen |= r
+        reasons = [name for bit, name in self.REASONS.items() if seen & bit and name != "gpu_idle"]
+        return {"sm_mhz": statistics.median(mhz), "sm_max_mhz": self.max_mhz, "sm_min_mhz": min(mhz),
+                "reasons": reasons, "samples": len(mhz)}
+
+
+# ---------------------------------------------------------------------------
+# peaks and profile figures
+# ---------------------------------------------------------------------------
+
+
+def measured_peaks() -> dict:
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return {"bf16_tflops": float(d["bf16_tflops"]), "bf16_tflops_sustained": float(d.get("bf16_tflops_sustained", 0)),
+                "hbm_gbs": float(d["hbm_gbs"]), "source": "measured"}
+    return {"bf16_tflops": FALLBACK_PEAK_TFLOPS, "bf16_tflops_sustained": 1400.0, "hbm_gbs": FALLBACK_HBM_GBS,
+            "source": "fallback"}
+
+
+def profile_traffic(kernel_key: str) -> float | None:
+    """DRAM bytes per launch of `kernel_key` from the committed ncu summary
+    (a line `traffic_bytes_per_launch[<key>]: <bytes>` under profiles/)."""
+    for p in sorted((ROOT / "profiles").glob("*.md")):
+        m = re.search(rf"traffic_bytes_per_launch\[{re.escape(kernel_key)}\]:\s*([0-9.eE+]+)", p.read_text())
+        if m:
+            return float(m.group(1))
+    return None
+
+
+# ---------------------------------------------------------------------------
+# workload
+# ---------------------------------------------------------------------------
+
+
+def make_inputs(w: dict, seed: int, device, dtype=torch.bfloat16):
+    """Seeded config inputs: q,k,v,dO ~ N(0,1); with quiet_frac > 0 a seeded
+    random fraction of the 64-row query blocks of every (b,h) is scaled by 0.05."""
+    B, H, N, D = w["B"], w["H"], w["N"], w["D"]
+    g = torch.Generator(device=device).manual_seed(seed)
+    q = torch.randn(B, H, N, D, generator=g, device=device, dtype=torch.float32)
+    if w["quiet_frac"] > 0:
+        nb = (N + 63) // 64
+        quiet = torch.rand(B, H, nb, generator=g, device=device) < w["quiet_frac"]
+        fac = torch.where(quiet, 0.05, 1.0).repeat_interleave(64, dim=-1)[..., :N]
+        q = q * fac[..., None]
+    k = torch.randn(B, H, N, D, generator=g, device=device)
+    v = torch.randn(B, H, N, D, generator=g, device=device)
+    do = torch.randn(B, H, N, D, generator=g, device=device)
+    return [t.to(dtype) for t in (q, k, v, do)]
+
+
+def flops_fwd_bwd(w: dict) -> float:
+    return 7.0 * w["B"] * w["H"] * w["N"] ** 2 * w["D"]
+
+
+def cpu_oracle_sample(w: dict, seconds: float, seed: int, steps: int | None = None):
+    """Times the CPU oracle (fp32 eager algorithm) on whole (b,h) slices of the
+    workload; returns (TFLOP/s, threads, slices, seconds)."""
+    from oracle import pnfirtau_oracle as O
+
+    torch.set_num_threads(len(os.sched_getaffinity(0)))
+    N, D = w["N"], w["D"]
+    flops_slice = 7.0 * N * N * D
+    g = torch.Generator().manual_seed(seed)
+
+    def one():
+        q, k, v, do = (torch.randn(1, 1, N, D, generator=g) for _ in range(4))
+        q.requires_grad_(True), k.requires_grad_(True), v.requires_grad_(True)
+        tau = torch.tensor(0.0, requires_grad=True)
+        out = O.pn_fir_tau_attention(q, k, v, tau)
+        torch.autograd.grad(out, (q, k, v, tau), do)
+
+    one()  # warm-up
+    t0 = time.perf_counter()
+    n = 0
+    while True:
+        one()
+        n += 1
+        el = time.perf_counter() - t0
+        if (steps is not None and n >= steps) or (steps is None and el >= seconds):
+            break
+    return flops_slice * n / el / 1e12, torch.get_num_threads(), n, el
+
+
+# ---------------------------------------------------------------------------
+# our arm
+# ---------------------------------------------------------------------------
+
+
+def bench_ours(args, dist_: Dist) -> dict:
+    import paper_01_anti_decoy_pnfirtau_b200 as P
+    from paper_01_anti_decoy_pnfirtau_b200 import _lib, pnfirtau_ops
+
+    dev = torch.device("cuda", dist_.local_rank)
+    torch.cuda.set_device(dev)
+    dist_.init("nccl")
+    if args.generic:
+        pnfirtau_ops._FORCE_GENERIC = True
+    w = WORKLOADS[args.workload]
+    q, k, v, do = make_inputs(w, args.seed + 1000 * dist_.rank, dev)
+    tau = torch.tensor(args.tau, device=dev, requires_grad=True)
+    leaves = [t.requires_grad_(True) for t in (q, k, v)]
+    path = P.flash_kernel_path(q, k, v)
+    flops = flops_fwd_bwd(w)
+
+    def step(evs=None):
+        if evs is not None:
+            evs[0].record()
+        out = P.flash_pn_fir_tau_attention(*leaves, tau)
+        if evs is not None:
+            evs[1].record()
+        grads = torch.autograd.grad(out, (*leaves, tau), do)
+        if evs is not None:
+            evs[2].record()
+        if dist_.active:
+            import torch.distributed as dist
+
+            dist.all_reduce(grads[3])
+        return out, grads
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    P.check_device_status(dev)
+    evs = [[torch.cuda.Event(enable_timing=True) for _ in range(3)] for _ in range(args.steps)]
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    dist_.barrier()
+    torch.cuda.synchronize()
+    n0 = _lib.launch_count()
+    with ClockSampler(dev) as clocks:
+        start.record()
+        for i in range(args.steps):
+            step(evs[i])
+        end.record()
+        torch.cuda.synchronize()
+    launches = _lib.launch_count() - n0
+    dist_.barrier()
+    P.check_device_status(dev)
+    ms_local = start.elapsed_time(end)
+    ms = dist_.max(ms_local, dev)
+    fwd_ms = statistics.mean(e[0].elapsed_time(e[1]) for e in evs)
+    bwd_ms = statistics.mean(e[1].elapsed_time(e[2]) for e in evs)
+    ms_per_step = ms / args.steps
+    value = dist_.world * flops * args.steps / (ms / 1e3) / 1e12
+    peaks = measured_peaks()
+
+    B, H, N, D = w["B"], w["H"], w["N"], w["D"]
+    if bwd_ms >= fwd_ms:
+        kname, kflops, kms = "flash_bwd", 5.0 * B * H * N * N * D, bwd_ms
+    else:
+        kname, kflops, kms = "flash_fwd", 2.0 * B * H * N * N * D, fwd_ms
+    achieved = kflops / (kms / 1e3) / 1e12
+    traffic = profile_traffic(f"{kname}:{args.workload}")
+    roofline = {
+        "bound": "tensor", "kernel": kname, "achieved": round(achieved, 2), "peak": peaks["bf16_tflops"],
+        "unit": "TFLOP/s", "frac": round(achieved / peaks["bf16_tflops"], 4), "traffic": traffic,
+        "peak_source": f"{peaks['source']} bf16 burst (sustained {peaks['bf16_tflops_sustained']})",
+        "flops_per_launch": kflops, "ms_per_launch": round(kms, 4),
+        "note": "flash_bwd time includes its per-row prep, dQ cast and tau-sum launches",
+    }
+    result = {
+        "metric": METRIC, "value": round(value, 3), "unit": "TFLOP/s", "n_gpus": dist_.world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": round(ms_per_step, 4), "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+        "config": {"workload": f"{args.workload}: {w['desc']}", "B": B, "H": H, "N": N, "d": D, "tau": args.tau,
+                   "kernel_path": path, "per_rank_shard": "each rank runs its own B*H shard of this size",
+                   "l2": f"inputs {4 * B * H * N * D * 2 / 2**20:.0f} MiB > 126 MiB L2 (no flush)",
+                   "parallelism": f"bh-shard x{dist_.world}" if dist_.world > 1 else "single GPU",
+                   "flops_per_step_per_gpu": flops},
+        "pct_of_peak": round(100.0 * value / dist_.world / peaks["bf16_tflops"], 2),
+        "fwd_ms": round(fwd_ms, 4), "bwd_ms": round(bwd_ms, 4),
+        "roofline": roofline, "gpu_launches": int(launches), "clocks": clocks.summary(),
+    }
+
+    if not args.no_e2e:
+        result["e2e"] = bench_e2e(args, dist_, w, dev, flops, P)
+    if not args.no_lm:
+        result["lm"] = bench_lm(args, dist_, dev)
+    if dist_.rank == 0 and dist_.world == 1 and not args.no_cpu:
+        tf, cores, n, el = cpu_oracle_sample(w, args.cpu_seconds, args.seed)
+        result["cpu_baseline"] = {"value": round(tf, 6), "unit": "TFLOP/s", "cores": cores, "kind": "port",
+                                  "sample": f"{n} (b,h) slices of [1,1,{N},{D}] fp32 fwd+bwd in {el:.1f} s "
+                                            f"(oracle/pnfirtau_oracle.py, torch CPU eager)"}
+    return result
+
+
+def bench_e2e(args, dist_: Dist, w: dict, dev, flops: float, P) -> dict:
+    """Same op through the public API with pinned host inputs and host outputs:
+    every step copies q,k,v,dO host->device and out,dq,dk,dv,dtau device->host."""
+    hq, hk, hv, hdo = (t.detach().cpu().pin_memory() for t in make_inputs(w, args.seed + 7, dev))
+    outs = [torch.empty_like(hq).pin_memory() for _ in range(4)]
+    htau = torch.empty((), dtype=torch.float32).pin_memory()
+    tau = torch.tensor(args.tau, device=dev, requires_grad=True)
+
+    def step():
+        q, k, v, do = (t.to(dev, non_blocking=True) for t in (hq, hk, hv, hdo))
+        q.requires_grad_(True), k.requires_grad_(True), v.requires_grad_(True)
+        out = P.flash_pn_fir_tau_attention(q, k, v, tau)
+        dq, dk, dv, dtau = torch.autograd.grad(out, (q, k, v, tau), do)
+        if dist_.active:
+            import torch.distributed as dist
+
+            dist.all_reduce(dtau)
+        for h, d in zip(outs, (out, dq, dk, dv)):
+            h.copy_(d, non_blocking=True)
+        htau.copy_(dtau, non_blocking=True)
+
+    for _ in range(max(2, min(args.warmup, 3))):
+        step()
+    torch.cuda.synchronize()
+    steps = args.steps
+    s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    dist_.barrier()
+    torch.cuda.synchronize()
+    s.record()
+    for _ in range(steps):
+        step()
+    e.record()
+    torch.cuda.synchronize()
+    ms = dist_.max(s.elapsed_time(e), dev)
+    h2d = sum(t.numel() * t.element_size() for t in (hq, hk, hv, hdo))
+    d2h = sum(t.numel() * t.element_size() for t in outs) + htau.element_size()
+    return {"value": round(dist_.world * flops * steps / (ms / 1e3) / 1e12, 3), "unit": "TFLOP/s",
+            "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h, "ms_per_step": round(ms / steps, 4),
+            "steps": steps, "api": "flash_pn_fir_tau_attention + torch.autograd.grad, pinned host buffers"}
+
+
+def bench_lm(args, dist_: Dist, dev) -> dict:
+    """Config 4: 6-layer LM training step, bf16 autocast, AdamW, DDP at N > 1."""
+    from paper_01_anti_decoy_pnfirtau_b200.lm import LMConfig, PnFirLM, make_optimizer, train_step
+
+    cfg = LMConfig()
+    torch.manual_seed(args.seed)
+    model = PnFirLM(cfg).to(dev)
+    nparams = model.param_count()
+    if dist_.active:
+        model = torch.nn.parallel.DistributedDataParallel(model, device_ids=[dev.index])
+    opt = make_optimizer(model)
+    B, N = 32, cfg.max_seq
+    g = torch.Generator(device=dev).manual_seed(args.seed + 17 * dist_.rank)
+    batches = [torch.randint(0, cfg.vocab, (B, N), generator=g, device=dev) for _ in range(4)]
+    for i in range(3):
+        train_step(model, opt, batches[i % 4])
+    torch.cuda.synchronize()
+    s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    dist_.barrier()
+    torch.cuda.synchronize()
+    s.record()
+    loss = None
+    for i in range(args.lm_steps):
+        loss = train_step(model, opt, batches[i % 4])
+    e.record()
+    torch.cuda.synchronize()
+    ms = dist_.max(s.elapsed_time(e), dev)
+    ms_step = ms / args.lm_steps
+    return {"tokens_per_s": round(dist_.world * B * N / (ms_step / 1e3), 1), "ms_per_step": round(ms_step, 3),
+            "steps": args.lm_steps, "global_batch": B * dist_.world, "seq_len": N, "params": nparams,
+            "loss": round(float(loss), 4), "model": "6-layer Pre-LN pn_fir_tau LM, D256 H4 MLP4x V33278, bf16 autocast, AdamW",
+            "parallelism": f"ddp{dist_.world}" if dist_.world > 1 else "single GPU"}
+
+
+# ---------------------------------------------------------------------------
+# reference arm: the reference's eager algorithm on the host cores
+# ---------------------------------------------------------------------------
+
+
+def bench_reference(args, dist_: Dist) -> dict | None:
+    if dist_.rank != 0:
+        return None
+    w = WORKLOADS[args.workload]
+    from oracle import pnfirtau_oracle as O  # noqa: F401  (imported for its CPU eager path)
+
+    for _ in range(args.warmup):
+        cpu_oracle_sample(w, 0.0, args.seed, steps=1)
+    tf, cores, n, el = cpu_oracle_sample(w, 0.0, args.seed, steps=args.steps)
+    sample = (f"each step = one (b,h) slice [1,1,{w['N']},{w['D']}] fp32 fwd+bwd of the {args.workload} workload "
+              f"(oracle/pnfirtau_oracle.py: the reference's eager torch algorithm), {cores} threads")
+    return {
+        "impl": "reference", "metric": METRIC, "value": round(tf, 6), "unit": "TFLOP/s", "n_gpus": dist_.world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(1e3 * el / n, 3), "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": {"workload": f"{args.workload}: {w['desc']}", "B": w["B"], "H": w["H"], "N": w["N"], "d": w["D"]},
+        "cpu_baseline": {"value": round(tf, 6), "unit": "TFLOP/s", "cores": cores, "kind": "port", "sample": sample},
+        "e2e": {"value": round(tf, 6), "unit": "TFLOP/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+
+
+def main():
+    args = parse_args()
+    dist_ = Dist()
+    if args.impl == "reference":
+        res = bench_reference(args, dist_)
+        if res is not None:
+            print(json.dumps(res), flush=True)
+        return
+    res = bench_ours(args, dist_)
+    if dist_.rank == 0:
+        print(json.dumps(res), flush=True)
+    dist_.close()
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,196 @@
+/*
+ * pnfirtau_b200.h - C ABI of the B200-native pn_fir_tau attention operator.
+ *
+ * One shared library (libpnfirtau_b200.so) exports these entry points. Every
+ * pointer is a DEVICE pointer unless stated otherwise, strides are in ELEMENTS,
+ * the CUDA stream is passed as an opaque `void*` (a cudaStream_t) and comes
+ * last. No entry point allocates device memory: outputs and workspaces are
+ * owned by the caller (the reference's Python wrappers allocate with
+ * torch.empty / torch.zeros and hand raw pointers to the kernels, which is the
+ * convention kept here). All launches are asynchronous on `stream` and are
+ * legal inside CUDA-graph capture.
+ *
+ * Return value of every entry point: PNFT_OK (0) on success, a negative
+ * PNFT_E* code for invalid arguments or a CUDA launch error. The message of
+ * the last failure on the calling thread is available from pnft_last_error().
+ * Kernels that wait on hardware barriers write a positive PNFT_DEV_* code to
+ * the caller's `status` word instead of hanging; the host reads it when it
+ * next synchronises.
+ *
+ * Reference interface replaced (paths inside the reference project):
+ *   src/triton_pnfirtau.py  - Triton kernels + autograd wrappers
+ *   src/pnfirtau_attention.py - eager primitives (power_norm_peak_gate, causal_fir)
+ */
+#ifndef PNFIRTAU_B200_H
+#define PNFIRTAU_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define PNFT_API __attribute__((visibility("default")))
+#else
+#define PNFT_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* element types of the tensors handed to the kernels */
+#define PNFT_DTYPE_F32 0
+#define PNFT_DTYPE_BF16 1
+#define PNFT_DTYPE_F16 2
+
+/* host-side status codes */
+#define PNFT_OK 0
+#define PNFT_EINVAL (-1)       /* bad shape / stride / pointer / parameter */
+#define PNFT_EUNSUPPORTED (-2) /* valid request this build cannot serve   */
+#define PNFT_ECUDA (-3)        /* CUDA runtime / launch error              */
+
+/* device-reported status codes (written to the caller's status word) */
+#define PNFT_DEV_OK 0
+#define PNFT_DEV_WAIT_TIMEOUT 1 /* a pipeline mbarrier wait hit its bound */
+
+/* silence modes of power_norm_peak_gate (src/pnfirtau_attention.py:108-116) */
+#define PNFT_SILENCE_PEAK 0
+#define PNFT_SILENCE_MASS_RELU 1
+#define PNFT_SILENCE_MASS_POW 2
+
+/* flags of the flash entry points */
+#define PNFT_FLASH_FORCE_GENERIC 0x1 /* use the SIMT kernel even where tcgen05 applies */
+#define PNFT_FLASH_DETERMINISTIC 0x2 /* reserved: ordered dQ accumulation             */
+
+/* Library version (major*10000 + minor*100 + patch). */
+PNFT_API int pnft_version(void);
+
+/* Number of kernels this library has launched in this process (all devices,
+ * all threads); lets callers attribute launches in a timed region. */
+PNFT_API uint64_t pnft_launch_count(void);
+
+/* Message of the last failed call on this thread ("" if none). Host pointer. */
+PNFT_API const char* pnft_last_error(void);
+
+/* Device capabilities relevant to kernel selection. Host pointers out.
+ * has_sm100a: 1 if the device is compute capability 10.0 (the sm_100a cubins
+ * of this library run on it). */
+PNFT_API int pnft_query_caps(int device, int* cc_major, int* cc_minor, int* sm_count,
+                    int* smem_optin_bytes, int* has_sm100a);
+
+/* ------------------------------------------------------------------------- */
+/* Depthwise causal FIR along N of x[B,N,C]                                   */
+/* ------------------------------------------------------------------------- */
+
+/* y[b,n,c] = sum_{u<ntaps} taps[ntaps-1-u] * x[b,n-u,c]   (x[b,<0,c] = 0),
+ * fp32 accumulation, y in the dtype of x. taps: fp32[ntaps], index ntaps-1 is
+ * lag 0 (oldest lag first, as the reference's fir_taps buffer).
+ * Replaces: src/triton_pnfirtau.py:40-87 (_causal_fir7_fwd_kernel) and its
+ * launch in _TritonCausalFir7Fn.forward (:631-658); also the eager
+ * causal_fir (src/pnfirtau_attention.py:65-74) for any ntaps <= 64. */
+PNFT_API int pnft_fir_fwd(const void* x, int64_t sxb, int64_t sxn, int64_t sxc, const float* taps,
+                 int ntaps, void* y, int64_t syb, int64_t syn, int64_t syc, int64_t B,
+                 int64_t N, int64_t C, int dtype, void* stream);
+
+/* Transpose (anti-causal) FIR: gx[b,n,c] = sum_u taps[ntaps-1-u] * gy[b,n+u,c].
+ * If x != NULL, also the tap gradient dtaps[ntaps-1-u] = sum gy[b,n,c]*x[b,n-u,c],
+ * reduced deterministically (fixed order, fp64) into dtaps (fp32[ntaps]).
+ * `workspace` must hold pnft_fir_bwd_workspace_size(B,N,C,ntaps) bytes when
+ * x != NULL (may be NULL otherwise). gx may be NULL to compute dtaps only.
+ * Replaces: src/triton_pnfirtau.py:89-135 (_causal_fir7_bwd_kernel) and
+ * _TritonCausalFir7Fn.backward (:660-682), which returns no tap gradient. */
+PNFT_API int pnft_fir_bwd(const void* gy, int64_t sgb, int64_t sgn, int64_t sgc, const float* taps,
+                 int ntaps, void* gx, int64_t sxb, int64_t sxn, int64_t sxc, const void* x,
+                 int64_t s0b, int64_t s0n, int64_t s0c, float* dtaps, void* workspace,
+                 size_t workspace_bytes, int64_t B, int64_t N, int64_t C, int dtype,
+                 void* stream);
+
+PNFT_API size_t pnft_fir_bwd_workspace_size(int64_t B, int64_t N, int64_t C, int ntaps);
+
+/* ------------------------------------------------------------------------- */
+/* Row-fused score -> weight op over R rows of length N                      */
+/* ------------------------------------------------------------------------- */
+
+/* For every row r (causal column limit t = r % N when causal != 0):
+ *   s = raw*scale - tau[0]; u = relu(s) on valid columns; pw = u^p;
+ *   strength = peak | sum u | sum pw (silence_mode); gate = strength/(strength+gamma)
+ *   (1 when has_gamma == 0); w = pw * gate / (sum pw + 1e-12).
+ * Stats (fp32/int32 [R]): stat_m = peak, stat_z = sum pw + 1e-12,
+ * stat_nmax = #columns with u == peak, stat_strength = strength.
+ * Silent rows (peak <= 0) write w = 0, M = 0, Z = 1e-12, Nmax = 0.
+ * p: exponent; p == 10 and p == 2 use repeated multiplication, other p powf.
+ * Replaces: src/triton_pnfirtau.py:141-212 (_pn_fir_tau_row_fwd_kernel) and
+ * _TritonPnFirTauScoresFn.forward (:694-752); the silence modes other than
+ * "peak" and general p follow power_norm_peak_gate (src/pnfirtau_attention.py:87-119). */
+PNFT_API int pnft_rows_fwd(const void* raw, int64_t raw_row_stride, const float* tau, void* w,
+                  int64_t w_row_stride, float* stat_m, float* stat_z, int32_t* stat_nmax,
+                  float* stat_strength, int64_t R, int64_t N, float scale, float p,
+                  float gamma, int has_gamma, int silence_mode, int causal, int dtype,
+                  void* stream);
+
+/* Analytic backward of pnft_rows_fwd: graw (dtype of raw) and the per-row
+ * tau gradient dtau_rows (fp32 [R], = -sum_j du). If dtau != NULL the rows are
+ * also reduced deterministically in fp64 into dtau[0] (fp32).
+ * Replaces: src/triton_pnfirtau.py:214-303 (_pn_fir_tau_row_bwd_kernel) and
+ * _TritonPnFirTauScoresFn.backward (:754-785). */
+PNFT_API int pnft_rows_bwd(const void* gw, int64_t gw_row_stride, const void* raw,
+                  int64_t raw_row_stride, const float* tau, const float* stat_m,
+                  const float* stat_z, const int32_t* stat_nmax, const float* stat_strength,
+                  void* graw, int64_t graw_row_stride, float* dtau_rows, float* dtau,
+                  int64_t R, int64_t N, float scale, float p, float gamma, int has_gamma,
+                  int silence_mode, int causal, int dtype, void* stream);
+
+/* Deterministic fp64 sum of n fp32 values into out[0] (fp32). */
+PNFT_API int pnft_sum_f32(const float* x, int64_t n, float* out, void* stream);
+
+/* ------------------------------------------------------------------------- */
+/* Flash pn_fir_tau attention (p = 10)                                       */
+/* ------------------------------------------------------------------------- */
+
+/* q,k,v: [B,H,N,D] with arbitrary 4-D element strides sq/sk/sv/so (host
+ * arrays of 4 int64: b,h,n,d); out in the same dtype with strides so.
+ * Stats stat_m/stat_z (fp32) and stat_nmax (int32) are contiguous [B,H,N].
+ * gamma is used when has_gamma != 0 (reference: gamma is not None and > 0).
+ * tile_flags (optional, may be NULL): uint8 [B*H, ceil(N/64), ceil(N/64)],
+ * zeroed by the caller; the kernel sets entry (bh, qi, kj) to 1 for every
+ * 64x64 tile it processed as live (some u > 0) and leaves skipped silent
+ * tiles and tiles above the causal diagonal at 0 - the silent-tile decisions
+ * of experiments/exp4b_mha6_instrumentation.py:91-111.
+ * status: device int32 word, set to PNFT_DEV_* if a pipeline wait times out
+ * (never cleared by the library).
+ * Replaces: src/triton_pnfirtau.py:313-443 (_flash_pn_fir_tau_fwd_kernel) and
+ * _FlashPnFirTauFn.forward (:814-898). */
+PNFT_API int pnft_flash_fwd(const void* q, const int64_t* sq, const void* k, const int64_t* sk,
+                   const void* v, const int64_t* sv, const float* tau, void* out,
+                   const int64_t* so, float* stat_m, float* stat_z, int32_t* stat_nmax,
+                   int64_t B, int64_t H, int64_t N, int64_t D, float scale, float gamma,
+                   int has_gamma, int causal, int dtype, int flags, uint8_t* tile_flags,
+                   int32_t* status, void* stream);
+
+/* Backward of pnft_flash_fwd. dout has strides sdo; dq/dk/dv (dtype of q)
+ * strides sdq/sdk/sdv. dtau: fp32[1], the tau gradient reduced in fp64 in a
+ * fixed order. workspace: pnft_flash_bwd_workspace_size(...) bytes (the fp32 dQ
+ * accumulator, per-row coefficients and per-tile tau partials).
+ * Replaces: src/triton_pnfirtau.py:445-621 (_flash_pn_fir_tau_bwd_kernel) and
+ * _FlashPnFirTauFn.backward (:900-968). */
+PNFT_API int pnft_flash_bwd(const void* q, const int64_t* sq, const void* k, const int64_t* sk,
+                   const void* v, const int64_t* sv, const float* tau, const void* out,
+                   const int64_t* so, const void* dout, const int64_t* sdo,
+                   const float* stat_m, const float* stat_z, const int32_t* stat_nmax,
+                   void* dq, const int64_t* sdq, void* dk, const int64_t* sdk, void* dv,
+                   const int64_t* sdv, float* dtau, void* workspace, size_t workspace_bytes,
+                   int64_t B, int64_t H, int64_t N, int64_t D, float scale, float gamma,
+                   int has_gamma, int causal, int dtype, int flags, int32_t* status,
+                   void* stream);
+
+PNFT_API size_t pnft_flash_bwd_workspace_size(int64_t B, int64_t H, int64_t N, int64_t D, int flags);
+
+/* Which kernel family pnft_flash_fwd / pnft_flash_bwd would launch for these
+ * arguments: 1 = sm_100a tcgen05/TMA kernels, 0 = generic SIMT kernels. */
+PNFT_API int pnft_flash_path(const void* q, const int64_t* sq, const void* k, const int64_t* sk,
+                    const void* v, const int64_t* sv, int64_t D, int dtype, int flags);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* PNFIRTAU_B200_H */

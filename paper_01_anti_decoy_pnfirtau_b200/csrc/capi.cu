@@ -1,0 +1,160 @@
+// C-ABI entry points of the flash op plus library-wide plumbing (version,
+// last-error message, device capabilities). Argument checking happens here so
+// the kernels can assume well-formed shapes.
+#include <stdarg.h>
+#include <stdio.h>
+#include <string.h>
+
+#include <atomic>
+
+#include "flash.cuh"
+
+namespace pnft {
+
+static thread_local char g_err[512] = "";
+
+void set_error(const char* fmt, ...) {
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(g_err, sizeof(g_err), fmt, ap);
+  va_end(ap);
+}
+
+int fail(int code, const char* fmt, ...) {
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(g_err, sizeof(g_err), fmt, ap);
+  va_end(ap);
+  return code;
+}
+
+static std::atomic<uint64_t> g_launches{0};
+
+int check_launch(const char* what, int nlaunch) {
+  const cudaError_t e = cudaGetLastError();
+  if (e == cudaSuccess) {
+    g_launches.fetch_add((uint64_t)nlaunch, std::memory_order_relaxed);
+    return PNFT_OK;
+  }
+  return fail(PNFT_ECUDA, "%s: %s (%s)", what, cudaGetErrorName(e), cudaGetErrorString(e));
+}
+
+}  // namespace pnft
+
+using namespace pnft;
+
+extern "C" uint64_t pnft_launch_count(void) { return g_launches.load(std::memory_order_relaxed); }
+
+extern "C" int pnft_version(void) { return 100; }
+
+extern "C" const char* pnft_last_error(void) { return g_err; }
+
+extern "C" int pnft_query_caps(int device, int* cc_major, int* cc_minor, int* sm_count, int* smem_optin_bytes,
+                               int* has_sm100a) {
+  cudaDeviceProp p;
+  const cudaError_t e = cudaGetDeviceProperties(&p, device);
+  if (e != cudaSuccess) return fail(PNFT_ECUDA, "query_caps: %s", cudaGetErrorString(e));
+  if (cc_major) *cc_major = p.major;
+  if (cc_minor) *cc_minor = p.minor;
+  if (sm_count) *sm_count = p.multiProcessorCount;
+  if (smem_optin_bytes) *smem_optin_bytes = (int)p.sharedMemPerBlockOptin;
+  if (has_sm100a) *has_sm100a = (p.major == 10 && p.minor == 0) ? 1 : 0;
+  return PNFT_OK;
+}
+
+static int fill_common(FlashArgs& a, const void* q, const int64_t* sq, const void* k, const int64_t* sk,
+                       const void* v, const int64_t* sv, const float* tau, int64_t B, int64_t H, int64_t N,
+                       int64_t D, float scale, float gamma, int has_gamma, int causal, int dtype, int flags,
+                       int32_t* status) {
+  memset(&a, 0, sizeof(a));
+  if (B < 0 || H < 0 || N < 0 || D < 0)
+    return fail(PNFT_EINVAL, "flash: negative size B=%lld H=%lld N=%lld D=%lld", (long long)B, (long long)H,
+                (long long)N, (long long)D);
+  if (dtype < PNFT_DTYPE_F32 || dtype > PNFT_DTYPE_F16) return fail(PNFT_EINVAL, "flash: unknown dtype %d", dtype);
+  if (D > 128) return fail(PNFT_EUNSUPPORTED, "flash: head dim %lld > 128 is not supported", (long long)D);
+  if (B * H > 65535LL * 1024) return fail(PNFT_EUNSUPPORTED, "flash: B*H = %lld too large", (long long)(B * H));
+  if (has_gamma && !(gamma > 0.f)) return fail(PNFT_EINVAL, "flash: has_gamma set with gamma <= 0");
+  if (!sq || !sk || !sv) return fail(PNFT_EINVAL, "flash: null stride array");
+  a.q = q; a.k = k; a.v = v; a.tau = tau;
+  for (int i = 0; i < 4; ++i) { a.sq[i] = sq[i]; a.sk[i] = sk[i]; a.sv[i] = sv[i]; }
+  a.B = B; a.H = H; a.N = N; a.D = D; a.scale = scale; a.gamma = gamma; a.has_gamma = has_gamma;
+  a.causal = causal; a.dtype = dtype; a.flags = flags; a.status = status;
+  return PNFT_OK;
+}
+
+static bool use_sm100(const FlashArgs& a) {
+  if (a.flags & PNFT_FLASH_FORCE_GENERIC) return false;
+  return flash_sm100_supported(a);
+}
+
+extern "C" int pnft_flash_path(const void* q, const int64_t* sq, const void* k, const int64_t* sk, const void* v,
+                               const int64_t* sv, int64_t D, int dtype, int flags) {
+  FlashArgs a;
+  float tau_dummy = 0.f;
+  if (fill_common(a, q, sq, k, sk, v, sv, &tau_dummy, 1, 1, 1, D, 1.f, 0.5f, 1, 1, dtype, flags, nullptr)) return 0;
+  return use_sm100(a) ? 1 : 0;
+}
+
+extern "C" int pnft_flash_fwd(const void* q, const int64_t* sq, const void* k, const int64_t* sk, const void* v,
+                              const int64_t* sv, const float* tau, void* out, const int64_t* so, float* stat_m,
+                              float* stat_z, int32_t* stat_nmax, int64_t B, int64_t H, int64_t N, int64_t D,
+                              float scale, float gamma, int has_gamma, int causal, int dtype, int flags,
+                              uint8_t* tile_flags, int32_t* status, void* stream) {
+  FlashArgs a;
+  int rc = fill_common(a, q, sq, k, sk, v, sv, tau, B, H, N, D, scale, gamma, has_gamma, causal, dtype, flags, status);
+  if (rc) return rc;
+  a.tile_flags = tile_flags;
+  if (B * H * N == 0) return PNFT_OK;
+  if (D == 0) return fail(PNFT_EINVAL, "flash fwd: head dim 0");
+  if (!q || !k || !v || !tau || !out || !so || !stat_m || !stat_z || !stat_nmax)
+    return fail(PNFT_EINVAL, "flash fwd: null pointer");
+  a.out = out;
+  for (int i = 0; i < 4; ++i) a.so[i] = so[i];
+  a.stat_m = stat_m; a.stat_z = stat_z; a.stat_nmax = stat_nmax;
+  cudaStream_t st = as_stream(stream);
+  if (use_sm100(a)) return flash_fwd_sm100(a, st);
+  return flash_fwd_generic(a, st);
+}
+
+extern "C" size_t pnft_flash_bwd_workspace_size(int64_t B, int64_t H, int64_t N, int64_t D, int flags) {
+  (void)flags;
+  if (B <= 0 || H <= 0 || N <= 0 || D <= 0) return 0;
+  return bwd_workspace_layout(B, H, N, D).total;
+}
+
+extern "C" int pnft_flash_bwd(const void* q, const int64_t* sq, const void* k, const int64_t* sk, const void* v,
+                              const int64_t* sv, const float* tau, const void* out, const int64_t* so,
+                              const void* dout, const int64_t* sdo, const float* stat_m, const float* stat_z,
+                              const int32_t* stat_nmax, void* dq, const int64_t* sdq, void* dk,
+                              const int64_t* sdk, void* dv, const int64_t* sdv, float* dtau, void* workspace,
+                              size_t workspace_bytes, int64_t B, int64_t H, int64_t N, int64_t D, float scale,
+                              float gamma, int has_gamma, int causal, int dtype, int flags, int32_t* status,
+                              void* stream) {
+  FlashArgs a;
+  int rc = fill_common(a, q, sq, k, sk, v, sv, tau, B, H, N, D, scale, gamma, has_gamma, causal, dtype, flags, status);
+  if (rc) return rc;
+  cudaStream_t st = as_stream(stream);
+  if (!dtau) return fail(PNFT_EINVAL, "flash bwd: null dtau");
+  if (B * H * N == 0) {
+    if (cudaMemsetAsync(dtau, 0, sizeof(float), st) != cudaSuccess) return check_launch("flash bwd: dtau memset");
+    return PNFT_OK;
+  }
+  if (D == 0) return fail(PNFT_EINVAL, "flash bwd: head dim 0");
+  if (!q || !k || !v || !tau || !out || !so || !dout || !sdo || !stat_m || !stat_z || !stat_nmax || !dq || !sdq ||
+      !dk || !sdk || !dv || !sdv)
+    return fail(PNFT_EINVAL, "flash bwd: null pointer");
+  const BwdWorkspace w = bwd_workspace_layout(B, H, N, D);
+  if (!workspace || workspace_bytes < w.total)
+    return fail(PNFT_EINVAL, "flash bwd: workspace of %zu bytes < required %zu", workspace_bytes, w.total);
+  if (reinterpret_cast<uintptr_t>(workspace) % 256 != 0) return fail(PNFT_EINVAL, "flash bwd: workspace not 256-byte aligned");
+  a.out_c = out; a.dout = dout; a.dq = dq; a.dk = dk; a.dv = dv; a.dtau = dtau;
+  for (int i = 0; i < 4; ++i) { a.so[i] = so[i]; a.sdo[i] = sdo[i]; a.sdq[i] = sdq[i]; a.sdk[i] = sdk[i]; a.sdv[i] = sdv[i]; }
+  a.stat_m = const_cast<float*>(stat_m); a.stat_z = const_cast<float*>(stat_z);
+  a.stat_nmax = const_cast<int32_t*>(stat_nmax);
+  char* ws = static_cast<char*>(workspace);
+  a.dq_acc = reinterpret_cast<float*>(ws + w.off_dq);
+  a.coef = reinterpret_cast<float4*>(ws + w.off_coef);
+  a.dtau_part = reinterpret_cast<float*>(ws + w.off_part);
+  if (use_sm100(a)) return flash_bwd_sm100(a, st);
+  return flash_bwd_generic(a, st);
+}

@@ -1,0 +1,311 @@
+// Depthwise causal FIR along the sequence axis of x[B,N,C] (and its transpose
+// and tap gradient). HBM-bound: every element is read once and written once;
+// threads own 16-byte channel vectors so a warp moves 512 contiguous bytes per
+// row, and each thread walks FIR_TN consecutive rows keeping the K-1 previous
+// rows in registers (the halo rows are re-read from L1/L2, never from DRAM
+// twice in practice because neighbouring row chunks run in the same block).
+//
+// Semantics follow the reference kernels src/triton_pnfirtau.py:40-135:
+//   fwd  y[b,n,c]  = sum_{u=0}^{K-1} taps[K-1-u] * x[b,n-u,c]   (x[<0] = 0)
+//   bwd  gx[b,n,c] = sum_{u=0}^{K-1} taps[K-1-u] * gy[b,n+u,c]  (gy[>=N] = 0)
+// with fp32 accumulation and the output in the input dtype. The tap gradient
+// (absent in the reference, whose taps are a non-trainable buffer,
+// src/triton_pnfirtau.py:682) is dtaps[K-1-u] = sum gy[b,n,c] * x[b,n-u,c].
+#include <stdarg.h>
+#include <stdio.h>
+
+#include "common.cuh"
+
+namespace pnft {
+
+constexpr int FIR_TN = 8;         // consecutive rows per thread
+constexpr int FIR_MAX_TAPS = 64;  // runtime-K kernels
+constexpr int FIR_THREADS = 256;
+constexpr int FIR_DTAPS_MAX_BLOCKS = 512;
+
+template <typename T, int VEC>
+__device__ __forceinline__ void ld_vec(const T* p, float (&f)[VEC]) {
+  if constexpr (VEC * sizeof(T) == 16) {
+    uint4 r = __ldg(reinterpret_cast<const uint4*>(p));
+    const T* e = reinterpret_cast<const T*>(&r);
+#pragma unroll
+    for (int i = 0; i < VEC; ++i) f[i] = to_f32<T>(e[i]);
+  } else {
+#pragma unroll
+    for (int i = 0; i < VEC; ++i) f[i] = to_f32<T>(p[i]);
+  }
+}
+
+template <typename T, int VEC>
+__device__ __forceinline__ void st_vec(T* p, const float (&f)[VEC]) {
+  if constexpr (VEC * sizeof(T) == 16) {
+    uint4 r;
+    T* e = reinterpret_cast<T*>(&r);
+#pragma unroll
+    for (int i = 0; i < VEC; ++i) e[i] = from_f32<T>(f[i]);
+    *reinterpret_cast<uint4*>(p) = r;
+  } else {
+#pragma unroll
+    for (int i = 0; i < VEC; ++i) p[i] = from_f32<T>(f[i]);
+  }
+}
+
+struct FirGeom {
+  const void* in;
+  void* out;
+  int64_t sib, sin, sic, sob, son, soc;
+  int64_t B, N, C;
+};
+
+// Sliding-window kernel with compile-time tap count. DIR = +1: causal fwd
+// (window over past rows), DIR = -1: transpose (window over future rows).
+template <typename T, int VEC, int K, int DIR>
+__global__ void __launch_bounds__(FIR_THREADS) fir_sliding_kernel(FirGeom g, const float* __restrict__ taps) {
+  const T* __restrict__ x = static_cast<const T*>(g.in);
+  T* __restrict__ y = static_cast<T*>(g.out);
+  float h[K];  // h[u] multiplies the input at lag u
+#pragma unroll
+  for (int u = 0; u < K; ++u) h[u] = __ldg(taps + (K - 1 - u));
+  const int64_t CV = (g.C + VEC - 1) / VEC;
+  const int64_t chunks = (g.N + FIR_TN - 1) / FIR_TN;
+  const int64_t items = g.B * chunks * CV;
+  for (int64_t it = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; it < items;
+       it += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t cv = it % CV;
+    const int64_t rest = it / CV;
+    const int64_t chunk = rest % chunks;
+    const int64_t b = rest / chunks;
+    const int64_t c0 = cv * VEC;
+    const T* xb = x + b * g.sib + c0 * g.sic;
+    T* yb = y + b * g.sob + c0 * g.soc;
+    float win[K][VEC];
+    const int64_t n_first = chunk * FIR_TN;
+    const int64_t n_last = min(n_first + FIR_TN, g.N) - 1;
+    if (DIR > 0) {
+      // win[u] = x[n-u]; prime lags 1..K-1 for n = n_first
+#pragma unroll
+      for (int u = 1; u < K; ++u) {
+        const int64_t n = n_first - u;
+        if (n >= 0) {
+          if constexpr (VEC > 1) ld_vec<T, VEC>(xb + n * g.sin, win[u]);
+          else win[u][0] = to_f32<T>(xb[n * g.sin]);
+        } else {
+#pragma unroll
+          for (int v = 0; v < VEC; ++v) win[u][v] = 0.f;
+        }
+      }
+#pragma unroll
+      for (int t = 0; t < FIR_TN; ++t) {
+        const int64_t n = n_first + t;
+        if (n <= n_last) {
+          if constexpr (VEC > 1) ld_vec<T, VEC>(xb + n * g.sin, win[0]);
+          else win[0][0] = to_f32<T>(xb[n * g.sin]);
+          float acc[VEC];
+#pragma unroll
+          for (int v = 0; v < VEC; ++v) {
+            float a = win[0][v] * h[0];
+#pragma unroll
+            for (int u = 1; u < K; ++u) a = fmaf(win[u][v], h[u], a);
+            acc[v] = a;
+          }
+          if constexpr (VEC > 1) st_vec<T, VEC>(yb + n * g.son, acc);
+          else yb[n * g.son] = from_f32<T>(acc[0]);
+#pragma unroll
+          for (int u = K - 1; u > 0; --u)
+#pragma unroll
+            for (int v = 0; v < VEC; ++v) win[u][v] = win[u - 1][v];
+        }
+      }
+    } else {
+      // win[u] = gy[n+u]; prime lags 1..K-1 for n = n_last
+#pragma unroll
+      for (int u = 1; u < K; ++u) {
+        const int64_t n = n_last + u;
+        if (n < g.N) {
+          if constexpr (VEC > 1) ld_vec<T, VEC>(xb + n * g.sin, win[u]);
+          else win[u][0] = to_f32<T>(xb[n * g.sin]);
+        } else {
+#pragma unroll
+          for (int v = 0; v < VEC; ++v) win[u][v] = 0.f;
+        }
+      }
+#pragma unroll
+      for (int t = FIR_TN - 1; t >= 0; --t) {
+        const int64_t n = n_first + t;
+        if (n <= n_last) {
+          if constexpr (VEC > 1) ld_vec<T, VEC>(xb + n * g.sin, win[0]);
+          else win[0][0] = to_f32<T>(xb[n * g.sin]);
+          float acc[VEC];
+#pragma unroll
+          for (int v = 0; v < VEC; ++v) {
+            float a = win[0][v] * h[0];
+#pragma unroll
+            for (int u = 1; u < K; ++u) a = fmaf(win[u][v], h[u], a);
+            acc[v] = a;
+          }
+          if constexpr (VEC > 1) st_vec<T, VEC>(yb + n * g.son, acc);
+          else yb[n * g.son] = from_f32<T>(acc[0]);
+#pragma unroll
+          for (int u = K - 1; u > 0; --u)
+#pragma unroll
+            for (int v = 0; v < VEC; ++v) win[u][v] = win[u - 1][v];
+        }
+      }
+    }
+  }
+}
+
+// Any tap count (1..FIR_MAX_TAPS), any strides: one output element per thread.
+template <typename T, int DIR>
+__global__ void __launch_bounds__(FIR_THREADS) fir_generic_kernel(FirGeom g, const float* __restrict__ taps, int K) {
+  const T* __restrict__ x = static_cast<const T*>(g.in);
+  T* __restrict__ y = static_cast<T*>(g.out);
+  const int64_t total = g.B * g.N * g.C;
+  for (int64_t it = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; it < total;
+       it += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t c = it % g.C;
+    const int64_t n = (it / g.C) % g.N;
+    const int64_t b = it / (g.C * g.N);
+    const T* xb = x + b * g.sib + c * g.sic;
+    float a = 0.f;
+    for (int u = 0; u < K; ++u) {
+      const int64_t src = DIR > 0 ? n - u : n + u;  // causal: past rows; transpose: future rows
+      if (src < 0 || src >= g.N) continue;
+      a = fmaf(to_f32<T>(xb[src * g.sin]), __ldg(taps + (K - 1 - u)), a);
+    }
+    y[b * g.sob + n * g.son + c * g.soc] = from_f32<T>(a);
+  }
+}
+
+// Tap gradient, one lag per grid row: partial[u][blockIdx.x] =
+// sum over this block's elements of gy[b,n,c] * x[b,n-u,c].
+template <typename T>
+__global__ void __launch_bounds__(FIR_THREADS) fir_dtaps_partial_kernel(
+    const T* __restrict__ gy, int64_t sgb, int64_t sgn, int64_t sgc, const T* __restrict__ x,
+    int64_t sxb, int64_t sxn, int64_t sxc, int64_t B, int64_t N, int64_t C, float* __restrict__ partial) {
+  __shared__ float red[FIR_THREADS / 32];
+  const int u = blockIdx.y;
+  const int64_t total = B * N * C;
+  float acc = 0.f;
+  for (int64_t it = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; it < total;
+       it += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t c = it % C;
+    const int64_t n = (it / C) % N;
+    const int64_t b = it / (C * N);
+    if (n - u < 0) continue;
+    acc = fmaf(to_f32<T>(gy[b * sgb + n * sgn + c * sgc]), to_f32<T>(x[b * sxb + (n - u) * sxn + c * sxc]), acc);
+  }
+  const float s = block_sum(acc, red);
+  if (threadIdx.x == 0) partial[(int64_t)u * gridDim.x + blockIdx.x] = s;
+}
+
+// dtaps[K-1-u] = fp64 sum over the partials of lag u, in block order.
+__global__ void fir_dtaps_final_kernel(const float* __restrict__ partial, int nblk, int K, float* __restrict__ dtaps) {
+  const int u = threadIdx.x;
+  if (u >= K) return;
+  double s = 0.0;
+  for (int i = 0; i < nblk; ++i) s += (double)partial[(int64_t)u * nblk + i];
+  dtaps[K - 1 - u] = (float)s;
+}
+
+static int grid_for(int64_t items) {
+  int64_t g = (items + FIR_THREADS - 1) / FIR_THREADS;
+  if (g < 1) g = 1;
+  if (g > (int64_t)1 << 20) g = (int64_t)1 << 20;
+  return (int)g;
+}
+
+template <typename T>
+static bool vec_ok(const FirGeom& g) {
+  constexpr int VEC = 16 / sizeof(T);
+  const uintptr_t a = reinterpret_cast<uintptr_t>(g.in), b = reinterpret_cast<uintptr_t>(g.out);
+  return g.sic == 1 && g.soc == 1 && g.C % VEC == 0 && a % 16 == 0 && b % 16 == 0 && g.sin % VEC == 0 &&
+         g.sib % VEC == 0 && g.son % VEC == 0 && g.sob % VEC == 0;
+}
+
+template <typename T, int DIR>
+static int fir_launch(const FirGeom& g, const float* taps, int K, cudaStream_t st) {
+  constexpr int VEC = 16 / sizeof(T);
+  if (K == 7) {
+    const int64_t chunks = (g.N + FIR_TN - 1) / FIR_TN;
+    if (vec_ok<T>(g)) {
+      const int64_t items = g.B * chunks * (g.C / VEC);
+      fir_sliding_kernel<T, VEC, 7, DIR><<<grid_for(items), FIR_THREADS, 0, st>>>(g, taps);
+    } else {
+      const int64_t items = g.B * chunks * g.C;
+      fir_sliding_kernel<T, 1, 7, DIR><<<grid_for(items), FIR_THREADS, 0, st>>>(g, taps);
+    }
+  } else {
+    fir_generic_kernel<T, DIR><<<grid_for(g.B * g.N * g.C), FIR_THREADS, 0, st>>>(g, taps, K);
+  }
+  return check_launch(DIR > 0 ? "fir fwd" : "fir bwd");
+}
+
+static int64_t dtaps_blocks(int64_t B, int64_t N, int64_t C) {
+  int64_t g = (B * N * C + FIR_THREADS - 1) / FIR_THREADS;
+  if (g < 1) g = 1;
+  if (g > FIR_DTAPS_MAX_BLOCKS) g = FIR_DTAPS_MAX_BLOCKS;
+  return g;
+}
+
+}  // namespace pnft
+
+using namespace pnft;
+
+extern "C" size_t pnft_fir_bwd_workspace_size(int64_t B, int64_t N, int64_t C, int ntaps) {
+  if (B <= 0 || N <= 0 || C <= 0 || ntaps <= 0) return 0;
+  return (size_t)dtaps_blocks(B, N, C) * (size_t)ntaps * sizeof(float);
+}
+
+static int fir_check_common(const void* in, const void* out, const float* taps, int ntaps, int64_t B,
+                            int64_t N, int64_t C, bool need_out) {
+  if (B < 0 || N < 0 || C < 0) return fail(PNFT_EINVAL, "fir: negative size B=%lld N=%lld C=%lld", (long long)B, (long long)N, (long long)C);
+  if (ntaps < 1 || ntaps > FIR_MAX_TAPS) return fail(PNFT_EINVAL, "fir: ntaps=%d outside [1,%d]", ntaps, FIR_MAX_TAPS);
+  if (!in || (need_out && !out) || !taps) return fail(PNFT_EINVAL, "fir: null pointer");
+  return PNFT_OK;
+}
+
+extern "C" int pnft_fir_fwd(const void* x, int64_t sxb, int64_t sxn, int64_t sxc, const float* taps, int ntaps,
+                            void* y, int64_t syb, int64_t syn, int64_t syc, int64_t B, int64_t N, int64_t C,
+                            int dtype, void* stream) {
+  if (B == 0 || N == 0 || C == 0) return PNFT_OK;
+  int rc = fir_check_common(x, y, taps, ntaps, B, N, C, true);
+  if (rc) return rc;
+  FirGeom g{x, y, sxb, sxn, sxc, syb, syn, syc, B, N, C};
+  PNFT_DISPATCH_DTYPE(dtype, T, return fir_launch<T, +1>(g, taps, ntaps, as_stream(stream)));
+  return PNFT_OK;
+}
+
+extern "C" int pnft_fir_bwd(const void* gy, int64_t sgb, int64_t sgn, int64_t sgc, const float* taps, int ntaps,
+                            void* gx, int64_t sxb, int64_t sxn, int64_t sxc, const void* x, int64_t s0b,
+                            int64_t s0n, int64_t s0c, float* dtaps, void* workspace, size_t workspace_bytes,
+                            int64_t B, int64_t N, int64_t C, int dtype, void* stream) {
+  int rc = fir_check_common(gy, gx, taps, ntaps, B, N, C, false);
+  if (rc) return rc;
+  if (!gx && !x) return fail(PNFT_EINVAL, "fir bwd: nothing to compute (gx and x are both NULL)");
+  cudaStream_t st = as_stream(stream);
+  if (x) {
+    if (!dtaps) return fail(PNFT_EINVAL, "fir bwd: x given but dtaps is NULL");
+    if (B == 0 || N == 0 || C == 0) {
+      if (cudaMemsetAsync(dtaps, 0, sizeof(float) * ntaps, st) != cudaSuccess) return check_launch("fir dtaps memset");
+    } else {
+      const size_t need = pnft_fir_bwd_workspace_size(B, N, C, ntaps);
+      if (!workspace || workspace_bytes < need)
+        return fail(PNFT_EINVAL, "fir bwd: workspace of %zu bytes < required %zu", workspace_bytes, need);
+      const int nblk = (int)dtaps_blocks(B, N, C);
+      float* part = static_cast<float*>(workspace);
+      PNFT_DISPATCH_DTYPE(dtype, T, {
+        fir_dtaps_partial_kernel<T><<<dim3(nblk, ntaps), FIR_THREADS, 0, st>>>(
+            static_cast<const T*>(gy), sgb, sgn, sgc, static_cast<const T*>(x), s0b, s0n, s0c, B, N, C, part);
+      });
+      fir_dtaps_final_kernel<<<1, FIR_MAX_TAPS, 0, st>>>(part, nblk, ntaps, dtaps);
+      rc = check_launch("fir dtaps", 2);
+      if (rc) return rc;
+    }
+  }
+  if (gx && B > 0 && N > 0 && C > 0) {
+    FirGeom g{gy, gx, sgb, sgn, sgc, sxb, sxn, sxc, B, N, C};
+    PNFT_DISPATCH_DTYPE(dtype, T, return fir_launch<T, -1>(g, taps, ntaps, st));
+  }
+  return PNFT_OK;
+}

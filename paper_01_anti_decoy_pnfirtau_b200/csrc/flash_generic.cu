@@ -1,0 +1,478 @@
+// Generic (SIMT, fp32-FMA) flash pn_fir_tau kernels: any dtype, any strides,
+// head dim D <= 128, any N. They serve every shape the tcgen05 kernels do not
+// (fp32 inputs for the reference's fp32 parity harness, D of 16/32, odd
+// strides) and define the arithmetic the fast kernels are checked against.
+//
+// Forward (src/triton_pnfirtau.py:313-443), per 64-query block:
+//   for each 64-key tile j <= the diagonal (causal):
+//     S = Q K^T ; s = S*scale - tau ; u = relu(s) on col <= row
+//     if max(u) over the tile <= 0: skip (no u^10, no V load, no PV)
+//     peak' = max(peak, rowmax u); ties counted against peak'; mass += sum u^10
+//     acc += u^10 V
+//   O = acc * gate/(mass+1e-12), gate = peak/(peak+gamma) (1 without gamma, 0 if silent)
+// Backward (src/triton_pnfirtau.py:445-621), per 64-key block, over query
+// blocks at or below the diagonal: recompute S and u, W = u^10*gate/z,
+// dV += W^T dO, dP = dO V^T, du = 10*gate/z*u^9*(dP - D) + [u==peak]*tie,
+// dS = du*scale, dK += dS^T Q, dQ += dS K (fp32 atomics), dtau -= sum du.
+// D = <dO,O>/gate and the tie coefficient are per-row values computed once by
+// flash_bwd_prep.
+//
+// S is recomputed in the backward by the same `tile_dot` routine (same FMA
+// order), so u == peak identifies exactly the forward's maxima.
+#include "flash.cuh"
+
+namespace pnft {
+
+constexpr int GB = 64;        // query and key tile
+constexpr int GTHREADS = 256; // 16 row groups x 16 column groups
+
+template <int DP>
+struct GenSmem {
+  static constexpr int LD = DP + 1;  // padded row: conflict-free row and column walks
+  static constexpr int TILE = GB * LD;
+  static constexpr int LDP = GB + 1;
+  static constexpr size_t fwd_bytes = (size_t)(3 * TILE + GB * LDP) * sizeof(float);
+  static constexpr size_t bwd_bytes = (size_t)(4 * TILE + 2 * GB * LDP + 4 * GB) * sizeof(float);
+};
+
+// dst[r][e] (row stride ld) = src[n0 + r, e] for r < 64, e < DP; zero outside N/D.
+template <typename T, int DP>
+__device__ __forceinline__ void load_tile(float* __restrict__ dst, const T* __restrict__ src, int64_t s_n,
+                                          int64_t s_d, int64_t n0, int64_t N, int D) {
+  constexpr int LD = DP + 1;
+  for (int idx = threadIdx.x; idx < GB * DP; idx += GTHREADS) {
+    const int r = idx / DP, e = idx % DP;
+    const int64_t n = n0 + r;
+    float v = 0.f;
+    if (n < N && e < D) v = to_f32<T>(src[n * s_n + e * s_d]);
+    dst[r * LD + e] = v;
+  }
+}
+
+// acc[ii][jj] = sum_e A[rg+16ii][e] * Bm[cg+16jj][e]  (both row-major, ld = DP+1)
+template <int DP>
+__device__ __forceinline__ void tile_dot(float (&acc)[4][4], const float* __restrict__ A,
+                                         const float* __restrict__ Bm, int rg, int cg) {
+  constexpr int LD = DP + 1;
+#pragma unroll
+  for (int ii = 0; ii < 4; ++ii)
+#pragma unroll
+    for (int jj = 0; jj < 4; ++jj) acc[ii][jj] = 0.f;
+#pragma unroll 8
+  for (int e = 0; e < DP; ++e) {
+    float a[4], bv[4];
+#pragma unroll
+    for (int ii = 0; ii < 4; ++ii) a[ii] = A[(rg + 16 * ii) * LD + e];
+#pragma unroll
+    for (int jj = 0; jj < 4; ++jj) bv[jj] = Bm[(cg + 16 * jj) * LD + e];
+#pragma unroll
+    for (int ii = 0; ii < 4; ++ii)
+#pragma unroll
+      for (int jj = 0; jj < 4; ++jj) acc[ii][jj] = fmaf(a[ii], bv[jj], acc[ii][jj]);
+  }
+}
+
+__device__ __forceinline__ float pow10f_(float u) {
+  const float u2 = u * u, u4 = u2 * u2;
+  return u4 * u4 * u2;
+}
+
+template <typename T, int DP>
+__global__ void __launch_bounds__(GTHREADS) flash_fwd_generic_kernel(FlashArgs a) {
+  extern __shared__ float smem[];
+  using SM = GenSmem<DP>;
+  constexpr int LD = SM::LD, LDP = SM::LDP, NJ = DP / 16;
+  float* sQ = smem;
+  float* sK = sQ + SM::TILE;
+  float* sV = sK + SM::TILE;
+  float* sP = sV + SM::TILE;
+  const int tid = threadIdx.x, rg = tid >> 4, cg = tid & 15;
+  const int64_t q0 = (int64_t)blockIdx.x * GB;
+  const int64_t bh = blockIdx.y, b = bh / a.H, h = bh % a.H;
+  const int D = (int)a.D;
+  const int64_t N = a.N;
+  const T* Q = static_cast<const T*>(a.q) + b * a.sq[0] + h * a.sq[1];
+  const T* K = static_cast<const T*>(a.k) + b * a.sk[0] + h * a.sk[1];
+  const T* V = static_cast<const T*>(a.v) + b * a.sv[0] + h * a.sv[1];
+  load_tile<T, DP>(sQ, Q, a.sq[2], a.sq[3], q0, N, D);
+  const float tau = __ldg(a.tau);
+  float peak[4], mass[4], acc[4][NJ];
+  int nmax[4];
+#pragma unroll
+  for (int ii = 0; ii < 4; ++ii) {
+    peak[ii] = 0.f; mass[ii] = 0.f; nmax[ii] = 0;
+#pragma unroll
+    for (int jj = 0; jj < NJ; ++jj) acc[ii][jj] = 0.f;
+  }
+  const int64_t hi = a.causal ? min(q0 + GB, N) : N;
+  for (int64_t k0 = 0; k0 < hi; k0 += GB) {
+    __syncthreads();
+    load_tile<T, DP>(sK, K, a.sk[2], a.sk[3], k0, N, D);
+    __syncthreads();
+    float u[4][4];
+    tile_dot<DP>(u, sQ, sK, rg, cg);
+    int live = 0;
+#pragma unroll
+    for (int ii = 0; ii < 4; ++ii) {
+      const int64_t row = q0 + rg + 16 * ii;
+#pragma unroll
+      for (int jj = 0; jj < 4; ++jj) {
+        const int64_t col = k0 + cg + 16 * jj;
+        const bool valid = row < N && col < N && (!a.causal || col <= row);
+        const float s = u[ii][jj] * a.scale - tau;
+        u[ii][jj] = (valid && s > 0.f) ? s : 0.f;
+        live |= u[ii][jj] > 0.f;
+      }
+    }
+    if (!__syncthreads_or(live)) continue;  // silent tile: no u^10, no V load, no PV
+    if (a.tile_flags && tid == 0) {
+      const int64_t nt = (N + GB - 1) / GB;
+      a.tile_flags[(bh * nt + blockIdx.x) * nt + k0 / GB] = 1;
+    }
+#pragma unroll
+    for (int ii = 0; ii < 4; ++ii) {
+      float tmax = fmaxf(fmaxf(u[ii][0], u[ii][1]), fmaxf(u[ii][2], u[ii][3]));
+      tmax = group_max<16>(tmax);
+      const float np = fmaxf(peak[ii], tmax);
+      int cnt = 0;
+      float rm = 0.f;
+#pragma unroll
+      for (int jj = 0; jj < 4; ++jj) {
+        cnt += (np > 0.f && u[ii][jj] == np) ? 1 : 0;
+        const float pw = pow10f_(u[ii][jj]);
+        rm += pw;
+        sP[(rg + 16 * ii) * LDP + cg + 16 * jj] = pw;
+      }
+      cnt = group_sum_i<16>(cnt);
+      rm = group_sum<16>(rm);
+      nmax[ii] = np > peak[ii] ? cnt : nmax[ii] + cnt;
+      peak[ii] = np;
+      mass[ii] += rm;
+    }
+    load_tile<T, DP>(sV, V, a.sv[2], a.sv[3], k0, N, D);
+    __syncthreads();
+#pragma unroll 4
+    for (int j = 0; j < GB; ++j) {
+      float p[4], vv[NJ];
+#pragma unroll
+      for (int ii = 0; ii < 4; ++ii) p[ii] = sP[(rg + 16 * ii) * LDP + j];
+#pragma unroll
+      for (int jj = 0; jj < NJ; ++jj) vv[jj] = sV[j * LD + cg + 16 * jj];
+#pragma unroll
+      for (int ii = 0; ii < 4; ++ii)
+#pragma unroll
+        for (int jj = 0; jj < NJ; ++jj) acc[ii][jj] = fmaf(p[ii], vv[jj], acc[ii][jj]);
+    }
+  }
+  T* O = static_cast<T*>(a.out) + b * a.so[0] + h * a.so[1];
+#pragma unroll
+  for (int ii = 0; ii < 4; ++ii) {
+    const int64_t row = q0 + rg + 16 * ii;
+    if (row >= N) continue;
+    const float z = mass[ii] + 1e-12f;
+    float gate = 0.f;
+    if (peak[ii] > 0.f) gate = a.has_gamma ? peak[ii] / (peak[ii] + a.gamma) : 1.f;
+    const float so = gate / z;
+#pragma unroll
+    for (int jj = 0; jj < NJ; ++jj) {
+      const int e = cg + 16 * jj;
+      if (e < D) O[row * a.so[2] + e * a.so[3]] = from_f32<T>(acc[ii][jj] * so);
+    }
+    if (cg == 0) {
+      const int64_t si = bh * N + row;
+      a.stat_m[si] = peak[ii];
+      a.stat_z[si] = z;
+      a.stat_nmax[si] = nmax[ii];
+    }
+  }
+}
+
+// Per query row: coef = {peak, gate/z, D = <dO,O>/gate (0 if gate == 0), tie}
+// with tie = D*gamma/(peak+gamma)^2/Nmax (0 without gamma or for silent rows).
+template <typename T>
+__global__ void __launch_bounds__(256) flash_bwd_prep_kernel(FlashArgs a) {
+  const int64_t rows = a.B * a.H * a.N;
+  const int lane = threadIdx.x & 31;
+  for (int64_t r = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5; r < rows;
+       r += ((int64_t)gridDim.x * blockDim.x) >> 5) {
+    const int64_t n = r % a.N, bh = r / a.N, b = bh / a.H, h = bh % a.H;
+    const T* O = static_cast<const T*>(a.out_c) + b * a.so[0] + h * a.so[1] + n * a.so[2];
+    const T* dO = static_cast<const T*>(a.dout) + b * a.sdo[0] + h * a.sdo[1] + n * a.sdo[2];
+    float dot = 0.f;
+    for (int e = lane; e < a.D; e += 32) dot = fmaf(to_f32<T>(dO[e * a.sdo[3]]), to_f32<T>(O[e * a.so[3]]), dot);
+    dot = group_sum<32>(dot);
+    if (lane == 0) {
+      const float peak = a.stat_m[r], z = a.stat_z[r];
+      float gate = 0.f;
+      if (peak > 0.f) gate = a.has_gamma ? peak / (peak + a.gamma) : 1.f;
+      const float Dg = gate > 0.f ? dot / gate : 0.f;
+      float tie = 0.f;
+      if (a.has_gamma && peak > 0.f) {
+        const float pg = peak + a.gamma;
+        tie = Dg * (a.gamma / (pg * pg)) / (float)a.stat_nmax[r];
+      }
+      a.coef[r] = make_float4(peak, gate / z, Dg, tie);
+    }
+  }
+}
+
+template <typename T, int DP>
+__global__ void __launch_bounds__(GTHREADS) flash_bwd_generic_kernel(FlashArgs a) {
+  extern __shared__ float smem[];
+  using SM = GenSmem<DP>;
+  constexpr int LD = SM::LD, LDP = SM::LDP, NJ = DP / 16;
+  float* sK = smem;
+  float* sV = sK + SM::TILE;
+  float* sQ = sV + SM::TILE;
+  float* sdO = sQ + SM::TILE;
+  float* sW = sdO + SM::TILE;
+  float* sdS = sW + GB * LDP;
+  float4* sC = reinterpret_cast<float4*>(sdS + GB * LDP);
+  const int tid = threadIdx.x, rg = tid >> 4, cg = tid & 15;
+  const int64_t kt = blockIdx.x, k0 = kt * GB;
+  const int64_t bh = blockIdx.y, b = bh / a.H, h = bh % a.H;
+  const int D = (int)a.D;
+  const int64_t N = a.N;
+  const T* Q = static_cast<const T*>(a.q) + b * a.sq[0] + h * a.sq[1];
+  const T* K = static_cast<const T*>(a.k) + b * a.sk[0] + h * a.sk[1];
+  const T* V = static_cast<const T*>(a.v) + b * a.sv[0] + h * a.sv[1];
+  const T* dO = static_cast<const T*>(a.dout) + b * a.sdo[0] + h * a.sdo[1];
+  float* dQa = a.dq_acc + bh * N * a.D;
+  load_tile<T, DP>(sK, K, a.sk[2], a.sk[3], k0, N, D);
+  load_tile<T, DP>(sV, V, a.sv[2], a.sv[3], k0, N, D);
+  const float tau = __ldg(a.tau);
+  float dk[4][NJ], dv[4][NJ];
+#pragma unroll
+  for (int ii = 0; ii < 4; ++ii)
+#pragma unroll
+    for (int jj = 0; jj < NJ; ++jj) dk[ii][jj] = dv[ii][jj] = 0.f;
+  float dtau = 0.f;
+  const int64_t lo = a.causal ? k0 : 0;
+  for (int64_t q0 = lo; q0 < N; q0 += GB) {
+    __syncthreads();
+    int live_row = 0;
+    if (tid < GB) {
+      const int64_t row = q0 + tid;
+      float4 c = make_float4(0.f, 0.f, 0.f, 0.f);
+      if (row < N) c = a.coef[bh * N + row];
+      sC[tid] = c;
+      live_row = c.x > 0.f;
+    }
+    if (!__syncthreads_or(live_row)) continue;  // every query row of the block is silent
+    load_tile<T, DP>(sQ, Q, a.sq[2], a.sq[3], q0, N, D);
+    __syncthreads();
+    float u[4][4];
+    tile_dot<DP>(u, sQ, sK, rg, cg);
+    int live = 0;
+#pragma unroll
+    for (int ii = 0; ii < 4; ++ii) {
+      const int64_t row = q0 + rg + 16 * ii;
+#pragma unroll
+      for (int jj = 0; jj < 4; ++jj) {
+        const int64_t col = k0 + cg + 16 * jj;
+        const bool valid = row < N && col < N && (!a.causal || col <= row);
+        const float s = u[ii][jj] * a.scale - tau;
+        u[ii][jj] = (valid && s > 0.f) ? s : 0.f;
+        live |= u[ii][jj] > 0.f;
+      }
+    }
+    if (!__syncthreads_or(live)) continue;  // silent tile
+    load_tile<T, DP>(sdO, dO, a.sdo[2], a.sdo[3], q0, N, D);
+    __syncthreads();
+    float dp[4][4];
+    tile_dot<DP>(dp, sdO, sV, rg, cg);
+#pragma unroll
+    for (int ii = 0; ii < 4; ++ii) {
+      const int r = rg + 16 * ii;
+      const float4 c = sC[r];  // peak, gate/z, D, tie
+#pragma unroll
+      for (int jj = 0; jj < 4; ++jj) {
+        const float x = u[ii][jj];
+        const float x2 = x * x, x4 = x2 * x2, x8 = x4 * x4, x9 = x8 * x;
+        const float w = x8 * x2 * c.y;
+        float du = 0.f;
+        if (x > 0.f) {
+          du = (10.f * c.y) * x9 * (dp[ii][jj] - c.z);
+          if (c.x > 0.f && x == c.x) du += c.w;
+        }
+        dtau -= du;
+        sW[r * LDP + cg + 16 * jj] = w;
+        sdS[r * LDP + cg + 16 * jj] = du * a.scale;
+      }
+    }
+    __syncthreads();
+    // dV[key][e] += sum_q W[q][key] dO[q][e];  dK[key][e] += sum_q dS[q][key] Q[q][e]
+#pragma unroll 4
+    for (int qq = 0; qq < GB; ++qq) {
+      float w[4], s[4], d[NJ], qv[NJ];
+#pragma unroll
+      for (int ii = 0; ii < 4; ++ii) {
+        w[ii] = sW[qq * LDP + rg + 16 * ii];
+        s[ii] = sdS[qq * LDP + rg + 16 * ii];
+      }
+#pragma unroll
+      for (int jj = 0; jj < NJ; ++jj) {
+        d[jj] = sdO[qq * LD + cg + 16 * jj];
+        qv[jj] = sQ[qq * LD + cg + 16 * jj];
+      }
+#pragma unroll
+      for (int ii = 0; ii < 4; ++ii)
+#pragma unroll
+        for (int jj = 0; jj < NJ; ++jj) {
+          dv[ii][jj] = fmaf(w[ii], d[jj], dv[ii][jj]);
+          dk[ii][jj] = fmaf(s[ii], qv[jj], dk[ii][jj]);
+        }
+    }
+    // dQ[q][e] += sum_key dS[q][key] K[key][e]
+    float dq[4][NJ];
+#pragma unroll
+    for (int ii = 0; ii < 4; ++ii)
+#pragma unroll
+      for (int jj = 0; jj < NJ; ++jj) dq[ii][jj] = 0.f;
+#pragma unroll 4
+    for (int kk = 0; kk < GB; ++kk) {
+      float s[4], kv[NJ];
+#pragma unroll
+      for (int ii = 0; ii < 4; ++ii) s[ii] = sdS[(rg + 16 * ii) * LDP + kk];
+#pragma unroll
+      for (int jj = 0; jj < NJ; ++jj) kv[jj] = sK[kk * LD + cg + 16 * jj];
+#pragma unroll
+      for (int ii = 0; ii < 4; ++ii)
+#pragma unroll
+        for (int jj = 0; jj < NJ; ++jj) dq[ii][jj] = fmaf(s[ii], kv[jj], dq[ii][jj]);
+    }
+#pragma unroll
+    for (int ii = 0; ii < 4; ++ii) {
+      const int64_t row = q0 + rg + 16 * ii;
+      if (row >= N) continue;
+#pragma unroll
+      for (int jj = 0; jj < NJ; ++jj) {
+        const int e = cg + 16 * jj;
+        if (e < D) atomicAdd(dQa + row * a.D + e, dq[ii][jj]);
+      }
+    }
+  }
+  T* dK = static_cast<T*>(a.dk) + b * a.sdk[0] + h * a.sdk[1];
+  T* dV = static_cast<T*>(a.dv) + b * a.sdv[0] + h * a.sdv[1];
+#pragma unroll
+  for (int ii = 0; ii < 4; ++ii) {
+    const int64_t key = k0 + rg + 16 * ii;
+    if (key >= N) continue;
+#pragma unroll
+    for (int jj = 0; jj < NJ; ++jj) {
+      const int e = cg + 16 * jj;
+      if (e < D) {
+        dK[key * a.sdk[2] + e * a.sdk[3]] = from_f32<T>(dk[ii][jj]);
+        dV[key * a.sdv[2] + e * a.sdv[3]] = from_f32<T>(dv[ii][jj]);
+      }
+    }
+  }
+  __shared__ float red[GTHREADS / 32];
+  const float t = block_sum(dtau, red);
+  if (tid == 0) a.dtau_part[bh * gridDim.x + kt] = t;
+}
+
+template <typename T>
+__global__ void __launch_bounds__(256) dq_cast_kernel(FlashArgs a) {
+  const int64_t total = a.B * a.H * a.N * a.D;
+  T* dq = static_cast<T*>(a.dq);
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t e = i % a.D, n = (i / a.D) % a.N, bh = i / (a.D * a.N), b = bh / a.H, h = bh % a.H;
+    dq[b * a.sdq[0] + h * a.sdq[1] + n * a.sdq[2] + e * a.sdq[3]] = from_f32<T>(a.dq_acc[i]);
+  }
+}
+
+static unsigned grid_cap(int64_t items, int per_block) {
+  int64_t g = (items + per_block - 1) / per_block;
+  if (g < 1) g = 1;
+  if (g > 65535LL * 32) g = 65535LL * 32;
+  return (unsigned)g;
+}
+
+BwdWorkspace bwd_workspace_layout(int64_t B, int64_t H, int64_t N, int64_t D) {
+  auto up = [](size_t x) { return (x + 255) & ~(size_t)255; };
+  BwdWorkspace w{};
+  const size_t rows = (size_t)(B * H * N);
+  w.off_dq = 0;
+  w.off_coef = up(rows * (size_t)D * sizeof(float));
+  w.off_part = w.off_coef + up(rows * sizeof(float4));
+  const size_t nparts = (size_t)(B * H) * (size_t)((N + GB - 1) / GB);
+  w.total = w.off_part + up(nparts * sizeof(float));
+  return w;
+}
+
+template <typename T, int DP>
+static int fwd_launch(const FlashArgs& a, cudaStream_t st) {
+  constexpr size_t smem = GenSmem<DP>::fwd_bytes;
+  auto kern = flash_fwd_generic_kernel<T, DP>;
+  if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)
+    return check_launch("flash fwd generic: smem attribute");
+  dim3 grid((unsigned)((a.N + GB - 1) / GB), (unsigned)(a.B * a.H));
+  kern<<<grid, GTHREADS, smem, st>>>(a);
+  return check_launch("flash fwd generic");
+}
+
+template <typename T, int DP>
+static int bwd_launch(const FlashArgs& a, cudaStream_t st) {
+  constexpr size_t smem = GenSmem<DP>::bwd_bytes;
+  auto kern = flash_bwd_generic_kernel<T, DP>;
+  if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)
+    return check_launch("flash bwd generic: smem attribute");
+  dim3 grid((unsigned)((a.N + GB - 1) / GB), (unsigned)(a.B * a.H));
+  kern<<<grid, GTHREADS, smem, st>>>(a);
+  return check_launch("flash bwd generic");
+}
+
+#define PNFT_DISPATCH_DP(D, DPV, ...)                                                    \
+  if ((D) <= 16) {                                                                       \
+    constexpr int DPV = 16;                                                              \
+    __VA_ARGS__;                                                                         \
+  } else if ((D) <= 32) {                                                                \
+    constexpr int DPV = 32;                                                              \
+    __VA_ARGS__;                                                                         \
+  } else if ((D) <= 64) {                                                                \
+    constexpr int DPV = 64;                                                              \
+    __VA_ARGS__;                                                                         \
+  } else if ((D) <= 128) {                                                               \
+    constexpr int DPV = 128;                                                             \
+    __VA_ARGS__;                                                                         \
+  } else {                                                                               \
+    return fail(PNFT_EUNSUPPORTED, "flash: head dim %lld > 128 is not supported", (long long)(D)); \
+  }
+
+int flash_fwd_generic(const FlashArgs& a, cudaStream_t st) {
+  PNFT_DISPATCH_DTYPE(a.dtype, T, { PNFT_DISPATCH_DP(a.D, DP, return fwd_launch<T, DP>(a, st)); });
+  return PNFT_OK;
+}
+
+int flash_bwd_prep(const FlashArgs& a, cudaStream_t st) {
+  if (cudaMemsetAsync(a.dq_acc, 0, (size_t)(a.B * a.H * a.N * a.D) * sizeof(float), st) != cudaSuccess)
+    return check_launch("flash bwd: dq accumulator memset");
+  PNFT_DISPATCH_DTYPE(a.dtype, T, {
+    flash_bwd_prep_kernel<T><<<grid_cap(a.B * a.H * a.N * 32, 256), 256, 0, st>>>(a);
+  });
+  return check_launch("flash bwd prep");
+}
+
+int flash_bwd_finish(const FlashArgs& a, cudaStream_t st) {
+  PNFT_DISPATCH_DTYPE(a.dtype, T, {
+    dq_cast_kernel<T><<<grid_cap(a.B * a.H * a.N * a.D, 256), 256, 0, st>>>(a);
+  });
+  int rc = check_launch("flash bwd dq cast");
+  if (rc) return rc;
+  return pnft_sum_f32(a.dtau_part, a.n_dtau_part, a.dtau, st);
+}
+
+int flash_bwd_generic(const FlashArgs& a0, cudaStream_t st) {
+  FlashArgs a = a0;
+  a.n_dtau_part = a.B * a.H * ((a.N + GB - 1) / GB);
+  int rc = flash_bwd_prep(a, st);
+  if (rc) return rc;
+  PNFT_DISPATCH_DTYPE(a.dtype, T, {
+    PNFT_DISPATCH_DP(a.D, DP, { rc = bwd_launch<T, DP>(a, st); });
+  });
+  if (rc) return rc;
+  return flash_bwd_finish(a, st);
+}
+
+}  // namespace pnft

@@ -1,0 +1,103 @@
+"""Pre-LN decoder LM with pn_fir_tau attention in every layer - the caller of
+the operator in the reference's language-model experiments
+(experiments/exp4_wikitext2_lm.py:183-259, ``Block`` and ``WikiLM``;
+experiments/exp4f_scaleout.py:260-271 for the D=256 / N=512 shape).
+
+Token embedding + learned positions -> n_layers x Block(x + attn(ln1 x);
+x + ffn(ln2 x)) -> ln_f -> head tied to the embedding.
+"""
+from __future__ import annotations
+
+from dataclasses import dataclass
+
+import torch
+import torch.nn as nn
+
+from .pnfirtau_attention import PnFirConfig, PnFirTauFlashMHA, PnFirTauMHA, PnFirTauTritonMHA
+
+_VARIANTS = {"pn_fir_tau": PnFirTauMHA, "pn_fir_tau_triton": PnFirTauTritonMHA, "pn_fir_tau_flash": PnFirTauFlashMHA}
+
+
+@dataclass(frozen=True)
+class LMConfig:
+    vocab: int = 33278
+    d_model: int = 256
+    n_heads: int = 4
+    n_layers: int = 6
+    d_ff: int = 1024
+    max_seq: int = 512
+    dropout: float = 0.0
+    p: float = 10.0
+    silence_gamma: float | None = 0.5
+    tau_init: float = 0.0
+    fir_k: int = 7
+
+
+class Block(nn.Module):
+    """exp4_wikitext2_lm.py:183-200."""
+
+    def __init__(self, d_model: int, attn: nn.Module, dropout: float, d_ff: int):
+        super().__init__()
+        self.ln1 = nn.LayerNorm(d_model)
+        self.attn = attn
+        self.ln2 = nn.LayerNorm(d_model)
+        self.ffn = nn.Sequential(nn.Linear(d_model, d_ff), nn.GELU(), nn.Linear(d_ff, d_model), nn.Dropout(dropout))
+        self.drop = nn.Dropout(dropout)
+
+    def forward(self, x: torch.Tensor) -> torch.Tensor:
+        x = x + self.drop(self.attn(self.ln1(x)))
+        return x + self.ffn(self.ln2(x))
+
+
+class PnFirLM(nn.Module):
+    """exp4_wikitext2_lm.py:203-247 (``WikiLM``) with a pn_fir_tau variant."""
+
+    def __init__(self, cfg: LMConfig = LMConfig(), variant: str = "pn_fir_tau_flash"):
+        super().__init__()
+        self.cfg = cfg
+        self.variant = variant
+        self.embed = nn.Embedding(cfg.vocab, cfg.d_model)
+        self.pos = nn.Embedding(cfg.max_seq, cfg.d_model)
+        self.drop = nn.Dropout(cfg.dropout)
+        acfg = PnFirConfig(d_model=cfg.d_model, n_heads=cfg.n_heads, p=cfg.p, silence_gamma=cfg.silence_gamma,
+                           tau_init=cfg.tau_init, fir_k=cfg.fir_k, dropout=cfg.dropout, causal_mask=True, bias=False)
+        cls = _VARIANTS[variant]
+        self.blocks = nn.ModuleList(Block(cfg.d_model, cls(acfg), cfg.dropout, cfg.d_ff) for _ in range(cfg.n_layers))
+        self.ln_f = nn.LayerNorm(cfg.d_model)
+        self.head = nn.Linear(cfg.d_model, cfg.vocab, bias=False)
+        self.head.weight = self.embed.weight
+
+    def forward(self, idx: torch.Tensor) -> torch.Tensor:
+        B, N = idx.shape
+        pos = torch.arange(N, device=idx.device).unsqueeze(0)
+        h = self.drop(self.embed(idx) + self.pos(pos))
+        for blk in self.blocks:
+            h = blk(h)
+        return self.head(self.ln_f(h))
+
+    def param_count(self) -> int:
+        return sum(p.numel() for p in {id(p): p for p in self.parameters()}.values())
+
+
+def lm_loss(model: nn.Module, idx: torch.Tensor) -> torch.Tensor:
+    """Next-token cross-entropy: logits of all N positions, scored on the
+    shifted ids (exp4_wikitext2_lm.py:714-719)."""
+    logits = model(idx)
+    return nn.functional.cross_entropy(logits[:, :-1].reshape(-1, logits.size(-1)), idx[:, 1:].reshape(-1))
+
+
+def train_step(model: nn.Module, opt: torch.optim.Optimizer, idx: torch.Tensor, clip: float = 1.0) -> torch.Tensor:
+    """One bf16-autocast step: loss, backward, clip_grad_norm_(1.0), AdamW
+    (exp4_wikitext2_lm.py:712-729). Returns the loss tensor (no host sync)."""
+    opt.zero_grad(set_to_none=True)
+    with torch.autocast(device_type="cuda", dtype=torch.bfloat16):
+        loss = lm_loss(model, idx)
+    loss.backward()
+    torch.nn.utils.clip_grad_norm_(model.parameters(), clip)
+    opt.step()
+    return loss.detach()
+
+
+def make_optimizer(model: nn.Module, lr: float = 3e-4) -> torch.optim.Optimizer:
+    """AdamW(betas=(0.9, 0.95), weight_decay=0.1) as exp4_wikitext2_lm.py:684-689."""
+    return torch.optim.AdamW(model.parameters(), lr=lr, betas=(0.9, 0.95), weight_decay=0.1)

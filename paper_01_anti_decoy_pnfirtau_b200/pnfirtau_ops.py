@@ -1,0 +1,409 @@
+"""CUDA operators of pn_fir_tau with PyTorch autograd (counterpart of the
+reference's ``src/triton_pnfirtau.py``).
+
+Public functions keep the reference's names, signatures, defaults and return
+types:
+
+* ``triton_causal_fir(x, taps)``                      (src/triton_pnfirtau.py:685)
+* ``triton_pn_fir_tau_scores(raw_scores, score_tau, scale=1.0, p=10.0,
+  gamma=0.5, causal_mask=True)``                      (src/triton_pnfirtau.py:788)
+* ``flash_pn_fir_tau_attention(q, k_tilde, v, score_tau, scale=None,
+  gamma=0.5, causal_mask=True)``                      (src/triton_pnfirtau.py:971)
+
+Every call runs hand-written sm_100a CUDA from libpnfirtau_b200.so through its
+C ABI, on the caller's current CUDA stream. There is no Triton, no CPU path and
+no silent fallback: CPU tensors raise ``RuntimeError``. Where the reference fell
+back to eager PyTorch (more than 7 taps, C > 1024, N > 4096) these kernels
+simply serve the shape.
+"""
+from __future__ import annotations
+
+import math
+
+import torch
+
+from . import _lib
+
+__all__ = [
+    "triton_causal_fir",
+    "triton_pn_fir_tau_scores",
+    "flash_pn_fir_tau_attention",
+    "pn_rows",
+    "check_device_status",
+    "flash_kernel_path",
+]
+
+_DTYPES = {torch.float32: _lib.DTYPE_F32, torch.bfloat16: _lib.DTYPE_BF16, torch.float16: _lib.DTYPE_F16}
+_SILENCE = {"peak": _lib.SILENCE_PEAK, "mass_relu": _lib.SILENCE_MASS_RELU, "mass_pow": _lib.SILENCE_MASS_POW}
+
+
+def _dtype_code(t: torch.Tensor) -> int:
+    try:
+        return _DTYPES[t.dtype]
+    except KeyError:
+        raise RuntimeError(f"pn_fir_tau CUDA kernels support float32/bfloat16/float16, got {t.dtype}") from None
+
+
+def _require_cuda(what: str, *tensors: torch.Tensor) -> torch.device:
+    dev = None
+    for t in tensors:
+        if not t.is_cuda:
+            raise RuntimeError(
+                f"{what}: tensors must be on a CUDA device (this library has no CPU path); got {t.device}"
+            )
+        if dev is None:
+            dev = t.device
+        elif t.device != dev:
+            raise RuntimeError(f"{what}: all tensors must be on the same device ({dev} vs {t.device})")
+    return dev
+
+
+def _stream(dev: torch.device) -> int:
+    return torch.cuda.current_stream(dev).cuda_stream
+
+
+def _ptr(t: torch.Tensor | None) -> int | None:
+    return None if t is None else t.data_ptr()
+
+
+_status: dict[int, torch.Tensor] = {}
+
+
+def _status_word(dev: torch.device) -> torch.Tensor:
+    """Per-device int32 word where pipelined kernels report a timed-out wait."""
+    idx = dev.index if dev.index is not None else torch.cuda.current_device()
+    t = _status.get(idx)
+    if t is None:
+        t = torch.zeros(1, dtype=torch.int32, device=torch.device("cuda", idx))
+        _status[idx] = t
+    return t
+
+
+def check_device_status(device: torch.device | int | None = None, reset: bool = True) -> None:
+    """Synchronise and raise if a kernel on ``device`` reported a device-side error."""
+    if device is None:
+        device = torch.cuda.current_device()
+    dev = torch.device("cuda", device) if isinstance(device, int) else torch.device(device)
+    w = _status_word(dev)
+    v = int(w.item())
+    if v != _lib.DEV_OK:
+        if reset:
+            w.zero_()
+        raise RuntimeError(f"pn_fir_tau kernel reported device status {v} (pipeline wait timed out)")
+
+
+def _taps_f32(taps: torch.Tensor, dev: torch.device) -> torch.Tensor:
+    if taps.dtype == torch.float32 and taps.is_contiguous() and taps.device == dev:
+        return taps.detach()
+    return taps.detach().contiguous().to(device=dev, dtype=torch.float32)
+
+
+# ---------------------------------------------------------------------------
+# 1. causal FIR
+# ---------------------------------------------------------------------------
+
+
+class _CausalFirFn(torch.autograd.Function):
+    """Depthwise causal FIR along N of x[B,N,C] (src/triton_pnfirtau.py:629-682).
+
+    The backward applies the transpose filter and, when ``taps`` requires grad,
+    also returns the tap gradient (the reference returns None, :682).
+    """
+
+    @staticmethod
+    def forward(ctx, x: torch.Tensor, taps: torch.Tensor) -> torch.Tensor:
+        dev = _require_cuda("triton_causal_fir", x)
+        B, N, C = x.shape
+        taps_f32 = _taps_f32(taps, dev)
+        y = torch.empty((B, N, C), device=dev, dtype=x.dtype)
+        L = _lib.lib()
+        _lib.check(
+            L.pnft_fir_fwd(_ptr(x), *x.stride(), _ptr(taps_f32), taps_f32.numel(), _ptr(y), *y.stride(), B, N, C,
+                           _dtype_code(x), _stream(dev)),
+            "pnft_fir_fwd",
+        )
+        ctx.save_for_backward(taps_f32, x if ctx.needs_input_grad[1] else None)
+        ctx.taps_dtype = taps.dtype
+        return y
+
+    @staticmethod
+    def backward(ctx, grad_y: torch.Tensor):
+        taps_f32, x = ctx.saved_tensors
+        dev = grad_y.device
+        B, N, C = grad_y.shape
+        L = _lib.lib()
+        gx = torch.empty((B, N, C), device=dev, dtype=grad_y.dtype) if ctx.needs_input_grad[0] else None
+        dtaps = ws = None
+        if x is not None:
+            if grad_y.dtype != x.dtype:
+                grad_y = grad_y.to(x.dtype)
+            dtaps = torch.empty(taps_f32.numel(), device=dev, dtype=torch.float32)
+            nbytes = L.pnft_fir_bwd_workspace_size(B, N, C, taps_f32.numel())
+            ws = torch.empty(max(nbytes, 1), device=dev, dtype=torch.uint8)
+        if gx is None and x is None:
+            return None, None
+        _lib.check(
+            L.pnft_fir_bwd(
+                _ptr(grad_y), *grad_y.stride(), _ptr(taps_f32), taps_f32.numel(),
+                _ptr(gx), *(gx.stride() if gx is not None else (0, 0, 0)),
+                _ptr(x), *(x.stride() if x is not None else (0, 0, 0)),
+                _ptr(dtaps), _ptr(ws), ws.numel() if ws is not None else 0,
+                B, N, C, _dtype_code(grad_y), _stream(dev),
+            ),
+            "pnft_fir_bwd",
+        )
+        return gx, (dtaps.to(ctx.taps_dtype) if dtaps is not None else None)
+
+
+def triton_causal_fir(x: torch.Tensor, taps: torch.Tensor) -> torch.Tensor:
+    """Fused zero-copy depthwise 1D causal FIR along axis N for x: [B, N, C].
+
+    Reference: src/triton_pnfirtau.py:685-691. Any tap count (1 tap or fewer is
+    the identity, as the eager causal_fir, src/pnfirtau_attention.py:69-70)
+    and any C run on the CUDA kernel.
+    """
+    if taps.numel() <= 1:
+        _require_cuda("triton_causal_fir", x)
+        return x
+    return _CausalFirFn.apply(x, taps)
+
+
+# ---------------------------------------------------------------------------
+# 2. row-fused score -> weight op
+# ---------------------------------------------------------------------------
+
+
+def _gamma_args(gamma: float | None) -> tuple[int, float]:
+    has_gamma = gamma is not None and gamma > 0.0
+    return int(has_gamma), float(gamma) if has_gamma else 0.0
+
+
+class _PnRowsFn(torch.autograd.Function):
+    """Row-fused scale, -tau, causal mask, ReLU, u^p, peak/mass stats and gate.
+
+    Forward/backward follow src/triton_pnfirtau.py:694-785, with the
+    ``mass_relu`` / ``mass_pow`` silence modes and general p of the eager
+    power_norm_peak_gate (src/pnfirtau_attention.py:87-119).
+    """
+
+    @staticmethod
+    def forward(ctx, raw_scores, score_tau, scale, p, gamma, causal_mask, silence_mode):
+        dev = _require_cuda("pn_fir_tau rows", raw_scores, score_tau)
+        orig_shape = raw_scores.shape
+        N = orig_shape[-1]
+        s_2d = raw_scores.contiguous().view(-1, N)
+        R = s_2d.shape[0]
+        w_2d = torch.empty_like(s_2d)
+        stats = torch.empty((4, R), device=dev, dtype=torch.float32)
+        nmax = torch.empty(R, device=dev, dtype=torch.int32)
+        tau_f32 = score_tau.detach().to(torch.float32).contiguous()
+        has_gamma, gamma_val = _gamma_args(gamma)
+        mode = _SILENCE[silence_mode]
+        L = _lib.lib()
+        _lib.check(
+            L.pnft_rows_fwd(_ptr(s_2d), s_2d.stride(0), _ptr(tau_f32), _ptr(w_2d), w_2d.stride(0),
+                            _ptr(stats[0]), _ptr(stats[1]), _ptr(nmax), _ptr(stats[2]), R, N, float(scale),
+                            float(p), gamma_val, has_gamma, mode, int(bool(causal_mask)), _dtype_code(s_2d),
+                            _stream(dev)),
+            "pnft_rows_fwd",
+        )
+        ctx.save_for_backward(s_2d, tau_f32, stats, nmax)
+        ctx.orig_shape = orig_shape
+        ctx.args = (float(scale), float(p), gamma_val, has_gamma, mode, int(bool(causal_mask)))
+        ctx.tau_dtype = score_tau.dtype
+        ctx.tau_shape = score_tau.shape
+        return w_2d.view(orig_shape)
+
+    @staticmethod
+    def backward(ctx, grad_w):
+        s_2d, tau_f32, stats, nmax = ctx.saved_tensors
+        scale, p, gamma_val, has_gamma, mode, causal = ctx.args
+        R, N = s_2d.shape
+        dev = s_2d.device
+        gw_2d = grad_w.to(s_2d.dtype).contiguous().view(R, N)
+        grad_s = torch.empty_like(s_2d)
+        dtau_rows = torch.empty(R, device=dev, dtype=torch.float32)
+        dtau = torch.empty((), device=dev, dtype=torch.float32)
+        L = _lib.lib()
+        _lib.check(
+            L.pnft_rows_bwd(_ptr(gw_2d), gw_2d.stride(0), _ptr(s_2d), s_2d.stride(0), _ptr(tau_f32),
+                            _ptr(stats[0]), _ptr(stats[1]), _ptr(nmax), _ptr(stats[2]), _ptr(grad_s),
+                            grad_s.stride(0), _ptr(dtau_rows), _ptr(dtau), R, N, scale, p, gamma_val, has_gamma,
+                            mode, causal, _dtype_code(s_2d), _stream(dev)),
+            "pnft_rows_bwd",
+        )
+        grad_tau = dtau.to(ctx.tau_dtype).reshape(ctx.tau_shape)
+        return grad_s.view(ctx.orig_shape), grad_tau, None, None, None, None, None
+
+
+def pn_rows(raw_scores, score_tau, scale=1.0, p=10.0, gamma=0.5, causal_mask=True, silence_mode="peak"):
+    """Row op with every silence mode of power_norm_peak_gate (peak, mass_relu, mass_pow)."""
+    if silence_mode not in _SILENCE:
+        if gamma is not None and gamma > 0:
+            raise ValueError(f"unknown silence_mode={silence_mode}")
+        silence_mode = "peak"  # the eager primitive only inspects the mode when a gate is applied
+    N = raw_scores.shape[-1]
+    assert raw_scores.shape[-2] == N or not causal_mask, "Expected [..., N, N] scores tensor"
+    return _PnRowsFn.apply(raw_scores, score_tau, scale, p, gamma, causal_mask, silence_mode)
+
+
+def triton_pn_fir_tau_scores(
+    raw_scores: torch.Tensor,
+    score_tau: torch.Tensor,
+    scale: float = 1.0,
+    p: float = 10.0,
+    gamma: float | None = 0.5,
+    causal_mask: bool = True,
+) -> torch.Tensor:
+    """Fused row-wise score-to-weight kernel for ``pn_fir_tau`` (src/triton_pnfirtau.py:788-811).
+
+    Same contract as the reference: ``raw_scores`` is ``[..., N, N]``; the
+    result has its shape and dtype; the silence test is the row peak.
+    """
+    N = raw_scores.shape[-1]
+    assert raw_scores.shape[-2] == N, "Expected [..., N, N] scores tensor"
+    return _PnRowsFn.apply(raw_scores, score_tau, scale, p, gamma, causal_mask, "peak")
+
+
+# ---------------------------------------------------------------------------
+# 3. flash pn_fir_tau attention
+# ---------------------------------------------------------------------------
+
+
+def _flash_flags() -> int:
+    return _lib.FLASH_FORCE_GENERIC if _FORCE_GENERIC else 0
+
+
+_FORCE_GENERIC = False
+
+
+def flash_kernel_path(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor) -> str:
+    """'sm100' if the tcgen05/TMA kernels serve these tensors, else 'generic'."""
+    L = _lib.lib()
+    r = L.pnft_flash_path(_ptr(q), _lib.i64x4(q.stride()), _ptr(k), _lib.i64x4(k.stride()), _ptr(v),
+                          _lib.i64x4(v.stride()), q.shape[-1], _dtype_code(q), _flash_flags())
+    return "sm100" if r == 1 else "generic"
+
+
+class _FlashPnFirTauFn(torch.autograd.Function):
+    """O(N)-memory tiled pn_fir_tau attention, p = 10 (src/triton_pnfirtau.py:814-968).
+
+    q, k, v are read through their strides (no .contiguous() copies). The
+    output is allocated ``[B,H,N,D]`` contiguous, or, with ``out_layout ==
+    'bnhd'``, as a ``[B,N,H,D]`` buffer returned through a transposed view so
+    the module's ``transpose(1,2).reshape`` is free.
+    """
+
+    @staticmethod
+    def forward(ctx, q, k, v, score_tau, scale, gamma, causal_mask, out_layout):
+        dev = _require_cuda("flash_pn_fir_tau_attention", q, k, v, score_tau)
+        if not (q.dtype == k.dtype == v.dtype):
+            raise RuntimeError(f"flash_pn_fir_tau_attention: q/k/v dtypes differ ({q.dtype}, {k.dtype}, {v.dtype})")
+        B, H, N, D = q.shape
+        if k.shape != q.shape or v.shape != q.shape:
+            raise RuntimeError(f"flash_pn_fir_tau_attention: q {tuple(q.shape)}, k {tuple(k.shape)}, v {tuple(v.shape)} must match")
+        if out_layout == "bnhd":
+            out = torch.empty((B, N, H, D), device=dev, dtype=q.dtype).transpose(1, 2)
+        else:
+            out = torch.empty((B, H, N, D), device=dev, dtype=q.dtype)
+        stats = torch.empty((2, B, H, N), device=dev, dtype=torch.float32)
+        nmax = torch.empty((B, H, N), device=dev, dtype=torch.int32)
+        tau_f32 = score_tau.detach().to(torch.float32).contiguous()
+        has_gamma, gamma_val = _gamma_args(gamma)
+        flags = _flash_flags()
+        L = _lib.lib()
+        _lib.check(
+            L.pnft_flash_fwd(_ptr(q), _lib.i64x4(q.stride()), _ptr(k), _lib.i64x4(k.stride()), _ptr(v),
+                             _lib.i64x4(v.stride()), _ptr(tau_f32), _ptr(out), _lib.i64x4(out.stride()),
+                             _ptr(stats[0]), _ptr(stats[1]), _ptr(nmax), B, H, N, D, float(scale), gamma_val,
+                             has_gamma, int(bool(causal_mask)), _dtype_code(q), flags, None,
+                             _ptr(_status_word(dev)), _stream(dev)),
+            "pnft_flash_fwd",
+        )
+        ctx.save_for_backward(q, k, v, tau_f32, out, stats, nmax)
+        ctx.args = (float(scale), gamma_val, has_gamma, int(bool(causal_mask)), flags)
+        ctx.tau_dtype = score_tau.dtype
+        ctx.tau_shape = score_tau.shape
+        return out
+
+    @staticmethod
+    def backward(ctx, grad_out):
+        q, k, v, tau_f32, out, stats, nmax = ctx.saved_tensors
+        scale, gamma_val, has_gamma, causal, flags = ctx.args
+        B, H, N, D = q.shape
+        dev = q.device
+        if grad_out.dtype != q.dtype:
+            grad_out = grad_out.to(q.dtype)
+        dq = torch.empty((B, H, N, D), device=dev, dtype=q.dtype)
+        dk = torch.empty((B, H, N, D), device=dev, dtype=k.dtype)
+        dv = torch.empty((B, H, N, D), device=dev, dtype=v.dtype)
+        dtau = torch.empty((), device=dev, dtype=torch.float32)
+        L = _lib.lib()
+        nbytes = L.pnft_flash_bwd_workspace_size(B, H, N, D, flags)
+        ws = torch.empty(max(nbytes, 1), device=dev, dtype=torch.uint8)
+        _lib.check(
+            L.pnft_flash_bwd(_ptr(q), _lib.i64x4(q.stride()), _ptr(k), _lib.i64x4(k.stride()), _ptr(v),
+                             _lib.i64x4(v.stride()), _ptr(tau_f32), _ptr(out), _lib.i64x4(out.stride()),
+                             _ptr(grad_out), _lib.i64x4(grad_out.stride()), _ptr(stats[0]), _ptr(stats[1]),
+                             _ptr(nmax), _ptr(dq), _lib.i64x4(dq.stride()), _ptr(dk), _lib.i64x4(dk.stride()),
+                             _ptr(dv), _lib.i64x4(dv.stride()), _ptr(dtau), _ptr(ws), ws.numel(), B, H, N, D,
+                             scale, gamma_val, has_gamma, causal, _dtype_code(q), flags,
+                             _ptr(_status_word(dev)), _stream(dev)),
+            "pnft_flash_bwd",
+        )
+        grad_tau = dtau.to(ctx.tau_dtype).reshape(ctx.tau_shape)
+        return dq, dk, dv, grad_tau, None, None, None, None
+
+
+def flash_pn_fir_tau_attention(
+    q: torch.Tensor,
+    k_tilde: torch.Tensor,
+    v: torch.Tensor,
+    score_tau: torch.Tensor,
+    scale: float | None = None,
+    gamma: float | None = 0.5,
+    causal_mask: bool = True,
+) -> torch.Tensor:
+    """FlashAttention-style O(N)-memory tiled attention for ``pn_fir_tau`` (p = 10).
+
+    Reference: src/triton_pnfirtau.py:971-983. ``scale`` defaults to
+    1/sqrt(head_dim). Returns ``[B, H, N, D]`` in q's dtype.
+    """
+    if scale is None:
+        scale = 1.0 / math.sqrt(q.shape[-1])
+    return _FlashPnFirTauFn.apply(q, k_tilde, v, score_tau, scale, gamma, causal_mask, "bhnd")
+
+
+@torch.no_grad()
+def flash_pn_fir_tau_forward_stats(q, k_tilde, v, score_tau, scale=None, gamma=0.5, causal_mask=True):
+    """Forward only, also returning the per-row statistics and the kernel's
+    silent-tile decisions: ``(out, M, Z, Nmax, tile_live)`` with M/Z/Nmax
+    ``[B,H,N]`` (peak, mass + 1e-12, tie count, src/triton_pnfirtau.py:440-443)
+    and ``tile_live`` bool ``[B,H,nT,nT]`` (nT = ceil(N/64)) true for every
+    64x64 tile the kernel processed as live."""
+    dev = _require_cuda("flash_pn_fir_tau_forward_stats", q, k_tilde, v, score_tau)
+    if scale is None:
+        scale = 1.0 / math.sqrt(q.shape[-1])
+    B, H, N, D = q.shape
+    out = torch.empty((B, H, N, D), device=dev, dtype=q.dtype)
+    stats = torch.empty((2, B, H, N), device=dev, dtype=torch.float32)
+    nmax = torch.empty((B, H, N), device=dev, dtype=torch.int32)
+    nT = (N + 63) // 64
+    tiles = torch.zeros((B, H, nT, nT), device=dev, dtype=torch.uint8)
+    tau_f32 = score_tau.detach().to(torch.float32).contiguous()
+    has_gamma, gamma_val = _gamma_args(gamma)
+    L = _lib.lib()
+    _lib.check(
+        L.pnft_flash_fwd(_ptr(q), _lib.i64x4(q.stride()), _ptr(k_tilde), _lib.i64x4(k_tilde.stride()), _ptr(v),
+                         _lib.i64x4(v.stride()), _ptr(tau_f32), _ptr(out), _lib.i64x4(out.stride()),
+                         _ptr(stats[0]), _ptr(stats[1]), _ptr(nmax), B, H, N, D, float(scale), gamma_val,
+                         has_gamma, int(bool(causal_mask)), _dtype_code(q), _flash_flags(), _ptr(tiles),
+                         _ptr(_status_word(dev)), _stream(dev)),
+        "pnft_flash_fwd",
+    )
+    return out, stats[0], stats[1], nmax, tiles.bool()
+
+
+def _flash_bnhd(q, k_tilde, v, score_tau, scale, gamma, causal_mask):
+    """Same op; the result's storage is [B,N,H,D] (free transpose back to tokens)."""
+    return _FlashPnFirTauFn.apply(q, k_tilde, v, score_tau, scale, gamma, causal_mask, "bnhd")
