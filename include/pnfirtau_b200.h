@@ -60,6 +60,7 @@ extern "C" {
 /* flags of the flash entry points */
 #define PNFT_FLASH_FORCE_GENERIC 0x1 /* use the SIMT kernel even where tcgen05 applies */
 #define PNFT_FLASH_DETERMINISTIC 0x2 /* reserved: ordered dQ accumulation             */
+#define PNFT_FLASH_PREFER_SM100 0x4  /* tcgen05 kernels wherever their shape rules allow */
 
 /* Library version (major*10000 + minor*100 + patch). */
 PNFT_API int pnft_version(void);
@@ -148,8 +149,15 @@ PNFT_API int pnft_sum_f32(const float* x, int64_t n, float* out, void* stream);
 
 /* q,k,v: [B,H,N,D] with arbitrary 4-D element strides sq/sk/sv/so (host
  * arrays of 4 int64: b,h,n,d); out in the same dtype with strides so.
- * Stats stat_m/stat_z (fp32) and stat_nmax (int32) are contiguous [B,H,N].
+ * Stats stat_m/stat_z (fp32) and stat_nmax (int32) are contiguous [B,H,N];
+ * stat_arg (int32 [B,H,N]) receives the first key index attaining each row's
+ * peak (-1 for silent rows): the backward routes the gate gradient of a row
+ * with a single maximum to that key, independently of how S is recomputed.
  * gamma is used when has_gamma != 0 (reference: gamma is not None and > 0).
+ * out_f32 (optional, may be NULL): fp32 [B,H,N,D] contiguous copy of the
+ * output before rounding to the input dtype; handing it to pnft_flash_bwd keeps
+ * the per-row term <dO,O>/gate exact (u^10 rows are so peaked that dP - <dO,O>
+ * cancels at the peak and would amplify bf16 rounding of O into the gradients).
  * tile_flags (optional, may be NULL): uint8 [B*H, ceil(N/64), ceil(N/64)],
  * zeroed by the caller; the kernel sets entry (bh, qi, kj) to 1 for every
  * 64x64 tile it processed as live (some u > 0) and leaves skipped silent
@@ -161,12 +169,13 @@ PNFT_API int pnft_sum_f32(const float* x, int64_t n, float* out, void* stream);
  * _FlashPnFirTauFn.forward (:814-898). */
 PNFT_API int pnft_flash_fwd(const void* q, const int64_t* sq, const void* k, const int64_t* sk,
                    const void* v, const int64_t* sv, const float* tau, void* out,
-                   const int64_t* so, float* stat_m, float* stat_z, int32_t* stat_nmax,
-                   int64_t B, int64_t H, int64_t N, int64_t D, float scale, float gamma,
-                   int has_gamma, int causal, int dtype, int flags, uint8_t* tile_flags,
+                   const int64_t* so, float* out_f32, float* stat_m, float* stat_z, int32_t* stat_nmax,
+                   int32_t* stat_arg, int64_t B, int64_t H, int64_t N, int64_t D, float scale,
+                   float gamma, int has_gamma, int causal, int dtype, int flags, uint8_t* tile_flags,
                    int32_t* status, void* stream);
 
-/* Backward of pnft_flash_fwd. dout has strides sdo; dq/dk/dv (dtype of q)
+/* Backward of pnft_flash_fwd. out_f32: the forward's fp32 output copy, or NULL
+ * to use `out`. dout has strides sdo; dq/dk/dv (dtype of q)
  * strides sdq/sdk/sdv. dtau: fp32[1], the tau gradient reduced in fp64 in a
  * fixed order. workspace: pnft_flash_bwd_workspace_size(...) bytes (the fp32 dQ
  * accumulator, per-row coefficients and per-tile tau partials).
@@ -174,9 +183,9 @@ PNFT_API int pnft_flash_fwd(const void* q, const int64_t* sq, const void* k, con
  * _FlashPnFirTauFn.backward (:900-968). */
 PNFT_API int pnft_flash_bwd(const void* q, const int64_t* sq, const void* k, const int64_t* sk,
                    const void* v, const int64_t* sv, const float* tau, const void* out,
-                   const int64_t* so, const void* dout, const int64_t* sdo,
+                   const int64_t* so, const float* out_f32, const void* dout, const int64_t* sdo,
                    const float* stat_m, const float* stat_z, const int32_t* stat_nmax,
-                   void* dq, const int64_t* sdq, void* dk, const int64_t* sdk, void* dv,
+                   const int32_t* stat_arg, void* dq, const int64_t* sdq, void* dk, const int64_t* sdk, void* dv,
                    const int64_t* sdv, float* dtau, void* workspace, size_t workspace_bytes,
                    int64_t B, int64_t H, int64_t N, int64_t D, float scale, float gamma,
                    int has_gamma, int causal, int dtype, int flags, int32_t* status,

@@ -16,7 +16,7 @@ DTYPE_F32, DTYPE_BF16, DTYPE_F16 = 0, 1, 2
 OK, EINVAL, EUNSUPPORTED, ECUDA = 0, -1, -2, -3
 DEV_OK, DEV_WAIT_TIMEOUT = 0, 1
 SILENCE_PEAK, SILENCE_MASS_RELU, SILENCE_MASS_POW = 0, 1, 2
-FLASH_FORCE_GENERIC, FLASH_DETERMINISTIC = 0x1, 0x2
+FLASH_FORCE_GENERIC, FLASH_DETERMINISTIC, FLASH_PREFER_SM100 = 0x1, 0x2, 0x4
 
 _I64x4 = c_int64 * 4
 _P = c_void_p
@@ -50,12 +50,12 @@ SIGNATURES: dict[str, tuple] = {
     "pnft_sum_f32": (c_int, [_P, c_int64, _P, _P]),
     "pnft_flash_fwd": (
         c_int,
-        [_P, _I64x4, _P, _I64x4, _P, _I64x4, _P, _P, _I64x4, _P, _P, _P, c_int64, c_int64, c_int64, c_int64,
-         c_float, c_float, c_int, c_int, c_int, c_int, _P, _P, _P],
+        [_P, _I64x4, _P, _I64x4, _P, _I64x4, _P, _P, _I64x4, _P, _P, _P, _P, _P, c_int64, c_int64, c_int64,
+         c_int64, c_float, c_float, c_int, c_int, c_int, c_int, _P, _P, _P],
     ),
     "pnft_flash_bwd": (
         c_int,
-        [_P, _I64x4, _P, _I64x4, _P, _I64x4, _P, _P, _I64x4, _P, _I64x4, _P, _P, _P, _P, _I64x4, _P, _I64x4, _P,
+        [_P, _I64x4, _P, _I64x4, _P, _I64x4, _P, _P, _I64x4, _P, _P, _I64x4, _P, _P, _P, _P, _P, _I64x4, _P, _I64x4, _P,
          _I64x4, _P, _P, c_size_t, c_int64, c_int64, c_int64, c_int64, c_float, c_float, c_int, c_int, c_int,
          c_int, _P, _P],
     ),

@@ -96,21 +96,22 @@ extern "C" int pnft_flash_path(const void* q, const int64_t* sq, const void* k, 
 }
 
 extern "C" int pnft_flash_fwd(const void* q, const int64_t* sq, const void* k, const int64_t* sk, const void* v,
-                              const int64_t* sv, const float* tau, void* out, const int64_t* so, float* stat_m,
-                              float* stat_z, int32_t* stat_nmax, int64_t B, int64_t H, int64_t N, int64_t D,
-                              float scale, float gamma, int has_gamma, int causal, int dtype, int flags,
-                              uint8_t* tile_flags, int32_t* status, void* stream) {
+                              const int64_t* sv, const float* tau, void* out, const int64_t* so, float* out_f32,
+                              float* stat_m, float* stat_z, int32_t* stat_nmax, int32_t* stat_arg, int64_t B,
+                              int64_t H, int64_t N, int64_t D, float scale, float gamma, int has_gamma, int causal,
+                              int dtype, int flags, uint8_t* tile_flags, int32_t* status, void* stream) {
   FlashArgs a;
   int rc = fill_common(a, q, sq, k, sk, v, sv, tau, B, H, N, D, scale, gamma, has_gamma, causal, dtype, flags, status);
   if (rc) return rc;
   a.tile_flags = tile_flags;
   if (B * H * N == 0) return PNFT_OK;
   if (D == 0) return fail(PNFT_EINVAL, "flash fwd: head dim 0");
-  if (!q || !k || !v || !tau || !out || !so || !stat_m || !stat_z || !stat_nmax)
+  if (!q || !k || !v || !tau || !out || !so || !stat_m || !stat_z || !stat_nmax || !stat_arg)
     return fail(PNFT_EINVAL, "flash fwd: null pointer");
   a.out = out;
+  a.out32 = out_f32;
   for (int i = 0; i < 4; ++i) a.so[i] = so[i];
-  a.stat_m = stat_m; a.stat_z = stat_z; a.stat_nmax = stat_nmax;
+  a.stat_m = stat_m; a.stat_z = stat_z; a.stat_nmax = stat_nmax; a.stat_arg = stat_arg;
   cudaStream_t st = as_stream(stream);
   if (use_sm100(a)) return flash_fwd_sm100(a, st);
   return flash_fwd_generic(a, st);
@@ -124,8 +125,8 @@ extern "C" size_t pnft_flash_bwd_workspace_size(int64_t B, int64_t H, int64_t N,
 
 extern "C" int pnft_flash_bwd(const void* q, const int64_t* sq, const void* k, const int64_t* sk, const void* v,
                               const int64_t* sv, const float* tau, const void* out, const int64_t* so,
-                              const void* dout, const int64_t* sdo, const float* stat_m, const float* stat_z,
-                              const int32_t* stat_nmax, void* dq, const int64_t* sdq, void* dk,
+                              const float* out_f32, const void* dout, const int64_t* sdo, const float* stat_m, const float* stat_z,
+                              const int32_t* stat_nmax, const int32_t* stat_arg, void* dq, const int64_t* sdq, void* dk,
                               const int64_t* sdk, void* dv, const int64_t* sdv, float* dtau, void* workspace,
                               size_t workspace_bytes, int64_t B, int64_t H, int64_t N, int64_t D, float scale,
                               float gamma, int has_gamma, int causal, int dtype, int flags, int32_t* status,
@@ -140,20 +141,22 @@ extern "C" int pnft_flash_bwd(const void* q, const int64_t* sq, const void* k, c
     return PNFT_OK;
   }
   if (D == 0) return fail(PNFT_EINVAL, "flash bwd: head dim 0");
-  if (!q || !k || !v || !tau || !out || !so || !dout || !sdo || !stat_m || !stat_z || !stat_nmax || !dq || !sdq ||
-      !dk || !sdk || !dv || !sdv)
+  if (!q || !k || !v || !tau || !out || !so || !dout || !sdo || !stat_m || !stat_z || !stat_nmax || !stat_arg || !dq ||
+      !sdq || !dk || !sdk || !dv || !sdv)
     return fail(PNFT_EINVAL, "flash bwd: null pointer");
   const BwdWorkspace w = bwd_workspace_layout(B, H, N, D);
   if (!workspace || workspace_bytes < w.total)
     return fail(PNFT_EINVAL, "flash bwd: workspace of %zu bytes < required %zu", workspace_bytes, w.total);
   if (reinterpret_cast<uintptr_t>(workspace) % 256 != 0) return fail(PNFT_EINVAL, "flash bwd: workspace not 256-byte aligned");
-  a.out_c = out; a.dout = dout; a.dq = dq; a.dk = dk; a.dv = dv; a.dtau = dtau;
+  a.out_c = out; a.out32 = const_cast<float*>(out_f32); a.dout = dout; a.dq = dq; a.dk = dk; a.dv = dv; a.dtau = dtau;
   for (int i = 0; i < 4; ++i) { a.so[i] = so[i]; a.sdo[i] = sdo[i]; a.sdq[i] = sdq[i]; a.sdk[i] = sdk[i]; a.sdv[i] = sdv[i]; }
   a.stat_m = const_cast<float*>(stat_m); a.stat_z = const_cast<float*>(stat_z);
   a.stat_nmax = const_cast<int32_t*>(stat_nmax);
+  a.stat_arg = const_cast<int32_t*>(stat_arg);
   char* ws = static_cast<char*>(workspace);
   a.dq_acc = reinterpret_cast<float*>(ws + w.off_dq);
   a.coef = reinterpret_cast<float4*>(ws + w.off_coef);
+  a.live64 = reinterpret_cast<int32_t*>(ws + w.off_live);
   a.dtau_part = reinterpret_cast<float*>(ws + w.off_part);
   if (use_sm100(a)) return flash_bwd_sm100(a, st);
   return flash_bwd_generic(a, st);

@@ -53,6 +53,12 @@ __device__ __forceinline__ float group_sum(float v) {
   return v;
 }
 template <int WIDTH>
+__device__ __forceinline__ int group_min_i(int v) {
+#pragma unroll
+  for (int o = WIDTH / 2; o > 0; o >>= 1) v = min(v, __shfl_xor_sync(0xffffffffu, v, o));
+  return v;
+}
+template <int WIDTH>
 __device__ __forceinline__ int group_sum_i(int v) {
 #pragma unroll
   for (int o = WIDTH / 2; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);

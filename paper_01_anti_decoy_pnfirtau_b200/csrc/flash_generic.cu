@@ -32,7 +32,7 @@ struct GenSmem {
   static constexpr int TILE = GB * LD;
   static constexpr int LDP = GB + 1;
   static constexpr size_t fwd_bytes = (size_t)(3 * TILE + GB * LDP) * sizeof(float);
-  static constexpr size_t bwd_bytes = (size_t)(4 * TILE + 2 * GB * LDP + 4 * GB) * sizeof(float);
+  static constexpr size_t bwd_bytes = (size_t)(4 * TILE + 2 * GB * LDP + 4 * GB + 3 * GB) * sizeof(float);
 };
 
 // dst[r][e] (row stride ld) = src[n0 + r, e] for r < 64, e < DP; zero outside N/D.
@@ -97,10 +97,10 @@ __global__ void __launch_bounds__(GTHREADS) flash_fwd_generic_kernel(FlashArgs a
   load_tile<T, DP>(sQ, Q, a.sq[2], a.sq[3], q0, N, D);
   const float tau = __ldg(a.tau);
   float peak[4], mass[4], acc[4][NJ];
-  int nmax[4];
+  int nmax[4], arg[4];
 #pragma unroll
   for (int ii = 0; ii < 4; ++ii) {
-    peak[ii] = 0.f; mass[ii] = 0.f; nmax[ii] = 0;
+    peak[ii] = 0.f; mass[ii] = 0.f; nmax[ii] = 0; arg[ii] = -1;
 #pragma unroll
     for (int jj = 0; jj < NJ; ++jj) acc[ii][jj] = 0.f;
   }
@@ -134,17 +134,21 @@ __global__ void __launch_bounds__(GTHREADS) flash_fwd_generic_kernel(FlashArgs a
       float tmax = fmaxf(fmaxf(u[ii][0], u[ii][1]), fmaxf(u[ii][2], u[ii][3]));
       tmax = group_max<16>(tmax);
       const float np = fmaxf(peak[ii], tmax);
-      int cnt = 0;
+      int cnt = 0, first = 0x7fffffff;
       float rm = 0.f;
 #pragma unroll
       for (int jj = 0; jj < 4; ++jj) {
-        cnt += (np > 0.f && u[ii][jj] == np) ? 1 : 0;
+        const bool hit = np > 0.f && u[ii][jj] == np;
+        cnt += hit ? 1 : 0;
+        if (hit) first = min(first, (int)(k0 + cg + 16 * jj));
         const float pw = pow10f_(u[ii][jj]);
         rm += pw;
         sP[(rg + 16 * ii) * LDP + cg + 16 * jj] = pw;
       }
       cnt = group_sum_i<16>(cnt);
+      first = group_min_i<16>(first);
       rm = group_sum<16>(rm);
+      if (np > peak[ii]) arg[ii] = first;  // a tie with an earlier tile keeps the earlier key
       nmax[ii] = np > peak[ii] ? cnt : nmax[ii] + cnt;
       peak[ii] = np;
       mass[ii] += rm;
@@ -176,33 +180,48 @@ __global__ void __launch_bounds__(GTHREADS) flash_fwd_generic_kernel(FlashArgs a
 #pragma unroll
     for (int jj = 0; jj < NJ; ++jj) {
       const int e = cg + 16 * jj;
-      if (e < D) O[row * a.so[2] + e * a.so[3]] = from_f32<T>(acc[ii][jj] * so);
+      if (e < D) {
+        O[row * a.so[2] + e * a.so[3]] = from_f32<T>(acc[ii][jj] * so);
+        if (a.out32) a.out32[(bh * N + row) * D + e] = acc[ii][jj] * so;
+      }
     }
     if (cg == 0) {
       const int64_t si = bh * N + row;
       a.stat_m[si] = peak[ii];
       a.stat_z[si] = z;
       a.stat_nmax[si] = nmax[ii];
+      a.stat_arg[si] = arg[ii];
     }
   }
 }
 
-// Per query row: coef = {peak, gate/z, D = <dO,O>/gate (0 if gate == 0), tie}
-// with tie = D*gamma/(peak+gamma)^2/Nmax (0 without gamma or for silent rows).
+// Per query row (RowCoef in flash.cuh): D = <dO,O>/gate (0 if gate == 0) and
+// tie = D*gamma/(peak+gamma)^2/Nmax (0 without gamma or for silent rows). One
+// block per (64-row tile, b*h) also records whether any row of the tile is live.
 template <typename T>
 __global__ void __launch_bounds__(256) flash_bwd_prep_kernel(FlashArgs a) {
-  const int64_t rows = a.B * a.H * a.N;
-  const int lane = threadIdx.x & 31;
-  for (int64_t r = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5; r < rows;
-       r += ((int64_t)gridDim.x * blockDim.x) >> 5) {
-    const int64_t n = r % a.N, bh = r / a.N, b = bh / a.H, h = bh % a.H;
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int64_t bh = blockIdx.y, b = bh / a.H, h = bh % a.H;
+  const int64_t nt = (a.N + 63) / 64;
+  int live = 0;
+  for (int rr = warp; rr < 64; rr += 8) {
+    const int64_t n = (int64_t)blockIdx.x * 64 + rr;
+    if (n >= a.N) break;
+    const int64_t r = bh * a.N + n;
     const T* O = static_cast<const T*>(a.out_c) + b * a.so[0] + h * a.so[1] + n * a.so[2];
     const T* dO = static_cast<const T*>(a.dout) + b * a.sdo[0] + h * a.sdo[1] + n * a.sdo[2];
     float dot = 0.f;
-    for (int e = lane; e < a.D; e += 32) dot = fmaf(to_f32<T>(dO[e * a.sdo[3]]), to_f32<T>(O[e * a.so[3]]), dot);
+    if (a.out32) {
+      const float* O32 = a.out32 + r * a.D;
+      for (int e = lane; e < a.D; e += 32) dot = fmaf(to_f32<T>(dO[e * a.sdo[3]]), O32[e], dot);
+    } else {
+      for (int e = lane; e < a.D; e += 32) dot = fmaf(to_f32<T>(dO[e * a.sdo[3]]), to_f32<T>(O[e * a.so[3]]), dot);
+    }
     dot = group_sum<32>(dot);
+    const float peak = a.stat_m[r];
+    live |= peak > 0.f;
     if (lane == 0) {
-      const float peak = a.stat_m[r], z = a.stat_z[r];
+      const float z = a.stat_z[r];
       float gate = 0.f;
       if (peak > 0.f) gate = a.has_gamma ? peak / (peak + a.gamma) : 1.f;
       const float Dg = gate > 0.f ? dot / gate : 0.f;
@@ -211,9 +230,18 @@ __global__ void __launch_bounds__(256) flash_bwd_prep_kernel(FlashArgs a) {
         const float pg = peak + a.gamma;
         tie = Dg * (a.gamma / (pg * pg)) / (float)a.stat_nmax[r];
       }
-      a.coef[r] = make_float4(peak, gate / z, Dg, tie);
+      const float c1 = gate / z;
+      a.coef[r * kCoefStride + 0] = make_float4(peak, c1, (10.f * a.scale) * c1, Dg);
+      // single maximum: matched by key index; genuine ties (Nmax > 1): by value
+      const float pcmp = a.stat_nmax[r] > 1 ? peak : __int_as_float(0x7fc00000);  // NaN never compares equal
+      a.coef[r * kCoefStride + 1] = make_float4(a.scale * tie, __int_as_float(a.stat_arg[r]), pcmp, 0.f);
     }
   }
+  live = __syncthreads_or(live);
+  if (threadIdx.x == 0) a.live64[bh * nt + blockIdx.x] = live;
+  // zero tail: tile loads of the last rows may read up to 64 records past B*H*N
+  if (blockIdx.x == 0 && blockIdx.y == 0 && threadIdx.x < 64 * kCoefStride)
+    a.coef[a.B * a.H * a.N * kCoefStride + threadIdx.x] = make_float4(0.f, 0.f, 0.f, 0.f);
 }
 
 template <typename T, int DP>
@@ -227,7 +255,10 @@ __global__ void __launch_bounds__(GTHREADS) flash_bwd_generic_kernel(FlashArgs a
   float* sdO = sQ + SM::TILE;
   float* sW = sdO + SM::TILE;
   float* sdS = sW + GB * LDP;
-  float4* sC = reinterpret_cast<float4*>(sdS + GB * LDP);
+  float4* sC = reinterpret_cast<float4*>(sdS + GB * LDP);  // {peak, gate/z, 10*scale*gate/z, D}
+  float* sTie = reinterpret_cast<float*>(sC + GB);          // scale * tie coefficient
+  int* sArg = reinterpret_cast<int*>(sTie + GB);            // argmax key of the row
+  float* sPc = reinterpret_cast<float*>(sArg + GB);         // peak for the value test (NaN: unused)
   const int tid = threadIdx.x, rg = tid >> 4, cg = tid & 15;
   const int64_t kt = blockIdx.x, k0 = kt * GB;
   const int64_t bh = blockIdx.y, b = bh / a.H, h = bh % a.H;
@@ -254,8 +285,15 @@ __global__ void __launch_bounds__(GTHREADS) flash_bwd_generic_kernel(FlashArgs a
     if (tid < GB) {
       const int64_t row = q0 + tid;
       float4 c = make_float4(0.f, 0.f, 0.f, 0.f);
-      if (row < N) c = a.coef[bh * N + row];
+      float4 c1 = make_float4(0.f, __int_as_float(-1), __int_as_float(0x7fc00000), 0.f);
+      if (row < N) {
+        c = a.coef[(bh * N + row) * kCoefStride];
+        c1 = a.coef[(bh * N + row) * kCoefStride + 1];
+      }
       sC[tid] = c;
+      sTie[tid] = c1.x;
+      sArg[tid] = __float_as_int(c1.y);
+      sPc[tid] = c1.z;
       live_row = c.x > 0.f;
     }
     if (!__syncthreads_or(live_row)) continue;  // every query row of the block is silent
@@ -284,20 +322,22 @@ __global__ void __launch_bounds__(GTHREADS) flash_bwd_generic_kernel(FlashArgs a
 #pragma unroll
     for (int ii = 0; ii < 4; ++ii) {
       const int r = rg + 16 * ii;
-      const float4 c = sC[r];  // peak, gate/z, D, tie
+      const float4 c = sC[r];  // peak, gate/z, 10*scale*gate/z, D
+      const float tie = sTie[r], pcmp = sPc[r];
+      const int arg = sArg[r];
 #pragma unroll
       for (int jj = 0; jj < 4; ++jj) {
         const float x = u[ii][jj];
         const float x2 = x * x, x4 = x2 * x2, x8 = x4 * x4, x9 = x8 * x;
         const float w = x8 * x2 * c.y;
-        float du = 0.f;
+        float ds = 0.f;  // du * scale
         if (x > 0.f) {
-          du = (10.f * c.y) * x9 * (dp[ii][jj] - c.z);
-          if (c.x > 0.f && x == c.x) du += c.w;
+          ds = c.z * x9 * (dp[ii][jj] - c.w);
+          if ((int)(k0 + cg + 16 * jj) == arg || x == pcmp) ds += tie;
         }
-        dtau -= du;
+        dtau += ds;
         sW[r * LDP + cg + 16 * jj] = w;
-        sdS[r * LDP + cg + 16 * jj] = du * a.scale;
+        sdS[r * LDP + cg + 16 * jj] = ds;
       }
     }
     __syncthreads();
@@ -368,8 +408,8 @@ __global__ void __launch_bounds__(GTHREADS) flash_bwd_generic_kernel(FlashArgs a
     }
   }
   __shared__ float red[GTHREADS / 32];
-  const float t = block_sum(dtau, red);
-  if (tid == 0) a.dtau_part[bh * gridDim.x + kt] = t;
+  const float t = block_sum(dtau, red);  // sum of du*scale over this key block
+  if (tid == 0) a.dtau_part[bh * gridDim.x + kt] = -t / a.scale;
 }
 
 template <typename T>
@@ -393,11 +433,12 @@ BwdWorkspace bwd_workspace_layout(int64_t B, int64_t H, int64_t N, int64_t D) {
   auto up = [](size_t x) { return (x + 255) & ~(size_t)255; };
   BwdWorkspace w{};
   const size_t rows = (size_t)(B * H * N);
+  const size_t ntiles64 = (size_t)(B * H) * (size_t)((N + GB - 1) / GB);
   w.off_dq = 0;
   w.off_coef = up(rows * (size_t)D * sizeof(float));
-  w.off_part = w.off_coef + up(rows * sizeof(float4));
-  const size_t nparts = (size_t)(B * H) * (size_t)((N + GB - 1) / GB);
-  w.total = w.off_part + up(nparts * sizeof(float));
+  w.off_live = w.off_coef + up((rows + 64) * kCoefStride * sizeof(float4));
+  w.off_part = w.off_live + up(ntiles64 * sizeof(int32_t));
+  w.total = w.off_part + up(ntiles64 * sizeof(float));
   return w;
 }
 
@@ -449,7 +490,7 @@ int flash_bwd_prep(const FlashArgs& a, cudaStream_t st) {
   if (cudaMemsetAsync(a.dq_acc, 0, (size_t)(a.B * a.H * a.N * a.D) * sizeof(float), st) != cudaSuccess)
     return check_launch("flash bwd: dq accumulator memset");
   PNFT_DISPATCH_DTYPE(a.dtype, T, {
-    flash_bwd_prep_kernel<T><<<grid_cap(a.B * a.H * a.N * 32, 256), 256, 0, st>>>(a);
+    flash_bwd_prep_kernel<T><<<dim3((unsigned)((a.N + 63) / 64), (unsigned)(a.B * a.H)), 256, 0, st>>>(a);
   });
   return check_launch("flash bwd prep");
 }

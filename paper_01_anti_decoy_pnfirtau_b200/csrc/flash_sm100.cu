@@ -1,21 +1,525 @@
-// sm_100a tcgen05 / TMA / TMEM flash pn_fir_tau kernels (bf16, fp16).
+// sm_100a flash pn_fir_tau kernels: TMA -> shared memory, tcgen05 MMAs with
+// TMEM accumulators, warp-specialised pipelines. bf16 inputs, head dim 64/128.
+//
+// Forward, one CTA per (128 query rows, b*h), 384 threads:
+//   warp 0      TMA producer: Q once; K tile j+1 ahead; V halves of tile j only
+//               after the elementwise warps voted them live (silent halves are
+//               never loaded).
+//   warp 1      MMA issuer and TMEM owner: S_j = Q K_j^T (SS, M=N=128) into one
+//               of two S buffers; O += P_j V_j (TS: P read from TMEM) for the live
+//               64-key halves only.
+//   warps 4-11  two elementwise warpgroups; warpgroup g owns key columns
+//               [64g, 64g+64) of every tile, thread = TMEM lane = query row:
+//               s = S*scale - tau (computed as h = S*scale/2 - tau/2, u = h+|h|),
+//               row max via 3-input max, per-half silent vote, u^10 by repeated
+//               squaring (no exp), running peak / tie count / mass, P = bf16(u^10)
+//               stored back to TMEM for the PV MMA.
+// TMEM (512 columns): S0 [0,128) S1 [128,256) P0 [256,320) P1 [320,384) O [384,384+D).
+// Epilogue: O * gate/(mass + 1e-12) with gate = peak/(peak+gamma), stats M, Z, Nmax.
+// Semantics follow src/triton_pnfirtau.py:313-443 (the reference skips 64x64
+// tiles; here the skip unit is 128 query rows x 64 keys, and the optional
+// tile_flags record reports the 64x64 decisions of the same u values).
+//
+// Every mbarrier wait is bounded (sm100_ptx.cuh): on timeout the CTA sets the
+// caller's status word, drains its own TMA/MMA work and frees TMEM.
+#include <string.h>
+
+#include <mutex>
+
 #include "flash.cuh"
+#include "sm100_ptx.cuh"
 
 namespace pnft {
 
+using namespace sm100;
+
+namespace {
+
+constexpr int FM = 128;  // query rows per CTA (TMEM lanes)
+constexpr int FN = 128;  // keys per tile
+constexpr int F_THREADS = 384;
+
+// barrier slots
+enum : int {
+  B_QFULL = 0,
+  B_KFULL = 1,   // [2]
+  B_KEMPTY = 3,  // [2]
+  B_VFULL = 5,   // [2]
+  B_VEMPTY = 7,  // [2]
+  B_SFULL = 9,   // [2]
+  B_SEMPTY = 11, // [2]
+  B_VOTE = 13,   // [2]
+  B_PFULL = 15,  // [2]
+  B_PEMPTY = 17, // [2]
+  B_OFULL = 19,
+  B_FLAG = 20,  // plain arrive after the o_written flag is stored (release for the flag)
+  B_COUNT = 21
+};
+
+template <int D>
+struct FwdLayout {
+  static constexpr int GROUP = FM * 128;            // bytes of one 64-column (128 B) group of a 128-row tile
+  static constexpr int QBYTES = FM * D * 2;
+  static constexpr int KBYTES = FN * D * 2;
+  static constexpr int VBYTES = FN * D * 2;
+  static constexpr int OFF_Q = 0;
+  static constexpr int OFF_K = OFF_Q + QBYTES;       // 2 stages
+  static constexpr int OFF_V = OFF_K + 2 * KBYTES;   // 2 stages
+  static constexpr int OFF_BAR = OFF_V + 2 * VBYTES;
+  static constexpr int OFF_TMEM = OFF_BAR + B_COUNT * 8;
+  static constexpr int OFF_ABORT = OFF_TMEM + 4;
+  static constexpr int OFF_OWR = OFF_ABORT + 4;
+  static constexpr int OFF_VPART = OFF_OWR + 8;      // int [2 buf][2 half][4 warps]
+  static constexpr int OFF_LIVE = OFF_VPART + 64;    // int [2 buf][2 half]
+  static constexpr int OFF_STATS = OFF_LIVE + 16;    // float [2 half][4][128]: peak, mass, count, argmax
+  static constexpr int END = OFF_STATS + 2 * 4 * FM * 4;
+  static constexpr int ALLOC = END + 1024;           // slack to align the base to 1024
+  static constexpr int SMEM = ALLOC < 116 * 1024 ? 116 * 1024 : ALLOC;  // one CTA per SM (it owns all TMEM)
+};
+
+constexpr uint32_t TM_S = 0, TM_P = 256, TM_O = 384, TM_COLS = 512;
+
+struct FwdParams {
+  CUtensorMap tq, tk, tv;
+  void* out;
+  int64_t so[4];
+  float* out32;
+  float* stat_m;
+  float* stat_z;
+  int32_t* stat_nmax;
+  int32_t* stat_arg;
+  uint8_t* tile_flags;
+  const float* tau;
+  int32_t* status;
+  int H, N, nq;
+  float scale, gamma;
+  int has_gamma, causal;
+};
+
+template <int D>
+__global__ void __launch_bounds__(F_THREADS, 1) flash_fwd_sm100_kernel(const __grid_constant__ FwdParams p) {
+  using L = FwdLayout<D>;
+  constexpr int DG = D / 64;  // 64-column groups of a row
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  const uint32_t sb0 = smem_u32(smem);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int qt = p.nq - 1 - (int)blockIdx.x;  // longest causal rows first
+  const int bh = blockIdx.y, b = bh / p.H, hd = bh % p.H;
+  const int q0 = qt * FM;
+  const int ntiles = p.causal ? qt + 1 : p.nq;
+  auto bar = [&](int i) -> uint32_t { return sb0 + L::OFF_BAR + 8u * (uint32_t)i; };
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + L::OFF_ABORT);
+  volatile int* vpart = reinterpret_cast<volatile int*>(smem + L::OFF_VPART);
+  volatile int* live = reinterpret_cast<volatile int*>(smem + L::OFF_LIVE);
+  const Abort ab{abort_flag, p.status};
+
+  if (threadIdx.x == 0) {
+    mbar_init(bar(B_QFULL), 1);
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(bar(B_KFULL + i), 1);
+      mbar_init(bar(B_KEMPTY + i), 1);
+      mbar_init(bar(B_VFULL + i), 1);
+      mbar_init(bar(B_VEMPTY + i), 1);
+      mbar_init(bar(B_SFULL + i), 1);
+      mbar_init(bar(B_SEMPTY + i), 8);
+      mbar_init(bar(B_VOTE + i), 2);
+      mbar_init(bar(B_PFULL + i), 8);
+      mbar_init(bar(B_PEMPTY + i), 1);
+    }
+    mbar_init(bar(B_OFULL), 1);
+    mbar_init(bar(B_FLAG), 1);
+    *abort_flag = 0;
+    *reinterpret_cast<volatile int*>(smem + L::OFF_OWR) = 0;
+    fence_barrier_init();
+  }
+  if (warp == 0 && lane == 0) {
+    prefetch_tmap(&p.tq);
+    prefetch_tmap(&p.tk);
+    prefetch_tmap(&p.tv);
+  }
+  if (warp == 1) {
+    tmem_alloc(sb0 + L::OFF_TMEM, TM_COLS);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *reinterpret_cast<volatile uint32_t*>(smem + L::OFF_TMEM);
+  const uint32_t sQ = sb0 + L::OFF_Q;
+  auto sK = [&](int s) -> uint32_t { return sb0 + L::OFF_K + (uint32_t)s * L::KBYTES; };
+  auto sV = [&](int s) -> uint32_t { return sb0 + L::OFF_V + (uint32_t)s * L::VBYTES; };
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ producer
+    if (lane == 0) {
+      int k_last = -1, v_last = -1;
+      mbar_arrive_expect_tx(bar(B_QFULL), L::QBYTES);
+      for (int g = 0; g < DG; ++g) tma_load_4d(sQ + g * L::GROUP, &p.tq, bar(B_QFULL), 64 * g, q0, hd, b);
+      auto issue_k = [&](int j) -> bool {
+        const int s = j & 1;
+        if (!mbar_wait(bar(B_KEMPTY + s), ((j >> 1) & 1) ^ 1, ab)) return false;
+        mbar_arrive_expect_tx(bar(B_KFULL + s), L::KBYTES);
+        for (int g = 0; g < DG; ++g) tma_load_4d(sK(s) + g * L::GROUP, &p.tk, bar(B_KFULL + s), 64 * g, j * FN, hd, b);
+        k_last = j;
+        return true;
+      };
+      auto issue_v = [&](int j) -> bool {
+        const int s = j & 1;
+        if (!mbar_wait(bar(B_VOTE + s), (j >> 1) & 1, ab)) return false;
+        const int l0 = live[s * 2 + 0], l1 = live[s * 2 + 1];
+        if (!mbar_wait(bar(B_VEMPTY + s), ((j >> 1) & 1) ^ 1, ab)) return false;
+        mbar_arrive_expect_tx(bar(B_VFULL + s), (uint32_t)(l0 + l1) * (L::VBYTES / 2));
+        for (int hh = 0; hh < 2; ++hh) {
+          if (!(hh ? l1 : l0)) continue;
+          for (int g = 0; g < DG; ++g)
+            tma_load_4d(sV(s) + g * L::GROUP + hh * (L::GROUP / 2), &p.tv, bar(B_VFULL + s), 64 * g,
+                        j * FN + 64 * hh, hd, b);
+        }
+        v_last = j;
+        return true;
+      };
+      bool ok = issue_k(0);
+      for (int j = 0; ok && j < ntiles; ++j) {
+        if (j + 1 < ntiles) ok = issue_k(j + 1);
+        if (ok) ok = issue_v(j);
+      }
+      // drain: never leave a copy in flight into this CTA's shared memory
+      drain_wait(bar(B_QFULL), 0);
+      for (int j = k_last; j >= 0 && j > k_last - 2; --j) drain_wait(bar(B_KFULL + (j & 1)), (j >> 1) & 1);
+      for (int j = v_last; j >= 0 && j > v_last - 2; --j) drain_wait(bar(B_VFULL + (j & 1)), (j >> 1) & 1);
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------ MMA issuer
+    if (lane == 0) {
+      constexpr uint32_t ID_S = idesc_f16(FM, FN, 1, 0, 0);
+      constexpr uint32_t ID_O = idesc_f16(FM, D, 1, 0, 1);
+      uint32_t o_acc = 0;
+      auto issue_s = [&](int j) -> bool {
+        const int s = j & 1;
+        if (!mbar_wait(bar(B_KFULL + s), (j >> 1) & 1, ab)) return false;
+        if (!mbar_wait(bar(B_SEMPTY + s), ((j >> 1) & 1) ^ 1, ab)) return false;
+        tc_fence_after();
+#pragma unroll
+        for (int kk = 0; kk < D / 16; ++kk) {
+          const uint32_t off = (kk >> 2) * L::GROUP + (kk & 3) * 32;
+          mma_ss(tmem + TM_S + 128u * s, sw128_desc(sQ + off, 16, 1024), sw128_desc(sK(s) + off, 16, 1024), ID_S,
+                 kk > 0);
+        }
+        mma_commit(bar(B_SFULL + s));
+        mma_commit(bar(B_KEMPTY + s));
+        return true;
+      };
+      auto issue_pv = [&](int j) -> bool {
+        const int s = j & 1;
+        if (!mbar_wait(bar(B_PFULL + s), (j >> 1) & 1, ab)) return false;
+        if (!mbar_wait(bar(B_VFULL + s), (j >> 1) & 1, ab)) return false;
+        tc_fence_after();
+        const int l0 = live[s * 2 + 0], l1 = live[s * 2 + 1];
+        for (int hh = 0; hh < 2; ++hh) {
+          if (!(hh ? l1 : l0)) continue;
+#pragma unroll
+          for (int kq = 0; kq < 4; ++kq) {
+            const int kk = hh * 4 + kq;  // 16 keys per MMA
+            mma_ts(tmem + TM_O, tmem + TM_P + 64u * s + 8u * kk, sw128_desc(sV(s) + kk * 2048, L::GROUP, 1024), ID_O,
+                   o_acc);
+            o_acc = 1;
+          }
+        }
+        mma_commit(bar(B_PEMPTY + s));
+        mma_commit(bar(B_VEMPTY + s));
+        return true;
+      };
+      if (mbar_wait(bar(B_QFULL), 0, ab)) {
+        bool ok = true;
+        for (int j = 0; ok && j < ntiles; ++j) {
+          ok = issue_s(j);
+          if (ok && j >= 1) ok = issue_pv(j - 1);
+        }
+        if (ok) issue_pv(ntiles - 1);
+      }
+      *reinterpret_cast<volatile int*>(smem + L::OFF_OWR) = (int)o_acc;
+      mbar_arrive(bar(B_FLAG));
+      mma_commit(bar(B_OFULL));
+      drain_wait(bar(B_OFULL), 0);  // no MMA may still be writing TMEM at teardown
+    }
+  } else if (warp >= 4) {
+    // ------------------------------------------------------------ elementwise
+    const int ew = warp - 4, hh = ew >> 2, wq = warp & 3;
+    const int rl = 32 * wq + lane;  // TMEM lane = local query row
+    const int row = q0 + rl;
+    const uint32_t lane_off = (uint32_t)(32 * wq) << 16;
+    const float tau = __ldg(p.tau);
+    const float hs = 0.5f * p.scale, ht = -0.5f * tau;  // h = s/2 exactly
+    const int nT64 = (p.N + 63) >> 6;
+    float peak = 0.f, cnt = 0.f;
+    int arg = -1;  // first key attaining the running peak in this column half
+    float ms[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) ms[i] = 0.f;
+    // `dead` (warp-uniform) turns the rest of the loop into no-ops after an
+    // abort, while every warp still passes the warpgroup's named barriers.
+    bool dead = false;
+    for (int j = 0; j < ntiles; ++j) {
+      const int s = j & 1;
+      if (!dead) dead = !warp_wait(bar(B_SFULL + s), (j >> 1) & 1, ab);
+      uint32_t r0[32], r1[32];
+      if (!dead) {
+        tc_fence_after();
+        tmem_ld32(tmem + lane_off + TM_S + 128u * s + 64u * hh, r0);
+        tmem_ld32(tmem + lane_off + TM_S + 128u * s + 64u * hh + 32u, r1);
+        tmem_wait_ld();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(bar(B_SEMPTY + s));
+      } else {
+#pragma unroll
+        for (int c = 0; c < 32; ++c) r0[c] = r1[c] = 0xbf800000u;  // -1.0f: silent
+      }
+      float x[64];
+#pragma unroll
+      for (int c = 0; c < 32; ++c) {
+        x[c] = fmaf(__uint_as_float(r0[c]), hs, ht);
+        x[32 + c] = fmaf(__uint_as_float(r1[c]), hs, ht);
+      }
+      const int kb = j * FN + 64 * hh;
+      const int lim = row < p.N ? (p.causal ? row : p.N - 1) - kb : -1;  // last valid column offset
+      if (lim < 63) {
+#pragma unroll
+        for (int c = 0; c < 64; ++c) x[c] = c > lim ? -1.f : x[c];
+      }
+      float m = max3(x[0], x[1], x[2]);
+#pragma unroll
+      for (int c = 3; c < 63; c += 2) m = max3(m, x[c], x[c + 1]);
+      m = fmaxf(m, x[63]);
+      const unsigned live_w = __any_sync(0xffffffffu, m > 0.f);
+      if (lane == 0) {
+        vpart[(s * 2 + hh) * 4 + wq] = (int)live_w;
+        if (p.tile_flags && live_w) {
+          const int qi = (q0 >> 6) + (wq >> 1), kj = kb >> 6;
+          if (qi < nT64 && kj < nT64) p.tile_flags[((int64_t)bh * nT64 + qi) * nT64 + kj] = 1;
+        }
+      }
+      named_bar_sync(1 + hh, 128);
+      const int live_h = vpart[(s * 2 + hh) * 4 + 0] | vpart[(s * 2 + hh) * 4 + 1] | vpart[(s * 2 + hh) * 4 + 2] |
+                         vpart[(s * 2 + hh) * 4 + 3];
+      if (ew == 4 * hh && lane == 0) {
+        live[s * 2 + hh] = live_h;
+        mbar_arrive(bar(B_VOTE + s));
+      }
+      if (live_h && !dead) dead = !warp_wait(bar(B_PEMPTY + s), ((j >> 1) & 1) ^ 1, ab);
+      if (live_h && !dead) {
+        tc_fence_after();
+        const float mu = m > 0.f ? 2.f * m : 0.f;  // row max of u over this half tile
+        if (mu > 0.f && mu >= peak) {
+          float c = 0.f;
+          int first = 64;
+#pragma unroll
+          for (int i = 63; i >= 0; --i) {
+            const bool hit = x[i] == m;
+            c += hit ? 1.f : 0.f;
+            first = hit ? i : first;
+          }
+          if (mu > peak) arg = kb + first;  // equal to an earlier tile's peak: keep the earlier key
+          cnt = mu > peak ? c : cnt + c;
+          peak = mu;
+        }
+        uint32_t pk[32];
+#pragma unroll
+        for (int c = 0; c < 32; ++c) {
+          const float u0 = x[2 * c] + fabsf(x[2 * c]);
+          const float u1 = x[2 * c + 1] + fabsf(x[2 * c + 1]);
+          const float a2 = u0 * u0, a4 = a2 * a2, p0 = a4 * a4 * a2;
+          const float b2 = u1 * u1, b4 = b2 * b2, p1 = b4 * b4 * b2;
+          ms[c & 7] += p0 + p1;
+          pk[c] = pack_bf16x2(p0, p1);
+        }
+        tmem_st32(tmem + lane_off + TM_P + 64u * s + 32u * hh, pk);
+        tmem_wait_st();
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(bar(B_PFULL + s));
+    }
+    // ---- epilogue: merge the two column halves of every row, scale O, store
+    float* st = reinterpret_cast<float*>(smem + L::OFF_STATS);
+    const float mass_h = ((ms[0] + ms[1]) + (ms[2] + ms[3])) + ((ms[4] + ms[5]) + (ms[6] + ms[7]));
+    st[(hh * 4 + 0) * FM + rl] = peak;
+    st[(hh * 4 + 1) * FM + rl] = mass_h;
+    st[(hh * 4 + 2) * FM + rl] = cnt;
+    st[(hh * 4 + 3) * FM + rl] = __int_as_float(arg);
+    named_bar_sync(3, 256);
+    const float p0 = st[0 * FM + rl], p1 = st[4 * FM + rl];
+    const float pk = fmaxf(p0, p1);
+    const float mass = st[1 * FM + rl] + st[5 * FM + rl];
+    const float nm = pk > 0.f ? (p0 == pk ? st[2 * FM + rl] : 0.f) + (p1 == pk ? st[6 * FM + rl] : 0.f) : 0.f;
+    // first key of the row maximum: the lower key half wins a tie between halves of one tile,
+    // otherwise the earlier tile (each half already kept its earliest key)
+    const int a0 = __float_as_int(st[3 * FM + rl]), a1 = __float_as_int(st[7 * FM + rl]);
+    int amax = -1;
+    if (pk > 0.f) amax = (p0 == pk && p1 == pk) ? min(a0, a1) : (p0 == pk ? a0 : a1);
+    const float z = mass + 1e-12f;
+    float gate = 0.f;
+    if (pk > 0.f) gate = p.has_gamma ? pk / (pk + p.gamma) : 1.f;
+    const float so = gate / z;
+    const bool o_ok = warp_wait(bar(B_OFULL), 0, ab) && warp_wait(bar(B_FLAG), 0, ab);
+    tc_fence_after();
+    const bool o_written = o_ok && *reinterpret_cast<volatile int*>(smem + L::OFF_OWR) != 0;
+    __nv_bfloat16* O = static_cast<__nv_bfloat16*>(p.out) + (int64_t)b * p.so[0] + (int64_t)hd * p.so[1] +
+                       (int64_t)row * p.so[2];
+#pragma unroll
+    for (int cb = 0; cb < D / 2; cb += 32) {
+      const int d0 = hh * (D / 2) + cb;
+      uint32_t r[32];
+      if (o_written) {
+        tmem_ld32(tmem + lane_off + TM_O + (uint32_t)d0, r);
+        tmem_wait_ld();
+      }
+      if (row < p.N && o_ok && p.out32) {
+        float4* o32 = reinterpret_cast<float4*>(p.out32 + ((int64_t)bh * p.N + row) * D + d0);
+#pragma unroll
+        for (int v = 0; v < 8; ++v) {
+          float4 f;
+          f.x = o_written ? __uint_as_float(r[4 * v + 0]) * so : 0.f;
+          f.y = o_written ? __uint_as_float(r[4 * v + 1]) * so : 0.f;
+          f.z = o_written ? __uint_as_float(r[4 * v + 2]) * so : 0.f;
+          f.w = o_written ? __uint_as_float(r[4 * v + 3]) * so : 0.f;
+          o32[v] = f;
+        }
+      }
+      if (row < p.N && o_ok) {
+        if (p.so[3] == 1 && (reinterpret_cast<uintptr_t>(O + d0) & 15) == 0) {
+#pragma unroll
+          for (int v = 0; v < 4; ++v) {
+            uint4 w;
+            uint32_t* wp = reinterpret_cast<uint32_t*>(&w);
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+              const float lo = o_written ? __uint_as_float(r[8 * v + 2 * e]) * so : 0.f;
+              const float hi = o_written ? __uint_as_float(r[8 * v + 2 * e + 1]) * so : 0.f;
+              wp[e] = pack_bf16x2(lo, hi);
+            }
+            *reinterpret_cast<uint4*>(O + d0 + 8 * v) = w;
+          }
+        } else {
+#pragma unroll
+          for (int e = 0; e < 32; ++e)
+            O[(int64_t)(d0 + e) * p.so[3]] = __float2bfloat16_rn(o_written ? __uint_as_float(r[e]) * so : 0.f);
+        }
+      }
+    }
+    if (hh == 0 && row < p.N && o_ok) {
+      const int64_t si = (int64_t)bh * p.N + row;
+      p.stat_m[si] = pk;
+      p.stat_z[si] = z;
+      p.stat_nmax[si] = (int32_t)nm;
+      p.stat_arg[si] = amax;
+    }
+  }
+  // ---------------------------------------------------------------- teardown
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, TM_COLS);
+  }
+}
+
+}  // namespace
+
+// ------------------------------------------------------------------ host side
+typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                  const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+static EncodeTiledFn encode_fn() {
+  static EncodeTiledFn fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* f = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &f, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeTiledFn>(f);
+  });
+  return fn;
+}
+
+int tma_map_bhnd(CUtensorMap* m, const void* base, const int64_t* s, int64_t B, int64_t H, int64_t N, int64_t D,
+                 int rows) {
+  EncodeTiledFn enc = encode_fn();
+  if (!enc) return fail(PNFT_ECUDA, "cuTensorMapEncodeTiled unavailable from the driver");
+  const cuuint64_t dims[4] = {(cuuint64_t)D, (cuuint64_t)N, (cuuint64_t)H, (cuuint64_t)B};
+  const cuuint64_t strides[3] = {(cuuint64_t)s[2] * 2, (cuuint64_t)s[1] * 2, (cuuint64_t)s[0] * 2};
+  const cuuint32_t box[4] = {64, (cuuint32_t)rows, 1, 1};
+  const cuuint32_t estr[4] = {1, 1, 1, 1};
+  const CUresult r = enc(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 4, const_cast<void*>(base), dims, strides, box, estr,
+                         CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                         CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return fail(PNFT_ECUDA, "cuTensorMapEncodeTiled failed (%d)", (int)r);
+  return PNFT_OK;
+}
+
+bool tma_ok_bhnd(const void* ptr, const int64_t* s) {
+  if ((reinterpret_cast<uintptr_t>(ptr) & 15) != 0) return false;
+  if (s[3] != 1) return false;
+  for (int i = 0; i < 3; ++i)
+    if (s[i] <= 0 || (s[i] % 8) != 0 || s[i] >= ((int64_t)1 << 38)) return false;
+  return true;
+}
+
+bool device_is_sm100() {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return false;
+  int major = 0, minor = 0;
+  if (cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, dev) != cudaSuccess) return false;
+  if (cudaDeviceGetAttribute(&minor, cudaDevAttrComputeCapabilityMinor, dev) != cudaSuccess) return false;
+  return major == 10 && minor == 0;
+}
+
+// Both passes of a bf16 call run on the same kernel family: the backward's tie
+// test u == peak needs the forward's S recomputed by the same arithmetic.
 bool flash_sm100_supported(const FlashArgs& a) {
-  (void)a;
-  return false;
+  if (a.dtype != PNFT_DTYPE_BF16) return false;
+  if (a.D != 64 && a.D != 128) return false;
+  if (a.N < 1 || a.N > (int64_t)1 << 30) return false;
+  if (!tma_ok_bhnd(a.q, a.sq) || !tma_ok_bhnd(a.k, a.sk) || !tma_ok_bhnd(a.v, a.sv)) return false;
+  return device_is_sm100();
 }
 
 int flash_fwd_sm100(const FlashArgs& a, cudaStream_t st) {
-  (void)a; (void)st;
-  return fail(PNFT_EUNSUPPORTED, "flash fwd sm100: not built");
-}
-
-int flash_bwd_sm100(const FlashArgs& a, cudaStream_t st) {
-  (void)a; (void)st;
-  return fail(PNFT_EUNSUPPORTED, "flash bwd sm100: not built");
+  FwdParams p;
+  memset(&p, 0, sizeof(p));
+  int rc = tma_map_bhnd(&p.tq, a.q, a.sq, a.B, a.H, a.N, a.D, FM);
+  if (!rc) rc = tma_map_bhnd(&p.tk, a.k, a.sk, a.B, a.H, a.N, a.D, FN);
+  if (!rc) rc = tma_map_bhnd(&p.tv, a.v, a.sv, a.B, a.H, a.N, a.D, FN / 2);
+  if (rc) return rc;
+  p.out = a.out;
+  for (int i = 0; i < 4; ++i) p.so[i] = a.so[i];
+  p.out32 = a.out32;
+  p.stat_m = a.stat_m;
+  p.stat_z = a.stat_z;
+  p.stat_nmax = a.stat_nmax;
+  p.stat_arg = a.stat_arg;
+  p.tile_flags = a.tile_flags;
+  p.tau = a.tau;
+  p.status = a.status;
+  p.H = (int)a.H;
+  p.N = (int)a.N;
+  p.nq = (int)((a.N + FM - 1) / FM);
+  p.scale = a.scale;
+  p.gamma = a.gamma;
+  p.has_gamma = a.has_gamma;
+  p.causal = a.causal;
+  const dim3 grid((unsigned)p.nq, (unsigned)(a.B * a.H));
+  auto launch = [&](auto kern, int smem) -> int {
+    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess)
+      return check_launch("flash fwd sm100: smem attribute", 0);
+    kern<<<grid, F_THREADS, smem, st>>>(p);
+    return check_launch("flash fwd sm100");
+  };
+  if (a.D == 64) return launch(flash_fwd_sm100_kernel<64>, FwdLayout<64>::SMEM);
+  return launch(flash_fwd_sm100_kernel<128>, FwdLayout<128>::SMEM);
 }
 
 }  // namespace pnft

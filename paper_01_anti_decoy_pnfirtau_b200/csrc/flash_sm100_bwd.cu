@@ -1,0 +1,487 @@
+// sm_100a backward of flash pn_fir_tau (bf16, head dim 64/128).
+//
+// One CTA per (128 keys, b*h), KV-parallel over the 64-query tiles at or below
+// the causal diagonal whose rows are not all silent (per-tile flags from the
+// prep kernel). 512 threads:
+//   warp 0       TMA producer: K, V once; per query tile Q, dO (2 stages) and
+//                the 64 per-row coefficient records.
+//   warp 1       MMA issuer + TMEM owner. Per tile t:
+//                  S^T = K Q^T, dP^T = V dO^T            (SS, M=128 keys, N=64)
+//                then for tile t-1 (overlapping tile t's elementwise work):
+//                  dV += P^T dO   (TS: P^T bf16 from TMEM)
+//                  dK += dS^T Q   (SS: dS^T bf16 from shared memory)
+//                  dQ  = dS K     (D=64: M=64 queries) or
+//                  dQ^T = K^T dS^T (D=128: M=128 head dims), into TMEM
+//   warps 4-11   elementwise, thread = TMEM lane = key; warpgroup g owns query
+//                columns [32g, 32g+32). Each thread pulls its whole S/dP slice
+//                into registers and releases TMEM at once, then computes
+//                u = relu(S*scale - tau), W = u^10 gate/z (-> P^T in TMEM) and
+//                dS = 10 scale gate/z u^9 (dP - D) + [u == peak] tie (-> smem,
+//                128-byte swizzled), accumulating dtau = -sum dS / scale.
+//   warps 12-15  dQ drain: TMEM -> fp32 staging tile in smem -> one
+//                cp.reduce.async.bulk add into the fp32 dQ accumulator.
+// Finally the elementwise warps write dK, dV (bf16) from TMEM.
+// TMEM columns: S [0,64) dP [64,128) P^T x2 [128,192) dV [192,192+D)
+//               dK [192+D,192+2D) dQ (x2 for D=64) [192+2D, 512).
+// Semantics: src/triton_pnfirtau.py:445-621 with the per-row terms of
+// flash_bwd_prep (RowCoef). S is recomputed by the tensor core exactly as in
+// the tcgen05 forward, so u == peak finds the forward's maxima.
+#include <string.h>
+
+#include "flash.cuh"
+#include "sm100_ptx.cuh"
+
+namespace pnft {
+
+using namespace sm100;
+
+namespace {
+
+constexpr int BN = 128;  // keys per CTA (TMEM lanes)
+constexpr int BM = 64;   // queries per tile
+constexpr int B_THREADS = 512;
+
+enum : int {
+  C_KV = 0,
+  C_QDFULL = 1,    // [2]
+  C_QDEMPTY = 3,   // [2]
+  C_SDPFULL = 5,
+  C_SDPEMPTY = 6,
+  C_PDSFULL = 7,   // [2]
+  C_PDSEMPTY = 9,  // [2]
+  C_DQFULL = 11,   // [2]
+  C_DQEMPTY = 13,  // [2]
+  C_DKV = 15,
+  C_FLAG = 16,  // plain arrive after dkv_written is stored (release for the flag)
+  C_COUNT = 17
+};
+
+template <int D>
+struct BwdLayout {
+  static constexpr int KGROUP = BN * 128;  // one 64-column group of the K / V tile
+  static constexpr int QGROUP = BM * 128;  // one 64-column group of a Q / dO tile
+  static constexpr int KBYTES = BN * D * 2;
+  static constexpr int QBYTES = BM * D * 2;
+  static constexpr int NDQ = D == 64 ? 2 : 1;   // dQ buffers in TMEM
+  static constexpr int NSTG = D == 64 ? 2 : 1;  // dQ staging tiles in smem
+  static constexpr int STG_BYTES = BM * D * 4;
+  static constexpr int DS_BYTES = BN * BM * 2;
+  static constexpr int COEF_BYTES = BM * 32;
+  static constexpr int OFF_K = 0;
+  static constexpr int OFF_V = OFF_K + KBYTES;
+  static constexpr int OFF_Q = OFF_V + KBYTES;
+  static constexpr int OFF_DO = OFF_Q + 2 * QBYTES;
+  static constexpr int OFF_DS = OFF_DO + 2 * QBYTES;
+  static constexpr int OFF_STG = OFF_DS + 2 * DS_BYTES;
+  static constexpr int OFF_COEF = OFF_STG + NSTG * STG_BYTES;
+  static constexpr int OFF_BAR = OFF_COEF + 2 * COEF_BYTES;
+  static constexpr int OFF_TMEM = OFF_BAR + C_COUNT * 8;
+  static constexpr int OFF_ABORT = OFF_TMEM + 4;
+  static constexpr int OFF_DKVW = OFF_ABORT + 4;
+  static constexpr int OFF_RED = OFF_DKVW + 8;  // 8 floats
+  static constexpr int END = OFF_RED + 32;
+  static constexpr int SMEM = END + 1024;
+  static constexpr uint32_t TM_S = 0, TM_DP = 64, TM_P = 128, TM_DV = 192, TM_DK = 192 + D, TM_DQ = 192 + 2 * D;
+};
+
+struct BwdParams {
+  CUtensorMap tk, tv, tq, tdo;
+  const float4* coef;
+  const int32_t* live64;
+  float* dq_acc;
+  void* dk;
+  int64_t sdk[4];
+  void* dv;
+  int64_t sdv[4];
+  float* dtau_part;
+  const float* tau;
+  int32_t* status;
+  int H, N, nq64, nkt;
+  float scale;
+  int causal;
+};
+
+__device__ __forceinline__ void st_shared_v4(uint32_t addr, uint32_t a, uint32_t b, uint32_t c, uint32_t d) {
+  asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "r"(a), "r"(b), "r"(c), "r"(d) : "memory");
+}
+
+template <int D>
+__global__ void __launch_bounds__(B_THREADS, 1) flash_bwd_sm100_kernel(const __grid_constant__ BwdParams p) {
+  using L = BwdLayout<D>;
+  constexpr int DG = D / 64;
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  const uint32_t sb0 = smem_u32(smem);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int kt = blockIdx.x, bh = blockIdx.y, b = bh / p.H, hd = bh % p.H;
+  const int k0 = kt * BN;
+  const int i_first = p.causal ? k0 / BM : 0;
+  const int32_t* live = p.live64 + (int64_t)bh * p.nq64;
+  auto bar = [&](int i) -> uint32_t { return sb0 + L::OFF_BAR + 8u * (uint32_t)i; };
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + L::OFF_ABORT);
+  volatile int* dkv_written = reinterpret_cast<volatile int*>(smem + L::OFF_DKVW);
+  const Abort ab{abort_flag, p.status};
+  const uint32_t sK = sb0 + L::OFF_K, sV = sb0 + L::OFF_V;
+  auto sQ = [&](int s) -> uint32_t { return sb0 + L::OFF_Q + (uint32_t)s * L::QBYTES; };
+  auto sdO = [&](int s) -> uint32_t { return sb0 + L::OFF_DO + (uint32_t)s * L::QBYTES; };
+  auto sdS = [&](int s) -> uint32_t { return sb0 + L::OFF_DS + (uint32_t)s * L::DS_BYTES; };
+
+  if (threadIdx.x == 0) {
+    mbar_init(bar(C_KV), 1);
+    mbar_init(bar(C_SDPFULL), 1);
+    mbar_init(bar(C_SDPEMPTY), 8);
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(bar(C_QDFULL + i), 1);
+      mbar_init(bar(C_QDEMPTY + i), 1);
+      mbar_init(bar(C_PDSFULL + i), 8);
+      mbar_init(bar(C_PDSEMPTY + i), 1);
+      mbar_init(bar(C_DQFULL + i), 1);
+      mbar_init(bar(C_DQEMPTY + i), 4);
+    }
+    mbar_init(bar(C_DKV), 1);
+    mbar_init(bar(C_FLAG), 1);
+    *abort_flag = 0;
+    *dkv_written = 0;
+    fence_barrier_init();
+  }
+  if (warp == 0 && lane == 0) {
+    prefetch_tmap(&p.tk);
+    prefetch_tmap(&p.tv);
+    prefetch_tmap(&p.tq);
+    prefetch_tmap(&p.tdo);
+  }
+  if (warp == 1) {
+    tmem_alloc(sb0 + L::OFF_TMEM, 512);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *reinterpret_cast<volatile uint32_t*>(smem + L::OFF_TMEM);
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ producer
+    if (lane == 0) {
+      mbar_arrive_expect_tx(bar(C_KV), 2 * L::KBYTES);
+      for (int g = 0; g < DG; ++g) {
+        tma_load_4d(sK + g * L::KGROUP, &p.tk, bar(C_KV), 64 * g, k0, hd, b);
+        tma_load_4d(sV + g * L::KGROUP, &p.tv, bar(C_KV), 64 * g, k0, hd, b);
+      }
+      int t = 0;
+      bool ok = true;
+      for (int i = i_first; ok && i < p.nq64; ++i) {
+        if (!live[i]) continue;
+        const int s = t & 1;
+        if (!(ok = mbar_wait(bar(C_QDEMPTY + s), ((t >> 1) & 1) ^ 1, ab))) break;
+        const int q0 = i * BM;
+        mbar_arrive_expect_tx(bar(C_QDFULL + s), 2 * L::QBYTES + L::COEF_BYTES);
+        for (int g = 0; g < DG; ++g) {
+          tma_load_4d(sQ(s) + g * L::QGROUP, &p.tq, bar(C_QDFULL + s), 64 * g, q0, hd, b);
+          tma_load_4d(sdO(s) + g * L::QGROUP, &p.tdo, bar(C_QDFULL + s), 64 * g, q0, hd, b);
+        }
+        // 64 records always: the coefficient buffer carries 64 zero records past its end
+        bulk_load(sb0 + L::OFF_COEF + s * L::COEF_BYTES, p.coef + ((int64_t)bh * p.N + q0) * kCoefStride,
+                  L::COEF_BYTES, bar(C_QDFULL + s));
+        ++t;
+      }
+      drain_wait(bar(C_KV), 0);
+      for (int u = t - 1; u >= 0 && u > t - 3; --u) drain_wait(bar(C_QDFULL + (u & 1)), (u >> 1) & 1);
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------ MMA issuer
+    if (lane == 0) {
+      constexpr uint32_t ID_S = idesc_f16(BN, BM, 1, 0, 0);   // S^T, dP^T: K-major A and B
+      constexpr uint32_t ID_G = idesc_f16(BN, D, 1, 0, 1);    // dV (A in TMEM), dK (A K-major); B MN-major
+      constexpr uint32_t ID_DQ = idesc_f16(D, BM, 1, 1, 1);   // dQ^T: M = head dims
+      uint32_t dv_acc = 0, dk_acc = 0;
+      auto grads = [&](int u) -> bool {
+        const int s = u & 1;
+        if (!mbar_wait(bar(C_PDSFULL + s), (u >> 1) & 1, ab)) return false;
+        tc_fence_after();
+#pragma unroll
+        for (int kk = 0; kk < BM / 16; ++kk) {
+          mma_ts(tmem + L::TM_DV, tmem + L::TM_P + 32u * s + 8u * kk, sw128_desc(sdO(s) + kk * 2048, L::QGROUP, 1024),
+                 ID_G, dv_acc);
+          dv_acc = 1;
+        }
+#pragma unroll
+        for (int kk = 0; kk < BM / 16; ++kk) {
+          mma_ss(tmem + L::TM_DK, sw128_desc(sdS(s) + kk * 32, 16, 1024),
+                 sw128_desc(sQ(s) + kk * 2048, L::QGROUP, 1024), ID_G, dk_acc);
+          dk_acc = 1;
+        }
+        const int bq = u % L::NDQ;
+        if (!mbar_wait(bar(C_DQEMPTY + bq), ((u / L::NDQ) & 1) ^ 1, ab)) return false;
+        tc_fence_after();
+        // dQ^T[D x 64 q] = K^T[D x keys] dS^T[keys x q]: both operands MN-major in smem
+#pragma unroll
+        for (int kk = 0; kk < BN / 16; ++kk)
+          mma_ss(tmem + L::TM_DQ + 64u * bq, sw128_desc(sK + kk * 2048, L::KGROUP, 1024),
+                 sw128_desc(sdS(s) + kk * 2048, L::KGROUP, 1024), ID_DQ, kk > 0);
+        mma_commit(bar(C_DQFULL + bq));
+        mma_commit(bar(C_PDSEMPTY + s));
+        mma_commit(bar(C_QDEMPTY + s));
+        return true;
+      };
+      int t = 0;
+      bool ok = mbar_wait(bar(C_KV), 0, ab);
+      for (int i = i_first; ok && i < p.nq64; ++i) {
+        if (!live[i]) continue;
+        const int s = t & 1;
+        if (!(ok = mbar_wait(bar(C_QDFULL + s), (t >> 1) & 1, ab))) break;
+        if (!(ok = mbar_wait(bar(C_SDPEMPTY), (t & 1) ^ 1, ab))) break;
+        tc_fence_after();
+#pragma unroll
+        for (int kk = 0; kk < D / 16; ++kk) {
+          const uint32_t ok_ = (kk >> 2) * L::KGROUP + (kk & 3) * 32, oq = (kk >> 2) * L::QGROUP + (kk & 3) * 32;
+          mma_ss(tmem + L::TM_S, sw128_desc(sK + ok_, 16, 1024), sw128_desc(sQ(s) + oq, 16, 1024), ID_S, kk > 0);
+        }
+#pragma unroll
+        for (int kk = 0; kk < D / 16; ++kk) {
+          const uint32_t ok_ = (kk >> 2) * L::KGROUP + (kk & 3) * 32, oq = (kk >> 2) * L::QGROUP + (kk & 3) * 32;
+          mma_ss(tmem + L::TM_DP, sw128_desc(sV + ok_, 16, 1024), sw128_desc(sdO(s) + oq, 16, 1024), ID_S, kk > 0);
+        }
+        mma_commit(bar(C_SDPFULL));
+        if (t >= 1) ok = grads(t - 1);
+        ++t;
+      }
+      if (ok && t >= 1) ok = grads(t - 1);
+      *dkv_written = (ok && t >= 1) ? 1 : 0;
+      mbar_arrive(bar(C_FLAG));
+      mma_commit(bar(C_DKV));
+      drain_wait(bar(C_DKV), 0);
+    }
+  } else if (warp >= 4 && warp < 12) {
+    // ------------------------------------------------------------ elementwise
+    const int ew = warp - 4, hh = ew >> 2, wq = warp & 3;
+    const int rl = 32 * wq + lane;
+    const int key = k0 + rl;
+    const uint32_t lane_off = (uint32_t)(32 * wq) << 16;
+    const float tau = __ldg(p.tau);
+    const float hs = 0.5f * p.scale, ht = -0.5f * tau;
+    float ds_sum = 0.f;
+    bool dead = false;
+    int t = 0;
+    for (int i = i_first; i < p.nq64; ++i) {
+      if (!live[i]) continue;
+      const int s = t & 1;
+      const int q0 = i * BM;
+      if (!dead) dead = !warp_wait(bar(C_SDPFULL), t & 1, ab);
+      uint32_t rs[32], rp[32];
+      if (!dead) {
+        tc_fence_after();
+        tmem_ld32(tmem + lane_off + L::TM_S + 32u * hh, rs);
+        tmem_ld32(tmem + lane_off + L::TM_DP + 32u * hh, rp);
+        tmem_wait_ld();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(bar(C_SDPEMPTY));
+      }
+      if (!dead) dead = !warp_wait(bar(C_QDFULL + s), (t >> 1) & 1, ab);     // coefficient records
+      if (!dead) dead = !warp_wait(bar(C_PDSEMPTY + s), ((t >> 1) & 1) ^ 1, ab);  // P^T / dS buffers
+      if (!dead) {
+        tc_fence_after();
+        const float4* cf = reinterpret_cast<const float4*>(smem + L::OFF_COEF + s * L::COEF_BYTES);
+        // columns past the diagonal or the sequence end hold u = 0
+        const int qb = q0 + 32 * hh;
+        const int lim = key < p.N ? (p.causal ? key : 0) : 0x7fffffff;  // first valid query
+        const int qend = p.N;
+#pragma unroll
+        for (int half = 0; half < 2; ++half) {
+          uint32_t pw_pk[8], ds_pk[8];
+#pragma unroll
+          for (int c2 = 0; c2 < 8; ++c2) {
+            float wv[2], dv2[2];
+#pragma unroll
+            for (int e = 0; e < 2; ++e) {
+              const int c = half * 16 + 2 * c2 + e;
+              const int q = qb + c;
+              float x = fmaf(__uint_as_float(rs[c]), hs, ht);
+              x = (q >= lim && q < qend) ? x : -1.f;
+              const float u = x + fabsf(x);
+              const float4 c0 = cf[(32 * hh + c) * kCoefStride];      // peak, gate/z, 10 scale gate/z, D
+              const float4 c1 = cf[(32 * hh + c) * kCoefStride + 1];  // tie, argmax key, peak for ties
+              const float u2 = u * u, u4 = u2 * u2, u8 = u4 * u4, u9 = u8 * u;
+              wv[e] = u8 * u2 * c0.y;
+              const bool at_peak = u > 0.f && (key == __float_as_int(c1.y) || u == c1.z);
+              const float ds = fmaf(c0.z * u9, __uint_as_float(rp[c]) - c0.w, at_peak ? c1.x : 0.f);
+              dv2[e] = ds;
+              ds_sum += ds;
+            }
+            pw_pk[c2] = pack_bf16x2(wv[0], wv[1]);
+            ds_pk[c2] = pack_bf16x2(dv2[0], dv2[1]);
+          }
+          tmem_st8(tmem + lane_off + L::TM_P + 32u * s + 16u * hh + 8u * half, pw_pk);
+#pragma unroll
+          for (int cc = 0; cc < 2; ++cc) {
+            const uint32_t chunk = 4 * hh + 2 * half + cc;  // 16-byte chunk of the 128-byte key row
+            st_shared_v4(sdS(s) + rl * 128 + ((chunk ^ (rl & 7)) << 4), ds_pk[4 * cc], ds_pk[4 * cc + 1],
+                         ds_pk[4 * cc + 2], ds_pk[4 * cc + 3]);
+          }
+        }
+        tmem_wait_st();
+        fence_proxy_async_smem();
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(bar(C_PDSFULL + s));
+      ++t;
+    }
+    // ---- dK, dV: rows of this CTA's keys, warpgroup g writes head dims [g*D/2, (g+1)*D/2)
+    const bool ok = warp_wait(bar(C_DKV), 0, ab) && warp_wait(bar(C_FLAG), 0, ab);
+    tc_fence_after();
+    const bool have = ok && *dkv_written != 0;
+#pragma unroll
+    for (int m = 0; m < 2; ++m) {
+      __nv_bfloat16* G = static_cast<__nv_bfloat16*>(m == 0 ? p.dv : p.dk);
+      const int64_t* sg = m == 0 ? p.sdv : p.sdk;
+      const uint32_t tcol = m == 0 ? L::TM_DV : L::TM_DK;
+      __nv_bfloat16* row = G + (int64_t)b * sg[0] + (int64_t)hd * sg[1] + (int64_t)key * sg[2];
+#pragma unroll
+      for (int cb = 0; cb < D / 2; cb += 32) {
+        const int d0 = hh * (D / 2) + cb;
+        uint32_t r[32];
+        if (have) {
+          tmem_ld32(tmem + lane_off + tcol + (uint32_t)d0, r);
+          tmem_wait_ld();
+        } else {
+#pragma unroll
+          for (int e = 0; e < 32; ++e) r[e] = 0u;
+        }
+        if (key < p.N && ok) {
+          if (sg[3] == 1 && (reinterpret_cast<uintptr_t>(row + d0) & 15) == 0) {
+#pragma unroll
+            for (int v = 0; v < 4; ++v) {
+              uint4 w;
+              w.x = pack_bf16x2(__uint_as_float(r[8 * v + 0]), __uint_as_float(r[8 * v + 1]));
+              w.y = pack_bf16x2(__uint_as_float(r[8 * v + 2]), __uint_as_float(r[8 * v + 3]));
+              w.z = pack_bf16x2(__uint_as_float(r[8 * v + 4]), __uint_as_float(r[8 * v + 5]));
+              w.w = pack_bf16x2(__uint_as_float(r[8 * v + 6]), __uint_as_float(r[8 * v + 7]));
+              *reinterpret_cast<uint4*>(row + d0 + 8 * v) = w;
+            }
+          } else {
+#pragma unroll
+            for (int e = 0; e < 32; ++e) row[(int64_t)(d0 + e) * sg[3]] = __float2bfloat16_rn(__uint_as_float(r[e]));
+          }
+        }
+      }
+    }
+    // ---- tau gradient partial of this CTA (fixed reduction order)
+    float v = ds_sum;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    float* red = reinterpret_cast<float*>(smem + L::OFF_RED);
+    if (lane == 0) red[ew] = v;
+    named_bar_sync(3, 256);
+    if (ew == 0 && lane == 0) {
+      float tot = 0.f;
+#pragma unroll
+      for (int w = 0; w < 8; ++w) tot += red[w];
+      p.dtau_part[(int64_t)bh * p.nkt + kt] = -tot / p.scale;
+    }
+  } else if (warp >= 12) {
+    // ------------------------------------------------------------ dQ drain
+    const int wq = warp & 3;
+    const uint32_t lane_off = (uint32_t)(32 * wq) << 16;
+    const bool leader = warp == 12 && lane == 0;
+    bool dead = false;
+    int t = 0;
+    for (int i = i_first; i < p.nq64; ++i) {
+      if (!live[i]) continue;
+      const int bq = t % L::NDQ, sg = t % L::NSTG;
+      const int q0 = i * BM;
+      if (!dead) dead = !warp_wait(bar(C_DQFULL + bq), (t / L::NDQ) & 1, ab);
+      uint32_t r0[32], r1[32];
+      if (!dead) {
+        tc_fence_after();
+        tmem_ld32(tmem + lane_off + L::TM_DQ + 64u * bq, r0);
+        tmem_ld32(tmem + lane_off + L::TM_DQ + 64u * bq + 32u, r1);
+        tmem_wait_ld();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(bar(C_DQEMPTY + bq));
+      }
+      if (leader) bulk_wait_read<L::NSTG - 1>();  // the staging tile's previous reduce has read it
+      named_bar_sync(4, 128);
+      float* stg = reinterpret_cast<float*>(smem + L::OFF_STG + sg * L::STG_BYTES);  // [64 q][D] fp32
+      // dQ^T accumulator, columns = the 64 queries. D=128 (M=128): head dim d in
+      // lane d. D=64 (M=64 layout): head dim 16*wq + l in lane l < 16 of quadrant wq.
+      const bool holds = D == 128 || lane < 16;
+      const int d = D == 128 ? 32 * wq + lane : 16 * wq + lane;
+      if (holds) {
+#pragma unroll
+        for (int q = 0; q < 32; ++q) {
+          stg[q * D + d] = __uint_as_float(r0[q]);
+          stg[(q + 32) * D + d] = __uint_as_float(r1[q]);
+        }
+      }
+      fence_proxy_async_smem();
+      named_bar_sync(4, 128);
+      if (leader && !dead) {
+        const int rows = min(BM, p.N - q0);
+        bulk_reduce_add_f32(p.dq_acc + ((int64_t)bh * p.N + q0) * D, smem_u32(stg), (uint32_t)(rows * D * 4));
+        bulk_commit();
+      }
+      ++t;
+    }
+    if (leader) bulk_wait_all();
+  }
+  // ---------------------------------------------------------------- teardown
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 512);
+  }
+}
+
+}  // namespace
+
+int flash_bwd_sm100(const FlashArgs& a0, cudaStream_t st) {
+  if (!tma_ok_bhnd(a0.dout, a0.sdo))
+    return fail(PNFT_EINVAL,
+                "flash bwd: dout needs unit head-dim stride and 16-byte aligned rows when q/k/v take the sm100 path");
+  FlashArgs a = a0;
+  const int nkt = (int)((a.N + BN - 1) / BN);
+  a.n_dtau_part = a.B * a.H * nkt;
+  int rc = flash_bwd_prep(a, st);
+  if (rc) return rc;
+  BwdParams p;
+  memset(&p, 0, sizeof(p));
+  rc = tma_map_bhnd(&p.tk, a.k, a.sk, a.B, a.H, a.N, a.D, BN);
+  if (!rc) rc = tma_map_bhnd(&p.tv, a.v, a.sv, a.B, a.H, a.N, a.D, BN);
+  if (!rc) rc = tma_map_bhnd(&p.tq, a.q, a.sq, a.B, a.H, a.N, a.D, BM);
+  if (!rc) rc = tma_map_bhnd(&p.tdo, a.dout, a.sdo, a.B, a.H, a.N, a.D, BM);
+  if (rc) return rc;
+  p.coef = a.coef;
+  p.live64 = a.live64;
+  p.dq_acc = a.dq_acc;
+  p.dk = a.dk;
+  p.dv = a.dv;
+  for (int i = 0; i < 4; ++i) {
+    p.sdk[i] = a.sdk[i];
+    p.sdv[i] = a.sdv[i];
+  }
+  p.dtau_part = a.dtau_part;
+  p.tau = a.tau;
+  p.status = a.status;
+  p.H = (int)a.H;
+  p.N = (int)a.N;
+  p.nq64 = (int)((a.N + BM - 1) / BM);
+  p.nkt = nkt;
+  p.scale = a.scale;
+  p.causal = a.causal;
+  const dim3 grid((unsigned)nkt, (unsigned)(a.B * a.H));
+  auto launch = [&](auto kern, int smem) -> int {
+    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess)
+      return check_launch("flash bwd sm100: smem attribute", 0);
+    kern<<<grid, B_THREADS, smem, st>>>(p);
+    return check_launch("flash bwd sm100");
+  };
+  rc = a.D == 64 ? launch(flash_bwd_sm100_kernel<64>, BwdLayout<64>::SMEM)
+                 : launch(flash_bwd_sm100_kernel<128>, BwdLayout<128>::SMEM);
+  if (rc) return rc;
+  return flash_bwd_finish(a, st);
+}
+
+}  // namespace pnft

@@ -306,21 +306,32 @@ class _FlashPnFirTauFn(torch.autograd.Function):
             out = torch.empty((B, N, H, D), device=dev, dtype=q.dtype).transpose(1, 2)
         else:
             out = torch.empty((B, H, N, D), device=dev, dtype=q.dtype)
-        stats = torch.empty((2, B, H, N), device=dev, dtype=torch.float32)
-        nmax = torch.empty((B, H, N), device=dev, dtype=torch.int32)
+        stats = torch.empty((2, B, H, N), device=dev, dtype=torch.float32)  # peak, mass + 1e-12
+        nmax = torch.empty((2, B, H, N), device=dev, dtype=torch.int32)    # tie count, argmax key
         tau_f32 = score_tau.detach().to(torch.float32).contiguous()
         has_gamma, gamma_val = _gamma_args(gamma)
         flags = _flash_flags()
+        # fp32 copy of O for the backward's per-row <dO,O>/gate (see pnft_flash_fwd)
+        needs_grad = any(ctx.needs_input_grad[:4])
+        out32 = None
+        if needs_grad and q.dtype != torch.float32:
+            out32 = torch.empty((B, H, N, D), device=dev, dtype=torch.float32)
         L = _lib.lib()
+        # the backward must recompute S with the forward's arithmetic (its tie test
+        # is u == peak), so it is pinned to the kernel family the forward used
+        if L.pnft_flash_path(_ptr(q), _lib.i64x4(q.stride()), _ptr(k), _lib.i64x4(k.stride()), _ptr(v),
+                             _lib.i64x4(v.stride()), D, _dtype_code(q), flags) == 0:
+            flags |= _lib.FLASH_FORCE_GENERIC
         _lib.check(
             L.pnft_flash_fwd(_ptr(q), _lib.i64x4(q.stride()), _ptr(k), _lib.i64x4(k.stride()), _ptr(v),
                              _lib.i64x4(v.stride()), _ptr(tau_f32), _ptr(out), _lib.i64x4(out.stride()),
-                             _ptr(stats[0]), _ptr(stats[1]), _ptr(nmax), B, H, N, D, float(scale), gamma_val,
-                             has_gamma, int(bool(causal_mask)), _dtype_code(q), flags, None,
+                             _ptr(out32), _ptr(stats[0]), _ptr(stats[1]), _ptr(nmax[0]), _ptr(nmax[1]), B, H, N,
+                             D, float(scale), gamma_val, has_gamma, int(bool(causal_mask)), _dtype_code(q), flags,
+                             None,
                              _ptr(_status_word(dev)), _stream(dev)),
             "pnft_flash_fwd",
         )
-        ctx.save_for_backward(q, k, v, tau_f32, out, stats, nmax)
+        ctx.save_for_backward(q, k, v, tau_f32, out, out32, stats, nmax)
         ctx.args = (float(scale), gamma_val, has_gamma, int(bool(causal_mask)), flags)
         ctx.tau_dtype = score_tau.dtype
         ctx.tau_shape = score_tau.shape
@@ -328,12 +339,14 @@ class _FlashPnFirTauFn(torch.autograd.Function):
 
     @staticmethod
     def backward(ctx, grad_out):
-        q, k, v, tau_f32, out, stats, nmax = ctx.saved_tensors
+        q, k, v, tau_f32, out, out32, stats, nmax = ctx.saved_tensors
         scale, gamma_val, has_gamma, causal, flags = ctx.args
         B, H, N, D = q.shape
         dev = q.device
         if grad_out.dtype != q.dtype:
             grad_out = grad_out.to(q.dtype)
+        if grad_out.stride(-1) != 1 or any(s % 8 for s in grad_out.stride()[:3]):
+            grad_out = grad_out.contiguous()  # TMA-loadable, so the backward keeps the forward's path
         dq = torch.empty((B, H, N, D), device=dev, dtype=q.dtype)
         dk = torch.empty((B, H, N, D), device=dev, dtype=k.dtype)
         dv = torch.empty((B, H, N, D), device=dev, dtype=v.dtype)
@@ -344,8 +357,9 @@ class _FlashPnFirTauFn(torch.autograd.Function):
         _lib.check(
             L.pnft_flash_bwd(_ptr(q), _lib.i64x4(q.stride()), _ptr(k), _lib.i64x4(k.stride()), _ptr(v),
                              _lib.i64x4(v.stride()), _ptr(tau_f32), _ptr(out), _lib.i64x4(out.stride()),
-                             _ptr(grad_out), _lib.i64x4(grad_out.stride()), _ptr(stats[0]), _ptr(stats[1]),
-                             _ptr(nmax), _ptr(dq), _lib.i64x4(dq.stride()), _ptr(dk), _lib.i64x4(dk.stride()),
+                             _ptr(out32), _ptr(grad_out), _lib.i64x4(grad_out.stride()), _ptr(stats[0]),
+                             _ptr(stats[1]), _ptr(nmax[0]), _ptr(nmax[1]), _ptr(dq), _lib.i64x4(dq.stride()),
+                             _ptr(dk), _lib.i64x4(dk.stride()),
                              _ptr(dv), _lib.i64x4(dv.stride()), _ptr(dtau), _ptr(ws), ws.numel(), B, H, N, D,
                              scale, gamma_val, has_gamma, causal, _dtype_code(q), flags,
                              _ptr(_status_word(dev)), _stream(dev)),
@@ -375,19 +389,21 @@ def flash_pn_fir_tau_attention(
 
 
 @torch.no_grad()
-def flash_pn_fir_tau_forward_stats(q, k_tilde, v, score_tau, scale=None, gamma=0.5, causal_mask=True):
+def flash_pn_fir_tau_forward_stats(q, k_tilde, v, score_tau, scale=None, gamma=0.5, causal_mask=True,
+                                   extra_flags: int = 0):
     """Forward only, also returning the per-row statistics and the kernel's
     silent-tile decisions: ``(out, M, Z, Nmax, tile_live)`` with M/Z/Nmax
     ``[B,H,N]`` (peak, mass + 1e-12, tie count, src/triton_pnfirtau.py:440-443)
     and ``tile_live`` bool ``[B,H,nT,nT]`` (nT = ceil(N/64)) true for every
-    64x64 tile the kernel processed as live."""
+    64x64 tile the kernel processed as live. ``extra_flags`` are PNFT_FLASH_*
+    bits (e.g. to select a kernel family for a comparison)."""
     dev = _require_cuda("flash_pn_fir_tau_forward_stats", q, k_tilde, v, score_tau)
     if scale is None:
         scale = 1.0 / math.sqrt(q.shape[-1])
     B, H, N, D = q.shape
     out = torch.empty((B, H, N, D), device=dev, dtype=q.dtype)
     stats = torch.empty((2, B, H, N), device=dev, dtype=torch.float32)
-    nmax = torch.empty((B, H, N), device=dev, dtype=torch.int32)
+    nmax = torch.empty((2, B, H, N), device=dev, dtype=torch.int32)
     nT = (N + 63) // 64
     tiles = torch.zeros((B, H, nT, nT), device=dev, dtype=torch.uint8)
     tau_f32 = score_tau.detach().to(torch.float32).contiguous()
@@ -395,13 +411,13 @@ def flash_pn_fir_tau_forward_stats(q, k_tilde, v, score_tau, scale=None, gamma=0
     L = _lib.lib()
     _lib.check(
         L.pnft_flash_fwd(_ptr(q), _lib.i64x4(q.stride()), _ptr(k_tilde), _lib.i64x4(k_tilde.stride()), _ptr(v),
-                         _lib.i64x4(v.stride()), _ptr(tau_f32), _ptr(out), _lib.i64x4(out.stride()),
-                         _ptr(stats[0]), _ptr(stats[1]), _ptr(nmax), B, H, N, D, float(scale), gamma_val,
-                         has_gamma, int(bool(causal_mask)), _dtype_code(q), _flash_flags(), _ptr(tiles),
-                         _ptr(_status_word(dev)), _stream(dev)),
+                         _lib.i64x4(v.stride()), _ptr(tau_f32), _ptr(out), _lib.i64x4(out.stride()), None,
+                         _ptr(stats[0]), _ptr(stats[1]), _ptr(nmax[0]), _ptr(nmax[1]), B, H, N, D, float(scale),
+                         gamma_val, has_gamma, int(bool(causal_mask)), _dtype_code(q), _flash_flags() | extra_flags,
+                         _ptr(tiles), _ptr(_status_word(dev)), _stream(dev)),
         "pnft_flash_fwd",
     )
-    return out, stats[0], stats[1], nmax, tiles.bool()
+    return out, stats[0], stats[1], nmax[0], tiles.bool()
 
 
 def _flash_bnhd(q, k_tilde, v, score_tau, scale, gamma, causal_mask):

@@ -87,18 +87,18 @@ def test_fir_empty_is_noop():
 def test_flash_rejects_large_head_dim_and_bad_dtype():
     L = _lib.lib()
     s = _lib.i64x4([1, 1, 1, 1])
-    rc = L.pnft_flash_fwd(1, s, 1, s, 1, s, 1, 1, s, 1, 1, 1, 1, 1, 8, 256, 1.0, 0.5, 1, 1, _lib.DTYPE_BF16, 0, None, None, None)
+    rc = L.pnft_flash_fwd(1, s, 1, s, 1, s, 1, 1, s, None, 1, 1, 1, 1, 1, 1, 8, 256, 1.0, 0.5, 1, 1, _lib.DTYPE_BF16, 0, None, None, None)
     assert rc == _lib.EUNSUPPORTED and "head dim" in _lib.last_error()
-    rc = L.pnft_flash_fwd(1, s, 1, s, 1, s, 1, 1, s, 1, 1, 1, 1, 1, 8, 64, 1.0, 0.5, 1, 1, 7, 0, None, None, None)
+    rc = L.pnft_flash_fwd(1, s, 1, s, 1, s, 1, 1, s, None, 1, 1, 1, 1, 1, 1, 8, 64, 1.0, 0.5, 1, 1, 7, 0, None, None, None)
     assert rc == _lib.EINVAL
-    rc = L.pnft_flash_fwd(1, s, 1, s, 1, s, 1, 1, s, 1, 1, 1, 1, 1, 8, 64, 1.0, -1.0, 1, 1, 1, 0, None, None, None)
+    rc = L.pnft_flash_fwd(1, s, 1, s, 1, s, 1, 1, s, None, 1, 1, 1, 1, 1, 1, 8, 64, 1.0, -1.0, 1, 1, 1, 0, None, None, None)
     assert rc == _lib.EINVAL and "gamma" in _lib.last_error()
 
 
 def test_flash_bwd_checks_workspace():
     L = _lib.lib()
     s = _lib.i64x4([1, 1, 1, 1])
-    rc = L.pnft_flash_bwd(1, s, 1, s, 1, s, 1, 1, s, 1, s, 1, 1, 1, 1, s, 1, s, 1, s, 1, 1, 16, 2, 2, 64, 64, 0.125,
+    rc = L.pnft_flash_bwd(1, s, 1, s, 1, s, 1, 1, s, None, 1, s, 1, 1, 1, 1, 1, s, 1, s, 1, s, 1, 1, 16, 2, 2, 64, 64, 0.125,
                           0.5, 1, 1, _lib.DTYPE_BF16, 0, None, None)
     assert rc == _lib.EINVAL and "workspace" in _lib.last_error()
 
