@@ -12,10 +12,12 @@
 //               [64g, 64g+64) of every tile, thread = TMEM lane = query row:
 //               s = S*scale - tau (computed as h = S*scale/2 - tau/2, u = h+|h|),
 //               row max via 3-input max, per-half silent vote, u^10 by repeated
-//               squaring (no exp), running peak / tie count / mass, P = bf16(u^10)
-//               stored back to TMEM for the PV MMA.
-// TMEM (512 columns): S0 [0,128) S1 [128,256) P0 [256,320) P1 [320,384) O [384,384+D).
-// Epilogue: O * gate/(mass + 1e-12) with gate = peak/(peak+gamma), stats M, Z, Nmax.
+//               squaring (no exp), running peak / tie count / argmax / mass, and
+//               P = u^10 split into two bf16 terms P_hi + P_lo written back over
+//               the tile's own S columns in TMEM for the two PV MMAs.
+// TMEM: S/P buffers [0,128) and [128,256), O [256, 256+D).
+// Epilogue: O * gate/(mass + 1e-12) with gate = peak/(peak+gamma), stats M, Z,
+// Nmax, argmax.
 // Semantics follow src/triton_pnfirtau.py:313-443 (the reference skips 64x64
 // tiles; here the skip unit is 128 query rows x 64 keys, and the optional
 // tile_flags record reports the 64x64 decisions of the same u values).
@@ -77,7 +79,9 @@ struct FwdLayout {
   static constexpr int SMEM = ALLOC < 116 * 1024 ? 116 * 1024 : ALLOC;  // one CTA per SM (it owns all TMEM)
 };
 
-constexpr uint32_t TM_S = 0, TM_P = 256, TM_O = 384, TM_COLS = 512;
+// S buffer s at [128 s, 128 s + 128); warpgroup g's P_hi / P_lo of that tile overwrite
+// its own S columns [128 s + 64 g, +32) / [+32, +32) once they are in registers.
+constexpr uint32_t TM_S = 0, TM_O = 256, TM_COLS = 512;
 
 struct FwdParams {
   CUtensorMap tq, tk, tv;
@@ -197,8 +201,9 @@ __global__ void __launch_bounds__(F_THREADS, 1) flash_fwd_sm100_kernel(const __g
       uint32_t o_acc = 0;
       auto issue_s = [&](int j) -> bool {
         const int s = j & 1;
+        // buffer s last held P_{j-2}: its PV MMAs were issued before this one and
+        // tcgen05 MMAs of one thread execute in order
         if (!mbar_wait(bar(B_KFULL + s), (j >> 1) & 1, ab)) return false;
-        if (!mbar_wait(bar(B_SEMPTY + s), ((j >> 1) & 1) ^ 1, ab)) return false;
         tc_fence_after();
 #pragma unroll
         for (int kk = 0; kk < D / 16; ++kk) {
@@ -221,12 +226,13 @@ __global__ void __launch_bounds__(F_THREADS, 1) flash_fwd_sm100_kernel(const __g
 #pragma unroll
           for (int kq = 0; kq < 4; ++kq) {
             const int kk = hh * 4 + kq;  // 16 keys per MMA
-            mma_ts(tmem + TM_O, tmem + TM_P + 64u * s + 8u * kk, sw128_desc(sV(s) + kk * 2048, L::GROUP, 1024), ID_O,
-                   o_acc);
+            const uint32_t a_hi = tmem + TM_S + 128u * s + 64u * hh + 8u * kq;
+            const uint64_t bdesc = sw128_desc(sV(s) + kk * 2048, L::GROUP, 1024);
+            mma_ts(tmem + TM_O, a_hi, bdesc, ID_O, o_acc);  // O += P_hi V
+            mma_ts(tmem + TM_O, a_hi + 32u, bdesc, ID_O, 1u);  // O += P_lo V
             o_acc = 1;
           }
         }
-        mma_commit(bar(B_PEMPTY + s));
         mma_commit(bar(B_VEMPTY + s));
         return true;
       };
@@ -269,9 +275,6 @@ __global__ void __launch_bounds__(F_THREADS, 1) flash_fwd_sm100_kernel(const __g
         tmem_ld32(tmem + lane_off + TM_S + 128u * s + 64u * hh, r0);
         tmem_ld32(tmem + lane_off + TM_S + 128u * s + 64u * hh + 32u, r1);
         tmem_wait_ld();
-        tc_fence_before();
-        __syncwarp();
-        if (lane == 0) mbar_arrive(bar(B_SEMPTY + s));
       } else {
 #pragma unroll
         for (int c = 0; c < 32; ++c) r0[c] = r1[c] = 0xbf800000u;  // -1.0f: silent
@@ -307,9 +310,7 @@ __global__ void __launch_bounds__(F_THREADS, 1) flash_fwd_sm100_kernel(const __g
         live[s * 2 + hh] = live_h;
         mbar_arrive(bar(B_VOTE + s));
       }
-      if (live_h && !dead) dead = !warp_wait(bar(B_PEMPTY + s), ((j >> 1) & 1) ^ 1, ab);
       if (live_h && !dead) {
-        tc_fence_after();
         const float mu = m > 0.f ? 2.f * m : 0.f;  // row max of u over this half tile
         if (mu > 0.f && mu >= peak) {
           float c = 0.f;
@@ -324,7 +325,10 @@ __global__ void __launch_bounds__(F_THREADS, 1) flash_fwd_sm100_kernel(const __g
           cnt = mu > peak ? c : cnt + c;
           peak = mu;
         }
-        uint32_t pk[32];
+        // P = u^10 as P_hi + P_lo (two bf16 terms, ~2^-17 relative): O, and with it the
+        // backward's <dO,O>/gate, stays fp32-accurate; the tau gradient is a small
+        // residual of cancelling per-row sums and needs that accuracy
+        uint32_t hi[32], lo[32];
 #pragma unroll
         for (int c = 0; c < 32; ++c) {
           const float u0 = x[2 * c] + fabsf(x[2 * c]);
@@ -332,9 +336,11 @@ __global__ void __launch_bounds__(F_THREADS, 1) flash_fwd_sm100_kernel(const __g
           const float a2 = u0 * u0, a4 = a2 * a2, p0 = a4 * a4 * a2;
           const float b2 = u1 * u1, b4 = b2 * b2, p1 = b4 * b4 * b2;
           ms[c & 7] += p0 + p1;
-          pk[c] = pack_bf16x2(p0, p1);
+          hi[c] = pack_bf16x2(p0, p1);
+          lo[c] = pack_bf16x2(p0 - __uint_as_float(hi[c] << 16), p1 - __uint_as_float(hi[c] & 0xffff0000u));
         }
-        tmem_st32(tmem + lane_off + TM_P + 64u * s + 32u * hh, pk);
+        tmem_st32(tmem + lane_off + TM_S + 128u * s + 64u * hh, hi);
+        tmem_st32(tmem + lane_off + TM_S + 128u * s + 64u * hh + 32u, lo);
         tmem_wait_st();
       }
       tc_fence_before();

@@ -46,7 +46,7 @@ def _check_fwd(q, k, v, tau, causal=True, gamma=0.5):
     assert torch.equal((M > 0)[~near], (peak > 0)[~near])
     assert rel_max(M, peak) < 1e-3
     live = peak > 1e-3
-    assert torch.allclose(Z[live], z[live], rtol=1e-3, atol=0)
+    assert torch.allclose(Z[live], z[live], rtol=2e-4, atol=0)
     # rows whose two largest u differ by a few ulps may count a tie in one
     # accumulation order and not in the other; exact ties must agree
     sc = O.thresholded_scores(q.float() @ k.float().transpose(-2, -1), t, 1.0 / math.sqrt(q.shape[-1]), causal)
@@ -57,7 +57,12 @@ def _check_fwd(q, k, v, tau, causal=True, gamma=0.5):
     else:
         fuzzy = torch.zeros_like(near)
     keep = ~near & ~fuzzy
-    assert torch.equal(Nmax[keep], nmax[keep])
+    bad = keep & (Nmax != nmax)
+    if bad.any():
+        idx = bad.nonzero()[:4].tolist()
+        info = [(i, int(Nmax[tuple(i)]), int(nmax[tuple(i)]), float(peak[tuple(i)]),
+                 [float(v) for v in torch.relu(sc[tuple(i)]).topk(min(3, sc.shape[-1])).values]) for i in idx]
+        raise AssertionError(f"Nmax differs on {int(bad.sum())} rows (row, ours, ref, peak, top3 u): {info}")
     if causal:
         ref_tiles, _, _ = O.tile_silence(q.float(), k.float(), tau)
         nT = ref_tiles.shape[-1]
