@@ -107,6 +107,27 @@ PNFT_API int pnft_fir_bwd(const void* gy, int64_t sgb, int64_t sgn, int64_t sgc,
 
 PNFT_API size_t pnft_fir_bwd_workspace_size(int64_t B, int64_t N, int64_t C, int ntaps);
 
+/* pnft_fir_bwd with the tap gradient, for callers that cannot allocate device
+ * memory on the library's behalf: code that runs while a stream is being
+ * captured (cudaMalloc is not permitted then), serving loops that must never
+ * enter the allocator after start-up, and foreign-language bindings that only
+ * receive the input and output buffers from a host runtime owning all device
+ * memory. The per-block partial sums that pnft_fir_bwd keeps in the caller's
+ * workspace live instead in a static 128 KiB device array of the library,
+ * which every GPU that loads the library holds until the process exits.
+ * x and dtaps are required; gx may be NULL. ntaps above 64 is rejected with
+ * PNFT_EINVAL. The first call on each device looks the array's address up
+ * (make that first call before any stream capture). All calls share the
+ * array, so calls that overlap on the GPU (other streams or threads) race;
+ * each call overwrites every element it reads, so none needs clearing.
+ * Results equal pnft_fir_bwd's. No counterpart in the reference (an addition
+ * of this library). */
+PNFT_API int pnft_fir_bwd_noalloc(const void* gy, int64_t sgb, int64_t sgn, int64_t sgc,
+                                  const float* taps, int ntaps, void* gx, int64_t sxb, int64_t sxn,
+                                  int64_t sxc, const void* x, int64_t s0b, int64_t s0n, int64_t s0c,
+                                  float* dtaps, int64_t B, int64_t N, int64_t C, int dtype,
+                                  void* stream);
+
 /* ------------------------------------------------------------------------- */
 /* Row-fused score -> weight op over R rows of length N                      */
 /* ------------------------------------------------------------------------- */

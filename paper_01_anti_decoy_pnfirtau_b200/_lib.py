@@ -37,6 +37,11 @@ SIGNATURES: dict[str, tuple] = {
          _P, _P, c_size_t, c_int64, c_int64, c_int64, c_int, _P],
     ),
     "pnft_fir_bwd_workspace_size": (c_size_t, [c_int64, c_int64, c_int64, c_int]),
+    "pnft_fir_bwd_noalloc": (
+        c_int,
+        [_P, c_int64, c_int64, c_int64, _P, c_int, _P, c_int64, c_int64, c_int64, _P, c_int64, c_int64, c_int64,
+         _P, c_int64, c_int64, c_int64, c_int, _P],
+    ),
     "pnft_rows_fwd": (
         c_int,
         [_P, c_int64, _P, _P, c_int64, _P, _P, _P, _P, c_int64, c_int64, c_float, c_float, c_float, c_int, c_int,

@@ -14,6 +14,8 @@
 #include <stdarg.h>
 #include <stdio.h>
 
+#include <mutex>
+
 #include "common.cuh"
 
 namespace pnft {
@@ -248,6 +250,37 @@ static int64_t dtaps_blocks(int64_t B, int64_t N, int64_t C) {
   return g;
 }
 
+// Scratch of pnft_fir_bwd_noalloc: the per-block, per-lag partial sums of the tap
+// gradient (at most FIR_MAX_TAPS lags x FIR_DTAPS_MAX_BLOCKS blocks = 128 KiB).
+// It lives in the module image, so every GPU that loads the library holds it
+// until the process exits. Each call writes every slot it later reads before
+// reading it, so nothing has to start at zero; two calls that overlap on the
+// GPU (different streams, or host threads) share it and race.
+static __device__ __align__(256) float g_dtaps_scratch[FIR_MAX_TAPS * FIR_DTAPS_MAX_BLOCKS];
+
+constexpr int kMaxDevices = 64;
+
+// Device address of g_dtaps_scratch on the current device, looked up once per
+// device (the host-side symbol is only a stand-in, never a device address).
+static int dtaps_scratch_ptr(float** out) {
+  static std::mutex mu;
+  static float* ptrs[kMaxDevices] = {};
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return fail(PNFT_ECUDA, "fir bwd noalloc: cudaGetDevice: %s", cudaGetErrorString(e));
+  if (dev < 0 || dev >= kMaxDevices) return fail(PNFT_EUNSUPPORTED, "fir bwd noalloc: device %d >= %d", dev, kMaxDevices);
+  std::lock_guard<std::mutex> lock(mu);
+  if (!ptrs[dev]) {
+    void* p = nullptr;
+    e = cudaGetSymbolAddress(&p, g_dtaps_scratch);
+    if (e != cudaSuccess)
+      return fail(PNFT_ECUDA, "fir bwd noalloc: cudaGetSymbolAddress: %s", cudaGetErrorString(e));
+    ptrs[dev] = static_cast<float*>(p);
+  }
+  *out = ptrs[dev];
+  return PNFT_OK;
+}
+
 }  // namespace pnft
 
 using namespace pnft;
@@ -304,6 +337,44 @@ extern "C" int pnft_fir_bwd(const void* gy, int64_t sgb, int64_t sgn, int64_t sg
     }
   }
   if (gx && B > 0 && N > 0 && C > 0) {
+    FirGeom g{gy, gx, sgb, sgn, sgc, sxb, sxn, sxc, B, N, C};
+    PNFT_DISPATCH_DTYPE(dtype, T, return fir_launch<T, -1>(g, taps, ntaps, st));
+  }
+  return PNFT_OK;
+}
+
+// Allocation-free variant of pnft_fir_bwd for callers that cannot hand the
+// library device memory of its choosing (see the header): identical results,
+// with the tap-gradient partial sums kept in the static g_dtaps_scratch. The
+// first call on a device looks the scratch address up (keep that first call
+// out of any stream capture); calls that overlap on the GPU share the scratch.
+extern "C" int pnft_fir_bwd_noalloc(const void* gy, int64_t sgb, int64_t sgn, int64_t sgc, const float* taps,
+                                    int ntaps, void* gx, int64_t sxb, int64_t sxn, int64_t sxc, const void* x,
+                                    int64_t s0b, int64_t s0n, int64_t s0c, float* dtaps, int64_t B, int64_t N,
+                                    int64_t C, int dtype, void* stream) {
+  if (ntaps > FIR_MAX_TAPS)
+    return fail(PNFT_EINVAL, "fir bwd noalloc: ntaps=%d exceeds the %d lags its static scratch holds", ntaps,
+                FIR_MAX_TAPS);
+  int rc = fir_check_common(gy, gx, taps, ntaps, B, N, C, false);
+  if (rc) return rc;
+  if (!x || !dtaps) return fail(PNFT_EINVAL, "fir bwd noalloc: x and dtaps are required (tap gradient entry point)");
+  cudaStream_t st = as_stream(stream);
+  if (B == 0 || N == 0 || C == 0) {
+    if (cudaMemsetAsync(dtaps, 0, sizeof(float) * ntaps, st) != cudaSuccess) return check_launch("fir dtaps memset", 0);
+    return PNFT_OK;
+  }
+  float* part = nullptr;
+  rc = dtaps_scratch_ptr(&part);
+  if (rc) return rc;
+  const int nblk = (int)dtaps_blocks(B, N, C);  // <= FIR_DTAPS_MAX_BLOCKS by construction
+  PNFT_DISPATCH_DTYPE(dtype, T, {
+    fir_dtaps_partial_kernel<T><<<dim3(nblk, ntaps), FIR_THREADS, 0, st>>>(
+        static_cast<const T*>(gy), sgb, sgn, sgc, static_cast<const T*>(x), s0b, s0n, s0c, B, N, C, part);
+  });
+  fir_dtaps_final_kernel<<<1, FIR_MAX_TAPS, 0, st>>>(part, nblk, ntaps, dtaps);
+  rc = check_launch("fir dtaps noalloc", 2);
+  if (rc) return rc;
+  if (gx) {
     FirGeom g{gy, gx, sgb, sgn, sgc, sxb, sxn, sxc, B, N, C};
     PNFT_DISPATCH_DTYPE(dtype, T, return fir_launch<T, -1>(g, taps, ntaps, st));
   }

@@ -1,0 +1,83 @@
+"""The allocation-free FIR backward (pnft_fir_bwd_noalloc) against the
+workspace entry point (pnft_fir_bwd), both called through the C ABI.
+
+pnft_fir_bwd_noalloc exists for callers that cannot allocate device memory for
+the library: code running inside CUDA stream capture, serving loops that must
+not touch an allocator after start-up, and foreign-language bindings that only
+hold the buffers their host runtime gave them. It keeps the tap-gradient
+partial sums in a static device array instead of a caller workspace. Two calls
+in a row (the second smaller, so the first call's leftovers stay in the shared
+array) must both reproduce the workspace entry point's results.
+
+This file is named to be collected last; it must pass alone in a fresh process
+and after the rest of the suite.
+"""
+import pytest
+import torch
+
+from paper_01_anti_decoy_pnfirtau_b200 import _lib
+
+pytestmark = pytest.mark.gpu
+
+DTYPES = {torch.float32: _lib.DTYPE_F32, torch.bfloat16: _lib.DTYPE_BF16}
+
+
+def _case(B, N, C, dtype, seed, device):
+    g = torch.Generator().manual_seed(seed)
+    gy = torch.randn(B, N, C, generator=g).to(device, dtype)
+    x = torch.randn(B, N, C, generator=g).to(device, dtype)
+    taps = torch.rand(7, generator=g).to(device)
+    return gy, x, taps / taps.sum()
+
+
+def _with_workspace(gy, x, taps):
+    L = _lib.lib()
+    B, N, C = gy.shape
+    gx = torch.empty_like(gy)
+    dtaps = torch.empty(taps.numel(), device=gy.device)
+    ws = torch.empty(max(L.pnft_fir_bwd_workspace_size(B, N, C, taps.numel()), 1), device=gy.device,
+                     dtype=torch.uint8)
+    rc = L.pnft_fir_bwd(gy.data_ptr(), *gy.stride(), taps.data_ptr(), taps.numel(), gx.data_ptr(), *gx.stride(),
+                        x.data_ptr(), *x.stride(), dtaps.data_ptr(), ws.data_ptr(), ws.numel(), B, N, C,
+                        DTYPES[gy.dtype], torch.cuda.current_stream().cuda_stream)
+    _lib.check(rc, "pnft_fir_bwd")
+    return gx, dtaps
+
+
+def _without_workspace(gy, x, taps):
+    L = _lib.lib()
+    B, N, C = gy.shape
+    gx = torch.empty_like(gy)
+    dtaps = torch.empty(taps.numel(), device=gy.device)
+    rc = L.pnft_fir_bwd_noalloc(gy.data_ptr(), *gy.stride(), taps.data_ptr(), taps.numel(), gx.data_ptr(),
+                                *gx.stride(), x.data_ptr(), *x.stride(), dtaps.data_ptr(), B, N, C,
+                                DTYPES[gy.dtype], torch.cuda.current_stream().cuda_stream)
+    _lib.check(rc, "pnft_fir_bwd_noalloc")
+    return gx, dtaps
+
+
+def _rel(a, b):
+    return float((a.double() - b.double()).abs().max() / b.double().abs().max().clamp_min(1e-30))
+
+
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
+def test_noalloc_matches_workspace_entry_point_twice(cuda, dtype):
+    # first call: large enough to use all 512 partial-sum blocks; second: fewer blocks
+    for B, N, C, seed in ((32, 512, 256, 1), (2, 37, 24, 2)):
+        gy, x, taps = _case(B, N, C, dtype, seed, cuda)
+        gx_ref, dt_ref = _with_workspace(gy, x, taps)
+        gx, dt = _without_workspace(gy, x, taps)
+        torch.cuda.synchronize()
+        assert _rel(gx, gx_ref) <= 1e-6
+        assert _rel(dt, dt_ref) <= 1e-6
+
+
+def test_noalloc_rejects_too_many_taps(cuda):
+    L = _lib.lib()
+    gy, x, _ = _case(1, 8, 8, torch.float32, 3, cuda)
+    taps = torch.ones(65, device=cuda)
+    dtaps = torch.empty(65, device=cuda)
+    rc = L.pnft_fir_bwd_noalloc(gy.data_ptr(), *gy.stride(), taps.data_ptr(), 65, None, 0, 0, 0, x.data_ptr(),
+                                *x.stride(), dtaps.data_ptr(), 1, 8, 8, _lib.DTYPE_F32,
+                                torch.cuda.current_stream().cuda_stream)
+    assert rc == _lib.EINVAL and "65" in _lib.last_error()
