@@ -200,27 +200,31 @@ __global__ void __launch_bounds__(GTHREADS) flash_fwd_generic_kernel(FlashArgs a
 // block per (64-row tile, b*h) also records whether any row of the tile is live.
 template <typename T>
 __global__ void __launch_bounds__(256) flash_bwd_prep_kernel(FlashArgs a) {
-  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  // 8 lanes per row, 4 rows per warp and pass, 2 passes: 64 rows per block
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, sub = lane >> 3, sl = lane & 7;
   const int64_t bh = blockIdx.y, b = bh / a.H, h = bh % a.H;
   const int64_t nt = (a.N + 63) / 64;
   int live = 0;
-  for (int rr = warp; rr < 64; rr += 8) {
-    const int64_t n = (int64_t)blockIdx.x * 64 + rr;
-    if (n >= a.N) break;
-    const int64_t r = bh * a.N + n;
-    const T* O = static_cast<const T*>(a.out_c) + b * a.so[0] + h * a.so[1] + n * a.so[2];
-    const T* dO = static_cast<const T*>(a.dout) + b * a.sdo[0] + h * a.sdo[1] + n * a.sdo[2];
+#pragma unroll
+  for (int pass = 0; pass < 2; ++pass) {
+    const int64_t n = (int64_t)blockIdx.x * 64 + warp * 8 + pass * 4 + sub;
+    const bool ok = n < a.N;
+    const int64_t r = bh * a.N + (ok ? n : 0);
+    const T* O = static_cast<const T*>(a.out_c) + b * a.so[0] + h * a.so[1] + (ok ? n : 0) * a.so[2];
+    const T* dO = static_cast<const T*>(a.dout) + b * a.sdo[0] + h * a.sdo[1] + (ok ? n : 0) * a.sdo[2];
     float dot = 0.f;
-    if (a.out32) {
-      const float* O32 = a.out32 + r * a.D;
-      for (int e = lane; e < a.D; e += 32) dot = fmaf(to_f32<T>(dO[e * a.sdo[3]]), O32[e], dot);
-    } else {
-      for (int e = lane; e < a.D; e += 32) dot = fmaf(to_f32<T>(dO[e * a.sdo[3]]), to_f32<T>(O[e * a.so[3]]), dot);
+    if (ok) {
+      if (a.out32) {
+        const float* O32 = a.out32 + r * a.D;
+        for (int e = sl; e < a.D; e += 8) dot = fmaf(to_f32<T>(dO[e * a.sdo[3]]), O32[e], dot);
+      } else {
+        for (int e = sl; e < a.D; e += 8) dot = fmaf(to_f32<T>(dO[e * a.sdo[3]]), to_f32<T>(O[e * a.so[3]]), dot);
+      }
     }
-    dot = group_sum<32>(dot);
-    const float peak = a.stat_m[r];
+    dot = group_sum<8>(dot);
+    const float peak = ok ? a.stat_m[r] : 0.f;
     live |= peak > 0.f;
-    if (lane == 0) {
+    if (ok && sl == 0) {
       const float z = a.stat_z[r];
       float gate = 0.f;
       if (peak > 0.f) gate = a.has_gamma ? peak / (peak + a.gamma) : 1.f;
@@ -414,8 +418,32 @@ __global__ void __launch_bounds__(GTHREADS) flash_bwd_generic_kernel(FlashArgs a
 
 template <typename T>
 __global__ void __launch_bounds__(256) dq_cast_kernel(FlashArgs a) {
-  const int64_t total = a.B * a.H * a.N * a.D;
   T* dq = static_cast<T*>(a.dq);
+  const bool vec = (a.D % 8) == 0 && a.sdq[3] == 1 && (a.sdq[2] % 8) == 0 && (a.sdq[1] % 8) == 0 &&
+                   (a.sdq[0] % 8) == 0 && (reinterpret_cast<uintptr_t>(a.dq) % 16) == 0;
+  if (vec) {  // 8 consecutive head dims per thread: two float4 loads, one or two 16-byte stores
+    const int64_t per_row = a.D / 8, total = a.B * a.H * a.N * per_row;
+    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total;
+         i += (int64_t)gridDim.x * blockDim.x) {
+      const int64_t row = i / per_row, c = (i - row * per_row) * 8;
+      const int64_t n = row % a.N, bh = row / a.N, b = bh / a.H, h = bh % a.H;
+      const float4* src = reinterpret_cast<const float4*>(a.dq_acc + row * a.D + c);
+      const float4 f0 = src[0], f1 = src[1];
+      T* dst = dq + b * a.sdq[0] + h * a.sdq[1] + n * a.sdq[2] + c;
+      if constexpr (sizeof(T) == 2) {
+        uint4 w;
+        T* e = reinterpret_cast<T*>(&w);
+        e[0] = from_f32<T>(f0.x); e[1] = from_f32<T>(f0.y); e[2] = from_f32<T>(f0.z); e[3] = from_f32<T>(f0.w);
+        e[4] = from_f32<T>(f1.x); e[5] = from_f32<T>(f1.y); e[6] = from_f32<T>(f1.z); e[7] = from_f32<T>(f1.w);
+        *reinterpret_cast<uint4*>(dst) = w;
+      } else {
+        reinterpret_cast<float4*>(dst)[0] = f0;
+        reinterpret_cast<float4*>(dst)[1] = f1;
+      }
+    }
+    return;
+  }
+  const int64_t total = a.B * a.H * a.N * a.D;
   for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
     const int64_t e = i % a.D, n = (i / a.D) % a.N, bh = i / (a.D * a.N), b = bh / a.H, h = bh % a.H;
     dq[b * a.sdq[0] + h * a.sdq[1] + n * a.sdq[2] + e * a.sdq[3]] = from_f32<T>(a.dq_acc[i]);
@@ -497,7 +525,8 @@ int flash_bwd_prep(const FlashArgs& a, cudaStream_t st) {
 
 int flash_bwd_finish(const FlashArgs& a, cudaStream_t st) {
   PNFT_DISPATCH_DTYPE(a.dtype, T, {
-    dq_cast_kernel<T><<<grid_cap(a.B * a.H * a.N * a.D, 256), 256, 0, st>>>(a);
+    const int64_t items = a.B * a.H * a.N * (a.D % 8 == 0 ? a.D / 8 : a.D);
+    dq_cast_kernel<T><<<grid_cap(items, 256), 256, 0, st>>>(a);
   });
   int rc = check_launch("flash bwd dq cast");
   if (rc) return rc;
