@@ -282,6 +282,7 @@ def cpu_oracle_sample(w: dict, seconds: float, seed: int, steps: int | None = No
 def bench_ours(args, dist_: Dist) -> dict:
     import paper_01_anti_decoy_pnfirtau_b200 as P
     from paper_01_anti_decoy_pnfirtau_b200 import _lib, pnfirtau_ops
+    from paper_01_anti_decoy_pnfirtau_b200.sharding import sharded_flash_pn_fir_tau_attention
 
     dev = torch.device("cuda", dist_.local_rank)
     torch.cuda.set_device(dev)
@@ -298,16 +299,13 @@ def bench_ours(args, dist_: Dist) -> dict:
     def step(evs=None):
         if evs is not None:
             evs[0].record()
-        out = P.flash_pn_fir_tau_attention(*leaves, tau)
+        # this rank's B*H shard; tau's gradient is summed over the ranks (fp64)
+        out = sharded_flash_pn_fir_tau_attention(*leaves, tau)
         if evs is not None:
             evs[1].record()
         grads = torch.autograd.grad(out, (*leaves, tau), do)
         if evs is not None:
             evs[2].record()
-        if dist_.active:
-            import torch.distributed as dist
-
-            dist.all_reduce(grads[3])
         return out, grads
 
     for _ in range(args.warmup):
@@ -379,6 +377,8 @@ def bench_ours(args, dist_: Dist) -> dict:
 def bench_e2e(args, dist_: Dist, w: dict, dev, flops: float, P) -> dict:
     """Same op through the public API with pinned host inputs and host outputs:
     every step copies q,k,v,dO host->device and out,dq,dk,dv,dtau device->host."""
+    from paper_01_anti_decoy_pnfirtau_b200.sharding import sharded_flash_pn_fir_tau_attention
+
     hq, hk, hv, hdo = (t.detach().cpu().pin_memory() for t in make_inputs(w, args.seed + 7, dev))
     outs = [torch.empty_like(hq).pin_memory() for _ in range(4)]
     htau = torch.empty((), dtype=torch.float32).pin_memory()
@@ -387,12 +387,8 @@ def bench_e2e(args, dist_: Dist, w: dict, dev, flops: float, P) -> dict:
     def step():
         q, k, v, do = (t.to(dev, non_blocking=True) for t in (hq, hk, hv, hdo))
         q.requires_grad_(True), k.requires_grad_(True), v.requires_grad_(True)
-        out = P.flash_pn_fir_tau_attention(q, k, v, tau)
+        out = sharded_flash_pn_fir_tau_attention(q, k, v, tau)
         dq, dk, dv, dtau = torch.autograd.grad(out, (q, k, v, tau), do)
-        if dist_.active:
-            import torch.distributed as dist
-
-            dist.all_reduce(dtau)
         for h, d in zip(outs, (out, dq, dk, dv)):
             h.copy_(d, non_blocking=True)
         htau.copy_(dtau, non_blocking=True)

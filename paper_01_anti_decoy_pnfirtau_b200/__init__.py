@@ -21,6 +21,7 @@ from .pnfirtau_ops import (
     triton_causal_fir,
     triton_pn_fir_tau_scores,
 )
+from .sharding import bh_range, shard_bh, share_tau, sharded_flash_pn_fir_tau_attention, unshard_bh
 
 __all__ = [
     "PnFirConfig",
@@ -36,4 +37,9 @@ __all__ = [
     "pn_rows",
     "check_device_status",
     "flash_kernel_path",
+    "bh_range",
+    "shard_bh",
+    "unshard_bh",
+    "share_tau",
+    "sharded_flash_pn_fir_tau_attention",
 ]

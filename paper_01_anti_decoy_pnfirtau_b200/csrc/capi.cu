@@ -155,7 +155,12 @@ extern "C" int pnft_flash_bwd(const void* q, const int64_t* sq, const void* k, c
   a.stat_arg = const_cast<int32_t*>(stat_arg);
   char* ws = static_cast<char*>(workspace);
   a.dq_acc = reinterpret_cast<float*>(ws + w.off_dq);
-  a.coef = reinterpret_cast<float4*>(ws + w.off_coef);
+  {
+    const size_t recs = (size_t)(B * H * rec_rows(N));
+    a.coefP = reinterpret_cast<float4*>(ws + w.off_coef);
+    a.argv = reinterpret_cast<int32_t*>(a.coefP + recs);
+    a.pcmpv = reinterpret_cast<float*>(a.argv + recs);
+  }
   a.live64 = reinterpret_cast<int32_t*>(ws + w.off_live);
   a.dtau_part = reinterpret_cast<float*>(ws + w.off_part);
   if (use_sm100(a)) return flash_bwd_sm100(a, st);

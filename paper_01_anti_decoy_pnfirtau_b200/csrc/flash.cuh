@@ -32,20 +32,39 @@ struct FlashArgs {
   int has_gamma, causal, dtype, flags;
   // bwd workspace carve-up
   float* dq_acc;       // fp32 [B,H,N,D] contiguous
-  float4* coef;        // [B*H*N + 64] records of 2 float4 (RowCoef), zero tail
-  int32_t* live64;     // [B*H, ceil(N/64)]: 1 if any row of the 64-row tile has peak > 0
+  // per-row backward coefficients (see below): record of row n of head bh at
+  // r = bh * rec_rows(N) + n; the padding rows past N hold silent-row records
+  float4* coefP;       // rows 2j, 2j+1 interleaved: {c1_0, c1_1, c10_0, c10_1}, {-D_0, -D_1, tie_0, tie_1}
+  int32_t* argv;       // argmax key (-1: silent row)
+  float* pcmpv;        // peak for the value test (NaN when Nmax == 1)
+  int32_t* live64;     // [B*H, ceil(N/64)]: bit 0 any row live (peak > 0), bit 1 any row with Nmax > 1
   float* dtau_part;    // per (bh, key tile) partial of -sum du
   int64_t n_dtau_part;
 };
 
-// Per query row backward coefficients, two float4 per row:
-//   c0 = {peak, gate/z, 10*scale*gate/z, D = <dO,O>/gate}
-//   c1 = {tie = scale * D*gamma/(peak+gamma)^2/Nmax, argmax key (int bits),
-//         peak for the value test (NaN when Nmax == 1), 0}
-// so that dS = 10*scale*gate/z * u^9 * (dP - D) + [key == argmax || u == c1.z] * tie:
-// a row with one maximum takes the gate gradient at its recorded argmax (exact
-// whatever arithmetic recomputes S); genuine ties (Nmax > 1) are found by value.
-constexpr int kCoefStride = 2;  // float4 per row
+// Per query row backward coefficients (c1 = gate/z, c10 = 10*scale*gate/z,
+// D = <dO,O>/gate, tie = scale * D * gamma/(peak+gamma)^2 / Nmax, pcmp = peak
+// when Nmax > 1 else NaN):
+//   W  = c1 * u^10                  (the normalised, gated weight: P)
+//   dS = c10 * u^9 * (dP - D) + [key == argmax || u == pcmp] * tie
+// A row with one maximum takes the gate gradient at its recorded argmax (exact
+// whatever arithmetic recomputes S); genuine ties (Nmax > 1) are found by value
+// and split evenly, like the eager amax backward. A silent row has argmax -1
+// and all-zero coefficients.
+constexpr int kLiveRow = 1, kMultiTie = 2;  // live64 bits
+
+struct RowCoef {
+  float c1, c10, D, tie;
+};
+__device__ __forceinline__ RowCoef load_row_coef(const float4* coefP, int64_t r) {
+  const float* p = reinterpret_cast<const float*>(coefP) + (r >> 1) * 8 + (r & 1);
+  return RowCoef{p[0], p[2], -p[4], p[6]};
+}
+
+// Rows per head in the coefficient arrays: N rounded up to whole 64-row tiles,
+// so every tile's records start 256-byte aligned and a tile load never reads
+// past its head.
+__host__ __device__ __forceinline__ int64_t rec_rows(int64_t N) { return (N + 63) / 64 * 64; }
 
 // Workspace layout shared by both kernel families (256-byte aligned sections).
 struct BwdWorkspace {

@@ -203,8 +203,8 @@ __global__ void __launch_bounds__(256) flash_bwd_prep_kernel(FlashArgs a) {
   // 8 lanes per row, 4 rows per warp and pass, 2 passes: 64 rows per block
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, sub = lane >> 3, sl = lane & 7;
   const int64_t bh = blockIdx.y, b = bh / a.H, h = bh % a.H;
-  const int64_t nt = (a.N + 63) / 64;
-  int live = 0;
+  const int64_t nt = (a.N + 63) / 64, npad = nt * 64;
+  int live = 0, multi = 0;
 #pragma unroll
   for (int pass = 0; pass < 2; ++pass) {
     const int64_t n = (int64_t)blockIdx.x * 64 + warp * 8 + pass * 4 + sub;
@@ -224,28 +224,42 @@ __global__ void __launch_bounds__(256) flash_bwd_prep_kernel(FlashArgs a) {
     dot = group_sum<8>(dot);
     const float peak = ok ? a.stat_m[r] : 0.f;
     live |= peak > 0.f;
-    if (ok && sl == 0) {
-      const float z = a.stat_z[r];
-      float gate = 0.f;
-      if (peak > 0.f) gate = a.has_gamma ? peak / (peak + a.gamma) : 1.f;
-      const float Dg = gate > 0.f ? dot / gate : 0.f;
-      float tie = 0.f;
-      if (a.has_gamma && peak > 0.f) {
-        const float pg = peak + a.gamma;
-        tie = Dg * (a.gamma / (pg * pg)) / (float)a.stat_nmax[r];
+    if (sl == 0) {
+      // rows past N get the record of a silent row (the tile loads read all 64)
+      float4 cA = make_float4(0.f, 0.f, 0.f, 0.f);
+      int arg = -1, nm = 0;
+      float pcmp = __int_as_float(0x7fc00000);  // NaN never compares equal
+      if (ok) {
+        const float z = a.stat_z[r];
+        nm = a.stat_nmax[r];
+        arg = a.stat_arg[r];
+        float gate = 0.f;
+        if (peak > 0.f) gate = a.has_gamma ? peak / (peak + a.gamma) : 1.f;
+        const float Dg = gate > 0.f ? dot / gate : 0.f;
+        float tie = 0.f;
+        if (a.has_gamma && peak > 0.f) {
+          const float pg = peak + a.gamma;
+          tie = Dg * (a.gamma / (pg * pg)) / (float)nm;
+        }
+        const float c1 = gate / z;
+        cA = make_float4(c1, (10.f * a.scale) * c1, Dg, a.scale * tie);
+        // single maximum: matched by key index; genuine ties (Nmax > 1): by value
+        if (nm > 1) pcmp = peak;
       }
-      const float c1 = gate / z;
-      a.coef[r * kCoefStride + 0] = make_float4(peak, c1, (10.f * a.scale) * c1, Dg);
-      // single maximum: matched by key index; genuine ties (Nmax > 1): by value
-      const float pcmp = a.stat_nmax[r] > 1 ? peak : __int_as_float(0x7fc00000);  // NaN never compares equal
-      a.coef[r * kCoefStride + 1] = make_float4(a.scale * tie, __int_as_float(a.stat_arg[r]), pcmp, 0.f);
+      const int64_t rr = bh * npad + n;
+      float* cp = reinterpret_cast<float*>(a.coefP) + (rr >> 1) * 8 + (rr & 1);
+      cp[0] = cA.x;
+      cp[2] = cA.y;
+      cp[4] = -cA.z;
+      cp[6] = cA.w;
+      a.argv[rr] = arg;
+      a.pcmpv[rr] = pcmp;
+      if (nm > 1) multi = 1;
     }
   }
   live = __syncthreads_or(live);
-  if (threadIdx.x == 0) a.live64[bh * nt + blockIdx.x] = live;
-  // zero tail: tile loads of the last rows may read up to 64 records past B*H*N
-  if (blockIdx.x == 0 && blockIdx.y == 0 && threadIdx.x < 64 * kCoefStride)
-    a.coef[a.B * a.H * a.N * kCoefStride + threadIdx.x] = make_float4(0.f, 0.f, 0.f, 0.f);
+  multi = __syncthreads_or(multi);
+  if (threadIdx.x == 0) a.live64[bh * nt + blockIdx.x] = (live ? kLiveRow : 0) | (multi ? kMultiTie : 0);
 }
 
 template <typename T, int DP>
@@ -259,7 +273,7 @@ __global__ void __launch_bounds__(GTHREADS) flash_bwd_generic_kernel(FlashArgs a
   float* sdO = sQ + SM::TILE;
   float* sW = sdO + SM::TILE;
   float* sdS = sW + GB * LDP;
-  float4* sC = reinterpret_cast<float4*>(sdS + GB * LDP);  // {peak, gate/z, 10*scale*gate/z, D}
+  float4* sC = reinterpret_cast<float4*>(sdS + GB * LDP);  // {-, gate/z, 10*scale*gate/z, D}
   float* sTie = reinterpret_cast<float*>(sC + GB);          // scale * tie coefficient
   int* sArg = reinterpret_cast<int*>(sTie + GB);            // argmax key of the row
   float* sPc = reinterpret_cast<float*>(sArg + GB);         // peak for the value test (NaN: unused)
@@ -288,17 +302,20 @@ __global__ void __launch_bounds__(GTHREADS) flash_bwd_generic_kernel(FlashArgs a
     int live_row = 0;
     if (tid < GB) {
       const int64_t row = q0 + tid;
-      float4 c = make_float4(0.f, 0.f, 0.f, 0.f);
-      float4 c1 = make_float4(0.f, __int_as_float(-1), __int_as_float(0x7fc00000), 0.f);
+      RowCoef c{0.f, 0.f, 0.f, 0.f};
+      int arg = -1;
+      float pcmp = __int_as_float(0x7fc00000);
       if (row < N) {
-        c = a.coef[(bh * N + row) * kCoefStride];
-        c1 = a.coef[(bh * N + row) * kCoefStride + 1];
+        const int64_t rr = bh * rec_rows(N) + row;
+        c = load_row_coef(a.coefP, rr);
+        arg = a.argv[rr];
+        pcmp = a.pcmpv[rr];
       }
-      sC[tid] = c;
-      sTie[tid] = c1.x;
-      sArg[tid] = __float_as_int(c1.y);
-      sPc[tid] = c1.z;
-      live_row = c.x > 0.f;
+      sC[tid] = make_float4(0.f, c.c1, c.c10, c.D);  // -, gate/z, 10*scale*gate/z, D
+      sTie[tid] = c.tie;
+      sArg[tid] = arg;
+      sPc[tid] = pcmp;
+      live_row = arg >= 0;
     }
     if (!__syncthreads_or(live_row)) continue;  // every query row of the block is silent
     load_tile<T, DP>(sQ, Q, a.sq[2], a.sq[3], q0, N, D);
@@ -326,7 +343,7 @@ __global__ void __launch_bounds__(GTHREADS) flash_bwd_generic_kernel(FlashArgs a
 #pragma unroll
     for (int ii = 0; ii < 4; ++ii) {
       const int r = rg + 16 * ii;
-      const float4 c = sC[r];  // peak, gate/z, 10*scale*gate/z, D
+      const float4 c = sC[r];  // -, gate/z, 10*scale*gate/z, D
       const float tie = sTie[r], pcmp = sPc[r];
       const int arg = sArg[r];
 #pragma unroll
@@ -460,11 +477,12 @@ static unsigned grid_cap(int64_t items, int per_block) {
 BwdWorkspace bwd_workspace_layout(int64_t B, int64_t H, int64_t N, int64_t D) {
   auto up = [](size_t x) { return (x + 255) & ~(size_t)255; };
   BwdWorkspace w{};
-  const size_t rows = (size_t)(B * H * N);
+  const size_t rows = (size_t)(B * H * N), recs = (size_t)(B * H * rec_rows(N));
   const size_t ntiles64 = (size_t)(B * H) * (size_t)((N + GB - 1) / GB);
   w.off_dq = 0;
   w.off_coef = up(rows * (size_t)D * sizeof(float));
-  w.off_live = w.off_coef + up((rows + 64) * kCoefStride * sizeof(float4));
+  // coefA, coefB (float4), argv (int32), pcmpv (float): recs records each
+  w.off_live = w.off_coef + up(recs * (2 * sizeof(float4) + sizeof(int32_t) + sizeof(float)));
   w.off_part = w.off_live + up(ntiles64 * sizeof(int32_t));
   w.total = w.off_part + up(ntiles64 * sizeof(float));
   return w;

@@ -10,7 +10,7 @@
 //               64-key halves only.
 //   warps 4-11  two elementwise warpgroups; warpgroup g owns key columns
 //               [64g, 64g+64) of every tile, thread = TMEM lane = query row:
-//               s = S*scale - tau (computed as h = S*scale/2 - tau/2, u = h+|h|),
+//               s = S*scale - tau (packed f32x2 FMA, rounded once), u = max(s, 0),
 //               row max via 3-input max, per-half silent vote, u^10 by repeated
 //               squaring (no exp), running peak / tie count / argmax / mass, and
 //               P = u^10 split into two bf16 terms P_hi + P_lo written back over
@@ -256,13 +256,14 @@ __global__ void __launch_bounds__(F_THREADS, 1) flash_fwd_sm100_kernel(const __g
     const int row = q0 + rl;
     const uint32_t lane_off = (uint32_t)(32 * wq) << 16;
     const float tau = __ldg(p.tau);
-    const float hs = 0.5f * p.scale, ht = -0.5f * tau;  // h = s/2 exactly
+    // s = S*scale - tau, rounded once, two columns per packed f32x2 FMA
+    const float2 sc2 = make_float2(p.scale, p.scale), nt2 = make_float2(-tau, -tau);
     const int nT64 = (p.N + 63) >> 6;
     float peak = 0.f, cnt = 0.f;
     int arg = -1;  // first key attaining the running peak in this column half
-    float ms[8];
+    float2 ms[4];  // mass partial sums
 #pragma unroll
-    for (int i = 0; i < 8; ++i) ms[i] = 0.f;
+    for (int i = 0; i < 4; ++i) ms[i] = make_float2(0.f, 0.f);
     // `dead` (warp-uniform) turns the rest of the loop into no-ops after an
     // abort, while every warp still passes the warpgroup's named barriers.
     bool dead = false;
@@ -275,18 +276,20 @@ __global__ void __launch_bounds__(F_THREADS, 1) flash_fwd_sm100_kernel(const __g
         tmem_ld32(tmem + lane_off + TM_S + 128u * s + 64u * hh, r0);
         tmem_ld32(tmem + lane_off + TM_S + 128u * s + 64u * hh + 32u, r1);
         tmem_wait_ld();
-      } else {
-#pragma unroll
-        for (int c = 0; c < 32; ++c) r0[c] = r1[c] = 0xbf800000u;  // -1.0f: silent
       }
       float x[64];
 #pragma unroll
-      for (int c = 0; c < 32; ++c) {
-        x[c] = fmaf(__uint_as_float(r0[c]), hs, ht);
-        x[32 + c] = fmaf(__uint_as_float(r1[c]), hs, ht);
+      for (int c = 0; c < 32; c += 2) {
+        const float2 a = __ffma2_rn(make_float2(__uint_as_float(r0[c]), __uint_as_float(r0[c + 1])), sc2, nt2);
+        const float2 e = __ffma2_rn(make_float2(__uint_as_float(r1[c]), __uint_as_float(r1[c + 1])), sc2, nt2);
+        x[c] = a.x;
+        x[c + 1] = a.y;
+        x[32 + c] = e.x;
+        x[33 + c] = e.y;
       }
       const int kb = j * FN + 64 * hh;
-      const int lim = row < p.N ? (p.causal ? row : p.N - 1) - kb : -1;  // last valid column offset
+      int lim = row < p.N ? (p.causal ? row : p.N - 1) - kb : -1;  // last valid column offset
+      if (dead) lim = -1;                                                // after an abort: silent
       if (lim < 63) {
 #pragma unroll
         for (int c = 0; c < 64; ++c) x[c] = c > lim ? -1.f : x[c];
@@ -311,16 +314,17 @@ __global__ void __launch_bounds__(F_THREADS, 1) flash_fwd_sm100_kernel(const __g
         mbar_arrive(bar(B_VOTE + s));
       }
       if (live_h && !dead) {
-        const float mu = m > 0.f ? 2.f * m : 0.f;  // row max of u over this half tile
+        const float mu = m > 0.f ? m : 0.f;  // row max of u over this half tile
         if (mu > 0.f && mu >= peak) {
-          float c = 0.f;
-          int first = 64;
+          // columns attaining the maximum as a 64-bit mask: count and first key
+          uint32_t mlo = 0u, mhi = 0u;
 #pragma unroll
-          for (int i = 63; i >= 0; --i) {
-            const bool hit = x[i] == m;
-            c += hit ? 1.f : 0.f;
-            first = hit ? i : first;
+          for (int i = 0; i < 32; ++i) {
+            mlo |= x[i] == m ? 1u << i : 0u;
+            mhi |= x[32 + i] == m ? 1u << i : 0u;
           }
+          const float c = (float)(__popc(mlo) + __popc(mhi));
+          const int first = mlo ? __ffs(mlo) - 1 : 31 + __ffs(mhi);
           if (mu > peak) arg = kb + first;  // equal to an earlier tile's peak: keep the earlier key
           cnt = mu > peak ? c : cnt + c;
           peak = mu;
@@ -328,19 +332,25 @@ __global__ void __launch_bounds__(F_THREADS, 1) flash_fwd_sm100_kernel(const __g
         // P = u^10 as P_hi + P_lo (two bf16 terms, ~2^-17 relative): O, and with it the
         // backward's <dO,O>/gate, stays fp32-accurate; the tau gradient is a small
         // residual of cancelling per-row sums and needs that accuracy
-        uint32_t hi[32], lo[32];
+        const float2 neg1 = make_float2(-1.f, -1.f);
 #pragma unroll
-        for (int c = 0; c < 32; ++c) {
-          const float u0 = x[2 * c] + fabsf(x[2 * c]);
-          const float u1 = x[2 * c + 1] + fabsf(x[2 * c + 1]);
-          const float a2 = u0 * u0, a4 = a2 * a2, p0 = a4 * a4 * a2;
-          const float b2 = u1 * u1, b4 = b2 * b2, p1 = b4 * b4 * b2;
-          ms[c & 7] += p0 + p1;
-          hi[c] = pack_bf16x2(p0, p1);
-          lo[c] = pack_bf16x2(p0 - __uint_as_float(hi[c] << 16), p1 - __uint_as_float(hi[c] & 0xffff0000u));
+        for (int g = 0; g < 2; ++g) {  // 32 columns at a time: 16 packed hi words, 16 lo words
+          uint32_t hi[16], lo[16];
+#pragma unroll
+          for (int c = 0; c < 16; ++c) {
+            const int k = 32 * g + 2 * c;
+            const float2 u = make_float2(fmaxf(x[k], 0.f), fmaxf(x[k + 1], 0.f));
+            const float2 u2 = __fmul2_rn(u, u), u4 = __fmul2_rn(u2, u2);
+            const float2 pw = __fmul2_rn(__fmul2_rn(u4, u4), u2);
+            ms[c & 3] = __fadd2_rn(ms[c & 3], pw);
+            hi[c] = pack_bf16x2(pw.x, pw.y);
+            const float2 hf = make_float2(__uint_as_float(hi[c] << 16), __uint_as_float(hi[c] & 0xffff0000u));
+            const float2 lf = __ffma2_rn(hf, neg1, pw);  // exact: pw - hi
+            lo[c] = pack_bf16x2(lf.x, lf.y);
+          }
+          tmem_st16(tmem + lane_off + TM_S + 128u * s + 64u * hh + 16u * g, hi);
+          tmem_st16(tmem + lane_off + TM_S + 128u * s + 64u * hh + 32u + 16u * g, lo);
         }
-        tmem_st32(tmem + lane_off + TM_S + 128u * s + 64u * hh, hi);
-        tmem_st32(tmem + lane_off + TM_S + 128u * s + 64u * hh + 32u, lo);
         tmem_wait_st();
       }
       tc_fence_before();
@@ -349,7 +359,7 @@ __global__ void __launch_bounds__(F_THREADS, 1) flash_fwd_sm100_kernel(const __g
     }
     // ---- epilogue: merge the two column halves of every row, scale O, store
     float* st = reinterpret_cast<float*>(smem + L::OFF_STATS);
-    const float mass_h = ((ms[0] + ms[1]) + (ms[2] + ms[3])) + ((ms[4] + ms[5]) + (ms[6] + ms[7]));
+    const float mass_h = ((ms[0].x + ms[0].y) + (ms[1].x + ms[1].y)) + ((ms[2].x + ms[2].y) + (ms[3].x + ms[3].y));
     st[(hh * 4 + 0) * FM + rl] = peak;
     st[(hh * 4 + 1) * FM + rl] = mass_h;
     st[(hh * 4 + 2) * FM + rl] = cnt;

@@ -16,8 +16,12 @@
 //                columns [32g, 32g+32). Each thread pulls its whole S/dP slice
 //                into registers and releases TMEM at once, then computes
 //                u = relu(S*scale - tau), W = u^10 gate/z (-> P^T in TMEM) and
-//                dS = 10 scale gate/z u^9 (dP - D) + [u == peak] tie (-> smem,
+//                dS = 10 scale gate/z u^9 (dP - D) + [key == argmax] tie (-> smem,
 //                128-byte swizzled), accumulating dtau = -sum dS / scale.
+//                Two columns at a time in packed f32x2 arithmetic; masking only
+//                on tiles that cross the diagonal or a sequence end; the gate
+//                term is one patched entry per row (value tests only on tiles
+//                holding a row with several maxima).
 //   warps 12-15  dQ drain: TMEM -> fp32 staging tile in smem -> one
 //                cp.reduce.async.bulk add into the fp32 dQ accumulator.
 // Finally the elementwise warps write dK, dV (bf16) from TMEM.
@@ -27,6 +31,8 @@
 // flash_bwd_prep (RowCoef). S is recomputed by the tensor core exactly as in
 // the tcgen05 forward, so u == peak finds the forward's maxima.
 #include <string.h>
+
+#include <type_traits>
 
 #include "flash.cuh"
 #include "sm100_ptx.cuh"
@@ -66,7 +72,8 @@ struct BwdLayout {
   static constexpr int NSTG = D == 64 ? 2 : 1;  // dQ staging tiles in smem
   static constexpr int STG_BYTES = BM * D * 4;
   static constexpr int DS_BYTES = BN * BM * 2;
-  static constexpr int COEF_BYTES = BM * 32;
+  // per query tile: 64 interleaved coefficient records, 64 argmax keys, 64 tie peaks
+  static constexpr int CF_P = 0, CF_ARG = BM * 16, CF_PC = BM * 20, COEF_BYTES = BM * 24;
   static constexpr int OFF_K = 0;
   static constexpr int OFF_V = OFF_K + KBYTES;
   static constexpr int OFF_Q = OFF_V + KBYTES;
@@ -86,7 +93,10 @@ struct BwdLayout {
 
 struct BwdParams {
   CUtensorMap tk, tv, tq, tdo;
-  const float4* coef;
+  const float4* coefP;
+  const int32_t* argv;
+  const float* pcmpv;
+  int64_t npad;  // records per head
   const int32_t* live64;
   float* dq_acc;
   void* dk;
@@ -170,7 +180,7 @@ __global__ void __launch_bounds__(B_THREADS, 1) flash_bwd_sm100_kernel(const __g
       int t = 0;
       bool ok = true;
       for (int i = i_first; ok && i < p.nq64; ++i) {
-        if (!live[i]) continue;
+        if (!(live[i] & kLiveRow)) continue;
         const int s = t & 1;
         if (!(ok = mbar_wait(bar(C_QDEMPTY + s), ((t >> 1) & 1) ^ 1, ab))) break;
         const int q0 = i * BM;
@@ -179,9 +189,12 @@ __global__ void __launch_bounds__(B_THREADS, 1) flash_bwd_sm100_kernel(const __g
           tma_load_4d(sQ(s) + g * L::QGROUP, &p.tq, bar(C_QDFULL + s), 64 * g, q0, hd, b);
           tma_load_4d(sdO(s) + g * L::QGROUP, &p.tdo, bar(C_QDFULL + s), 64 * g, q0, hd, b);
         }
-        // 64 records always: the coefficient buffer carries 64 zero records past its end
-        bulk_load(sb0 + L::OFF_COEF + s * L::COEF_BYTES, p.coef + ((int64_t)bh * p.N + q0) * kCoefStride,
-                  L::COEF_BYTES, bar(C_QDFULL + s));
+        // 64 records always: each head's records are padded to whole 64-row tiles
+        const int64_t rec = (int64_t)bh * p.npad + q0;
+        const uint32_t cb = sb0 + L::OFF_COEF + s * L::COEF_BYTES;
+        bulk_load(cb + L::CF_P, p.coefP + rec, BM * 16, bar(C_QDFULL + s));
+        bulk_load(cb + L::CF_ARG, p.argv + rec, BM * 4, bar(C_QDFULL + s));
+        bulk_load(cb + L::CF_PC, p.pcmpv + rec, BM * 4, bar(C_QDFULL + s));
         ++t;
       }
       drain_wait(bar(C_KV), 0);
@@ -226,7 +239,7 @@ __global__ void __launch_bounds__(B_THREADS, 1) flash_bwd_sm100_kernel(const __g
       int t = 0;
       bool ok = mbar_wait(bar(C_KV), 0, ab);
       for (int i = i_first; ok && i < p.nq64; ++i) {
-        if (!live[i]) continue;
+        if (!(live[i] & kLiveRow)) continue;
         const int s = t & 1;
         if (!(ok = mbar_wait(bar(C_QDFULL + s), (t >> 1) & 1, ab))) break;
         if (!(ok = mbar_wait(bar(C_SDPEMPTY), (t & 1) ^ 1, ab))) break;
@@ -255,15 +268,19 @@ __global__ void __launch_bounds__(B_THREADS, 1) flash_bwd_sm100_kernel(const __g
     // ------------------------------------------------------------ elementwise
     const int ew = warp - 4, hh = ew >> 2, wq = warp & 3;
     const int rl = 32 * wq + lane;
-    const int key = k0 + rl;
+    const int key = k0 + rl, kb = k0 + 32 * wq;  // this thread's key, the warp's first key
     const uint32_t lane_off = (uint32_t)(32 * wq) << 16;
     const float tau = __ldg(p.tau);
-    const float hs = 0.5f * p.scale, ht = -0.5f * tau;
-    float ds_sum = 0.f;
+    // s = S*scale - tau rounded once; relu(s) is bit-identical to the forward's h + |h|
+    // with h = S*scale/2 - tau/2 (scaling by 2 commutes with rounding)
+    const float2 sc2 = make_float2(p.scale, p.scale), nt2 = make_float2(-tau, -tau);
+    const int lim = key < p.N ? (p.causal ? key : 0) : 0x7fffffff;  // first valid query of this key
+    float2 ds_sum = make_float2(0.f, 0.f);
     bool dead = false;
     int t = 0;
     for (int i = i_first; i < p.nq64; ++i) {
-      if (!live[i]) continue;
+      const int lv = live[i];
+      if (!(lv & kLiveRow)) continue;
       const int s = t & 1;
       const int q0 = i * BM;
       if (!dead) dead = !warp_wait(bar(C_SDPFULL), t & 1, ab);
@@ -281,42 +298,77 @@ __global__ void __launch_bounds__(B_THREADS, 1) flash_bwd_sm100_kernel(const __g
       if (!dead) dead = !warp_wait(bar(C_PDSEMPTY + s), ((t >> 1) & 1) ^ 1, ab);  // P^T / dS buffers
       if (!dead) {
         tc_fence_after();
-        const float4* cf = reinterpret_cast<const float4*>(smem + L::OFF_COEF + s * L::COEF_BYTES);
-        // columns past the diagonal or the sequence end hold u = 0
-        const int qb = q0 + 32 * hh;
-        const int lim = key < p.N ? (p.causal ? key : 0) : 0x7fffffff;  // first valid query
-        const int qend = p.N;
+        const uint8_t* cfb = smem + L::OFF_COEF + s * L::COEF_BYTES;
+        // this warp's 16 row pairs (two float4 each) for its 32 columns
+        const float4* cp4 = reinterpret_cast<const float4*>(cfb + L::CF_P) + 32 * hh;
+        const int* argw = reinterpret_cast<const int*>(cfb + L::CF_ARG) + 32 * hh;
+        const float* pcw = reinterpret_cast<const float*>(cfb + L::CF_PC) + 32 * hh;
+        const int qb = q0 + 32 * hh;  // first query of this warp's 32 columns
+        // One 32-column slice. MASK: zero u past the diagonal / the sequence ends.
+        // MULTI: per-element gate-gradient test (value ties); otherwise the single
+        // argmax entry of each row is patched in afterwards.
+        auto slice = [&](auto mask_c, auto multi_c) {
+          constexpr bool MASK = decltype(mask_c)::value, MULTI = decltype(multi_c)::value;
 #pragma unroll
-        for (int half = 0; half < 2; ++half) {
-          uint32_t pw_pk[8], ds_pk[8];
+          for (int half = 0; half < 2; ++half) {
+            uint32_t pw_pk[8], ds_pk[8];
 #pragma unroll
-          for (int c2 = 0; c2 < 8; ++c2) {
-            float wv[2], dv2[2];
-#pragma unroll
-            for (int e = 0; e < 2; ++e) {
-              const int c = half * 16 + 2 * c2 + e;
-              const int q = qb + c;
-              float x = fmaf(__uint_as_float(rs[c]), hs, ht);
-              x = (q >= lim && q < qend) ? x : -1.f;
-              const float u = x + fabsf(x);
-              const float4 c0 = cf[(32 * hh + c) * kCoefStride];      // peak, gate/z, 10 scale gate/z, D
-              const float4 c1 = cf[(32 * hh + c) * kCoefStride + 1];  // tie, argmax key, peak for ties
-              const float u2 = u * u, u4 = u2 * u2, u8 = u4 * u4, u9 = u8 * u;
-              wv[e] = u8 * u2 * c0.y;
-              const bool at_peak = u > 0.f && (key == __float_as_int(c1.y) || u == c1.z);
-              const float ds = fmaf(c0.z * u9, __uint_as_float(rp[c]) - c0.w, at_peak ? c1.x : 0.f);
-              dv2[e] = ds;
-              ds_sum += ds;
+            for (int c2 = 0; c2 < 8; ++c2) {
+              const int c = half * 16 + 2 * c2;
+              const float4 P0 = cp4[2 * (8 * half + c2)];      // c1 pair, c10 pair
+              const float4 P1 = cp4[2 * (8 * half + c2) + 1];  // -D pair, tie pair
+              float2 x = __ffma2_rn(make_float2(__uint_as_float(rs[c]), __uint_as_float(rs[c + 1])), sc2, nt2);
+              if constexpr (MASK) {
+                const int q = qb + c;
+                if (!(q >= lim && q < p.N)) x.x = -1.f;
+                if (!(q + 1 >= lim && q + 1 < p.N)) x.y = -1.f;
+              }
+              const float2 u = make_float2(fmaxf(x.x, 0.f), fmaxf(x.y, 0.f));
+              const float2 u2 = __fmul2_rn(u, u), u4 = __fmul2_rn(u2, u2), u8 = __fmul2_rn(u4, u4);
+              const float2 w = __fmul2_rn(__fmul2_rn(u8, u2), make_float2(P0.x, P0.y));
+              const float2 g = __fmul2_rn(__fmul2_rn(u8, u), make_float2(P0.z, P0.w));
+              const float2 dp = make_float2(__uint_as_float(rp[c]), __uint_as_float(rp[c + 1]));
+              float2 ds = __fmul2_rn(g, __fadd2_rn(dp, make_float2(P1.x, P1.y)));
+              if constexpr (MULTI) {
+                if (u.x > 0.f && (key == argw[c] || u.x == pcw[c])) ds.x += P1.z;
+                if (u.y > 0.f && (key == argw[c + 1] || u.y == pcw[c + 1])) ds.y += P1.w;
+              }
+              ds_sum = __fadd2_rn(ds_sum, ds);
+              pw_pk[c2] = pack_bf16x2(w.x, w.y);
+              ds_pk[c2] = pack_bf16x2(ds.x, ds.y);
             }
-            pw_pk[c2] = pack_bf16x2(wv[0], wv[1]);
-            ds_pk[c2] = pack_bf16x2(dv2[0], dv2[1]);
-          }
-          tmem_st8(tmem + lane_off + L::TM_P + 32u * s + 16u * hh + 8u * half, pw_pk);
+            tmem_st8(tmem + lane_off + L::TM_P + 32u * s + 16u * hh + 8u * half, pw_pk);
 #pragma unroll
-          for (int cc = 0; cc < 2; ++cc) {
-            const uint32_t chunk = 4 * hh + 2 * half + cc;  // 16-byte chunk of the 128-byte key row
-            st_shared_v4(sdS(s) + rl * 128 + ((chunk ^ (rl & 7)) << 4), ds_pk[4 * cc], ds_pk[4 * cc + 1],
-                         ds_pk[4 * cc + 2], ds_pk[4 * cc + 3]);
+            for (int cc = 0; cc < 2; ++cc) {
+              const uint32_t chunk = 4 * hh + 2 * half + cc;  // 16-byte chunk of the 128-byte key row
+              st_shared_v4(sdS(s) + rl * 128 + ((chunk ^ (rl & 7)) << 4), ds_pk[4 * cc], ds_pk[4 * cc + 1],
+                           ds_pk[4 * cc + 2], ds_pk[4 * cc + 3]);
+            }
+          }
+        };
+        using T_ = std::true_type;
+        using F_ = std::false_type;
+        const bool edge = (p.causal && qb < kb + 31) || qb + 32 > p.N || kb + 32 > p.N;
+        if (lv & kMultiTie) {
+          slice(T_{}, T_{});
+        } else {
+          if (edge) slice(T_{}, F_{});
+          else slice(F_{}, F_{});
+          // Gate gradient of the rows whose argmax key is one of this warp's keys:
+          // lane c patches column c's entry (key row arg - k0) of the bf16 dS tile.
+          __syncwarp();
+          const int col = 32 * hh + lane;
+          const int l = argw[lane] - kb;
+          if ((unsigned)l < 32u) {
+            const float tie = reinterpret_cast<const float*>(cp4)[(lane >> 1) * 8 + 6 + (lane & 1)];
+            const int r = 32 * wq + l;
+            const uint32_t addr = sdS(s) + r * 128 + ((((uint32_t)col >> 3) ^ (r & 7)) << 4) + (col & 7) * 2;
+            unsigned short hv;
+            asm volatile("ld.shared.u16 %0, [%1];" : "=h"(hv) : "r"(addr) : "memory");
+            const float nv = __bfloat162float(__ushort_as_bfloat16(hv)) + tie;
+            hv = __bfloat16_as_ushort(__float2bfloat16_rn(nv));
+            asm volatile("st.shared.u16 [%0], %1;" ::"r"(addr), "h"(hv) : "memory");
+            ds_sum.x += tie;
           }
         }
         tmem_wait_st();
@@ -367,7 +419,7 @@ __global__ void __launch_bounds__(B_THREADS, 1) flash_bwd_sm100_kernel(const __g
       }
     }
     // ---- tau gradient partial of this CTA (fixed reduction order)
-    float v = ds_sum;
+    float v = ds_sum.x + ds_sum.y;
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
     float* red = reinterpret_cast<float*>(smem + L::OFF_RED);
@@ -387,7 +439,7 @@ __global__ void __launch_bounds__(B_THREADS, 1) flash_bwd_sm100_kernel(const __g
     bool dead = false;
     int t = 0;
     for (int i = i_first; i < p.nq64; ++i) {
-      if (!live[i]) continue;
+      if (!(live[i] & kLiveRow)) continue;
       const int bq = t % L::NDQ, sg = t % L::NSTG;
       const int q0 = i * BM;
       if (!dead) dead = !warp_wait(bar(C_DQFULL + bq), (t / L::NDQ) & 1, ab);
@@ -453,7 +505,10 @@ int flash_bwd_sm100(const FlashArgs& a0, cudaStream_t st) {
   if (!rc) rc = tma_map_bhnd(&p.tq, a.q, a.sq, a.B, a.H, a.N, a.D, BM);
   if (!rc) rc = tma_map_bhnd(&p.tdo, a.dout, a.sdo, a.B, a.H, a.N, a.D, BM);
   if (rc) return rc;
-  p.coef = a.coef;
+  p.coefP = a.coefP;
+  p.argv = a.argv;
+  p.pcmpv = a.pcmpv;
+  p.npad = rec_rows(a.N);
   p.live64 = a.live64;
   p.dq_acc = a.dq_acc;
   p.dk = a.dk;

@@ -189,6 +189,14 @@ __device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t (&r)[32
       PNFT_W8(0), PNFT_W8(8), PNFT_W8(16), PNFT_W8(24)
       : "memory");
 }
+// 32 lanes x 16 consecutive columns <- r[0..15]
+__device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint32_t (&r)[16]) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16};" ::"r"(
+          taddr),
+      PNFT_W8(0), PNFT_W8(8)
+      : "memory");
+}
 // 32 lanes x 8 consecutive columns <- r[0..7]
 __device__ __forceinline__ void tmem_st8(uint32_t taddr, const uint32_t (&r)[8]) {
   asm volatile("tcgen05.st.sync.aligned.32x32b.x8.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8};" ::"r"(taddr), "r"(r[0]),
