@@ -158,11 +158,13 @@ extern "C" int pnft_flash_bwd(const void* q, const int64_t* sq, const void* k, c
   {
     const size_t recs = (size_t)(B * H * rec_rows(N));
     a.coefP = reinterpret_cast<float4*>(ws + w.off_coef);
-    a.argv = reinterpret_cast<int32_t*>(a.coefP + recs);
+    a.tiev = reinterpret_cast<float*>(a.coefP + recs / 2);
+    a.argv = reinterpret_cast<int32_t*>(a.tiev + recs);
     a.pcmpv = reinterpret_cast<float*>(a.argv + recs);
   }
   a.live64 = reinterpret_cast<int32_t*>(ws + w.off_live);
   a.dtau_part = reinterpret_cast<float*>(ws + w.off_part);
+  a.dq_scale = 1.f;
   if (use_sm100(a)) return flash_bwd_sm100(a, st);
   return flash_bwd_generic(a, st);
 }

@@ -34,31 +34,35 @@ struct FlashArgs {
   float* dq_acc;       // fp32 [B,H,N,D] contiguous
   // per-row backward coefficients (see below): record of row n of head bh at
   // r = bh * rec_rows(N) + n; the padding rows past N hold silent-row records
-  float4* coefP;       // rows 2j, 2j+1 interleaved: {c1_0, c1_1, c10_0, c10_1}, {-D_0, -D_1, tie_0, tie_1}
+  float4* coefP;       // rows 2j, 2j+1 interleaved: {c1_0, c1_1, -D_0, -D_1}
+  float* tiev;         // tie / 10 (the gate term in units of 10*scale)
   int32_t* argv;       // argmax key (-1: silent row)
   float* pcmpv;        // peak for the value test (NaN when Nmax == 1)
   int32_t* live64;     // [B*H, ceil(N/64)]: bit 0 any row live (peak > 0), bit 1 any row with Nmax > 1
   float* dtau_part;    // per (bh, key tile) partial of -sum du
   int64_t n_dtau_part;
+  float dq_scale;      // factor the dQ cast applies to the fp32 accumulator
 };
 
-// Per query row backward coefficients (c1 = gate/z, c10 = 10*scale*gate/z,
-// D = <dO,O>/gate, tie = scale * D * gamma/(peak+gamma)^2 / Nmax, pcmp = peak
-// when Nmax > 1 else NaN):
+// Per query row backward coefficients (c1 = gate/z, D = <dO,O>/gate,
+// tie = scale * D * gamma/(peak+gamma)^2 / Nmax, pcmp = peak when Nmax > 1
+// else NaN):
 //   W  = c1 * u^10                  (the normalised, gated weight: P)
-//   dS = c10 * u^9 * (dP - D) + [key == argmax || u == pcmp] * tie
-// A row with one maximum takes the gate gradient at its recorded argmax (exact
-// whatever arithmetic recomputes S); genuine ties (Nmax > 1) are found by value
-// and split evenly, like the eager amax backward. A silent row has argmax -1
-// and all-zero coefficients.
+//   dS = 10*scale*c1 * u^9 * (dP - D) + [key == argmax || u == pcmp] * tie
+// The records hold c1, -D and tie/10 (the tcgen05 kernel works with
+// dS' = dS / (10*scale)). A row with one maximum takes the gate gradient at its
+// recorded argmax (exact whatever arithmetic recomputes S); genuine ties
+// (Nmax > 1) are found by value and split evenly, like the eager amax
+// backward. A silent row has argmax -1 and all-zero coefficients.
 constexpr int kLiveRow = 1, kMultiTie = 2;  // live64 bits
 
 struct RowCoef {
-  float c1, c10, D, tie;
+  float c1, c10, D, tie;  // tie and c10 in dS units (scale included)
 };
-__device__ __forceinline__ RowCoef load_row_coef(const float4* coefP, int64_t r) {
-  const float* p = reinterpret_cast<const float*>(coefP) + (r >> 1) * 8 + (r & 1);
-  return RowCoef{p[0], p[2], -p[4], p[6]};
+__device__ __forceinline__ RowCoef load_row_coef(const float4* coefP, const float* tiev, int64_t r, float scale) {
+  const float* p = reinterpret_cast<const float*>(coefP) + (r >> 1) * 4 + (r & 1);
+  const float c1 = p[0], ts = 10.f * scale;
+  return RowCoef{c1, ts * c1, -p[2], ts * tiev[r]};
 }
 
 // Rows per head in the coefficient arrays: N rounded up to whole 64-row tiles,

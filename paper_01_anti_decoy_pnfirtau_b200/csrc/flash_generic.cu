@@ -226,7 +226,7 @@ __global__ void __launch_bounds__(256) flash_bwd_prep_kernel(FlashArgs a) {
     live |= peak > 0.f;
     if (sl == 0) {
       // rows past N get the record of a silent row (the tile loads read all 64)
-      float4 cA = make_float4(0.f, 0.f, 0.f, 0.f);
+      float c1 = 0.f, Dg = 0.f, tie = 0.f;
       int arg = -1, nm = 0;
       float pcmp = __int_as_float(0x7fc00000);  // NaN never compares equal
       if (ok) {
@@ -235,23 +235,20 @@ __global__ void __launch_bounds__(256) flash_bwd_prep_kernel(FlashArgs a) {
         arg = a.stat_arg[r];
         float gate = 0.f;
         if (peak > 0.f) gate = a.has_gamma ? peak / (peak + a.gamma) : 1.f;
-        const float Dg = gate > 0.f ? dot / gate : 0.f;
-        float tie = 0.f;
+        Dg = gate > 0.f ? dot / gate : 0.f;
         if (a.has_gamma && peak > 0.f) {
           const float pg = peak + a.gamma;
-          tie = Dg * (a.gamma / (pg * pg)) / (float)nm;
+          tie = Dg * (a.gamma / (pg * pg)) / (float)nm;  // d out / d peak per maximum (du units)
         }
-        const float c1 = gate / z;
-        cA = make_float4(c1, (10.f * a.scale) * c1, Dg, a.scale * tie);
+        c1 = gate / z;
         // single maximum: matched by key index; genuine ties (Nmax > 1): by value
         if (nm > 1) pcmp = peak;
       }
       const int64_t rr = bh * npad + n;
-      float* cp = reinterpret_cast<float*>(a.coefP) + (rr >> 1) * 8 + (rr & 1);
-      cp[0] = cA.x;
-      cp[2] = cA.y;
-      cp[4] = -cA.z;
-      cp[6] = cA.w;
+      float* cp = reinterpret_cast<float*>(a.coefP) + (rr >> 1) * 4 + (rr & 1);
+      cp[0] = c1;
+      cp[2] = -Dg;
+      a.tiev[rr] = 0.1f * tie;  // dS = scale * du; dS' = dS / (10 scale)
       a.argv[rr] = arg;
       a.pcmpv[rr] = pcmp;
       if (nm > 1) multi = 1;
@@ -307,7 +304,7 @@ __global__ void __launch_bounds__(GTHREADS) flash_bwd_generic_kernel(FlashArgs a
       float pcmp = __int_as_float(0x7fc00000);
       if (row < N) {
         const int64_t rr = bh * rec_rows(N) + row;
-        c = load_row_coef(a.coefP, rr);
+        c = load_row_coef(a.coefP, a.tiev, rr, a.scale);
         arg = a.argv[rr];
         pcmp = a.pcmpv[rr];
       }
@@ -436,6 +433,7 @@ __global__ void __launch_bounds__(GTHREADS) flash_bwd_generic_kernel(FlashArgs a
 template <typename T>
 __global__ void __launch_bounds__(256) dq_cast_kernel(FlashArgs a) {
   T* dq = static_cast<T*>(a.dq);
+  const float fs = a.dq_scale;
   const bool vec = (a.D % 8) == 0 && a.sdq[3] == 1 && (a.sdq[2] % 8) == 0 && (a.sdq[1] % 8) == 0 &&
                    (a.sdq[0] % 8) == 0 && (reinterpret_cast<uintptr_t>(a.dq) % 16) == 0;
   if (vec) {  // 8 consecutive head dims per thread: two float4 loads, one or two 16-byte stores
@@ -445,7 +443,9 @@ __global__ void __launch_bounds__(256) dq_cast_kernel(FlashArgs a) {
       const int64_t row = i / per_row, c = (i - row * per_row) * 8;
       const int64_t n = row % a.N, bh = row / a.N, b = bh / a.H, h = bh % a.H;
       const float4* src = reinterpret_cast<const float4*>(a.dq_acc + row * a.D + c);
-      const float4 f0 = src[0], f1 = src[1];
+      float4 f0 = src[0], f1 = src[1];
+      f0.x *= fs; f0.y *= fs; f0.z *= fs; f0.w *= fs;
+      f1.x *= fs; f1.y *= fs; f1.z *= fs; f1.w *= fs;
       T* dst = dq + b * a.sdq[0] + h * a.sdq[1] + n * a.sdq[2] + c;
       if constexpr (sizeof(T) == 2) {
         uint4 w;
@@ -463,7 +463,7 @@ __global__ void __launch_bounds__(256) dq_cast_kernel(FlashArgs a) {
   const int64_t total = a.B * a.H * a.N * a.D;
   for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
     const int64_t e = i % a.D, n = (i / a.D) % a.N, bh = i / (a.D * a.N), b = bh / a.H, h = bh % a.H;
-    dq[b * a.sdq[0] + h * a.sdq[1] + n * a.sdq[2] + e * a.sdq[3]] = from_f32<T>(a.dq_acc[i]);
+    dq[b * a.sdq[0] + h * a.sdq[1] + n * a.sdq[2] + e * a.sdq[3]] = from_f32<T>(fs * a.dq_acc[i]);
   }
 }
 
@@ -481,8 +481,8 @@ BwdWorkspace bwd_workspace_layout(int64_t B, int64_t H, int64_t N, int64_t D) {
   const size_t ntiles64 = (size_t)(B * H) * (size_t)((N + GB - 1) / GB);
   w.off_dq = 0;
   w.off_coef = up(rows * (size_t)D * sizeof(float));
-  // coefA, coefB (float4), argv (int32), pcmpv (float): recs records each
-  w.off_live = w.off_coef + up(recs * (2 * sizeof(float4) + sizeof(int32_t) + sizeof(float)));
+  // coefP (two floats per row), tiev, argv, pcmpv: recs records each
+  w.off_live = w.off_coef + up(recs * (sizeof(float2) + sizeof(float) + sizeof(int32_t) + sizeof(float)));
   w.off_part = w.off_live + up(ntiles64 * sizeof(int32_t));
   w.total = w.off_part + up(ntiles64 * sizeof(float));
   return w;

@@ -3,21 +3,23 @@
 // One CTA per (128 keys, b*h), KV-parallel over the 64-query tiles at or below
 // the causal diagonal whose rows are not all silent (per-tile flags from the
 // prep kernel). 512 threads:
-//   warp 0       TMA producer: K, V once; per query tile Q, dO (2 stages) and
-//                the 64 per-row coefficient records.
-//   warp 1       MMA issuer + TMEM owner. Per tile t:
+//   warp 0       TMA producer: K, V once; per query tile Q, dO (3 stages for
+//                D=64, 2 for D=128) and the tile's per-row coefficient records.
+//   warp 1       MMA issuer + TMEM owner (a converged warp; one elected lane
+//                issues, descriptors are precomputed bases plus constant
+//                offsets). Per tile t:
 //                  S^T = K Q^T, dP^T = V dO^T            (SS, M=128 keys, N=64)
 //                then for tile t-1 (overlapping tile t's elementwise work):
 //                  dV += P^T dO   (TS: P^T bf16 from TMEM)
 //                  dK += dS^T Q   (SS: dS^T bf16 from shared memory)
-//                  dQ  = dS K     (D=64: M=64 queries) or
-//                  dQ^T = K^T dS^T (D=128: M=128 head dims), into TMEM
+//                  dQ^T = K^T dS^T (SS, M = head dims), into TMEM
 //   warps 4-11   elementwise, thread = TMEM lane = key; warpgroup g owns query
 //                columns [32g, 32g+32). Each thread pulls its whole S/dP slice
 //                into registers and releases TMEM at once, then computes
-//                u = relu(S*scale - tau), W = u^10 gate/z (-> P^T in TMEM) and
-//                dS = 10 scale gate/z u^9 (dP - D) + [key == argmax] tie (-> smem,
-//                128-byte swizzled), accumulating dtau = -sum dS / scale.
+//                u = relu(S*scale - tau), W = c1 u^10 (-> P^T in TMEM) and
+//                dS' = c1 u^9 (dP - D) + [key == argmax] tie/10 (-> smem,
+//                128-byte swizzled), dS' = dS / (10 scale); the factor is applied
+//                to dK here and to dQ by the cast kernel, and dtau = -10 sum dS'.
 //                Two columns at a time in packed f32x2 arithmetic; masking only
 //                on tiles that cross the diagonal or a sequence end; the gate
 //                term is one patched entry per row (value tests only on tiles
@@ -26,7 +28,7 @@
 //                cp.reduce.async.bulk add into the fp32 dQ accumulator.
 // Finally the elementwise warps write dK, dV (bf16) from TMEM.
 // TMEM columns: S [0,64) dP [64,128) P^T x2 [128,192) dV [192,192+D)
-//               dK [192+D,192+2D) dQ (x2 for D=64) [192+2D, 512).
+//               dK [192+D,192+2D) dQ^T (x2 for D=64) [192+2D, 512).
 // Semantics: src/triton_pnfirtau.py:445-621 with the per-row terms of
 // flash_bwd_prep (RowCoef). S is recomputed by the tensor core exactly as in
 // the tcgen05 forward, so u == peak finds the forward's maxima.
@@ -49,21 +51,22 @@ constexpr int B_THREADS = 512;
 
 enum : int {
   C_KV = 0,
-  C_QDFULL = 1,    // [2]
-  C_QDEMPTY = 3,   // [2]
-  C_SDPFULL = 5,
-  C_SDPEMPTY = 6,
-  C_PDSFULL = 7,   // [2]
-  C_PDSEMPTY = 9,  // [2]
-  C_DQFULL = 11,   // [2]
-  C_DQEMPTY = 13,  // [2]
-  C_DKV = 15,
-  C_FLAG = 16,  // plain arrive after dkv_written is stored (release for the flag)
-  C_COUNT = 17
+  C_QDFULL = 1,    // [3]
+  C_QDEMPTY = 4,   // [3]
+  C_SDPFULL = 7,
+  C_SDPEMPTY = 8,
+  C_PDSFULL = 9,   // [2]
+  C_PDSEMPTY = 11, // [2]
+  C_DQFULL = 13,   // [2]
+  C_DQEMPTY = 15,  // [2]
+  C_DKV = 17,
+  C_FLAG = 18,  // plain arrive after dkv_written is stored (release for the flag)
+  C_COUNT = 19
 };
 
 template <int D>
 struct BwdLayout {
+  static constexpr int NQS = D == 64 ? 3 : 2;    // Q / dO / coefficient stages
   static constexpr int KGROUP = BN * 128;  // one 64-column group of the K / V tile
   static constexpr int QGROUP = BM * 128;  // one 64-column group of a Q / dO tile
   static constexpr int KBYTES = BN * D * 2;
@@ -72,16 +75,16 @@ struct BwdLayout {
   static constexpr int NSTG = D == 64 ? 2 : 1;  // dQ staging tiles in smem
   static constexpr int STG_BYTES = BM * D * 4;
   static constexpr int DS_BYTES = BN * BM * 2;
-  // per query tile: 64 interleaved coefficient records, 64 argmax keys, 64 tie peaks
-  static constexpr int CF_P = 0, CF_ARG = BM * 16, CF_PC = BM * 20, COEF_BYTES = BM * 24;
+  // per query tile: 32 coefficient pairs {c1, c1, -D, -D}, tie/10, argmax, tie peak
+  static constexpr int CF_P = 0, CF_TIE = BM * 8, CF_ARG = BM * 12, CF_PC = BM * 16, COEF_BYTES = BM * 20;
   static constexpr int OFF_K = 0;
   static constexpr int OFF_V = OFF_K + KBYTES;
   static constexpr int OFF_Q = OFF_V + KBYTES;
-  static constexpr int OFF_DO = OFF_Q + 2 * QBYTES;
-  static constexpr int OFF_DS = OFF_DO + 2 * QBYTES;
+  static constexpr int OFF_DO = OFF_Q + NQS * QBYTES;
+  static constexpr int OFF_DS = OFF_DO + NQS * QBYTES;
   static constexpr int OFF_STG = OFF_DS + 2 * DS_BYTES;
   static constexpr int OFF_COEF = OFF_STG + NSTG * STG_BYTES;
-  static constexpr int OFF_BAR = OFF_COEF + 2 * COEF_BYTES;
+  static constexpr int OFF_BAR = OFF_COEF + NQS * COEF_BYTES;
   static constexpr int OFF_TMEM = OFF_BAR + C_COUNT * 8;
   static constexpr int OFF_ABORT = OFF_TMEM + 4;
   static constexpr int OFF_DKVW = OFF_ABORT + 4;
@@ -89,11 +92,13 @@ struct BwdLayout {
   static constexpr int END = OFF_RED + 32;
   static constexpr int SMEM = END + 1024;
   static constexpr uint32_t TM_S = 0, TM_DP = 64, TM_P = 128, TM_DV = 192, TM_DK = 192 + D, TM_DQ = 192 + 2 * D;
+  static_assert(SMEM <= 227 * 1024, "shared memory budget");
 };
 
 struct BwdParams {
   CUtensorMap tk, tv, tq, tdo;
   const float4* coefP;
+  const float* tiev;
   const int32_t* argv;
   const float* pcmpv;
   int64_t npad;  // records per head
@@ -111,6 +116,38 @@ struct BwdParams {
   int causal;
 };
 
+// Warp-cooperative walk over the query tiles [i0, n) whose live bit is set: 32
+// flags per ballot, the next 32 already loaded (one flag per lane), so moving
+// from tile to tile never waits on global memory. All 32 lanes call next().
+struct LiveTiles {
+  const int32_t* f;
+  int n, base;
+  uint32_t live, multi;
+  int32_t ahead;  // this lane's flag of tile base + 32 + lane
+  __device__ __forceinline__ LiveTiles(const int32_t* flags, int i0, int n_) : f(flags), n(n_), base(i0) {
+    const int lane = threadIdx.x & 31;
+    const int32_t cur = i0 + lane < n ? f[i0 + lane] : 0;
+    ahead = i0 + 32 + lane < n ? f[i0 + 32 + lane] : 0;
+    live = __ballot_sync(0xffffffffu, cur & kLiveRow);
+    multi = __ballot_sync(0xffffffffu, cur & kMultiTie);
+  }
+  // Next live tile, -1 past the end; *is_multi: the tile holds a row with several maxima.
+  __device__ __forceinline__ int next(bool* is_multi) {
+    while (!live) {
+      if (base + 32 >= n) return -1;
+      base += 32;
+      live = __ballot_sync(0xffffffffu, ahead & kLiveRow);
+      multi = __ballot_sync(0xffffffffu, ahead & kMultiTie);
+      const int j = base + 32 + (int)(threadIdx.x & 31);
+      ahead = j < n ? f[j] : 0;
+    }
+    const int bit = __ffs(live) - 1;
+    live &= live - 1;
+    *is_multi = (multi >> bit) & 1u;
+    return base + bit;
+  }
+};
+
 __device__ __forceinline__ void st_shared_v4(uint32_t addr, uint32_t a, uint32_t b, uint32_t c, uint32_t d) {
   asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "r"(a), "r"(b), "r"(c), "r"(d) : "memory");
 }
@@ -119,8 +156,10 @@ template <int D>
 __global__ void __launch_bounds__(B_THREADS, 1) flash_bwd_sm100_kernel(const __grid_constant__ BwdParams p) {
   using L = BwdLayout<D>;
   constexpr int DG = D / 64;
+  constexpr int NQS = L::NQS;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
-  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  // offset from the __shared__ array itself, so the compiler keeps shared-space accesses
+  uint8_t* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
   const uint32_t sb0 = smem_u32(smem);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int kt = blockIdx.x, bh = blockIdx.y, b = bh / p.H, hd = bh % p.H;
@@ -140,9 +179,11 @@ __global__ void __launch_bounds__(B_THREADS, 1) flash_bwd_sm100_kernel(const __g
     mbar_init(bar(C_KV), 1);
     mbar_init(bar(C_SDPFULL), 1);
     mbar_init(bar(C_SDPEMPTY), 8);
-    for (int i = 0; i < 2; ++i) {
+    for (int i = 0; i < NQS; ++i) {
       mbar_init(bar(C_QDFULL + i), 1);
       mbar_init(bar(C_QDEMPTY + i), 1);
+    }
+    for (int i = 0; i < 2; ++i) {
       mbar_init(bar(C_PDSFULL + i), 8);
       mbar_init(bar(C_PDSEMPTY + i), 1);
       mbar_init(bar(C_DQFULL + i), 1);
@@ -170,100 +211,120 @@ __global__ void __launch_bounds__(B_THREADS, 1) flash_bwd_sm100_kernel(const __g
   const uint32_t tmem = *reinterpret_cast<volatile uint32_t*>(smem + L::OFF_TMEM);
 
   if (warp == 0) {
-    // ------------------------------------------------------------ producer
+    // ------------------------------------------------------------ producer (converged warp, lane 0 issues)
     if (lane == 0) {
       mbar_arrive_expect_tx(bar(C_KV), 2 * L::KBYTES);
       for (int g = 0; g < DG; ++g) {
         tma_load_4d(sK + g * L::KGROUP, &p.tk, bar(C_KV), 64 * g, k0, hd, b);
         tma_load_4d(sV + g * L::KGROUP, &p.tv, bar(C_KV), 64 * g, k0, hd, b);
       }
-      int t = 0;
-      bool ok = true;
-      for (int i = i_first; ok && i < p.nq64; ++i) {
-        if (!(live[i] & kLiveRow)) continue;
-        const int s = t & 1;
-        if (!(ok = mbar_wait(bar(C_QDEMPTY + s), ((t >> 1) & 1) ^ 1, ab))) break;
+    }
+    __syncwarp();
+    LiveTiles lt(live, i_first, p.nq64);
+    int t = 0;
+    bool ok = true, mt;
+    for (int i; ok && (i = lt.next(&mt)) >= 0;) {
+      const int s = t % NQS;
+      if (!(ok = warp_wait(bar(C_QDEMPTY + s), ((t / NQS) & 1) ^ 1, ab))) break;
+      if (lane == 0) {
         const int q0 = i * BM;
-        mbar_arrive_expect_tx(bar(C_QDFULL + s), 2 * L::QBYTES + L::COEF_BYTES);
+        const uint32_t full = bar(C_QDFULL + s);
+        mbar_arrive_expect_tx(full, 2 * L::QBYTES + L::COEF_BYTES);
         for (int g = 0; g < DG; ++g) {
-          tma_load_4d(sQ(s) + g * L::QGROUP, &p.tq, bar(C_QDFULL + s), 64 * g, q0, hd, b);
-          tma_load_4d(sdO(s) + g * L::QGROUP, &p.tdo, bar(C_QDFULL + s), 64 * g, q0, hd, b);
+          tma_load_4d(sQ(s) + g * L::QGROUP, &p.tq, full, 64 * g, q0, hd, b);
+          tma_load_4d(sdO(s) + g * L::QGROUP, &p.tdo, full, 64 * g, q0, hd, b);
         }
         // 64 records always: each head's records are padded to whole 64-row tiles
         const int64_t rec = (int64_t)bh * p.npad + q0;
         const uint32_t cb = sb0 + L::OFF_COEF + s * L::COEF_BYTES;
-        bulk_load(cb + L::CF_P, p.coefP + rec, BM * 16, bar(C_QDFULL + s));
-        bulk_load(cb + L::CF_ARG, p.argv + rec, BM * 4, bar(C_QDFULL + s));
-        bulk_load(cb + L::CF_PC, p.pcmpv + rec, BM * 4, bar(C_QDFULL + s));
-        ++t;
+        bulk_load(cb + L::CF_P, p.coefP + rec / 2, BM * 8, full);
+        bulk_load(cb + L::CF_TIE, p.tiev + rec, BM * 4, full);
+        bulk_load(cb + L::CF_ARG, p.argv + rec, BM * 4, full);
+        bulk_load(cb + L::CF_PC, p.pcmpv + rec, BM * 4, full);
       }
-      drain_wait(bar(C_KV), 0);
-      for (int u = t - 1; u >= 0 && u > t - 3; --u) drain_wait(bar(C_QDFULL + (u & 1)), (u >> 1) & 1);
+      __syncwarp();
+      ++t;
     }
-  } else if (warp == 1) {
-    // ------------------------------------------------------------ MMA issuer
     if (lane == 0) {
-      constexpr uint32_t ID_S = idesc_f16(BN, BM, 1, 0, 0);   // S^T, dP^T: K-major A and B
-      constexpr uint32_t ID_G = idesc_f16(BN, D, 1, 0, 1);    // dV (A in TMEM), dK (A K-major); B MN-major
-      constexpr uint32_t ID_DQ = idesc_f16(D, BM, 1, 1, 1);   // dQ^T: M = head dims
-      uint32_t dv_acc = 0, dk_acc = 0;
-      auto grads = [&](int u) -> bool {
-        const int s = u & 1;
-        if (!mbar_wait(bar(C_PDSFULL + s), (u >> 1) & 1, ab)) return false;
-        tc_fence_after();
+      drain_wait(bar(C_KV), 0);
+      for (int u = t - 1; u >= 0 && u > t - 1 - NQS; --u) drain_wait(bar(C_QDFULL + u % NQS), (u / NQS) & 1);
+    }
+    __syncwarp();
+  } else if (warp == 1) {
+    // ------------------------------------------------------------ MMA issuer (converged warp)
+    constexpr uint32_t ID_S = idesc_f16(BN, BM, 1, 0, 0);   // S^T, dP^T: K-major A and B
+    constexpr uint32_t ID_G = idesc_f16(BN, D, 1, 0, 1);    // dV (A in TMEM), dK (A K-major); B MN-major
+    constexpr uint32_t ID_DQ = idesc_f16(D, BM, 1, 1, 1);   // dQ^T: M = head dims
+    // Descriptors of k-step 0; a k-step moves +32 B inside a 128-byte K-major row
+    // (+2 in descriptor units, +GROUP bytes across 64-column groups) or +16 rows
+    // (2048 B, +128) of an MN-major tile.
+    const uint64_t dKk = sw128_desc(sK, 16, 1024), dVk = sw128_desc(sV, 16, 1024);
+    const uint64_t dKmn = sw128_desc(sK, L::KGROUP, 1024);
+    const uint64_t dQk = sw128_desc(sQ(0), 16, 1024), dOk = sw128_desc(sdO(0), 16, 1024);
+    const uint64_t dQmn = sw128_desc(sQ(0), L::QGROUP, 1024), dOmn = sw128_desc(sdO(0), L::QGROUP, 1024);
+    const uint64_t dSk = sw128_desc(sdS(0), 16, 1024), dSmn = sw128_desc(sdS(0), L::KGROUP, 1024);
+    constexpr uint64_t QSTEP = L::QBYTES >> 4, DSSTEP = L::DS_BYTES >> 4;
+    auto kmaj = [](int kk, int group) -> uint64_t { return (uint64_t)(((kk >> 2) * group + (kk & 3) * 32) >> 4); };
+    uint32_t dv_acc = 0, dk_acc = 0;
+    auto grads = [&](int u) -> bool {
+      const int s = u & 1, qs = u % NQS;
+      if (!warp_wait(bar(C_PDSFULL + s), (u >> 1) & 1, ab)) return false;
+      tc_fence_after();
+      if (elect_one()) {
 #pragma unroll
-        for (int kk = 0; kk < BM / 16; ++kk) {
-          mma_ts(tmem + L::TM_DV, tmem + L::TM_P + 32u * s + 8u * kk, sw128_desc(sdO(s) + kk * 2048, L::QGROUP, 1024),
-                 ID_G, dv_acc);
-          dv_acc = 1;
-        }
+        for (int kk = 0; kk < BM / 16; ++kk)
+          mma_ts(tmem + L::TM_DV, tmem + L::TM_P + 32u * s + 8u * kk, dOmn + qs * QSTEP + kk * 128, ID_G,
+                 dv_acc | (uint32_t)kk);
 #pragma unroll
-        for (int kk = 0; kk < BM / 16; ++kk) {
-          mma_ss(tmem + L::TM_DK, sw128_desc(sdS(s) + kk * 32, 16, 1024),
-                 sw128_desc(sQ(s) + kk * 2048, L::QGROUP, 1024), ID_G, dk_acc);
-          dk_acc = 1;
-        }
-        const int bq = u % L::NDQ;
-        if (!mbar_wait(bar(C_DQEMPTY + bq), ((u / L::NDQ) & 1) ^ 1, ab)) return false;
-        tc_fence_after();
+        for (int kk = 0; kk < BM / 16; ++kk)
+          mma_ss(tmem + L::TM_DK, dSk + s * DSSTEP + kk * 2, dQmn + qs * QSTEP + kk * 128, ID_G, dk_acc | (uint32_t)kk);
+      }
+      __syncwarp();
+      dv_acc = dk_acc = 1;
+      const int bq = u % L::NDQ;
+      if (!warp_wait(bar(C_DQEMPTY + bq), ((u / L::NDQ) & 1) ^ 1, ab)) return false;
+      tc_fence_after();
+      if (elect_one()) {
         // dQ^T[D x 64 q] = K^T[D x keys] dS^T[keys x q]: both operands MN-major in smem
 #pragma unroll
         for (int kk = 0; kk < BN / 16; ++kk)
-          mma_ss(tmem + L::TM_DQ + 64u * bq, sw128_desc(sK + kk * 2048, L::KGROUP, 1024),
-                 sw128_desc(sdS(s) + kk * 2048, L::KGROUP, 1024), ID_DQ, kk > 0);
+          mma_ss(tmem + L::TM_DQ + 64u * bq, dKmn + kk * 128, dSmn + s * DSSTEP + kk * 128, ID_DQ, kk > 0);
         mma_commit(bar(C_DQFULL + bq));
         mma_commit(bar(C_PDSEMPTY + s));
-        mma_commit(bar(C_QDEMPTY + s));
-        return true;
-      };
-      int t = 0;
-      bool ok = mbar_wait(bar(C_KV), 0, ab);
-      for (int i = i_first; ok && i < p.nq64; ++i) {
-        if (!(live[i] & kLiveRow)) continue;
-        const int s = t & 1;
-        if (!(ok = mbar_wait(bar(C_QDFULL + s), (t >> 1) & 1, ab))) break;
-        if (!(ok = mbar_wait(bar(C_SDPEMPTY), (t & 1) ^ 1, ab))) break;
-        tc_fence_after();
-#pragma unroll
-        for (int kk = 0; kk < D / 16; ++kk) {
-          const uint32_t ok_ = (kk >> 2) * L::KGROUP + (kk & 3) * 32, oq = (kk >> 2) * L::QGROUP + (kk & 3) * 32;
-          mma_ss(tmem + L::TM_S, sw128_desc(sK + ok_, 16, 1024), sw128_desc(sQ(s) + oq, 16, 1024), ID_S, kk > 0);
-        }
-#pragma unroll
-        for (int kk = 0; kk < D / 16; ++kk) {
-          const uint32_t ok_ = (kk >> 2) * L::KGROUP + (kk & 3) * 32, oq = (kk >> 2) * L::QGROUP + (kk & 3) * 32;
-          mma_ss(tmem + L::TM_DP, sw128_desc(sV + ok_, 16, 1024), sw128_desc(sdO(s) + oq, 16, 1024), ID_S, kk > 0);
-        }
-        mma_commit(bar(C_SDPFULL));
-        if (t >= 1) ok = grads(t - 1);
-        ++t;
+        mma_commit(bar(C_QDEMPTY + qs));
       }
-      if (ok && t >= 1) ok = grads(t - 1);
+      __syncwarp();
+      return true;
+    };
+    int t = 0;
+    bool ok = warp_wait(bar(C_KV), 0, ab), mt;
+    LiveTiles lt(live, i_first, p.nq64);
+    for (int i; ok && (i = lt.next(&mt)) >= 0;) {
+      const int qs = t % NQS;
+      if (!(ok = warp_wait(bar(C_QDFULL + qs), (t / NQS) & 1, ab))) break;
+      if (!(ok = warp_wait(bar(C_SDPEMPTY), (t & 1) ^ 1, ab))) break;
+      tc_fence_after();
+      if (elect_one()) {
+#pragma unroll
+        for (int kk = 0; kk < D / 16; ++kk)
+          mma_ss(tmem + L::TM_S, dKk + kmaj(kk, L::KGROUP), dQk + qs * QSTEP + kmaj(kk, L::QGROUP), ID_S, kk > 0);
+#pragma unroll
+        for (int kk = 0; kk < D / 16; ++kk)
+          mma_ss(tmem + L::TM_DP, dVk + kmaj(kk, L::KGROUP), dOk + qs * QSTEP + kmaj(kk, L::QGROUP), ID_S, kk > 0);
+        mma_commit(bar(C_SDPFULL));
+      }
+      __syncwarp();
+      if (t >= 1) ok = grads(t - 1);
+      ++t;
+    }
+    if (ok && t >= 1) ok = grads(t - 1);
+    if (elect_one()) {  // the same lane as every issue above: a commit tracks its own thread's MMAs
       *dkv_written = (ok && t >= 1) ? 1 : 0;
       mbar_arrive(bar(C_FLAG));
       mma_commit(bar(C_DKV));
       drain_wait(bar(C_DKV), 0);
     }
+    __syncwarp();
   } else if (warp >= 4 && warp < 12) {
     // ------------------------------------------------------------ elementwise
     const int ew = warp - 4, hh = ew >> 2, wq = warp & 3;
@@ -271,17 +332,16 @@ __global__ void __launch_bounds__(B_THREADS, 1) flash_bwd_sm100_kernel(const __g
     const int key = k0 + rl, kb = k0 + 32 * wq;  // this thread's key, the warp's first key
     const uint32_t lane_off = (uint32_t)(32 * wq) << 16;
     const float tau = __ldg(p.tau);
-    // s = S*scale - tau rounded once; relu(s) is bit-identical to the forward's h + |h|
-    // with h = S*scale/2 - tau/2 (scaling by 2 commutes with rounding)
+    // s = S*scale - tau rounded once; relu(s) is bit-identical to the forward's u
     const float2 sc2 = make_float2(p.scale, p.scale), nt2 = make_float2(-tau, -tau);
     const int lim = key < p.N ? (p.causal ? key : 0) : 0x7fffffff;  // first valid query of this key
     float2 ds_sum = make_float2(0.f, 0.f);
     bool dead = false;
     int t = 0;
-    for (int i = i_first; i < p.nq64; ++i) {
-      const int lv = live[i];
-      if (!(lv & kLiveRow)) continue;
-      const int s = t & 1;
+    LiveTiles lt(live, i_first, p.nq64);
+    bool multi_tile;
+    for (int i; (i = lt.next(&multi_tile)) >= 0;) {
+      const int s = t & 1, qs = t % NQS;
       const int q0 = i * BM;
       if (!dead) dead = !warp_wait(bar(C_SDPFULL), t & 1, ab);
       uint32_t rs[32], rp[32];
@@ -294,13 +354,13 @@ __global__ void __launch_bounds__(B_THREADS, 1) flash_bwd_sm100_kernel(const __g
         __syncwarp();
         if (lane == 0) mbar_arrive(bar(C_SDPEMPTY));
       }
-      if (!dead) dead = !warp_wait(bar(C_QDFULL + s), (t >> 1) & 1, ab);     // coefficient records
+      if (!dead) dead = !warp_wait(bar(C_QDFULL + qs), (t / NQS) & 1, ab);     // coefficient records
       if (!dead) dead = !warp_wait(bar(C_PDSEMPTY + s), ((t >> 1) & 1) ^ 1, ab);  // P^T / dS buffers
       if (!dead) {
         tc_fence_after();
-        const uint8_t* cfb = smem + L::OFF_COEF + s * L::COEF_BYTES;
-        // this warp's 16 row pairs (two float4 each) for its 32 columns
-        const float4* cp4 = reinterpret_cast<const float4*>(cfb + L::CF_P) + 32 * hh;
+        const uint8_t* cfb = smem + L::OFF_COEF + qs * L::COEF_BYTES;
+        const float4* cp4 = reinterpret_cast<const float4*>(cfb + L::CF_P) + 16 * hh;  // this warp's 16 pairs
+        const float* tiew = reinterpret_cast<const float*>(cfb + L::CF_TIE) + 32 * hh;
         const int* argw = reinterpret_cast<const int*>(cfb + L::CF_ARG) + 32 * hh;
         const float* pcw = reinterpret_cast<const float*>(cfb + L::CF_PC) + 32 * hh;
         const int qb = q0 + 32 * hh;  // first query of this warp's 32 columns
@@ -315,8 +375,7 @@ __global__ void __launch_bounds__(B_THREADS, 1) flash_bwd_sm100_kernel(const __g
 #pragma unroll
             for (int c2 = 0; c2 < 8; ++c2) {
               const int c = half * 16 + 2 * c2;
-              const float4 P0 = cp4[2 * (8 * half + c2)];      // c1 pair, c10 pair
-              const float4 P1 = cp4[2 * (8 * half + c2) + 1];  // -D pair, tie pair
+              const float4 cf = cp4[8 * half + c2];  // c1 pair, -D pair
               float2 x = __ffma2_rn(make_float2(__uint_as_float(rs[c]), __uint_as_float(rs[c + 1])), sc2, nt2);
               if constexpr (MASK) {
                 const int q = qb + c;
@@ -325,13 +384,13 @@ __global__ void __launch_bounds__(B_THREADS, 1) flash_bwd_sm100_kernel(const __g
               }
               const float2 u = make_float2(fmaxf(x.x, 0.f), fmaxf(x.y, 0.f));
               const float2 u2 = __fmul2_rn(u, u), u4 = __fmul2_rn(u2, u2), u8 = __fmul2_rn(u4, u4);
-              const float2 w = __fmul2_rn(__fmul2_rn(u8, u2), make_float2(P0.x, P0.y));
-              const float2 g = __fmul2_rn(__fmul2_rn(u8, u), make_float2(P0.z, P0.w));
+              const float2 g = __fmul2_rn(__fmul2_rn(u8, u), make_float2(cf.x, cf.y));  // c1 u^9
+              const float2 w = __fmul2_rn(g, u);                                        // c1 u^10
               const float2 dp = make_float2(__uint_as_float(rp[c]), __uint_as_float(rp[c + 1]));
-              float2 ds = __fmul2_rn(g, __fadd2_rn(dp, make_float2(P1.x, P1.y)));
+              float2 ds = __fmul2_rn(g, __fadd2_rn(dp, make_float2(cf.z, cf.w)));
               if constexpr (MULTI) {
-                if (u.x > 0.f && (key == argw[c] || u.x == pcw[c])) ds.x += P1.z;
-                if (u.y > 0.f && (key == argw[c + 1] || u.y == pcw[c + 1])) ds.y += P1.w;
+                if (u.x > 0.f && (key == argw[c] || u.x == pcw[c])) ds.x += tiew[c];
+                if (u.y > 0.f && (key == argw[c + 1] || u.y == pcw[c + 1])) ds.y += tiew[c + 1];
               }
               ds_sum = __fadd2_rn(ds_sum, ds);
               pw_pk[c2] = pack_bf16x2(w.x, w.y);
@@ -349,7 +408,7 @@ __global__ void __launch_bounds__(B_THREADS, 1) flash_bwd_sm100_kernel(const __g
         using T_ = std::true_type;
         using F_ = std::false_type;
         const bool edge = (p.causal && qb < kb + 31) || qb + 32 > p.N || kb + 32 > p.N;
-        if (lv & kMultiTie) {
+        if (multi_tile) {
           slice(T_{}, T_{});
         } else {
           if (edge) slice(T_{}, F_{});
@@ -360,7 +419,7 @@ __global__ void __launch_bounds__(B_THREADS, 1) flash_bwd_sm100_kernel(const __g
           const int col = 32 * hh + lane;
           const int l = argw[lane] - kb;
           if ((unsigned)l < 32u) {
-            const float tie = reinterpret_cast<const float*>(cp4)[(lane >> 1) * 8 + 6 + (lane & 1)];
+            const float tie = tiew[lane];
             const int r = 32 * wq + l;
             const uint32_t addr = sdS(s) + r * 128 + ((((uint32_t)col >> 3) ^ (r & 7)) << 4) + (col & 7) * 2;
             unsigned short hv;
@@ -383,11 +442,13 @@ __global__ void __launch_bounds__(B_THREADS, 1) flash_bwd_sm100_kernel(const __g
     const bool ok = warp_wait(bar(C_DKV), 0, ab) && warp_wait(bar(C_FLAG), 0, ab);
     tc_fence_after();
     const bool have = ok && *dkv_written != 0;
+    const float dk_scale = 10.f * p.scale;  // dS' -> dS
 #pragma unroll
     for (int m = 0; m < 2; ++m) {
       __nv_bfloat16* G = static_cast<__nv_bfloat16*>(m == 0 ? p.dv : p.dk);
       const int64_t* sg = m == 0 ? p.sdv : p.sdk;
       const uint32_t tcol = m == 0 ? L::TM_DV : L::TM_DK;
+      const float f = m == 0 ? 1.f : dk_scale;
       __nv_bfloat16* row = G + (int64_t)b * sg[0] + (int64_t)hd * sg[1] + (int64_t)key * sg[2];
 #pragma unroll
       for (int cb = 0; cb < D / 2; cb += 32) {
@@ -405,20 +466,21 @@ __global__ void __launch_bounds__(B_THREADS, 1) flash_bwd_sm100_kernel(const __g
 #pragma unroll
             for (int v = 0; v < 4; ++v) {
               uint4 w;
-              w.x = pack_bf16x2(__uint_as_float(r[8 * v + 0]), __uint_as_float(r[8 * v + 1]));
-              w.y = pack_bf16x2(__uint_as_float(r[8 * v + 2]), __uint_as_float(r[8 * v + 3]));
-              w.z = pack_bf16x2(__uint_as_float(r[8 * v + 4]), __uint_as_float(r[8 * v + 5]));
-              w.w = pack_bf16x2(__uint_as_float(r[8 * v + 6]), __uint_as_float(r[8 * v + 7]));
+              w.x = pack_bf16x2(f * __uint_as_float(r[8 * v + 0]), f * __uint_as_float(r[8 * v + 1]));
+              w.y = pack_bf16x2(f * __uint_as_float(r[8 * v + 2]), f * __uint_as_float(r[8 * v + 3]));
+              w.z = pack_bf16x2(f * __uint_as_float(r[8 * v + 4]), f * __uint_as_float(r[8 * v + 5]));
+              w.w = pack_bf16x2(f * __uint_as_float(r[8 * v + 6]), f * __uint_as_float(r[8 * v + 7]));
               *reinterpret_cast<uint4*>(row + d0 + 8 * v) = w;
             }
           } else {
 #pragma unroll
-            for (int e = 0; e < 32; ++e) row[(int64_t)(d0 + e) * sg[3]] = __float2bfloat16_rn(__uint_as_float(r[e]));
+            for (int e = 0; e < 32; ++e)
+              row[(int64_t)(d0 + e) * sg[3]] = __float2bfloat16_rn(f * __uint_as_float(r[e]));
           }
         }
       }
     }
-    // ---- tau gradient partial of this CTA (fixed reduction order)
+    // ---- tau gradient partial of this CTA (fixed reduction order): -sum dS / scale = -10 sum dS'
     float v = ds_sum.x + ds_sum.y;
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
@@ -429,7 +491,7 @@ __global__ void __launch_bounds__(B_THREADS, 1) flash_bwd_sm100_kernel(const __g
       float tot = 0.f;
 #pragma unroll
       for (int w = 0; w < 8; ++w) tot += red[w];
-      p.dtau_part[(int64_t)bh * p.nkt + kt] = -tot / p.scale;
+      p.dtau_part[(int64_t)bh * p.nkt + kt] = -10.f * tot;
     }
   } else if (warp >= 12) {
     // ------------------------------------------------------------ dQ drain
@@ -438,8 +500,9 @@ __global__ void __launch_bounds__(B_THREADS, 1) flash_bwd_sm100_kernel(const __g
     const bool leader = warp == 12 && lane == 0;
     bool dead = false;
     int t = 0;
-    for (int i = i_first; i < p.nq64; ++i) {
-      if (!(live[i] & kLiveRow)) continue;
+    LiveTiles lt(live, i_first, p.nq64);
+    bool mt;
+    for (int i; (i = lt.next(&mt)) >= 0;) {
       const int bq = t % L::NDQ, sg = t % L::NSTG;
       const int q0 = i * BM;
       if (!dead) dead = !warp_wait(bar(C_DQFULL + bq), (t / L::NDQ) & 1, ab);
@@ -496,6 +559,7 @@ int flash_bwd_sm100(const FlashArgs& a0, cudaStream_t st) {
   FlashArgs a = a0;
   const int nkt = (int)((a.N + BN - 1) / BN);
   a.n_dtau_part = a.B * a.H * nkt;
+  a.dq_scale = 10.f * a.scale;  // the kernel accumulates dS' = dS / (10 scale) into dQ
   int rc = flash_bwd_prep(a, st);
   if (rc) return rc;
   BwdParams p;
@@ -506,6 +570,7 @@ int flash_bwd_sm100(const FlashArgs& a0, cudaStream_t st) {
   if (!rc) rc = tma_map_bhnd(&p.tdo, a.dout, a.sdo, a.B, a.H, a.N, a.D, BM);
   if (rc) return rc;
   p.coefP = a.coefP;
+  p.tiev = a.tiev;
   p.argv = a.argv;
   p.pcmpv = a.pcmpv;
   p.npad = rec_rows(a.N);

@@ -72,14 +72,27 @@ __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, const A
   }
 }
 
-// Warp-uniform bounded wait: lane 0 polls, the outcome is broadcast, so a warp
-// never splits between lanes that waited and lanes that gave up.
+// Warp-uniform bounded wait: every lane polls and each decision is a warp vote,
+// so the warp never diverges (a lane-0 poll with the other lanes parked at a
+// shuffle costs hundreds of cycles of reconvergence after the phase lands).
 __device__ __forceinline__ bool warp_wait(uint32_t bar, uint32_t parity, const Abort& ab) {
-  int ok = 0;
-  if ((threadIdx.x & 31) == 0) ok = mbar_wait(bar, parity, ab) ? 1 : 0;
-  ok = __shfl_sync(0xffffffffu, ok, 0);
-  __syncwarp();
-  return ok != 0;
+  constexpr uint32_t kAll = 0xffffffffu;
+  if (__any_sync(kAll, mbar_try_wait(bar, parity))) return true;
+  const uint64_t t0 = globaltimer();
+  while (true) {
+#pragma unroll 1
+    for (int i = 0; i < 8; ++i)
+      if (__any_sync(kAll, mbar_try_wait(bar, parity))) return true;
+    if (__any_sync(kAll, *ab.flag != 0)) return false;
+    if (__any_sync(kAll, globaltimer() - t0 > kWaitTimeoutNs)) {
+      if ((threadIdx.x & 31) == 0) {
+        *ab.flag = 1;
+        if (ab.status) atomicExch(ab.status, PNFT_DEV_WAIT_TIMEOUT);
+      }
+      __syncwarp();
+      return false;
+    }
+  }
 }
 
 // Wait that ignores the abort flag: used at teardown to let this CTA's own
@@ -113,6 +126,18 @@ __device__ __forceinline__ void bulk_wait_all() { asm volatile("cp.async.bulk.wa
 // Order this thread's generic shared-memory writes before later async-proxy reads.
 __device__ __forceinline__ void fence_proxy_async_smem() {
   asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
+// One lane of a converged warp (the lowest active lane, so the same lane on
+// every call with all 32 active): the issuer of tcgen05 MMAs and their commits.
+__device__ __forceinline__ bool elect_one() {
+  uint32_t pred;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t.reg .b32 r;\n\t"
+      "elect.sync r|p, 0xffffffff;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(pred));
+  return pred != 0;
 }
 
 // ---------------------------------------------------------------- named barriers
