@@ -208,7 +208,7 @@ __global__ void __launch_bounds__(F_THREADS, 1) flash_fwd_sm100_kernel(const __g
 #pragma unroll
         for (int kk = 0; kk < D / 16; ++kk) {
           const uint32_t off = (kk >> 2) * L::GROUP + (kk & 3) * 32;
-          mma_ss(tmem + TM_S + 128u * s, sw128_desc(sQ + off, 16, 1024), sw128_desc(sK(s) + off, 16, 1024), ID_S,
+          mma_ss(tmem + TM_S + 128u * s, sw128_desc(sQ + off, 16), sw128_desc(sK(s) + off, 16), ID_S,
                  kk > 0);
         }
         mma_commit(bar(B_SFULL + s));
@@ -227,7 +227,7 @@ __global__ void __launch_bounds__(F_THREADS, 1) flash_fwd_sm100_kernel(const __g
           for (int kq = 0; kq < 4; ++kq) {
             const int kk = hh * 4 + kq;  // 16 keys per MMA
             const uint32_t a_hi = tmem + TM_S + 128u * s + 64u * hh + 8u * kq;
-            const uint64_t bdesc = sw128_desc(sV(s) + kk * 2048, L::GROUP, 1024);
+            const uint32_t bdesc = sw128_desc(sV(s) + kk * 2048, L::GROUP);
             mma_ts(tmem + TM_O, a_hi, bdesc, ID_O, o_acc);  // O += P_hi V
             mma_ts(tmem + TM_O, a_hi + 32u, bdesc, ID_O, 1u);  // O += P_lo V
             o_acc = 1;
@@ -273,9 +273,8 @@ __global__ void __launch_bounds__(F_THREADS, 1) flash_fwd_sm100_kernel(const __g
       uint32_t r0[32], r1[32];
       if (!dead) {
         tc_fence_after();
-        tmem_ld32(tmem + lane_off + TM_S + 128u * s + 64u * hh, r0);
-        tmem_ld32(tmem + lane_off + TM_S + 128u * s + 64u * hh + 32u, r1);
-        tmem_wait_ld();
+        tmem_load32x2(tmem + lane_off + TM_S + 128u * s + 64u * hh, r0, tmem + lane_off + TM_S + 128u * s + 64u * hh + 32u,
+                      r1);
       }
       float x[64];
 #pragma unroll
@@ -388,8 +387,7 @@ __global__ void __launch_bounds__(F_THREADS, 1) flash_fwd_sm100_kernel(const __g
       const int d0 = hh * (D / 2) + cb;
       uint32_t r[32];
       if (o_written) {
-        tmem_ld32(tmem + lane_off + TM_O + (uint32_t)d0, r);
-        tmem_wait_ld();
+        tmem_load32(tmem + lane_off + TM_O + (uint32_t)d0, r);
       }
       if (row < p.N && o_ok && p.out32) {
         float4* o32 = reinterpret_cast<float4*>(p.out32 + ((int64_t)bh * p.N + row) * D + d0);

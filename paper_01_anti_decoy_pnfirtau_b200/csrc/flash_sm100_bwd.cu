@@ -2,7 +2,7 @@
 //
 // One CTA per (128 keys, b*h), KV-parallel over the 64-query tiles at or below
 // the causal diagonal whose rows are not all silent (per-tile flags from the
-// prep kernel). 512 threads:
+// prep kernel). 768 threads:
 //   warp 0       TMA producer: K, V once; per query tile Q, dO (3 stages for
 //                D=64, 2 for D=128) and the tile's per-row coefficient records.
 //   warp 1       MMA issuer + TMEM owner (a converged warp; one elected lane
@@ -13,8 +13,8 @@
 //                  dV += P^T dO   (TS: P^T bf16 from TMEM)
 //                  dK += dS^T Q   (SS: dS^T bf16 from shared memory)
 //                  dQ^T = K^T dS^T (SS, M = head dims), into TMEM
-//   warps 4-11   elementwise, thread = TMEM lane = key; warpgroup g owns query
-//                columns [32g, 32g+32). Each thread pulls its whole S/dP slice
+//   warps 4-19   elementwise, thread = TMEM lane = key; warpgroup g owns query
+//                columns [16g, 16g+16). Each thread pulls its whole S/dP slice
 //                into registers and releases TMEM at once, then computes
 //                u = relu(S*scale - tau), W = c1 u^10 (-> P^T in TMEM) and
 //                dS' = c1 u^9 (dP - D) + [key == argmax] tie/10 (-> smem,
@@ -24,7 +24,7 @@
 //                on tiles that cross the diagonal or a sequence end; the gate
 //                term is one patched entry per row (value tests only on tiles
 //                holding a row with several maxima).
-//   warps 12-15  dQ drain: TMEM -> fp32 staging tile in smem -> one
+//   warps 20-23  dQ drain: TMEM -> fp32 staging tile in smem -> one
 //                cp.reduce.async.bulk add into the fp32 dQ accumulator.
 // Finally the elementwise warps write dK, dV (bf16) from TMEM.
 // TMEM columns: S [0,64) dP [64,128) P^T x2 [128,192) dV [192,192+D)
@@ -47,7 +47,10 @@ namespace {
 
 constexpr int BN = 128;  // keys per CTA (TMEM lanes)
 constexpr int BM = 64;   // queries per tile
-constexpr int B_THREADS = 512;
+constexpr int NEW = 4;                       // elementwise warpgroups
+constexpr int CW = BM / NEW;                 // query columns per elementwise warp
+constexpr int W_DRAIN = 4 + 4 * NEW;         // first dQ drain warp
+constexpr int B_THREADS = 32 * (W_DRAIN + 4);
 
 enum : int {
   C_KV = 0,
@@ -88,8 +91,8 @@ struct BwdLayout {
   static constexpr int OFF_TMEM = OFF_BAR + C_COUNT * 8;
   static constexpr int OFF_ABORT = OFF_TMEM + 4;
   static constexpr int OFF_DKVW = OFF_ABORT + 4;
-  static constexpr int OFF_RED = OFF_DKVW + 8;  // 8 floats
-  static constexpr int END = OFF_RED + 32;
+  static constexpr int OFF_RED = OFF_DKVW + 8;  // one float per elementwise warp
+  static constexpr int END = OFF_RED + 4 * 4 * NEW;
   static constexpr int SMEM = END + 1024;
   static constexpr uint32_t TM_S = 0, TM_DP = 64, TM_P = 128, TM_DV = 192, TM_DK = 192 + D, TM_DQ = 192 + 2 * D;
   static_assert(SMEM <= 227 * 1024, "shared memory budget");
@@ -178,13 +181,13 @@ __global__ void __launch_bounds__(B_THREADS, 1) flash_bwd_sm100_kernel(const __g
   if (threadIdx.x == 0) {
     mbar_init(bar(C_KV), 1);
     mbar_init(bar(C_SDPFULL), 1);
-    mbar_init(bar(C_SDPEMPTY), 8);
+    mbar_init(bar(C_SDPEMPTY), 4 * NEW);
     for (int i = 0; i < NQS; ++i) {
       mbar_init(bar(C_QDFULL + i), 1);
       mbar_init(bar(C_QDEMPTY + i), 1);
     }
     for (int i = 0; i < 2; ++i) {
-      mbar_init(bar(C_PDSFULL + i), 8);
+      mbar_init(bar(C_PDSFULL + i), 4 * NEW);
       mbar_init(bar(C_PDSEMPTY + i), 1);
       mbar_init(bar(C_DQFULL + i), 1);
       mbar_init(bar(C_DQEMPTY + i), 4);
@@ -258,13 +261,13 @@ __global__ void __launch_bounds__(B_THREADS, 1) flash_bwd_sm100_kernel(const __g
     // Descriptors of k-step 0; a k-step moves +32 B inside a 128-byte K-major row
     // (+2 in descriptor units, +GROUP bytes across 64-column groups) or +16 rows
     // (2048 B, +128) of an MN-major tile.
-    const uint64_t dKk = sw128_desc(sK, 16, 1024), dVk = sw128_desc(sV, 16, 1024);
-    const uint64_t dKmn = sw128_desc(sK, L::KGROUP, 1024);
-    const uint64_t dQk = sw128_desc(sQ(0), 16, 1024), dOk = sw128_desc(sdO(0), 16, 1024);
-    const uint64_t dQmn = sw128_desc(sQ(0), L::QGROUP, 1024), dOmn = sw128_desc(sdO(0), L::QGROUP, 1024);
-    const uint64_t dSk = sw128_desc(sdS(0), 16, 1024), dSmn = sw128_desc(sdS(0), L::KGROUP, 1024);
-    constexpr uint64_t QSTEP = L::QBYTES >> 4, DSSTEP = L::DS_BYTES >> 4;
-    auto kmaj = [](int kk, int group) -> uint64_t { return (uint64_t)(((kk >> 2) * group + (kk & 3) * 32) >> 4); };
+    const uint32_t dKk = sw128_desc(sK, 16), dVk = sw128_desc(sV, 16);
+    const uint32_t dKmn = sw128_desc(sK, L::KGROUP);
+    const uint32_t dQk = sw128_desc(sQ(0), 16), dOk = sw128_desc(sdO(0), 16);
+    const uint32_t dQmn = sw128_desc(sQ(0), L::QGROUP), dOmn = sw128_desc(sdO(0), L::QGROUP);
+    const uint32_t dSk = sw128_desc(sdS(0), 16), dSmn = sw128_desc(sdS(0), L::KGROUP);
+    constexpr uint32_t QSTEP = L::QBYTES >> 4, DSSTEP = L::DS_BYTES >> 4;
+    auto kmaj = [](int kk, int group) -> uint32_t { return (uint32_t)(((kk >> 2) * group + (kk & 3) * 32) >> 4); };
     uint32_t dv_acc = 0, dk_acc = 0;
     auto grads = [&](int u) -> bool {
       const int s = u & 1, qs = u % NQS;
@@ -325,7 +328,7 @@ __global__ void __launch_bounds__(B_THREADS, 1) flash_bwd_sm100_kernel(const __g
       drain_wait(bar(C_DKV), 0);
     }
     __syncwarp();
-  } else if (warp >= 4 && warp < 12) {
+  } else if (warp >= 4 && warp < W_DRAIN) {
     // ------------------------------------------------------------ elementwise
     const int ew = warp - 4, hh = ew >> 2, wq = warp & 3;
     const int rl = 32 * wq + lane;
@@ -343,81 +346,76 @@ __global__ void __launch_bounds__(B_THREADS, 1) flash_bwd_sm100_kernel(const __g
     for (int i; (i = lt.next(&multi_tile)) >= 0;) {
       const int s = t & 1, qs = t % NQS;
       const int q0 = i * BM;
-      if (!dead) dead = !warp_wait(bar(C_SDPFULL), t & 1, ab);
-      uint32_t rs[32], rp[32];
+      // S/dP of this tile, its coefficient records, and a free P^T / dS buffer
+      if (!dead)
+        dead = !warp_wait3(bar(C_SDPFULL), t & 1, bar(C_QDFULL + qs), (t / NQS) & 1, bar(C_PDSEMPTY + s),
+                           ((t >> 1) & 1) ^ 1, ab);
+      uint32_t rs[CW], rp[CW];
       if (!dead) {
         tc_fence_after();
-        tmem_ld32(tmem + lane_off + L::TM_S + 32u * hh, rs);
-        tmem_ld32(tmem + lane_off + L::TM_DP + 32u * hh, rp);
-        tmem_wait_ld();
+        tmem_load16x2(tmem + lane_off + L::TM_S + (uint32_t)(CW * hh), rs, tmem + lane_off + L::TM_DP + (uint32_t)(CW * hh),
+                      rp);
         tc_fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive(bar(C_SDPEMPTY));
-      }
-      if (!dead) dead = !warp_wait(bar(C_QDFULL + qs), (t / NQS) & 1, ab);     // coefficient records
-      if (!dead) dead = !warp_wait(bar(C_PDSEMPTY + s), ((t >> 1) & 1) ^ 1, ab);  // P^T / dS buffers
-      if (!dead) {
-        tc_fence_after();
         const uint8_t* cfb = smem + L::OFF_COEF + qs * L::COEF_BYTES;
-        const float4* cp4 = reinterpret_cast<const float4*>(cfb + L::CF_P) + 16 * hh;  // this warp's 16 pairs
-        const float* tiew = reinterpret_cast<const float*>(cfb + L::CF_TIE) + 32 * hh;
-        const int* argw = reinterpret_cast<const int*>(cfb + L::CF_ARG) + 32 * hh;
-        const float* pcw = reinterpret_cast<const float*>(cfb + L::CF_PC) + 32 * hh;
-        const int qb = q0 + 32 * hh;  // first query of this warp's 32 columns
-        // One 32-column slice. MASK: zero u past the diagonal / the sequence ends.
-        // MULTI: per-element gate-gradient test (value ties); otherwise the single
-        // argmax entry of each row is patched in afterwards.
+        const float4* cp4 = reinterpret_cast<const float4*>(cfb + L::CF_P) + (CW / 2) * hh;  // this warp's pairs
+        const float* tiew = reinterpret_cast<const float*>(cfb + L::CF_TIE) + CW * hh;
+        const int* argw = reinterpret_cast<const int*>(cfb + L::CF_ARG) + CW * hh;
+        const float* pcw = reinterpret_cast<const float*>(cfb + L::CF_PC) + CW * hh;
+        const int qb = q0 + CW * hh;  // first query of this warp's columns
+        // This warp's CW columns. MASK: zero u past the diagonal / the sequence
+        // ends. MULTI: per-element gate-gradient test (value ties); otherwise the
+        // single argmax entry of each row is patched in afterwards.
         auto slice = [&](auto mask_c, auto multi_c) {
           constexpr bool MASK = decltype(mask_c)::value, MULTI = decltype(multi_c)::value;
+          uint32_t pw_pk[CW / 2], ds_pk[CW / 2];
 #pragma unroll
-          for (int half = 0; half < 2; ++half) {
-            uint32_t pw_pk[8], ds_pk[8];
-#pragma unroll
-            for (int c2 = 0; c2 < 8; ++c2) {
-              const int c = half * 16 + 2 * c2;
-              const float4 cf = cp4[8 * half + c2];  // c1 pair, -D pair
-              float2 x = __ffma2_rn(make_float2(__uint_as_float(rs[c]), __uint_as_float(rs[c + 1])), sc2, nt2);
-              if constexpr (MASK) {
-                const int q = qb + c;
-                if (!(q >= lim && q < p.N)) x.x = -1.f;
-                if (!(q + 1 >= lim && q + 1 < p.N)) x.y = -1.f;
-              }
-              const float2 u = make_float2(fmaxf(x.x, 0.f), fmaxf(x.y, 0.f));
-              const float2 u2 = __fmul2_rn(u, u), u4 = __fmul2_rn(u2, u2), u8 = __fmul2_rn(u4, u4);
-              const float2 g = __fmul2_rn(__fmul2_rn(u8, u), make_float2(cf.x, cf.y));  // c1 u^9
-              const float2 w = __fmul2_rn(g, u);                                        // c1 u^10
-              const float2 dp = make_float2(__uint_as_float(rp[c]), __uint_as_float(rp[c + 1]));
-              float2 ds = __fmul2_rn(g, __fadd2_rn(dp, make_float2(cf.z, cf.w)));
-              if constexpr (MULTI) {
-                if (u.x > 0.f && (key == argw[c] || u.x == pcw[c])) ds.x += tiew[c];
-                if (u.y > 0.f && (key == argw[c + 1] || u.y == pcw[c + 1])) ds.y += tiew[c + 1];
-              }
-              ds_sum = __fadd2_rn(ds_sum, ds);
-              pw_pk[c2] = pack_bf16x2(w.x, w.y);
-              ds_pk[c2] = pack_bf16x2(ds.x, ds.y);
+          for (int c2 = 0; c2 < CW / 2; ++c2) {
+            const int c = 2 * c2;
+            const float4 cf = cp4[c2];  // c1 pair, -D pair
+            float2 x = __ffma2_rn(make_float2(__uint_as_float(rs[c]), __uint_as_float(rs[c + 1])), sc2, nt2);
+            if constexpr (MASK) {
+              const int q = qb + c;
+              if (!(q >= lim && q < p.N)) x.x = -1.f;
+              if (!(q + 1 >= lim && q + 1 < p.N)) x.y = -1.f;
             }
-            tmem_st8(tmem + lane_off + L::TM_P + 32u * s + 16u * hh + 8u * half, pw_pk);
-#pragma unroll
-            for (int cc = 0; cc < 2; ++cc) {
-              const uint32_t chunk = 4 * hh + 2 * half + cc;  // 16-byte chunk of the 128-byte key row
-              st_shared_v4(sdS(s) + rl * 128 + ((chunk ^ (rl & 7)) << 4), ds_pk[4 * cc], ds_pk[4 * cc + 1],
-                           ds_pk[4 * cc + 2], ds_pk[4 * cc + 3]);
+            const float2 u = make_float2(fmaxf(x.x, 0.f), fmaxf(x.y, 0.f));
+            const float2 u2 = __fmul2_rn(u, u), u4 = __fmul2_rn(u2, u2), u8 = __fmul2_rn(u4, u4);
+            const float2 g = __fmul2_rn(__fmul2_rn(u8, u), make_float2(cf.x, cf.y));  // c1 u^9
+            const float2 w = __fmul2_rn(g, u);                                        // c1 u^10
+            const float2 dp = make_float2(__uint_as_float(rp[c]), __uint_as_float(rp[c + 1]));
+            float2 ds = __fmul2_rn(g, __fadd2_rn(dp, make_float2(cf.z, cf.w)));
+            if constexpr (MULTI) {
+              if (u.x > 0.f && (key == argw[c] || u.x == pcw[c])) ds.x += tiew[c];
+              if (u.y > 0.f && (key == argw[c + 1] || u.y == pcw[c + 1])) ds.y += tiew[c + 1];
             }
+            ds_sum = __fadd2_rn(ds_sum, ds);
+            pw_pk[c2] = pack_bf16x2(w.x, w.y);
+            ds_pk[c2] = pack_bf16x2(ds.x, ds.y);
+          }
+          tmem_st8(tmem + lane_off + L::TM_P + 32u * s + (uint32_t)((CW / 2) * hh), pw_pk);
+#pragma unroll
+          for (int cc = 0; cc < CW / 8; ++cc) {
+            const uint32_t chunk = (CW / 8) * hh + cc;  // 16-byte chunk of the 128-byte key row
+            st_shared_v4(sdS(s) + rl * 128 + ((chunk ^ (rl & 7)) << 4), ds_pk[4 * cc], ds_pk[4 * cc + 1],
+                         ds_pk[4 * cc + 2], ds_pk[4 * cc + 3]);
           }
         };
+        static_assert(CW == 16, "one tmem_st8 of packed P^T and two 16-byte dS chunks per warp");
         using T_ = std::true_type;
         using F_ = std::false_type;
-        const bool edge = (p.causal && qb < kb + 31) || qb + 32 > p.N || kb + 32 > p.N;
+        const bool edge = (p.causal && qb < kb + 31) || qb + CW > p.N || kb + 32 > p.N;
         if (multi_tile) {
           slice(T_{}, T_{});
         } else {
           if (edge) slice(T_{}, F_{});
           else slice(F_{}, F_{});
           // Gate gradient of the rows whose argmax key is one of this warp's keys:
-          // lane c patches column c's entry (key row arg - k0) of the bf16 dS tile.
+          // lane c < CW patches column c's entry (key row arg - k0) of the bf16 dS tile.
           __syncwarp();
-          const int col = 32 * hh + lane;
-          const int l = argw[lane] - kb;
+          const int col = CW * hh + lane;
+          const int l = lane < CW ? argw[lane] - kb : -1;
           if ((unsigned)l < 32u) {
             const float tie = tiew[lane];
             const int r = 32 * wq + l;
@@ -438,7 +436,7 @@ __global__ void __launch_bounds__(B_THREADS, 1) flash_bwd_sm100_kernel(const __g
       if (lane == 0) mbar_arrive(bar(C_PDSFULL + s));
       ++t;
     }
-    // ---- dK, dV: rows of this CTA's keys, warpgroup g writes head dims [g*D/2, (g+1)*D/2)
+    // ---- dK, dV: rows of this CTA's keys, warpgroup g writes head dims [g*D/NEW, (g+1)*D/NEW)
     const bool ok = warp_wait(bar(C_DKV), 0, ab) && warp_wait(bar(C_FLAG), 0, ab);
     tc_fence_after();
     const bool have = ok && *dkv_written != 0;
@@ -451,20 +449,19 @@ __global__ void __launch_bounds__(B_THREADS, 1) flash_bwd_sm100_kernel(const __g
       const float f = m == 0 ? 1.f : dk_scale;
       __nv_bfloat16* row = G + (int64_t)b * sg[0] + (int64_t)hd * sg[1] + (int64_t)key * sg[2];
 #pragma unroll
-      for (int cb = 0; cb < D / 2; cb += 32) {
-        const int d0 = hh * (D / 2) + cb;
-        uint32_t r[32];
+      for (int cb = 0; cb < D / NEW; cb += 16) {
+        const int d0 = hh * (D / NEW) + cb;
+        uint32_t r[16];
         if (have) {
-          tmem_ld32(tmem + lane_off + tcol + (uint32_t)d0, r);
-          tmem_wait_ld();
+          tmem_load16(tmem + lane_off + tcol + (uint32_t)d0, r);
         } else {
 #pragma unroll
-          for (int e = 0; e < 32; ++e) r[e] = 0u;
+          for (int e = 0; e < 16; ++e) r[e] = 0u;
         }
         if (key < p.N && ok) {
           if (sg[3] == 1 && (reinterpret_cast<uintptr_t>(row + d0) & 15) == 0) {
 #pragma unroll
-            for (int v = 0; v < 4; ++v) {
+            for (int v = 0; v < 2; ++v) {
               uint4 w;
               w.x = pack_bf16x2(f * __uint_as_float(r[8 * v + 0]), f * __uint_as_float(r[8 * v + 1]));
               w.y = pack_bf16x2(f * __uint_as_float(r[8 * v + 2]), f * __uint_as_float(r[8 * v + 3]));
@@ -474,7 +471,7 @@ __global__ void __launch_bounds__(B_THREADS, 1) flash_bwd_sm100_kernel(const __g
             }
           } else {
 #pragma unroll
-            for (int e = 0; e < 32; ++e)
+            for (int e = 0; e < 16; ++e)
               row[(int64_t)(d0 + e) * sg[3]] = __float2bfloat16_rn(f * __uint_as_float(r[e]));
           }
         }
@@ -486,18 +483,18 @@ __global__ void __launch_bounds__(B_THREADS, 1) flash_bwd_sm100_kernel(const __g
     for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
     float* red = reinterpret_cast<float*>(smem + L::OFF_RED);
     if (lane == 0) red[ew] = v;
-    named_bar_sync(3, 256);
+    named_bar_sync(3, 128 * NEW);
     if (ew == 0 && lane == 0) {
       float tot = 0.f;
 #pragma unroll
-      for (int w = 0; w < 8; ++w) tot += red[w];
+      for (int w = 0; w < 4 * NEW; ++w) tot += red[w];
       p.dtau_part[(int64_t)bh * p.nkt + kt] = -10.f * tot;
     }
-  } else if (warp >= 12) {
+  } else if (warp >= W_DRAIN) {
     // ------------------------------------------------------------ dQ drain
     const int wq = warp & 3;
     const uint32_t lane_off = (uint32_t)(32 * wq) << 16;
-    const bool leader = warp == 12 && lane == 0;
+    const bool leader = warp == W_DRAIN && lane == 0;
     bool dead = false;
     int t = 0;
     LiveTiles lt(live, i_first, p.nq64);
@@ -506,16 +503,6 @@ __global__ void __launch_bounds__(B_THREADS, 1) flash_bwd_sm100_kernel(const __g
       const int bq = t % L::NDQ, sg = t % L::NSTG;
       const int q0 = i * BM;
       if (!dead) dead = !warp_wait(bar(C_DQFULL + bq), (t / L::NDQ) & 1, ab);
-      uint32_t r0[32], r1[32];
-      if (!dead) {
-        tc_fence_after();
-        tmem_ld32(tmem + lane_off + L::TM_DQ + 64u * bq, r0);
-        tmem_ld32(tmem + lane_off + L::TM_DQ + 64u * bq + 32u, r1);
-        tmem_wait_ld();
-        tc_fence_before();
-        __syncwarp();
-        if (lane == 0) mbar_arrive(bar(C_DQEMPTY + bq));
-      }
       if (leader) bulk_wait_read<L::NSTG - 1>();  // the staging tile's previous reduce has read it
       named_bar_sync(4, 128);
       float* stg = reinterpret_cast<float*>(smem + L::OFF_STG + sg * L::STG_BYTES);  // [64 q][D] fp32
@@ -523,11 +510,21 @@ __global__ void __launch_bounds__(B_THREADS, 1) flash_bwd_sm100_kernel(const __g
       // lane d. D=64 (M=64 layout): head dim 16*wq + l in lane l < 16 of quadrant wq.
       const bool holds = D == 128 || lane < 16;
       const int d = D == 128 ? 32 * wq + lane : 16 * wq + lane;
-      if (holds) {
+      if (!dead) tc_fence_after();
 #pragma unroll
-        for (int q = 0; q < 32; ++q) {
-          stg[q * D + d] = __uint_as_float(r0[q]);
-          stg[(q + 32) * D + d] = __uint_as_float(r1[q]);
+      for (int h2 = 0; h2 < 2; ++h2) {  // 32 query columns at a time
+        uint32_t r[32];
+        if (!dead) {
+          tmem_load32(tmem + lane_off + L::TM_DQ + 64u * bq + 32u * h2, r);
+        }
+        if (h2 == 1 && !dead) {
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(bar(C_DQEMPTY + bq));
+        }
+        if (holds && !dead) {
+#pragma unroll
+          for (int q = 0; q < 32; ++q) stg[(32 * h2 + q) * D + d] = __uint_as_float(r[q]);
         }
       }
       fence_proxy_async_smem();

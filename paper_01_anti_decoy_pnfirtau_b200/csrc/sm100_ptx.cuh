@@ -95,6 +95,29 @@ __device__ __forceinline__ bool warp_wait(uint32_t bar, uint32_t parity, const A
   }
 }
 
+// warp_wait on three phases at once (one poll and one vote per round).
+__device__ __forceinline__ bool warp_wait3(uint32_t b0, uint32_t p0, uint32_t b1, uint32_t p1, uint32_t b2,
+                                           uint32_t p2, const Abort& ab) {
+  constexpr uint32_t kAll = 0xffffffffu;
+  auto all3 = [&]() { return mbar_try_wait(b0, p0) && mbar_try_wait(b1, p1) && mbar_try_wait(b2, p2); };
+  if (__any_sync(kAll, all3())) return true;
+  const uint64_t t0 = globaltimer();
+  while (true) {
+#pragma unroll 1
+    for (int i = 0; i < 8; ++i)
+      if (__any_sync(kAll, all3())) return true;
+    if (__any_sync(kAll, *ab.flag != 0)) return false;
+    if (__any_sync(kAll, globaltimer() - t0 > kWaitTimeoutNs)) {
+      if ((threadIdx.x & 31) == 0) {
+        *ab.flag = 1;
+        if (ab.status) atomicExch(ab.status, PNFT_DEV_WAIT_TIMEOUT);
+      }
+      __syncwarp();
+      return false;
+    }
+  }
+}
+
 // Wait that ignores the abort flag: used at teardown to let this CTA's own
 // copies / MMAs land before its shared memory and TMEM are released.
 __device__ __forceinline__ void drain_wait(uint32_t bar, uint32_t parity) {
@@ -171,24 +194,35 @@ __device__ __forceinline__ void tmem_dealloc(uint32_t taddr, uint32_t ncols) {
 __device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
 __device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
 
+// Shared-memory matrix descriptors are passed as their low 32 bits (start
+// address >> 4, leading-byte offset >> 4) and assembled with the constant high
+// word inside the asm: every tile here is 128-byte swizzled with 1024-byte
+// 8-row groups, and a 64-bit descriptor operand was seen to reach the tensor
+// core without its high word in a register-tight build (MN-major B operands then
+// read as unswizzled, repeating every 8 columns).
+constexpr uint32_t kSw128DescHi = (1024u >> 4) | (1u << 14) | (2u << 29);  // SBO 1024, version 1, SWIZZLE_128B
+
 // D[tmem] (+)= A[smem desc] * B[smem desc]
-__device__ __forceinline__ void mma_ss(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc,
+__device__ __forceinline__ void mma_ss(uint32_t d_tmem, uint32_t a_lo, uint32_t b_lo, uint32_t idesc,
                                        uint32_t accumulate) {
   asm volatile(
-      "{\n\t.reg .pred p;\n\t"
+      "{\n\t.reg .pred p;\n\t.reg .b64 da, db;\n\t"
       "setp.ne.b32 p, %4, 0;\n\t"
-      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
-      "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
+      "mov.b64 da, {%1, %5};\n\t"
+      "mov.b64 db, {%2, %5};\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], da, db, %3, p;\n\t}" ::"r"(d_tmem),
+      "r"(a_lo), "r"(b_lo), "r"(idesc), "r"(accumulate), "r"(kSw128DescHi)
       : "memory");
 }
 // D[tmem] (+)= A[tmem] * B[smem desc]
-__device__ __forceinline__ void mma_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc, uint32_t idesc,
+__device__ __forceinline__ void mma_ts(uint32_t d_tmem, uint32_t a_tmem, uint32_t b_lo, uint32_t idesc,
                                        uint32_t accumulate) {
   asm volatile(
-      "{\n\t.reg .pred p;\n\t"
+      "{\n\t.reg .pred p;\n\t.reg .b64 db;\n\t"
       "setp.ne.b32 p, %4, 0;\n\t"
-      "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d_tmem),
-      "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accumulate)
+      "mov.b64 db, {%2, %5};\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], db, %3, p;\n\t}" ::"r"(d_tmem),
+      "r"(a_tmem), "r"(b_lo), "r"(idesc), "r"(accumulate), "r"(kSw128DescHi)
       : "memory");
 }
 // Arrive on `bar` once every tcgen05 op issued so far by this thread completes.
@@ -199,13 +233,51 @@ __device__ __forceinline__ void mma_commit(uint32_t bar) {
 #define PNFT_R8(i) "=r"(r[i + 0]), "=r"(r[i + 1]), "=r"(r[i + 2]), "=r"(r[i + 3]), "=r"(r[i + 4]), "=r"(r[i + 5]), "=r"(r[i + 6]), "=r"(r[i + 7])
 #define PNFT_W8(i) "r"(r[i + 0]), "r"(r[i + 1]), "r"(r[i + 2]), "r"(r[i + 3]), "r"(r[i + 4]), "r"(r[i + 5]), "r"(r[i + 6]), "r"(r[i + 7])
 
+// TMEM loads. Each helper issues its tcgen05.ld and the tcgen05.wait::ld in ONE
+// asm statement: the loaded registers are undefined until the wait, and with two
+// statements the compiler may schedule their consumers in between.
+#define PNFT_LD32 "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
+#define PNFT_LD16 "tcgen05.ld.sync.aligned.32x32b.x16.b32 "
+#define PNFT_WAIT_LD "tcgen05.wait::ld.sync.aligned;"
+
 // 32 lanes x 32 consecutive 32-bit columns -> r[0..31] of each thread (lane = row)
-__device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
-  asm volatile(
-      "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
-      "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
-      : PNFT_R8(0), PNFT_R8(8), PNFT_R8(16), PNFT_R8(24)
-      : "r"(taddr));
+__device__ __forceinline__ void tmem_load32(uint32_t taddr, uint32_t (&r)[32]) {
+  asm volatile(PNFT_LD32
+               "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
+               "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];\n\t" PNFT_WAIT_LD
+               : PNFT_R8(0), PNFT_R8(8), PNFT_R8(16), PNFT_R8(24)
+               : "r"(taddr)
+               : "memory");
+}
+// 32 lanes x 16 consecutive 32-bit columns -> r[0..15]
+__device__ __forceinline__ void tmem_load16(uint32_t taddr, uint32_t (&r)[16]) {
+  asm volatile(PNFT_LD16 "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];\n\t" PNFT_WAIT_LD
+               : PNFT_R8(0), PNFT_R8(8)
+               : "r"(taddr)
+               : "memory");
+}
+// two 16-column loads, one wait
+__device__ __forceinline__ void tmem_load16x2(uint32_t ta, uint32_t (&r)[16], uint32_t tb, uint32_t (&q)[16]) {
+  asm volatile(PNFT_LD16 "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%32];\n\t" PNFT_LD16
+                         "{%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%33];\n\t" PNFT_WAIT_LD
+               : PNFT_R8(0), PNFT_R8(8), "=r"(q[0]), "=r"(q[1]), "=r"(q[2]), "=r"(q[3]), "=r"(q[4]), "=r"(q[5]),
+                 "=r"(q[6]), "=r"(q[7]), "=r"(q[8]), "=r"(q[9]), "=r"(q[10]), "=r"(q[11]), "=r"(q[12]), "=r"(q[13]),
+                 "=r"(q[14]), "=r"(q[15])
+               : "r"(ta), "r"(tb)
+               : "memory");
+}
+// two 32-column loads, one wait
+__device__ __forceinline__ void tmem_load32x2(uint32_t ta, uint32_t (&r)[32], uint32_t tb, uint32_t (&q)[32]) {
+#define PNFT_Q8(i) "=r"(q[i + 0]), "=r"(q[i + 1]), "=r"(q[i + 2]), "=r"(q[i + 3]), "=r"(q[i + 4]), "=r"(q[i + 5]), "=r"(q[i + 6]), "=r"(q[i + 7])
+  asm volatile(PNFT_LD32
+               "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
+               "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%64];\n\t" PNFT_LD32
+               "{%32,%33,%34,%35,%36,%37,%38,%39,%40,%41,%42,%43,%44,%45,%46,%47,"
+               "%48,%49,%50,%51,%52,%53,%54,%55,%56,%57,%58,%59,%60,%61,%62,%63}, [%65];\n\t" PNFT_WAIT_LD
+               : PNFT_R8(0), PNFT_R8(8), PNFT_R8(16), PNFT_R8(24), PNFT_Q8(0), PNFT_Q8(8), PNFT_Q8(16), PNFT_Q8(24)
+               : "r"(ta), "r"(tb)
+               : "memory");
+#undef PNFT_Q8
 }
 __device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t (&r)[32]) {
   asm volatile(
@@ -228,18 +300,22 @@ __device__ __forceinline__ void tmem_st8(uint32_t taddr, const uint32_t (&r)[8])
                "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7])
                : "memory");
 }
-__device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
 __device__ __forceinline__ void tmem_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
 
 #undef PNFT_R8
 #undef PNFT_W8
+#undef PNFT_LD32
+#undef PNFT_LD16
+#undef PNFT_WAIT_LD
 
 // ---------------------------------------------------------------- descriptors
-// UMMA shared-memory descriptor of a 128-byte-swizzled tile (tile base 1024-aligned):
-// start>>4 [0,14), LBO>>4 [16,30), SBO>>4 [32,46), version 1 [46,48), layout SW128 = 2 [61,64).
-__device__ __forceinline__ uint64_t sw128_desc(uint32_t saddr, uint32_t lbo_bytes, uint32_t sbo_bytes) {
-  return (uint64_t)((saddr & 0x3FFFFu) >> 4) | ((uint64_t)((lbo_bytes >> 4) & 0x3FFFu) << 16) |
-         ((uint64_t)((sbo_bytes >> 4) & 0x3FFFu) << 32) | (1ull << 46) | (2ull << 61);
+// Low word of the UMMA shared-memory descriptor of a 128-byte-swizzled tile
+// (tile base 1024-aligned): start>>4 in [0,14), LBO>>4 in [16,30); the high word
+// (SBO>>4 = 64 in [32,46), version 1 at 46, layout SWIZZLE_128B = 2 in [61,64))
+// is kSw128DescHi. A k-step adds (bytes >> 4) to the low word: shared addresses
+// stay below 256 KB, so the start field never carries into LBO.
+__device__ __forceinline__ uint32_t sw128_desc(uint32_t saddr, uint32_t lbo_bytes) {
+  return ((saddr & 0x3FFFFu) >> 4) | (((lbo_bytes >> 4) & 0x3FFFu) << 16);
 }
 
 // kind::f16 instruction descriptor: f32 accumulate, A/B bf16 (fmt 1) or f16 (fmt 0),
