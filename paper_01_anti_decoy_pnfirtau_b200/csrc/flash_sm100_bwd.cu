@@ -56,15 +56,15 @@ enum : int {
   C_KV = 0,
   C_QDFULL = 1,    // [3]
   C_QDEMPTY = 4,   // [3]
-  C_SDPFULL = 7,
-  C_SDPEMPTY = 8,
-  C_PDSFULL = 9,   // [2]
-  C_PDSEMPTY = 11, // [2]
-  C_DQFULL = 13,   // [2]
-  C_DQEMPTY = 15,  // [2]
-  C_DKV = 17,
-  C_FLAG = 18,  // plain arrive after dkv_written is stored (release for the flag)
-  C_COUNT = 19
+  C_SDPFULL = 7,   // [2] (one per S/dP buffer)
+  C_SDPEMPTY = 9,  // single-buffer layout only
+  C_PDSFULL = 10,  // [2]
+  C_PDSEMPTY = 12, // [2]
+  C_DQFULL = 14,   // [2]
+  C_DQEMPTY = 16,  // [2]
+  C_DKV = 18,
+  C_FLAG = 19,  // plain arrive after dkv_written is stored (release for the flag)
+  C_COUNT = 20
 };
 
 template <int D>
@@ -94,7 +94,21 @@ struct BwdLayout {
   static constexpr int OFF_RED = OFF_DKVW + 8;  // one float per elementwise warp
   static constexpr int END = OFF_RED + 4 * 4 * NEW;
   static constexpr int SMEM = END + 1024;
-  static constexpr uint32_t TM_S = 0, TM_DP = 64, TM_P = 128, TM_DV = 192, TM_DK = 192 + D, TM_DQ = 192 + 2 * D;
+  // TMEM. D=64: two S/dP buffers [128b, 128b+128) (S at +0, dP at +64); a warp
+  // writes its packed P^T over the first 8 of its own 16 S columns once they are
+  // in registers, so buffer b is free again once dV of its tile has been issued
+  // (MMAs of one thread run in order). dV [256,320) dK [320,384) dQ^T x2 [384,512).
+  // D=128: one S/dP buffer [0,128), P^T x2 [128,192), dV [192,320), dK [320,448),
+  // dQ^T [448,512).
+  static constexpr int NSB = D == 64 ? 2 : 1;
+  static constexpr uint32_t TM_DV = NSB == 2 ? 256 : 192, TM_DK = TM_DV + D, TM_DQ = TM_DK + D;
+  static_assert(TM_DQ + 64 * NDQ <= 512, "TMEM budget");
+  __device__ static constexpr uint32_t tm_s(int b) { return 128u * (uint32_t)b; }
+  __device__ static constexpr uint32_t tm_dp(int b) { return 128u * (uint32_t)b + 64u; }
+  // packed P^T columns of queries [16k, 16k+16) of the tile in PDS buffer s
+  __device__ static constexpr uint32_t tm_p(int s, int k) {
+    return NSB == 2 ? 128u * (uint32_t)s + 16u * (uint32_t)k : 128u + 32u * (uint32_t)s + 8u * (uint32_t)k;
+  }
   static_assert(SMEM <= 227 * 1024, "shared memory budget");
 };
 
@@ -181,6 +195,7 @@ __global__ void __launch_bounds__(B_THREADS, 1) flash_bwd_sm100_kernel(const __g
   if (threadIdx.x == 0) {
     mbar_init(bar(C_KV), 1);
     mbar_init(bar(C_SDPFULL), 1);
+    mbar_init(bar(C_SDPFULL + 1), 1);
     mbar_init(bar(C_SDPEMPTY), 4 * NEW);
     for (int i = 0; i < NQS; ++i) {
       mbar_init(bar(C_QDFULL + i), 1);
@@ -268,23 +283,43 @@ __global__ void __launch_bounds__(B_THREADS, 1) flash_bwd_sm100_kernel(const __g
     const uint32_t dSk = sw128_desc(sdS(0), 16), dSmn = sw128_desc(sdS(0), L::KGROUP);
     constexpr uint32_t QSTEP = L::QBYTES >> 4, DSSTEP = L::DS_BYTES >> 4;
     auto kmaj = [](int kk, int group) -> uint32_t { return (uint32_t)(((kk >> 2) * group + (kk & 3) * 32) >> 4); };
-    uint32_t dv_acc = 0, dk_acc = 0;
-    auto grads = [&](int u) -> bool {
-      const int s = u & 1, qs = u % NQS;
-      if (!warp_wait(bar(C_PDSFULL + s), (u >> 1) & 1, ab)) return false;
+    constexpr int NSB = L::NSB;
+    auto issue_sdp = [&](int t) -> bool {
+      const int qs = t % NQS, sb = t % NSB;
+      if (!warp_wait(bar(C_QDFULL + qs), (t / NQS) & 1, ab)) return false;
+      if (NSB == 1 && !warp_wait(bar(C_SDPEMPTY), (t & 1) ^ 1, ab)) return false;
       tc_fence_after();
       if (elect_one()) {
 #pragma unroll
-        for (int kk = 0; kk < BM / 16; ++kk)
-          mma_ts(tmem + L::TM_DV, tmem + L::TM_P + 32u * s + 8u * kk, dOmn + qs * QSTEP + kk * 128, ID_G,
-                 dv_acc | (uint32_t)kk);
+        for (int kk = 0; kk < D / 16; ++kk)
+          mma_ss(tmem + L::tm_s(sb), dKk + kmaj(kk, L::KGROUP), dQk + qs * QSTEP + kmaj(kk, L::QGROUP), ID_S, kk > 0);
 #pragma unroll
-        for (int kk = 0; kk < BM / 16; ++kk)
-          mma_ss(tmem + L::TM_DK, dSk + s * DSSTEP + kk * 2, dQmn + qs * QSTEP + kk * 128, ID_G, dk_acc | (uint32_t)kk);
+        for (int kk = 0; kk < D / 16; ++kk)
+          mma_ss(tmem + L::tm_dp(sb), dVk + kmaj(kk, L::KGROUP), dOk + qs * QSTEP + kmaj(kk, L::QGROUP), ID_S, kk > 0);
+        mma_commit(bar(C_SDPFULL + sb));
       }
       __syncwarp();
-      dv_acc = dk_acc = 1;
-      const int bq = u % L::NDQ;
+      return true;
+    };
+    auto dvdk = [&](int u) -> bool {
+      const int s = u & 1, qs = u % NQS;
+      if (!warp_wait(bar(C_PDSFULL + s), (u >> 1) & 1, ab)) return false;
+      tc_fence_after();
+      const uint32_t acc0 = u > 0 ? 1u : 0u;
+      if (elect_one()) {
+#pragma unroll
+        for (int kk = 0; kk < BM / 16; ++kk)
+          mma_ts(tmem + L::TM_DV, tmem + L::tm_p(s, kk), dOmn + qs * QSTEP + kk * 128, ID_G, acc0 | (uint32_t)kk);
+#pragma unroll
+        for (int kk = 0; kk < BM / 16; ++kk)
+          mma_ss(tmem + L::TM_DK, dSk + s * DSSTEP + kk * 2, dQmn + qs * QSTEP + kk * 128, ID_G, acc0 | (uint32_t)kk);
+        mma_commit(bar(C_QDEMPTY + qs));  // Q / dO of tile u are no longer needed
+      }
+      __syncwarp();
+      return true;
+    };
+    auto dq = [&](int u) -> bool {
+      const int s = u & 1, bq = u % L::NDQ;
       if (!warp_wait(bar(C_DQEMPTY + bq), ((u / L::NDQ) & 1) ^ 1, ab)) return false;
       tc_fence_after();
       if (elect_one()) {
@@ -294,33 +329,45 @@ __global__ void __launch_bounds__(B_THREADS, 1) flash_bwd_sm100_kernel(const __g
           mma_ss(tmem + L::TM_DQ + 64u * bq, dKmn + kk * 128, dSmn + s * DSSTEP + kk * 128, ID_DQ, kk > 0);
         mma_commit(bar(C_DQFULL + bq));
         mma_commit(bar(C_PDSEMPTY + s));
-        mma_commit(bar(C_QDEMPTY + qs));
       }
       __syncwarp();
       return true;
     };
-    int t = 0;
+    int t = 0;  // tiles whose S / dP are issued
     bool ok = warp_wait(bar(C_KV), 0, ab), mt;
     LiveTiles lt(live, i_first, p.nq64);
-    for (int i; ok && (i = lt.next(&mt)) >= 0;) {
-      const int qs = t % NQS;
-      if (!(ok = warp_wait(bar(C_QDFULL + qs), (t / NQS) & 1, ab))) break;
-      if (!(ok = warp_wait(bar(C_SDPEMPTY), (t & 1) ^ 1, ab))) break;
-      tc_fence_after();
-      if (elect_one()) {
-#pragma unroll
-        for (int kk = 0; kk < D / 16; ++kk)
-          mma_ss(tmem + L::TM_S, dKk + kmaj(kk, L::KGROUP), dQk + qs * QSTEP + kmaj(kk, L::QGROUP), ID_S, kk > 0);
-#pragma unroll
-        for (int kk = 0; kk < D / 16; ++kk)
-          mma_ss(tmem + L::TM_DP, dVk + kmaj(kk, L::KGROUP), dOk + qs * QSTEP + kmaj(kk, L::QGROUP), ID_S, kk > 0);
-        mma_commit(bar(C_SDPFULL));
+    if constexpr (NSB == 2) {
+      // S/dP run two tiles ahead: per step j, dV/dK of tile j, then S/dP of tile
+      // j+2 (into tile j's buffer, behind dV(j) in the MMA pipe), then dQ of tile j.
+      int T = 0;  // live tiles known so far
+      bool more = true;
+      auto discover = [&]() { if (more && lt.next(&mt) >= 0) ++T; else more = false; };
+      discover();
+      discover();
+      for (int u = 0; ok && u < T && u < 2; ++u) {
+        ok = issue_sdp(u);
+        t = u + 1;
       }
-      __syncwarp();
-      if (t >= 1) ok = grads(t - 1);
-      ++t;
+      for (int j = 0; ok && j < T; ++j) {
+        if (!(ok = dvdk(j))) break;
+        discover();
+        if (j + 2 < T) {
+          if (!(ok = issue_sdp(j + 2))) break;
+          t = j + 3;
+        }
+        if (!(ok = dq(j))) break;
+      }
+    } else {
+      // one S/dP buffer: S/dP of tile j once every warp has read tile j-1's, then
+      // dV, dK, dQ of tile j-1
+      for (int i; ok && (i = lt.next(&mt)) >= 0;) {
+        if (!(ok = issue_sdp(t))) break;
+        if (t >= 1 && !(ok = dvdk(t - 1))) break;
+        if (t >= 1 && !(ok = dq(t - 1))) break;
+        ++t;
+      }
+      if (ok && t >= 1) ok = dvdk(t - 1) && dq(t - 1);
     }
-    if (ok && t >= 1) ok = grads(t - 1);
     if (elect_one()) {  // the same lane as every issue above: a commit tracks its own thread's MMAs
       *dkv_written = (ok && t >= 1) ? 1 : 0;
       mbar_arrive(bar(C_FLAG));
@@ -347,17 +394,20 @@ __global__ void __launch_bounds__(B_THREADS, 1) flash_bwd_sm100_kernel(const __g
       const int s = t & 1, qs = t % NQS;
       const int q0 = i * BM;
       // S/dP of this tile, its coefficient records, and a free P^T / dS buffer
+      const int sb = t % L::NSB;
       if (!dead)
-        dead = !warp_wait3(bar(C_SDPFULL), t & 1, bar(C_QDFULL + qs), (t / NQS) & 1, bar(C_PDSEMPTY + s),
-                           ((t >> 1) & 1) ^ 1, ab);
+        dead = !warp_wait3(bar(C_SDPFULL + sb), (t / L::NSB) & 1, bar(C_QDFULL + qs), (t / NQS) & 1,
+                           bar(C_PDSEMPTY + s), ((t >> 1) & 1) ^ 1, ab);
       uint32_t rs[CW], rp[CW];
       if (!dead) {
         tc_fence_after();
-        tmem_load16x2(tmem + lane_off + L::TM_S + (uint32_t)(CW * hh), rs, tmem + lane_off + L::TM_DP + (uint32_t)(CW * hh),
-                      rp);
-        tc_fence_before();
-        __syncwarp();
-        if (lane == 0) mbar_arrive(bar(C_SDPEMPTY));
+        tmem_load16x2(tmem + lane_off + L::tm_s(sb) + (uint32_t)(CW * hh), rs,
+                      tmem + lane_off + L::tm_dp(sb) + (uint32_t)(CW * hh), rp);
+        if constexpr (L::NSB == 1) {
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(bar(C_SDPEMPTY));
+        }
         const uint8_t* cfb = smem + L::OFF_COEF + qs * L::COEF_BYTES;
         const float4* cp4 = reinterpret_cast<const float4*>(cfb + L::CF_P) + (CW / 2) * hh;  // this warp's pairs
         const float* tiew = reinterpret_cast<const float*>(cfb + L::CF_TIE) + CW * hh;
@@ -394,7 +444,7 @@ __global__ void __launch_bounds__(B_THREADS, 1) flash_bwd_sm100_kernel(const __g
             pw_pk[c2] = pack_bf16x2(w.x, w.y);
             ds_pk[c2] = pack_bf16x2(ds.x, ds.y);
           }
-          tmem_st8(tmem + lane_off + L::TM_P + 32u * s + (uint32_t)((CW / 2) * hh), pw_pk);
+          tmem_st8(tmem + lane_off + L::tm_p(s, hh), pw_pk);
 #pragma unroll
           for (int cc = 0; cc < CW / 8; ++cc) {
             const uint32_t chunk = (CW / 8) * hh + cc;  // 16-byte chunk of the 128-byte key row
