@@ -168,25 +168,23 @@ __global__ void __launch_bounds__(F_THREADS, 1) flash_fwd_sm100_kernel(const __g
         k_last = j;
         return true;
       };
+      // V is fetched with its K tile, not after the silence vote: the vote still
+      // skips the PV MMAs of silent halves, but a V fetch on the critical path
+      // of every tile costs more than the L2 traffic it saves
       auto issue_v = [&](int j) -> bool {
         const int s = j & 1;
-        if (!mbar_wait(bar(B_VOTE + s), (j >> 1) & 1, ab)) return false;
-        const int l0 = live[s * 2 + 0], l1 = live[s * 2 + 1];
         if (!mbar_wait(bar(B_VEMPTY + s), ((j >> 1) & 1) ^ 1, ab)) return false;
-        mbar_arrive_expect_tx(bar(B_VFULL + s), (uint32_t)(l0 + l1) * (L::VBYTES / 2));
-        for (int hh = 0; hh < 2; ++hh) {
-          if (!(hh ? l1 : l0)) continue;
+        mbar_arrive_expect_tx(bar(B_VFULL + s), L::VBYTES);
+        for (int hh = 0; hh < 2; ++hh)
           for (int g = 0; g < DG; ++g)
             tma_load_4d(sV(s) + g * L::GROUP + hh * (L::GROUP / 2), &p.tv, bar(B_VFULL + s), 64 * g,
                         j * FN + 64 * hh, hd, b);
-        }
         v_last = j;
         return true;
       };
-      bool ok = issue_k(0);
+      bool ok = issue_k(0) && issue_v(0);
       for (int j = 0; ok && j < ntiles; ++j) {
-        if (j + 1 < ntiles) ok = issue_k(j + 1);
-        if (ok) ok = issue_v(j);
+        if (j + 1 < ntiles) ok = issue_k(j + 1) && issue_v(j + 1);
       }
       // drain: never leave a copy in flight into this CTA's shared memory
       drain_wait(bar(B_QFULL), 0);
