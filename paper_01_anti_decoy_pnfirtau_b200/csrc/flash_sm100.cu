@@ -1,17 +1,17 @@
 // sm_100a flash pn_fir_tau kernels: TMA -> shared memory, tcgen05 MMAs with
 // TMEM accumulators, warp-specialised pipelines. bf16 inputs, head dim 64/128.
 //
-// Forward, one CTA per (128 query rows, b*h), 384 threads:
+// Forward, one CTA per (128 query rows, b*h), 640 threads:
 //   warp 0      TMA producer: Q once; K tile j+1 ahead; V halves of tile j only
 //               after the elementwise warps voted them live (silent halves are
 //               never loaded).
 //   warp 1      MMA issuer and TMEM owner: S_j = Q K_j^T (SS, M=N=128) into one
 //               of two S buffers; O += P_j V_j (TS: P read from TMEM) for the live
 //               64-key halves only.
-//   warps 4-11  two elementwise warpgroups; warpgroup g owns key columns
-//               [64g, 64g+64) of every tile, thread = TMEM lane = query row:
+//   warps 4-19  four elementwise warpgroups; warpgroup g owns key columns
+//               [32g, 32g+32) of every tile, thread = TMEM lane = query row:
 //               s = S*scale - tau (packed f32x2 FMA, rounded once), u = max(s, 0),
-//               row max via 3-input max, per-half silent vote, u^10 by repeated
+//               row max via 3-input max, per-quarter silent vote, u^10 by repeated
 //               squaring (no exp), running peak / tie count / argmax / mass, and
 //               P = u^10 split into two bf16 terms P_hi + P_lo written back over
 //               the tile's own S columns in TMEM for the two PV MMAs.
@@ -39,7 +39,9 @@ namespace {
 
 constexpr int FM = 128;  // query rows per CTA (TMEM lanes)
 constexpr int FN = 128;  // keys per tile
-constexpr int F_THREADS = 384;
+constexpr int FQ = 32;                  // key columns per elementwise warpgroup
+constexpr int NQW = FN / FQ;            // elementwise warpgroups (4)
+constexpr int F_THREADS = 128 * (1 + NQW);
 
 // barrier slots
 enum : int {
@@ -49,13 +51,10 @@ enum : int {
   B_VFULL = 5,   // [2]
   B_VEMPTY = 7,  // [2]
   B_SFULL = 9,   // [2]
-  B_SEMPTY = 11, // [2]
-  B_VOTE = 13,   // [2]
-  B_PFULL = 15,  // [2]
-  B_PEMPTY = 17, // [2]
-  B_OFULL = 19,
-  B_FLAG = 20,  // plain arrive after the o_written flag is stored (release for the flag)
-  B_COUNT = 21
+  B_PFULL = 11,  // [2]
+  B_OFULL = 13,
+  B_FLAG = 14,  // plain arrive after the o_written flag is stored (release for the flag)
+  B_COUNT = 15
 };
 
 template <int D>
@@ -71,10 +70,10 @@ struct FwdLayout {
   static constexpr int OFF_TMEM = OFF_BAR + B_COUNT * 8;
   static constexpr int OFF_ABORT = OFF_TMEM + 4;
   static constexpr int OFF_OWR = OFF_ABORT + 4;
-  static constexpr int OFF_VPART = OFF_OWR + 8;      // int [2 buf][2 half][4 warps]
-  static constexpr int OFF_LIVE = OFF_VPART + 64;    // int [2 buf][2 half]
-  static constexpr int OFF_STATS = OFF_LIVE + 16;    // float [2 half][4][128]: peak, mass, count, argmax
-  static constexpr int END = OFF_STATS + 2 * 4 * FM * 4;
+  static constexpr int OFF_VPART = OFF_OWR + 8;      // int [2 buf][4 quarters][4 warps]
+  static constexpr int OFF_LIVE = OFF_VPART + 2 * NQW * 4 * 4;  // int [2 buf][4 quarters]
+  static constexpr int OFF_STATS = OFF_LIVE + 2 * NQW * 4;      // float [4 quarters][4][128]: peak, mass, count, argmax
+  static constexpr int END = OFF_STATS + NQW * 4 * FM * 4;
   static constexpr int ALLOC = END + 1024;           // slack to align the base to 1024
   static constexpr int SMEM = ALLOC < 116 * 1024 ? 116 * 1024 : ALLOC;  // one CTA per SM (it owns all TMEM)
 };
@@ -126,10 +125,7 @@ __global__ void __launch_bounds__(F_THREADS, 1) flash_fwd_sm100_kernel(const __g
       mbar_init(bar(B_VFULL + i), 1);
       mbar_init(bar(B_VEMPTY + i), 1);
       mbar_init(bar(B_SFULL + i), 1);
-      mbar_init(bar(B_SEMPTY + i), 8);
-      mbar_init(bar(B_VOTE + i), 2);
-      mbar_init(bar(B_PFULL + i), 8);
-      mbar_init(bar(B_PEMPTY + i), 1);
+      mbar_init(bar(B_PFULL + i), 4 * NQW);
     }
     mbar_init(bar(B_OFULL), 1);
     mbar_init(bar(B_FLAG), 1);
@@ -218,16 +214,15 @@ __global__ void __launch_bounds__(F_THREADS, 1) flash_fwd_sm100_kernel(const __g
         if (!mbar_wait(bar(B_PFULL + s), (j >> 1) & 1, ab)) return false;
         if (!mbar_wait(bar(B_VFULL + s), (j >> 1) & 1, ab)) return false;
         tc_fence_after();
-        const int l0 = live[s * 2 + 0], l1 = live[s * 2 + 1];
-        for (int hh = 0; hh < 2; ++hh) {
-          if (!(hh ? l1 : l0)) continue;
+        for (int g = 0; g < NQW; ++g) {
+          if (!live[s * NQW + g]) continue;  // silent 32-key quarter: P is zero
 #pragma unroll
-          for (int kq = 0; kq < 4; ++kq) {
-            const int kk = hh * 4 + kq;  // 16 keys per MMA
-            const uint32_t a_hi = tmem + TM_S + 128u * s + 64u * hh + 8u * kq;
+          for (int kq = 0; kq < FQ / 16; ++kq) {
+            const int kk = g * (FQ / 16) + kq;  // 16 keys per MMA
+            const uint32_t a_hi = tmem + TM_S + 128u * s + (uint32_t)FQ * g + 8u * kq;
             const uint32_t bdesc = sw128_desc(sV(s) + kk * 2048, L::GROUP);
-            mma_ts(tmem + TM_O, a_hi, bdesc, ID_O, o_acc);  // O += P_hi V
-            mma_ts(tmem + TM_O, a_hi + 32u, bdesc, ID_O, 1u);  // O += P_lo V
+            mma_ts(tmem + TM_O, a_hi, bdesc, ID_O, o_acc);             // O += P_hi V
+            mma_ts(tmem + TM_O, a_hi + FQ / 2, bdesc, ID_O, 1u);       // O += P_lo V
             o_acc = 1;
           }
         }
@@ -249,7 +244,7 @@ __global__ void __launch_bounds__(F_THREADS, 1) flash_fwd_sm100_kernel(const __g
     }
   } else if (warp >= 4) {
     // ------------------------------------------------------------ elementwise
-    const int ew = warp - 4, hh = ew >> 2, wq = warp & 3;
+    const int ew = warp - 4, g = ew >> 2, wq = warp & 3;  // warpgroup g owns key columns [32g, 32g+32)
     const int rl = 32 * wq + lane;  // TMEM lane = local query row
     const int row = q0 + rl;
     const uint32_t lane_off = (uint32_t)(32 * wq) << 16;
@@ -258,7 +253,7 @@ __global__ void __launch_bounds__(F_THREADS, 1) flash_fwd_sm100_kernel(const __g
     const float2 sc2 = make_float2(p.scale, p.scale), nt2 = make_float2(-tau, -tau);
     const int nT64 = (p.N + 63) >> 6;
     float peak = 0.f, cnt = 0.f;
-    int arg = -1;  // first key attaining the running peak in this column half
+    int arg = -1;  // first key attaining the running peak in this quarter
     float2 ms[4];  // mass partial sums
 #pragma unroll
     for (int i = 0; i < 4; ++i) ms[i] = make_float2(0.f, 0.f);
@@ -268,61 +263,51 @@ __global__ void __launch_bounds__(F_THREADS, 1) flash_fwd_sm100_kernel(const __g
     for (int j = 0; j < ntiles; ++j) {
       const int s = j & 1;
       if (!dead) dead = !warp_wait(bar(B_SFULL + s), (j >> 1) & 1, ab);
-      uint32_t r0[32], r1[32];
+      const uint32_t scol = tmem + lane_off + TM_S + 128u * s + (uint32_t)FQ * g;
+      uint32_t r[32];
       if (!dead) {
         tc_fence_after();
-        tmem_load32x2(tmem + lane_off + TM_S + 128u * s + 64u * hh, r0, tmem + lane_off + TM_S + 128u * s + 64u * hh + 32u,
-                      r1);
+        tmem_load32(scol, r);
       }
-      float x[64];
+      float x[32];
 #pragma unroll
       for (int c = 0; c < 32; c += 2) {
-        const float2 a = __ffma2_rn(make_float2(__uint_as_float(r0[c]), __uint_as_float(r0[c + 1])), sc2, nt2);
-        const float2 e = __ffma2_rn(make_float2(__uint_as_float(r1[c]), __uint_as_float(r1[c + 1])), sc2, nt2);
+        const float2 a = __ffma2_rn(make_float2(__uint_as_float(r[c]), __uint_as_float(r[c + 1])), sc2, nt2);
         x[c] = a.x;
         x[c + 1] = a.y;
-        x[32 + c] = e.x;
-        x[33 + c] = e.y;
       }
-      const int kb = j * FN + 64 * hh;
+      const int kb = j * FN + FQ * g;
       int lim = row < p.N ? (p.causal ? row : p.N - 1) - kb : -1;  // last valid column offset
       if (dead) lim = -1;                                                // after an abort: silent
-      if (lim < 63) {
+      if (lim < 31) {
 #pragma unroll
-        for (int c = 0; c < 64; ++c) x[c] = c > lim ? -1.f : x[c];
+        for (int c = 0; c < 32; ++c) x[c] = c > lim ? -1.f : x[c];
       }
       float m = max3(x[0], x[1], x[2]);
 #pragma unroll
-      for (int c = 3; c < 63; c += 2) m = max3(m, x[c], x[c + 1]);
-      m = fmaxf(m, x[63]);
+      for (int c = 3; c < 31; c += 2) m = max3(m, x[c], x[c + 1]);
+      m = fmaxf(m, x[31]);
       const unsigned live_w = __any_sync(0xffffffffu, m > 0.f);
       if (lane == 0) {
-        vpart[(s * 2 + hh) * 4 + wq] = (int)live_w;
+        vpart[(s * NQW + g) * 4 + wq] = (int)live_w;
         if (p.tile_flags && live_w) {
           const int qi = (q0 >> 6) + (wq >> 1), kj = kb >> 6;
           if (qi < nT64 && kj < nT64) p.tile_flags[((int64_t)bh * nT64 + qi) * nT64 + kj] = 1;
         }
       }
-      named_bar_sync(1 + hh, 128);
-      const int live_h = vpart[(s * 2 + hh) * 4 + 0] | vpart[(s * 2 + hh) * 4 + 1] | vpart[(s * 2 + hh) * 4 + 2] |
-                         vpart[(s * 2 + hh) * 4 + 3];
-      if (ew == 4 * hh && lane == 0) {
-        live[s * 2 + hh] = live_h;
-        mbar_arrive(bar(B_VOTE + s));
-      }
-      if (live_h && !dead) {
-        const float mu = m > 0.f ? m : 0.f;  // row max of u over this half tile
+      named_bar_sync(1 + g, 128);
+      const int live_q = vpart[(s * NQW + g) * 4 + 0] | vpart[(s * NQW + g) * 4 + 1] |
+                         vpart[(s * NQW + g) * 4 + 2] | vpart[(s * NQW + g) * 4 + 3];
+      if (wq == 0 && lane == 0) live[s * NQW + g] = live_q;
+      if (live_q && !dead) {
+        const float mu = m > 0.f ? m : 0.f;  // row max of u over this quarter of the tile
         if (mu > 0.f && mu >= peak) {
-          // columns attaining the maximum as a 64-bit mask: count and first key
-          uint32_t mlo = 0u, mhi = 0u;
+          // columns attaining the maximum as a bit mask: count and first key
+          uint32_t mk = 0u;
 #pragma unroll
-          for (int i = 0; i < 32; ++i) {
-            mlo |= x[i] == m ? 1u << i : 0u;
-            mhi |= x[32 + i] == m ? 1u << i : 0u;
-          }
-          const float c = (float)(__popc(mlo) + __popc(mhi));
-          const int first = mlo ? __ffs(mlo) - 1 : 31 + __ffs(mhi);
-          if (mu > peak) arg = kb + first;  // equal to an earlier tile's peak: keep the earlier key
+          for (int i = 0; i < 32; ++i) mk |= x[i] == m ? 1u << i : 0u;
+          const float c = (float)__popc(mk);
+          if (mu > peak) arg = kb + __ffs(mk) - 1;  // equal to an earlier tile's peak: keep the earlier key
           cnt = mu > peak ? c : cnt + c;
           peak = mu;
         }
@@ -330,47 +315,55 @@ __global__ void __launch_bounds__(F_THREADS, 1) flash_fwd_sm100_kernel(const __g
         // backward's <dO,O>/gate, stays fp32-accurate; the tau gradient is a small
         // residual of cancelling per-row sums and needs that accuracy
         const float2 neg1 = make_float2(-1.f, -1.f);
+        uint32_t hi[16], lo[16];
 #pragma unroll
-        for (int g = 0; g < 2; ++g) {  // 32 columns at a time: 16 packed hi words, 16 lo words
-          uint32_t hi[16], lo[16];
-#pragma unroll
-          for (int c = 0; c < 16; ++c) {
-            const int k = 32 * g + 2 * c;
-            const float2 u = make_float2(fmaxf(x[k], 0.f), fmaxf(x[k + 1], 0.f));
-            const float2 u2 = __fmul2_rn(u, u), u4 = __fmul2_rn(u2, u2);
-            const float2 pw = __fmul2_rn(__fmul2_rn(u4, u4), u2);
-            ms[c & 3] = __fadd2_rn(ms[c & 3], pw);
-            hi[c] = pack_bf16x2(pw.x, pw.y);
-            const float2 hf = make_float2(__uint_as_float(hi[c] << 16), __uint_as_float(hi[c] & 0xffff0000u));
-            const float2 lf = __ffma2_rn(hf, neg1, pw);  // exact: pw - hi
-            lo[c] = pack_bf16x2(lf.x, lf.y);
-          }
-          tmem_st16(tmem + lane_off + TM_S + 128u * s + 64u * hh + 16u * g, hi);
-          tmem_st16(tmem + lane_off + TM_S + 128u * s + 64u * hh + 32u + 16u * g, lo);
+        for (int c = 0; c < 16; ++c) {
+          const float2 u = make_float2(fmaxf(x[2 * c], 0.f), fmaxf(x[2 * c + 1], 0.f));
+          const float2 u2 = __fmul2_rn(u, u), u4 = __fmul2_rn(u2, u2);
+          const float2 pw = __fmul2_rn(__fmul2_rn(u4, u4), u2);
+          ms[c & 3] = __fadd2_rn(ms[c & 3], pw);
+          hi[c] = pack_bf16x2(pw.x, pw.y);
+          const float2 hf = make_float2(__uint_as_float(hi[c] << 16), __uint_as_float(hi[c] & 0xffff0000u));
+          const float2 lf = __ffma2_rn(hf, neg1, pw);  // exact: pw - hi
+          lo[c] = pack_bf16x2(lf.x, lf.y);
         }
+        // P_hi / P_lo over this warpgroup's own S columns [32g, +16) / [32g+16, +16)
+        tmem_st16(scol, hi);
+        tmem_st16(scol + FQ / 2, lo);
         tmem_wait_st();
       }
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(bar(B_PFULL + s));
     }
-    // ---- epilogue: merge the two column halves of every row, scale O, store
+    // ---- epilogue: merge the four column quarters of every row, scale O, store
     float* st = reinterpret_cast<float*>(smem + L::OFF_STATS);
-    const float mass_h = ((ms[0].x + ms[0].y) + (ms[1].x + ms[1].y)) + ((ms[2].x + ms[2].y) + (ms[3].x + ms[3].y));
-    st[(hh * 4 + 0) * FM + rl] = peak;
-    st[(hh * 4 + 1) * FM + rl] = mass_h;
-    st[(hh * 4 + 2) * FM + rl] = cnt;
-    st[(hh * 4 + 3) * FM + rl] = __int_as_float(arg);
-    named_bar_sync(3, 256);
-    const float p0 = st[0 * FM + rl], p1 = st[4 * FM + rl];
-    const float pk = fmaxf(p0, p1);
-    const float mass = st[1 * FM + rl] + st[5 * FM + rl];
-    const float nm = pk > 0.f ? (p0 == pk ? st[2 * FM + rl] : 0.f) + (p1 == pk ? st[6 * FM + rl] : 0.f) : 0.f;
-    // first key of the row maximum: the lower key half wins a tie between halves of one tile,
-    // otherwise the earlier tile (each half already kept its earliest key)
-    const int a0 = __float_as_int(st[3 * FM + rl]), a1 = __float_as_int(st[7 * FM + rl]);
+    const float mass_q = ((ms[0].x + ms[0].y) + (ms[1].x + ms[1].y)) + ((ms[2].x + ms[2].y) + (ms[3].x + ms[3].y));
+    st[(g * 4 + 0) * FM + rl] = peak;
+    st[(g * 4 + 1) * FM + rl] = mass_q;
+    st[(g * 4 + 2) * FM + rl] = cnt;
+    st[(g * 4 + 3) * FM + rl] = __int_as_float(arg);
+    named_bar_sync(1 + NQW, 128 * NQW);
+    float pk = 0.f, mass = 0.f;
+#pragma unroll
+    for (int q = 0; q < NQW; ++q) {
+      pk = fmaxf(pk, st[(q * 4 + 0) * FM + rl]);
+      mass += st[(q * 4 + 1) * FM + rl];
+    }
+    // first key of the row maximum: each quarter kept its earliest key (an earlier
+    // tile wins a tie), so the smallest key over the quarters holding the maximum
+    float nm = 0.f;
     int amax = -1;
-    if (pk > 0.f) amax = (p0 == pk && p1 == pk) ? min(a0, a1) : (p0 == pk ? a0 : a1);
+    if (pk > 0.f) {
+#pragma unroll
+      for (int q = 0; q < NQW; ++q) {
+        if (st[(q * 4 + 0) * FM + rl] == pk) {
+          nm += st[(q * 4 + 2) * FM + rl];
+          const int aq = __float_as_int(st[(q * 4 + 3) * FM + rl]);
+          amax = amax < 0 ? aq : min(amax, aq);
+        }
+      }
+    }
     const float z = mass + 1e-12f;
     float gate = 0.f;
     if (pk > 0.f) gate = p.has_gamma ? pk / (pk + p.gamma) : 1.f;
@@ -381,16 +374,16 @@ __global__ void __launch_bounds__(F_THREADS, 1) flash_fwd_sm100_kernel(const __g
     __nv_bfloat16* O = static_cast<__nv_bfloat16*>(p.out) + (int64_t)b * p.so[0] + (int64_t)hd * p.so[1] +
                        (int64_t)row * p.so[2];
 #pragma unroll
-    for (int cb = 0; cb < D / 2; cb += 32) {
-      const int d0 = hh * (D / 2) + cb;
-      uint32_t r[32];
+    for (int cb = 0; cb < D / NQW; cb += 16) {  // warpgroup g writes head dims [g*D/4, (g+1)*D/4)
+      const int d0 = g * (D / NQW) + cb;
+      uint32_t r[16];
       if (o_written) {
-        tmem_load32(tmem + lane_off + TM_O + (uint32_t)d0, r);
+        tmem_load16(tmem + lane_off + TM_O + (uint32_t)d0, r);
       }
       if (row < p.N && o_ok && p.out32) {
         float4* o32 = reinterpret_cast<float4*>(p.out32 + ((int64_t)bh * p.N + row) * D + d0);
 #pragma unroll
-        for (int v = 0; v < 8; ++v) {
+        for (int v = 0; v < 4; ++v) {
           float4 f;
           f.x = o_written ? __uint_as_float(r[4 * v + 0]) * so : 0.f;
           f.y = o_written ? __uint_as_float(r[4 * v + 1]) * so : 0.f;
@@ -402,7 +395,7 @@ __global__ void __launch_bounds__(F_THREADS, 1) flash_fwd_sm100_kernel(const __g
       if (row < p.N && o_ok) {
         if (p.so[3] == 1 && (reinterpret_cast<uintptr_t>(O + d0) & 15) == 0) {
 #pragma unroll
-          for (int v = 0; v < 4; ++v) {
+          for (int v = 0; v < 2; ++v) {
             uint4 w;
             uint32_t* wp = reinterpret_cast<uint32_t*>(&w);
 #pragma unroll
@@ -415,12 +408,12 @@ __global__ void __launch_bounds__(F_THREADS, 1) flash_fwd_sm100_kernel(const __g
           }
         } else {
 #pragma unroll
-          for (int e = 0; e < 32; ++e)
+          for (int e = 0; e < 16; ++e)
             O[(int64_t)(d0 + e) * p.so[3]] = __float2bfloat16_rn(o_written ? __uint_as_float(r[e]) * so : 0.f);
         }
       }
     }
-    if (hh == 0 && row < p.N && o_ok) {
+    if (g == 0 && row < p.N && o_ok) {
       const int64_t si = (int64_t)bh * p.N + row;
       p.stat_m[si] = pk;
       p.stat_z[si] = z;
