@@ -73,7 +73,10 @@ struct FwdLayout {
   static constexpr int OFF_VPART = OFF_OWR + 8;      // int [2 buf][4 quarters][4 warps]
   static constexpr int OFF_LIVE = OFF_VPART + 2 * NQW * 4 * 4;  // int [2 buf][4 quarters]
   static constexpr int OFF_STATS = OFF_LIVE + 2 * NQW * 4;      // float [4 quarters][4][128]: peak, mass, count, argmax
-  static constexpr int END = OFF_STATS + NQW * 4 * FM * 4;
+  // float4 per row (16-byte aligned for the vector loads): running peaks of the four quarters
+  static constexpr int OFF_RPK = (OFF_STATS + NQW * 4 * FM * 4 + 15) & ~15;
+  static_assert(OFF_RPK % 16 == 0, "float4 rows need 16-byte alignment");
+  static constexpr int END = OFF_RPK + FM * NQW * 4;
   static constexpr int ALLOC = END + 1024;           // slack to align the base to 1024
   static constexpr int SMEM = ALLOC < 116 * 1024 ? 116 * 1024 : ALLOC;  // one CTA per SM (it owns all TMEM)
 };
@@ -142,6 +145,7 @@ __global__ void __launch_bounds__(F_THREADS, 1) flash_fwd_sm100_kernel(const __g
     tmem_alloc(sb0 + L::OFF_TMEM, TM_COLS);
     tmem_relinquish();
   }
+  for (int i = threadIdx.x; i < FM * NQW; i += F_THREADS) reinterpret_cast<float*>(smem + L::OFF_RPK)[i] = 0.f;
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
@@ -254,6 +258,10 @@ __global__ void __launch_bounds__(F_THREADS, 1) flash_fwd_sm100_kernel(const __g
     const int nT64 = (p.N + 63) >> 6;
     float peak = 0.f, cnt = 0.f;
     int arg = -1;  // first key attaining the running peak in this quarter
+    // running peaks of this row's four quarters; a quarter whose tile maximum is
+    // below the row's best so far can never hold the row maximum, so it skips the
+    // per-column search (the estimate may lag: that only costs extra searches)
+    float4* rpk = reinterpret_cast<float4*>(smem + L::OFF_RPK) + rl;  // zeroed before the first __syncthreads
     float2 ms[4];  // mass partial sums
 #pragma unroll
     for (int i = 0; i < 4; ++i) ms[i] = make_float2(0.f, 0.f);
@@ -301,7 +309,9 @@ __global__ void __launch_bounds__(F_THREADS, 1) flash_fwd_sm100_kernel(const __g
       if (wq == 0 && lane == 0) live[s * NQW + g] = live_q;
       if (live_q && !dead) {
         const float mu = m > 0.f ? m : 0.f;  // row max of u over this quarter of the tile
-        if (mu > 0.f && mu >= peak) {
+        const float4 rp4 = *rpk;
+        const float row_best = fmaxf(fmaxf(rp4.x, rp4.y), fmaxf(rp4.z, rp4.w));
+        if (mu > 0.f && mu >= fmaxf(peak, row_best)) {
           // columns attaining the maximum as a bit mask: count and first key
           uint32_t mk = 0u;
 #pragma unroll
@@ -310,6 +320,7 @@ __global__ void __launch_bounds__(F_THREADS, 1) flash_fwd_sm100_kernel(const __g
           if (mu > peak) arg = kb + __ffs(mk) - 1;  // equal to an earlier tile's peak: keep the earlier key
           cnt = mu > peak ? c : cnt + c;
           peak = mu;
+          reinterpret_cast<float*>(rpk)[g] = peak;
         }
         // P = u^10 as P_hi + P_lo (two bf16 terms, ~2^-17 relative): O, and with it the
         // backward's <dO,O>/gate, stays fp32-accurate; the tau gradient is a small
