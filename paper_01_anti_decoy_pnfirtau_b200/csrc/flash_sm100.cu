@@ -2,16 +2,14 @@
 // TMEM accumulators, warp-specialised pipelines. bf16 inputs, head dim 64/128.
 //
 // Forward, one CTA per (128 query rows, b*h), 640 threads:
-//   warp 0      TMA producer: Q once; K tile j+1 ahead; V halves of tile j only
-//               after the elementwise warps voted them live (silent halves are
-//               never loaded).
+//   warp 0      TMA producer: Q once; K and V tile j+1 while tile j is computed.
 //   warp 1      MMA issuer and TMEM owner: S_j = Q K_j^T (SS, M=N=128) into one
 //               of two S buffers; O += P_j V_j (TS: P read from TMEM) for the live
-//               64-key halves only.
+//               32-key quarters only.
 //   warps 4-19  four elementwise warpgroups; warpgroup g owns key columns
 //               [32g, 32g+32) of every tile, thread = TMEM lane = query row:
 //               s = S*scale - tau (packed f32x2 FMA, rounded once), u = max(s, 0),
-//               row max via 3-input max, per-quarter silent vote, u^10 by repeated
+//               row max via 3-input max, per-warp silent vote, u^10 by repeated
 //               squaring (no exp), running peak / tie count / argmax / mass, and
 //               P = u^10 split into two bf16 terms P_hi + P_lo written back over
 //               the tile's own S columns in TMEM for the two PV MMAs.
@@ -19,7 +17,7 @@
 // Epilogue: O * gate/(mass + 1e-12) with gate = peak/(peak+gamma), stats M, Z,
 // Nmax, argmax.
 // Semantics follow src/triton_pnfirtau.py:313-443 (the reference skips 64x64
-// tiles; here the skip unit is 128 query rows x 64 keys, and the optional
+// tiles; here the skip unit is 128 query rows x 32 keys, and the optional
 // tile_flags record reports the 64x64 decisions of the same u values).
 //
 // Every mbarrier wait is bounded (sm100_ptx.cuh): on timeout the CTA sets the
@@ -70,9 +68,9 @@ struct FwdLayout {
   static constexpr int OFF_TMEM = OFF_BAR + B_COUNT * 8;
   static constexpr int OFF_ABORT = OFF_TMEM + 4;
   static constexpr int OFF_OWR = OFF_ABORT + 4;
-  static constexpr int OFF_VPART = OFF_OWR + 8;      // int [2 buf][4 quarters][4 warps]
-  static constexpr int OFF_LIVE = OFF_VPART + 2 * NQW * 4 * 4;  // int [2 buf][4 quarters]
-  static constexpr int OFF_STATS = OFF_LIVE + 2 * NQW * 4;      // float [4 quarters][4][128]: peak, mass, count, argmax
+  // u8 [2 buf][4 quarters][4 warps]: one word per quarter, nonzero when any warp saw a live row
+  static constexpr int OFF_VPART = OFF_OWR + 8;
+  static constexpr int OFF_STATS = OFF_VPART + 2 * NQW * 4;  // float [4 quarters][4][128]: peak, mass, count, argmax
   // float4 per row (16-byte aligned for the vector loads): running peaks of the four quarters
   static constexpr int OFF_RPK = (OFF_STATS + NQW * 4 * FM * 4 + 15) & ~15;
   static_assert(OFF_RPK % 16 == 0, "float4 rows need 16-byte alignment");
@@ -116,8 +114,7 @@ __global__ void __launch_bounds__(F_THREADS, 1) flash_fwd_sm100_kernel(const __g
   const int ntiles = p.causal ? qt + 1 : p.nq;
   auto bar = [&](int i) -> uint32_t { return sb0 + L::OFF_BAR + 8u * (uint32_t)i; };
   volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + L::OFF_ABORT);
-  volatile int* vpart = reinterpret_cast<volatile int*>(smem + L::OFF_VPART);
-  volatile int* live = reinterpret_cast<volatile int*>(smem + L::OFF_LIVE);
+  volatile uint8_t* vpart = smem + L::OFF_VPART;
   const Abort ab{abort_flag, p.status};
 
   if (threadIdx.x == 0) {
@@ -219,7 +216,8 @@ __global__ void __launch_bounds__(F_THREADS, 1) flash_fwd_sm100_kernel(const __g
         if (!mbar_wait(bar(B_VFULL + s), (j >> 1) & 1, ab)) return false;
         tc_fence_after();
         for (int g = 0; g < NQW; ++g) {
-          if (!live[s * NQW + g]) continue;  // silent 32-key quarter: P is zero
+          // the four warps' votes of this quarter, published before their PFULL arrives
+          if (!reinterpret_cast<volatile const uint32_t*>(vpart)[s * NQW + g]) continue;  // silent: P is zero
 #pragma unroll
           for (int kq = 0; kq < FQ / 16; ++kq) {
             const int kk = g * (FQ / 16) + kq;  // 16 keys per MMA
@@ -295,19 +293,18 @@ __global__ void __launch_bounds__(F_THREADS, 1) flash_fwd_sm100_kernel(const __g
 #pragma unroll
       for (int c = 3; c < 31; c += 2) m = max3(m, x[c], x[c + 1]);
       m = fmaxf(m, x[31]);
+      // silent vote of this warp's 32 rows; the MMA issuer ORs the four warps of
+      // the quarter after PFULL completes (no barrier between the warps). A silent
+      // warp writes zeros: another warp's rows may keep the quarter live.
       const unsigned live_w = __any_sync(0xffffffffu, m > 0.f);
       if (lane == 0) {
-        vpart[(s * NQW + g) * 4 + wq] = (int)live_w;
+        vpart[(s * NQW + g) * 4 + wq] = live_w ? 1 : 0;
         if (p.tile_flags && live_w) {
           const int qi = (q0 >> 6) + (wq >> 1), kj = kb >> 6;
           if (qi < nT64 && kj < nT64) p.tile_flags[((int64_t)bh * nT64 + qi) * nT64 + kj] = 1;
         }
       }
-      named_bar_sync(1 + g, 128);
-      const int live_q = vpart[(s * NQW + g) * 4 + 0] | vpart[(s * NQW + g) * 4 + 1] |
-                         vpart[(s * NQW + g) * 4 + 2] | vpart[(s * NQW + g) * 4 + 3];
-      if (wq == 0 && lane == 0) live[s * NQW + g] = live_q;
-      if (live_q && !dead) {
+      if (live_w && !dead) {
         const float mu = m > 0.f ? m : 0.f;  // row max of u over this quarter of the tile
         const float4 rp4 = *rpk;
         const float row_best = fmaxf(fmaxf(rp4.x, rp4.y), fmaxf(rp4.z, rp4.w));
@@ -341,6 +338,13 @@ __global__ void __launch_bounds__(F_THREADS, 1) flash_fwd_sm100_kernel(const __g
         // P_hi / P_lo over this warpgroup's own S columns [32g, +16) / [32g+16, +16)
         tmem_st16(scol, hi);
         tmem_st16(scol + FQ / 2, lo);
+        tmem_wait_st();
+      } else if (!dead) {
+        uint32_t zr[16];
+#pragma unroll
+        for (int c = 0; c < 16; ++c) zr[c] = 0u;
+        tmem_st16(scol, zr);
+        tmem_st16(scol + FQ / 2, zr);
         tmem_wait_st();
       }
       tc_fence_before();
