@@ -74,7 +74,13 @@ struct FwdLayout {
   // float4 per row (16-byte aligned for the vector loads): running peaks of the four quarters
   static constexpr int OFF_RPK = (OFF_STATS + NQW * 4 * FM * 4 + 15) & ~15;
   static_assert(OFF_RPK % 16 == 0, "float4 rows need 16-byte alignment");
-  static constexpr int END = OFF_RPK + FM * NQW * 4;
+  // d=64 only (d=128 has no room): per elementwise lane the 32 s-values of the tile
+  // that set its quarter's peak, rows 144 B apart (conflict-free 16-byte stores)
+  static constexpr bool DEFER = D == 64;
+  static constexpr int REC_STRIDE = 144;
+  static constexpr int OFF_REC = OFF_RPK + FM * NQW * 4;
+  static_assert(OFF_REC % 16 == 0, "16-byte rows");
+  static constexpr int END = OFF_REC + (DEFER ? NQW * FM * REC_STRIDE : 0);
   static constexpr int ALLOC = END + 1024;           // slack to align the base to 1024
   static constexpr int SMEM = ALLOC < 116 * 1024 ? 116 * 1024 : ALLOC;  // one CTA per SM (it owns all TMEM)
 };
@@ -256,6 +262,9 @@ __global__ void __launch_bounds__(F_THREADS, 1) flash_fwd_sm100_kernel(const __g
     const int nT64 = (p.N + 63) >> 6;
     float peak = 0.f, cnt = 0.f;
     int arg = -1;  // first key attaining the running peak in this quarter
+    // deferred search (d=64): the tile that set the peak is saved; `arg` holds its
+    // first key and `cnt` counts only the maxima of later tiles equal to the peak
+    float* rec = reinterpret_cast<float*>(smem + L::OFF_REC + (g * FM + rl) * L::REC_STRIDE);
     // running peaks of this row's four quarters; a quarter whose tile maximum is
     // below the row's best so far can never hold the row maximum, so it skips the
     // per-column search (the estimate may lag: that only costs extra searches)
@@ -309,13 +318,22 @@ __global__ void __launch_bounds__(F_THREADS, 1) flash_fwd_sm100_kernel(const __g
         const float4 rp4 = *rpk;
         const float row_best = fmaxf(fmaxf(rp4.x, rp4.y), fmaxf(rp4.z, rp4.w));
         if (mu > 0.f && mu >= fmaxf(peak, row_best)) {
-          // columns attaining the maximum as a bit mask: count and first key
-          uint32_t mk = 0u;
+          if (L::DEFER && mu > peak) {
+            // new peak: save the tile's values, search them once after the loop
 #pragma unroll
-          for (int i = 0; i < 32; ++i) mk |= x[i] == m ? 1u << i : 0u;
-          const float c = (float)__popc(mk);
-          if (mu > peak) arg = kb + __ffs(mk) - 1;  // equal to an earlier tile's peak: keep the earlier key
-          cnt = mu > peak ? c : cnt + c;
+            for (int k = 0; k < 8; ++k)
+              reinterpret_cast<float4*>(rec)[k] = make_float4(x[4 * k], x[4 * k + 1], x[4 * k + 2], x[4 * k + 3]);
+            arg = kb;
+            cnt = 0.f;
+          } else {
+            // columns attaining the maximum as a bit mask: count and first key
+            uint32_t mk = 0u;
+#pragma unroll
+            for (int i = 0; i < 32; ++i) mk |= x[i] == m ? 1u << i : 0u;
+            const float c = (float)__popc(mk);
+            if (mu > peak) arg = kb + __ffs(mk) - 1;  // equal to an earlier tile's peak: keep the earlier key
+            cnt = mu > peak ? c : cnt + c;
+          }
           peak = mu;
           reinterpret_cast<float*>(rpk)[g] = peak;
         }
@@ -350,6 +368,20 @@ __global__ void __launch_bounds__(F_THREADS, 1) flash_fwd_sm100_kernel(const __g
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(bar(B_PFULL + s));
+    }
+    if (L::DEFER && peak > 0.f) {
+      // search of the saved tile: its maximum equals the quarter's peak
+      uint32_t mk = 0u;
+#pragma unroll
+      for (int k = 0; k < 8; ++k) {
+        const float4 v4 = reinterpret_cast<const float4*>(rec)[k];
+        mk |= (v4.x == peak ? 1u : 0u) << (4 * k);
+        mk |= (v4.y == peak ? 2u : 0u) << (4 * k);
+        mk |= (v4.z == peak ? 4u : 0u) << (4 * k);
+        mk |= (v4.w == peak ? 8u : 0u) << (4 * k);
+      }
+      cnt += (float)__popc(mk);
+      arg += __ffs(mk) - 1;
     }
     // ---- epilogue: merge the four column quarters of every row, scale O, store
     float* st = reinterpret_cast<float*>(smem + L::OFF_STATS);

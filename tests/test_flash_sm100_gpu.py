@@ -209,3 +209,33 @@ def test_sm100_duplicate_key_ties(cuda):
     for name, a, r in zip(("out", "dq", "dk", "dv"), ours[:4], (outr, qr.grad, kr.grad, vr.grad)):
         assert rel_l2(a, r) < 1e-2, (name, rel_l2(a, r))
     assert abs(float(ours[4]) - float(tr.grad)) <= 1e-2 * abs(float(tr.grad)) + 1e-6
+
+
+def test_sm100_ties_within_one_key_quarter(cuda):
+    """Duplicates inside one 32-key quarter of one tile (keys 5 and 12) and two more
+    in a later tile's same quarter (140, 150): the per-row tie counts 1/2/3/4 and
+    the gradients that follow the first maximal key."""
+    g = torch.Generator().manual_seed(22)
+    B, H, N, D = 1, 1, 192, 64
+    q = torch.randn(B, H, N, D, generator=g)
+    k = torch.randn(B, H, N, D, generator=g)
+    v = torch.randn(B, H, N, D, generator=g)
+    k[:, :, 5] *= 5.0
+    for j in (12, 140, 150):
+        k[:, :, j] = k[:, :, 5]
+    q[:, :, 5:] = k[:, :, 5:6] * 0.3
+    q, k, v = (t.to(cuda, torch.bfloat16) for t in (q, k, v))
+    do = torch.randn(q.shape, generator=g).to(cuda, torch.bfloat16)
+    t = torch.tensor(0.0, device=cuda)
+    _, M, _, Nmax, _ = flash_pn_fir_tau_forward_stats(q, k, v, t, extra_flags=SM100)
+    check_device_status(cuda)
+    want = torch.tensor([1] * 7 + [2] * 128 + [3] * 10 + [4] * 42, dtype=torch.int32)
+    assert torch.equal(Nmax[0, 0, 5:].cpu(), want)
+    ours = _fwd_bwd(q, k, v, do, 0.0, generic=False)
+    qr, kr, vr = (x.double().requires_grad_(True) for x in (q, k, v))
+    tr = torch.tensor(0.0, dtype=torch.float64, device=cuda, requires_grad=True)
+    outr = O.pn_fir_tau_attention(qr, kr, vr, tr)
+    outr.backward(do.double())
+    for name, a, r in zip(("out", "dq", "dk", "dv"), ours[:4], (outr, qr.grad, kr.grad, vr.grad)):
+        assert rel_l2(a, r) < 1e-2, (name, rel_l2(a, r))
+    assert abs(float(ours[4]) - float(tr.grad)) <= 1e-2 * abs(float(tr.grad)) + 1e-6
