@@ -257,8 +257,11 @@ __global__ void __launch_bounds__(F_THREADS, 1) flash_fwd_sm100_kernel(const __g
     const int row = q0 + rl;
     const uint32_t lane_off = (uint32_t)(32 * wq) << 16;
     const float tau = __ldg(p.tau);
-    // s = S*scale - tau, rounded once, two columns per packed f32x2 FMA
-    const float2 sc2 = make_float2(p.scale, p.scale), nt2 = make_float2(-tau, -tau);
+    // h = (S*scale - tau)/2, rounded once, two columns per packed f32x2 FMA. The
+    // halving is exact, so maxima and ties of h are those of s, and the relu
+    // u = max(s, 0) = h + |h| is one FMA-pipe add instead of an ALU max. Peaks are
+    // kept as h until the epilogue doubles them.
+    const float2 sc2 = make_float2(0.5f * p.scale, 0.5f * p.scale), nt2 = make_float2(-0.5f * tau, -0.5f * tau);
     const int nT64 = (p.N + 63) >> 6;
     float peak = 0.f, cnt = 0.f;
     int arg = -1;  // first key attaining the running peak in this quarter
@@ -314,7 +317,7 @@ __global__ void __launch_bounds__(F_THREADS, 1) flash_fwd_sm100_kernel(const __g
         }
       }
       if (live_w && !dead) {
-        const float mu = m > 0.f ? m : 0.f;  // row max of u over this quarter of the tile
+        const float mu = m > 0.f ? m : 0.f;  // row max of u/2 over this quarter of the tile
         const float4 rp4 = *rpk;
         const float row_best = fmaxf(fmaxf(rp4.x, rp4.y), fmaxf(rp4.z, rp4.w));
         if (mu > 0.f && mu >= fmaxf(peak, row_best)) {
@@ -344,7 +347,7 @@ __global__ void __launch_bounds__(F_THREADS, 1) flash_fwd_sm100_kernel(const __g
         uint32_t hi[16], lo[16];
 #pragma unroll
         for (int c = 0; c < 16; ++c) {
-          const float2 u = make_float2(fmaxf(x[2 * c], 0.f), fmaxf(x[2 * c + 1], 0.f));
+          const float2 u = make_float2(__fadd_rn(x[2 * c], fabsf(x[2 * c])), __fadd_rn(x[2 * c + 1], fabsf(x[2 * c + 1])));
           const float2 u2 = __fmul2_rn(u, u), u4 = __fmul2_rn(u2, u2);
           const float2 pw = __fmul2_rn(__fmul2_rn(u4, u4), u2);
           ms[c & 3] = __fadd2_rn(ms[c & 3], pw);
@@ -411,6 +414,7 @@ __global__ void __launch_bounds__(F_THREADS, 1) flash_fwd_sm100_kernel(const __g
         }
       }
     }
+    pk *= 2.f;  // h -> s
     const float z = mass + 1e-12f;
     float gate = 0.f;
     if (pk > 0.f) gate = p.has_gamma ? pk / (pk + p.gamma) : 1.f;
