@@ -272,9 +272,7 @@ __global__ void __launch_bounds__(F_THREADS, 1) flash_fwd_sm100_kernel(const __g
     // below the row's best so far can never hold the row maximum, so it skips the
     // per-column search (the estimate may lag: that only costs extra searches)
     float4* rpk = reinterpret_cast<float4*>(smem + L::OFF_RPK) + rl;  // zeroed before the first __syncthreads
-    float2 ms[4];  // mass partial sums
-#pragma unroll
-    for (int i = 0; i < 4; ++i) ms[i] = make_float2(0.f, 0.f);
+    float2 ms[2] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f)};  // mass partial sums
     // `dead` (warp-uniform) turns the rest of the loop into no-ops after an
     // abort, while every warp still passes the warpgroup's named barriers.
     bool dead = false;
@@ -343,22 +341,29 @@ __global__ void __launch_bounds__(F_THREADS, 1) flash_fwd_sm100_kernel(const __g
         // P = u^10 as P_hi + P_lo (two bf16 terms, ~2^-17 relative): O, and with it the
         // backward's <dO,O>/gate, stays fp32-accurate; the tau gradient is a small
         // residual of cancelling per-row sums and needs that accuracy
+        // Two halves of 16 columns, each stored as soon as it is packed (fewer live
+        // registers): P_hi / P_lo over this warpgroup's own S columns
+        // [32g + 8hh, +8) / [32g + 16 + 8hh, +8).
         const float2 neg1 = make_float2(-1.f, -1.f);
-        uint32_t hi[16], lo[16];
 #pragma unroll
-        for (int c = 0; c < 16; ++c) {
-          const float2 u = make_float2(__fadd_rn(x[2 * c], fabsf(x[2 * c])), __fadd_rn(x[2 * c + 1], fabsf(x[2 * c + 1])));
-          const float2 u2 = __fmul2_rn(u, u), u4 = __fmul2_rn(u2, u2);
-          const float2 pw = __fmul2_rn(__fmul2_rn(u4, u4), u2);
-          ms[c & 3] = __fadd2_rn(ms[c & 3], pw);
-          hi[c] = pack_bf16x2(pw.x, pw.y);
-          const float2 hf = make_float2(__uint_as_float(hi[c] << 16), __uint_as_float(hi[c] & 0xffff0000u));
-          const float2 lf = __ffma2_rn(hf, neg1, pw);  // exact: pw - hi
-          lo[c] = pack_bf16x2(lf.x, lf.y);
+        for (int hh = 0; hh < 2; ++hh) {
+          uint32_t hi[8], lo[8];
+#pragma unroll
+          for (int cc = 0; cc < 8; ++cc) {
+            const int c = 8 * hh + cc;
+            const float2 u =
+                make_float2(__fadd_rn(x[2 * c], fabsf(x[2 * c])), __fadd_rn(x[2 * c + 1], fabsf(x[2 * c + 1])));
+            const float2 u2 = __fmul2_rn(u, u), u4 = __fmul2_rn(u2, u2);
+            const float2 pw = __fmul2_rn(__fmul2_rn(u4, u4), u2);
+            ms[c & 1] = __fadd2_rn(ms[c & 1], pw);
+            hi[cc] = pack_bf16x2(pw.x, pw.y);
+            const float2 hf = make_float2(__uint_as_float(hi[cc] << 16), __uint_as_float(hi[cc] & 0xffff0000u));
+            const float2 lf = __ffma2_rn(hf, neg1, pw);  // exact: pw - hi
+            lo[cc] = pack_bf16x2(lf.x, lf.y);
+          }
+          tmem_st8(scol + 8 * hh, hi);
+          tmem_st8(scol + FQ / 2 + 8 * hh, lo);
         }
-        // P_hi / P_lo over this warpgroup's own S columns [32g, +16) / [32g+16, +16)
-        tmem_st16(scol, hi);
-        tmem_st16(scol + FQ / 2, lo);
         tmem_wait_st();
       } else if (!dead) {
         uint32_t zr[16];
@@ -388,7 +393,7 @@ __global__ void __launch_bounds__(F_THREADS, 1) flash_fwd_sm100_kernel(const __g
     }
     // ---- epilogue: merge the four column quarters of every row, scale O, store
     float* st = reinterpret_cast<float*>(smem + L::OFF_STATS);
-    const float mass_q = ((ms[0].x + ms[0].y) + (ms[1].x + ms[1].y)) + ((ms[2].x + ms[2].y) + (ms[3].x + ms[3].y));
+    const float mass_q = (ms[0].x + ms[0].y) + (ms[1].x + ms[1].y);
     st[(g * 4 + 0) * FM + rl] = peak;
     st[(g * 4 + 1) * FM + rl] = mass_q;
     st[(g * 4 + 2) * FM + rl] = cnt;
