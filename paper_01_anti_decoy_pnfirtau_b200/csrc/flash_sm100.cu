@@ -114,8 +114,10 @@ __global__ void __launch_bounds__(F_THREADS, 1) flash_fwd_sm100_kernel(const __g
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   const uint32_t sb0 = smem_u32(smem);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int qt = p.nq - 1 - (int)blockIdx.x;  // longest causal rows first
-  const int bh = blockIdx.y, b = bh / p.H, hd = bh % p.H;
+  // b*h runs fastest and the query tiles go from the last (longest causal rows)
+  // down: the grid starts with its longest CTAs, so none starts late
+  const int qt = p.nq - 1 - (int)blockIdx.y;
+  const int bh = blockIdx.x, b = bh / p.H, hd = bh % p.H;
   const int q0 = qt * FM;
   const int ntiles = p.causal ? qt + 1 : p.nq;
   auto bar = [&](int i) -> uint32_t { return sb0 + L::OFF_BAR + 8u * (uint32_t)i; };
@@ -572,7 +574,8 @@ int flash_fwd_sm100(const FlashArgs& a, cudaStream_t st) {
   p.gamma = a.gamma;
   p.has_gamma = a.has_gamma;
   p.causal = a.causal;
-  const dim3 grid((unsigned)p.nq, (unsigned)(a.B * a.H));
+  if (p.nq > 65535) return fail(PNFT_EUNSUPPORTED, "flash fwd sm100: N = %lld needs more than 65535 query tiles", (long long)a.N);
+  const dim3 grid((unsigned)(a.B * a.H), (unsigned)p.nq);
   auto launch = [&](auto kern, int smem) -> int {
     if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess)
       return check_launch("flash fwd sm100: smem attribute", 0);

@@ -59,12 +59,12 @@ enum : int {
   C_SDPFULL = 7,   // [2] (one per S/dP buffer)
   C_SDPEMPTY = 9,  // single-buffer layout only
   C_PDSFULL = 10,  // [2]
-  C_PDSEMPTY = 12, // [2]
-  C_DQFULL = 14,   // [2]
-  C_DQEMPTY = 16,  // [2]
-  C_DKV = 18,
-  C_FLAG = 19,  // plain arrive after dkv_written is stored (release for the flag)
-  C_COUNT = 20
+  C_PDSEMPTY = 12, // [4] (one per dS buffer)
+  C_DQFULL = 16,   // [2]
+  C_DQEMPTY = 18,  // [2]
+  C_DKV = 20,
+  C_FLAG = 21,  // plain arrive after dkv_written is stored (release for the flag)
+  C_COUNT = 22
 };
 
 template <int D>
@@ -78,6 +78,10 @@ struct BwdLayout {
   static constexpr int NSTG = D == 64 ? 2 : 1;  // dQ staging tiles in smem
   static constexpr int STG_BYTES = BM * D * 4;
   static constexpr int DS_BYTES = BN * BM * 2;
+  // dS^T tiles in smem. d=64: four, so the elementwise warps' tile j+2 waits only
+  // for its S/dP (whose MMAs follow dV/dK of tile j) and not for dQ of tile j, the
+  // last reader of dS_j. d=128 has room for two.
+  static constexpr int NDS = D == 64 ? 4 : 2;
   // per query tile: 32 coefficient pairs {c1, c1, -D, -D}, tie/10, argmax, tie peak
   static constexpr int CF_P = 0, CF_TIE = BM * 8, CF_ARG = BM * 12, CF_PC = BM * 16, COEF_BYTES = BM * 20;
   static constexpr int OFF_K = 0;
@@ -85,7 +89,7 @@ struct BwdLayout {
   static constexpr int OFF_Q = OFF_V + KBYTES;
   static constexpr int OFF_DO = OFF_Q + NQS * QBYTES;
   static constexpr int OFF_DS = OFF_DO + NQS * QBYTES;
-  static constexpr int OFF_STG = OFF_DS + 2 * DS_BYTES;
+  static constexpr int OFF_STG = OFF_DS + NDS * DS_BYTES;
   static constexpr int OFF_COEF = OFF_STG + NSTG * STG_BYTES;
   static constexpr int OFF_BAR = OFF_COEF + NQS * COEF_BYTES;
   static constexpr int OFF_TMEM = OFF_BAR + C_COUNT * 8;
@@ -179,7 +183,9 @@ __global__ void __launch_bounds__(B_THREADS, 1) flash_bwd_sm100_kernel(const __g
   uint8_t* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
   const uint32_t sb0 = smem_u32(smem);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int kt = blockIdx.x, bh = blockIdx.y, b = bh / p.H, hd = bh % p.H;
+  // b*h runs fastest and key tile 0 (the most causal query tiles) comes first:
+  // the grid starts with its longest CTAs, so none starts late
+  const int kt = blockIdx.y, bh = blockIdx.x, b = bh / p.H, hd = bh % p.H;
   const int k0 = kt * BN;
   const int i_first = p.causal ? k0 / BM : 0;
   const int32_t* live = p.live64 + (int64_t)bh * p.nq64;
@@ -201,9 +207,9 @@ __global__ void __launch_bounds__(B_THREADS, 1) flash_bwd_sm100_kernel(const __g
       mbar_init(bar(C_QDFULL + i), 1);
       mbar_init(bar(C_QDEMPTY + i), 1);
     }
+    for (int i = 0; i < L::NDS; ++i) mbar_init(bar(C_PDSEMPTY + i), 1);
     for (int i = 0; i < 2; ++i) {
       mbar_init(bar(C_PDSFULL + i), 4 * NEW);
-      mbar_init(bar(C_PDSEMPTY + i), 1);
       mbar_init(bar(C_DQFULL + i), 1);
       mbar_init(bar(C_DQEMPTY + i), 4);
     }
@@ -302,7 +308,7 @@ __global__ void __launch_bounds__(B_THREADS, 1) flash_bwd_sm100_kernel(const __g
       return true;
     };
     auto dvdk = [&](int u) -> bool {
-      const int s = u & 1, qs = u % NQS;
+      const int s = u & 1, qs = u % NQS, ds = u % L::NDS;
       if (!warp_wait(bar(C_PDSFULL + s), (u >> 1) & 1, ab)) return false;
       tc_fence_after();
       const uint32_t acc0 = u > 0 ? 1u : 0u;
@@ -312,23 +318,23 @@ __global__ void __launch_bounds__(B_THREADS, 1) flash_bwd_sm100_kernel(const __g
           mma_ts(tmem + L::TM_DV, tmem + L::tm_p(s, kk), dOmn + qs * QSTEP + kk * 128, ID_G, acc0 | (uint32_t)kk);
 #pragma unroll
         for (int kk = 0; kk < BM / 16; ++kk)
-          mma_ss(tmem + L::TM_DK, dSk + s * DSSTEP + kk * 2, dQmn + qs * QSTEP + kk * 128, ID_G, acc0 | (uint32_t)kk);
+          mma_ss(tmem + L::TM_DK, dSk + ds * DSSTEP + kk * 2, dQmn + qs * QSTEP + kk * 128, ID_G, acc0 | (uint32_t)kk);
         mma_commit(bar(C_QDEMPTY + qs));  // Q / dO of tile u are no longer needed
       }
       __syncwarp();
       return true;
     };
     auto dq = [&](int u) -> bool {
-      const int s = u & 1, bq = u % L::NDQ;
+      const int ds = u % L::NDS, bq = u % L::NDQ;
       if (!warp_wait(bar(C_DQEMPTY + bq), ((u / L::NDQ) & 1) ^ 1, ab)) return false;
       tc_fence_after();
       if (elect_one()) {
         // dQ^T[D x 64 q] = K^T[D x keys] dS^T[keys x q]: both operands MN-major in smem
 #pragma unroll
         for (int kk = 0; kk < BN / 16; ++kk)
-          mma_ss(tmem + L::TM_DQ + 64u * bq, dKmn + kk * 128, dSmn + s * DSSTEP + kk * 128, ID_DQ, kk > 0);
+          mma_ss(tmem + L::TM_DQ + 64u * bq, dKmn + kk * 128, dSmn + ds * DSSTEP + kk * 128, ID_DQ, kk > 0);
         mma_commit(bar(C_DQFULL + bq));
-        mma_commit(bar(C_PDSEMPTY + s));
+        mma_commit(bar(C_PDSEMPTY + ds));  // dS_u (and, for d=128, P^T_u) are free
       }
       __syncwarp();
       return true;
@@ -391,13 +397,14 @@ __global__ void __launch_bounds__(B_THREADS, 1) flash_bwd_sm100_kernel(const __g
     LiveTiles lt(live, i_first, p.nq64);
     bool multi_tile;
     for (int i; (i = lt.next(&multi_tile)) >= 0;) {
-      const int s = t & 1, qs = t % NQS;
+      const int s = t & 1, qs = t % NQS, ds = t % L::NDS;
       const int q0 = i * BM;
-      // S/dP of this tile, its coefficient records, and a free P^T / dS buffer
+      // S/dP of this tile, its coefficient records, and a free dS buffer (d=128:
+      // also a free P^T buffer; d=64 writes P^T over its own S columns)
       const int sb = t % L::NSB;
       if (!dead)
         dead = !warp_wait3(bar(C_SDPFULL + sb), (t / L::NSB) & 1, bar(C_QDFULL + qs), (t / NQS) & 1,
-                           bar(C_PDSEMPTY + s), ((t >> 1) & 1) ^ 1, ab);
+                           bar(C_PDSEMPTY + ds), ((t / L::NDS) & 1) ^ 1, ab);
       uint32_t rs[CW], rp[CW];
       if (!dead) {
         tc_fence_after();
@@ -448,7 +455,7 @@ __global__ void __launch_bounds__(B_THREADS, 1) flash_bwd_sm100_kernel(const __g
 #pragma unroll
           for (int cc = 0; cc < CW / 8; ++cc) {
             const uint32_t chunk = (CW / 8) * hh + cc;  // 16-byte chunk of the 128-byte key row
-            st_shared_v4(sdS(s) + rl * 128 + ((chunk ^ (rl & 7)) << 4), ds_pk[4 * cc], ds_pk[4 * cc + 1],
+            st_shared_v4(sdS(ds) + rl * 128 + ((chunk ^ (rl & 7)) << 4), ds_pk[4 * cc], ds_pk[4 * cc + 1],
                          ds_pk[4 * cc + 2], ds_pk[4 * cc + 3]);
           }
         };
@@ -469,7 +476,7 @@ __global__ void __launch_bounds__(B_THREADS, 1) flash_bwd_sm100_kernel(const __g
           if ((unsigned)l < 32u) {
             const float tie = tiew[lane];
             const int r = 32 * wq + l;
-            const uint32_t addr = sdS(s) + r * 128 + ((((uint32_t)col >> 3) ^ (r & 7)) << 4) + (col & 7) * 2;
+            const uint32_t addr = sdS(ds) + r * 128 + ((((uint32_t)col >> 3) ^ (r & 7)) << 4) + (col & 7) * 2;
             unsigned short hv;
             asm volatile("ld.shared.u16 %0, [%1];" : "=h"(hv) : "r"(addr) : "memory");
             const float nv = __bfloat162float(__ushort_as_bfloat16(hv)) + tie;
@@ -638,7 +645,8 @@ int flash_bwd_sm100(const FlashArgs& a0, cudaStream_t st) {
   p.nkt = nkt;
   p.scale = a.scale;
   p.causal = a.causal;
-  const dim3 grid((unsigned)nkt, (unsigned)(a.B * a.H));
+  if (nkt > 65535) return fail(PNFT_EUNSUPPORTED, "flash bwd sm100: N = %lld needs more than 65535 key tiles", (long long)a.N);
+  const dim3 grid((unsigned)(a.B * a.H), (unsigned)nkt);
   auto launch = [&](auto kern, int smem) -> int {
     if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess)
       return check_launch("flash bwd sm100: smem attribute", 0);
