@@ -62,6 +62,11 @@ extern "C" {
 #define PNFT_FLASH_DETERMINISTIC 0x2 /* reserved: ordered dQ accumulation             */
 #define PNFT_FLASH_PREFER_SM100 0x4  /* tcgen05 kernels wherever their shape rules allow */
 
+/* Tap count of the FIR fused into the flash kernels (pnft_flash_fwd_fir): the
+ * module's causal filter on the keys, PnFirConfig.fir_k = 7
+ * (src/pnfirtau_attention.py:35-47). */
+#define PNFT_FIR_FUSED_TAPS 7
+
 /* Library version (major*10000 + minor*100 + patch). */
 PNFT_API int pnft_version(void);
 
@@ -213,6 +218,46 @@ PNFT_API int pnft_flash_bwd(const void* q, const int64_t* sq, const void* k, con
                    void* stream);
 
 PNFT_API size_t pnft_flash_bwd_workspace_size(int64_t B, int64_t H, int64_t N, int64_t D, int flags);
+
+/* pnft_flash_fwd with the causal FIR on the keys fused into the kernels' K-tile
+ * load: k is the RAW K (the projection output); each K tile is staged by TMA with
+ * its 8 preceding rows (zeros before the sequence start) and filtered in shared
+ * memory into k~ = causal_fir(k, taps), bit-identical to pnft_fir_fwd, before the
+ * QK^T MMA. taps: device fp32[PNFT_FIR_FUSED_TAPS], index 6 = lag 0. The other
+ * arguments as pnft_flash_fwd. Served by the sm_100a kernels only (bf16, head dim
+ * 64/128, 16-byte aligned rows with unit head-dim stride); other inputs return
+ * PNFT_EUNSUPPORTED.
+ * Replaces: triton_causal_fir(k) followed by flash_pn_fir_tau_attention in
+ * PnFirTauFlashMHA.forward (src/pnfirtau_attention.py:285-316,
+ * src/triton_pnfirtau.py:685-691, 971-983). */
+PNFT_API int pnft_flash_fwd_fir(const void* q, const int64_t* sq, const void* k, const int64_t* sk,
+                       const float* taps, int ntaps, const void* v, const int64_t* sv, const float* tau,
+                       void* out, const int64_t* so, float* out_f32, float* stat_m, float* stat_z,
+                       int32_t* stat_nmax, int32_t* stat_arg, int64_t B, int64_t H, int64_t N, int64_t D,
+                       float scale, float gamma, int has_gamma, int causal, int dtype, int flags,
+                       uint8_t* tile_flags, int32_t* status, void* stream);
+
+/* Backward of pnft_flash_fwd_fir. The kernel re-filters its K tile from the raw k
+ * in shared memory and writes d(k~) to the workspace; the transposed FIR
+ * (pnft_fir_bwd) then gives dk, the gradient of the RAW k (strides sdk), and
+ * dtaps (fp32[PNFT_FIR_FUSED_TAPS], may be NULL). k and dk need unit head-dim
+ * stride and either adjacent (h, d) axes (the module's [B,N,H*D] view) or
+ * adjacent (b, h) axes (a contiguous [B,H,N,D] tensor). workspace:
+ * pnft_flash_bwd_fir_workspace_size(...) bytes, 256-byte aligned. The other
+ * arguments as pnft_flash_bwd.
+ * Replaces: the backward of the same composition (src/triton_pnfirtau.py:445-621,
+ * 629-682). */
+PNFT_API int pnft_flash_bwd_fir(const void* q, const int64_t* sq, const void* k, const int64_t* sk,
+                       const float* taps, int ntaps, const void* v, const int64_t* sv, const float* tau,
+                       const void* out, const int64_t* so, const float* out_f32, const void* dout,
+                       const int64_t* sdo, const float* stat_m, const float* stat_z,
+                       const int32_t* stat_nmax, const int32_t* stat_arg, void* dq, const int64_t* sdq,
+                       void* dk, const int64_t* sdk, void* dv, const int64_t* sdv, float* dtau,
+                       float* dtaps, void* workspace, size_t workspace_bytes, int64_t B, int64_t H,
+                       int64_t N, int64_t D, float scale, float gamma, int has_gamma, int causal, int dtype,
+                       int flags, int32_t* status, void* stream);
+
+PNFT_API size_t pnft_flash_bwd_fir_workspace_size(int64_t B, int64_t H, int64_t N, int64_t D, int flags);
 
 /* Which kernel family pnft_flash_fwd / pnft_flash_bwd would launch for these
  * arguments: 1 = sm_100a tcgen05/TMA kernels, 0 = generic SIMT kernels. */

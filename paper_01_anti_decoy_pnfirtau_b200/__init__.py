@@ -17,6 +17,7 @@ from .pnfirtau_ops import (
     check_device_status,
     flash_kernel_path,
     flash_pn_fir_tau_attention,
+    flash_pn_fir_tau_attention_fir,
     pn_rows,
     triton_causal_fir,
     triton_pn_fir_tau_scores,
@@ -34,6 +35,7 @@ __all__ = [
     "triton_causal_fir",
     "triton_pn_fir_tau_scores",
     "flash_pn_fir_tau_attention",
+    "flash_pn_fir_tau_attention_fir",
     "pn_rows",
     "check_device_status",
     "flash_kernel_path",

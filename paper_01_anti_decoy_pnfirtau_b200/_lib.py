@@ -17,6 +17,7 @@ OK, EINVAL, EUNSUPPORTED, ECUDA = 0, -1, -2, -3
 DEV_OK, DEV_WAIT_TIMEOUT = 0, 1
 SILENCE_PEAK, SILENCE_MASS_RELU, SILENCE_MASS_POW = 0, 1, 2
 FLASH_FORCE_GENERIC, FLASH_DETERMINISTIC, FLASH_PREFER_SM100 = 0x1, 0x2, 0x4
+FIR_FUSED_TAPS = 7  # PNFT_FIR_FUSED_TAPS
 
 _I64x4 = c_int64 * 4
 _P = c_void_p
@@ -65,6 +66,18 @@ SIGNATURES: dict[str, tuple] = {
          c_int, _P, _P],
     ),
     "pnft_flash_bwd_workspace_size": (c_size_t, [c_int64, c_int64, c_int64, c_int64, c_int]),
+    "pnft_flash_fwd_fir": (
+        c_int,
+        [_P, _I64x4, _P, _I64x4, _P, c_int, _P, _I64x4, _P, _P, _I64x4, _P, _P, _P, _P, _P, c_int64, c_int64,
+         c_int64, c_int64, c_float, c_float, c_int, c_int, c_int, c_int, _P, _P, _P],
+    ),
+    "pnft_flash_bwd_fir": (
+        c_int,
+        [_P, _I64x4, _P, _I64x4, _P, c_int, _P, _I64x4, _P, _P, _I64x4, _P, _P, _I64x4, _P, _P, _P, _P, _P, _I64x4,
+         _P, _I64x4, _P, _I64x4, _P, _P, _P, c_size_t, c_int64, c_int64, c_int64, c_int64, c_float, c_float, c_int,
+         c_int, c_int, c_int, _P, _P],
+    ),
+    "pnft_flash_bwd_fir_workspace_size": (c_size_t, [c_int64, c_int64, c_int64, c_int64, c_int]),
     "pnft_flash_path": (c_int, [_P, _I64x4, _P, _I64x4, _P, _I64x4, c_int64, c_int, c_int]),
 }
 

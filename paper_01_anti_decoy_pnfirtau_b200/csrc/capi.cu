@@ -5,6 +5,7 @@
 #include <stdio.h>
 #include <string.h>
 
+#include <algorithm>
 #include <atomic>
 
 #include "flash.cuh"
@@ -95,15 +96,18 @@ extern "C" int pnft_flash_path(const void* q, const int64_t* sq, const void* k, 
   return use_sm100(a) ? 1 : 0;
 }
 
-extern "C" int pnft_flash_fwd(const void* q, const int64_t* sq, const void* k, const int64_t* sk, const void* v,
-                              const int64_t* sv, const float* tau, void* out, const int64_t* so, float* out_f32,
-                              float* stat_m, float* stat_z, int32_t* stat_nmax, int32_t* stat_arg, int64_t B,
-                              int64_t H, int64_t N, int64_t D, float scale, float gamma, int has_gamma, int causal,
-                              int dtype, int flags, uint8_t* tile_flags, int32_t* status, void* stream) {
+static int flash_fwd_entry(const void* q, const int64_t* sq, const void* k, const int64_t* sk, const void* v,
+                           const int64_t* sv, const float* tau, void* out, const int64_t* so, float* out_f32,
+                           float* stat_m, float* stat_z, int32_t* stat_nmax, int32_t* stat_arg, int64_t B, int64_t H,
+                           int64_t N, int64_t D, float scale, float gamma, int has_gamma, int causal, int dtype,
+                           int flags, uint8_t* tile_flags, int32_t* status, void* stream, const float* fir_taps,
+                           int fir_ntaps) {
   FlashArgs a;
   int rc = fill_common(a, q, sq, k, sk, v, sv, tau, B, H, N, D, scale, gamma, has_gamma, causal, dtype, flags, status);
   if (rc) return rc;
   a.tile_flags = tile_flags;
+  a.fir_taps = fir_taps;
+  a.fir_ntaps = fir_ntaps;
   if (B * H * N == 0) return PNFT_OK;
   if (D == 0) return fail(PNFT_EINVAL, "flash fwd: head dim 0");
   if (!q || !k || !v || !tau || !out || !so || !stat_m || !stat_z || !stat_nmax || !stat_arg)
@@ -114,7 +118,30 @@ extern "C" int pnft_flash_fwd(const void* q, const int64_t* sq, const void* k, c
   a.stat_m = stat_m; a.stat_z = stat_z; a.stat_nmax = stat_nmax; a.stat_arg = stat_arg;
   cudaStream_t st = as_stream(stream);
   if (use_sm100(a)) return flash_fwd_sm100(a, st);
+  if (fir_taps)
+    return fail(PNFT_EUNSUPPORTED, "flash fwd: the fused FIR runs on the sm_100a kernels only (bf16, head dim 64/128, "
+                                   "16-byte aligned rows with unit head-dim stride)");
   return flash_fwd_generic(a, st);
+}
+
+extern "C" int pnft_flash_fwd(const void* q, const int64_t* sq, const void* k, const int64_t* sk, const void* v,
+                              const int64_t* sv, const float* tau, void* out, const int64_t* so, float* out_f32,
+                              float* stat_m, float* stat_z, int32_t* stat_nmax, int32_t* stat_arg, int64_t B,
+                              int64_t H, int64_t N, int64_t D, float scale, float gamma, int has_gamma, int causal,
+                              int dtype, int flags, uint8_t* tile_flags, int32_t* status, void* stream) {
+  return flash_fwd_entry(q, sq, k, sk, v, sv, tau, out, so, out_f32, stat_m, stat_z, stat_nmax, stat_arg, B, H, N, D,
+                         scale, gamma, has_gamma, causal, dtype, flags, tile_flags, status, stream, nullptr, 0);
+}
+
+extern "C" int pnft_flash_fwd_fir(const void* q, const int64_t* sq, const void* k, const int64_t* sk,
+                                  const float* taps, int ntaps, const void* v, const int64_t* sv, const float* tau,
+                                  void* out, const int64_t* so, float* out_f32, float* stat_m, float* stat_z,
+                                  int32_t* stat_nmax, int32_t* stat_arg, int64_t B, int64_t H, int64_t N, int64_t D,
+                                  float scale, float gamma, int has_gamma, int causal, int dtype, int flags,
+                                  uint8_t* tile_flags, int32_t* status, void* stream) {
+  if (!taps) return fail(PNFT_EINVAL, "flash fwd fir: null taps");
+  return flash_fwd_entry(q, sq, k, sk, v, sv, tau, out, so, out_f32, stat_m, stat_z, stat_nmax, stat_arg, B, H, N, D,
+                         scale, gamma, has_gamma, causal, dtype, flags, tile_flags, status, stream, taps, ntaps);
 }
 
 extern "C" size_t pnft_flash_bwd_workspace_size(int64_t B, int64_t H, int64_t N, int64_t D, int flags) {
@@ -123,17 +150,19 @@ extern "C" size_t pnft_flash_bwd_workspace_size(int64_t B, int64_t H, int64_t N,
   return bwd_workspace_layout(B, H, N, D).total;
 }
 
-extern "C" int pnft_flash_bwd(const void* q, const int64_t* sq, const void* k, const int64_t* sk, const void* v,
-                              const int64_t* sv, const float* tau, const void* out, const int64_t* so,
-                              const float* out_f32, const void* dout, const int64_t* sdo, const float* stat_m, const float* stat_z,
-                              const int32_t* stat_nmax, const int32_t* stat_arg, void* dq, const int64_t* sdq, void* dk,
-                              const int64_t* sdk, void* dv, const int64_t* sdv, float* dtau, void* workspace,
-                              size_t workspace_bytes, int64_t B, int64_t H, int64_t N, int64_t D, float scale,
-                              float gamma, int has_gamma, int causal, int dtype, int flags, int32_t* status,
-                              void* stream) {
+static int flash_bwd_entry(const void* q, const int64_t* sq, const void* k, const int64_t* sk, const void* v,
+                           const int64_t* sv, const float* tau, const void* out, const int64_t* so,
+                           const float* out_f32, const void* dout, const int64_t* sdo, const float* stat_m,
+                           const float* stat_z, const int32_t* stat_nmax, const int32_t* stat_arg, void* dq,
+                           const int64_t* sdq, void* dk, const int64_t* sdk, void* dv, const int64_t* sdv, float* dtau,
+                           void* workspace, size_t workspace_bytes, int64_t B, int64_t H, int64_t N, int64_t D,
+                           float scale, float gamma, int has_gamma, int causal, int dtype, int flags, int32_t* status,
+                           void* stream, const float* fir_taps, int fir_ntaps) {
   FlashArgs a;
   int rc = fill_common(a, q, sq, k, sk, v, sv, tau, B, H, N, D, scale, gamma, has_gamma, causal, dtype, flags, status);
   if (rc) return rc;
+  a.fir_taps = fir_taps;
+  a.fir_ntaps = fir_ntaps;
   cudaStream_t st = as_stream(stream);
   if (!dtau) return fail(PNFT_EINVAL, "flash bwd: null dtau");
   if (B * H * N == 0) {
@@ -166,5 +195,94 @@ extern "C" int pnft_flash_bwd(const void* q, const int64_t* sq, const void* k, c
   a.dtau_part = reinterpret_cast<float*>(ws + w.off_part);
   a.dq_scale = 1.f;
   if (use_sm100(a)) return flash_bwd_sm100(a, st);
+  if (fir_taps) return fail(PNFT_EUNSUPPORTED, "flash bwd: the fused FIR runs on the sm_100a kernels only");
   return flash_bwd_generic(a, st);
+}
+
+extern "C" int pnft_flash_bwd(const void* q, const int64_t* sq, const void* k, const int64_t* sk, const void* v,
+                              const int64_t* sv, const float* tau, const void* out, const int64_t* so,
+                              const float* out_f32, const void* dout, const int64_t* sdo, const float* stat_m, const float* stat_z,
+                              const int32_t* stat_nmax, const int32_t* stat_arg, void* dq, const int64_t* sdq, void* dk,
+                              const int64_t* sdk, void* dv, const int64_t* sdv, float* dtau, void* workspace,
+                              size_t workspace_bytes, int64_t B, int64_t H, int64_t N, int64_t D, float scale,
+                              float gamma, int has_gamma, int causal, int dtype, int flags, int32_t* status,
+                              void* stream) {
+  return flash_bwd_entry(q, sq, k, sk, v, sv, tau, out, so, out_f32, dout, sdo, stat_m, stat_z, stat_nmax, stat_arg,
+                         dq, sdq, dk, sdk, dv, sdv, dtau, workspace, workspace_bytes, B, H, N, D, scale, gamma,
+                         has_gamma, causal, dtype, flags, status, stream, nullptr, 0);
+}
+
+// ---- fused-FIR backward: flash backward on the filtered keys (its d(k~) into the
+// workspace), then the transposed FIR for dk and the tap gradient
+static size_t align256(size_t x) { return (x + 255) & ~(size_t)255; }
+
+struct FirBwdPlan {
+  int64_t Bf, Cf;          // the FIR's [Bf, N, Cf] view of k / dk / d(k~)
+  int64_t sk_b, sk_n;      // k in that view (channel stride 1)
+  int64_t sdk_b, sdk_n;    // dk in that view
+  int64_t sg_b, sg_n;      // d(k~) in that view (contiguous)
+  int64_t st[4];           // d(k~) as [B,H,N,D]
+};
+
+// k and dk as [B, N, H*D] (head dims adjacent: the module's view of the qkv
+// projection) or as [B*H, N, D] (b and h adjacent: a contiguous tensor).
+static bool fir_bwd_plan(const int64_t* sk, const int64_t* sdk, int64_t B, int64_t H, int64_t N, int64_t D,
+                         FirBwdPlan* pl) {
+  if (sk[3] != 1 || sdk[3] != 1) return false;
+  if ((H == 1 || (sk[1] == D && sdk[1] == D))) {
+    *pl = FirBwdPlan{B, H * D, sk[0], sk[2], sdk[0], sdk[2], N * H * D, H * D, {N * H * D, D, H * D, 1}};
+    return true;
+  }
+  if (sk[0] == H * sk[1] && sdk[0] == H * sdk[1]) {
+    *pl = FirBwdPlan{B * H, D, sk[1], sk[2], sdk[1], sdk[2], N * D, D, {H * N * D, N * D, D, 1}};
+    return true;
+  }
+  return false;
+}
+
+extern "C" size_t pnft_flash_bwd_fir_workspace_size(int64_t B, int64_t H, int64_t N, int64_t D, int flags) {
+  if (B <= 0 || H <= 0 || N <= 0 || D <= 0) return 0;
+  const size_t fir_ws = std::max(pnft_fir_bwd_workspace_size(B, N, H * D, PNFT_FIR_FUSED_TAPS),
+                                 pnft_fir_bwd_workspace_size(B * H, N, D, PNFT_FIR_FUSED_TAPS));
+  return align256(pnft_flash_bwd_workspace_size(B, H, N, D, flags)) + align256((size_t)(B * H * N * D) * 2) +
+         align256(fir_ws);
+}
+
+extern "C" int pnft_flash_bwd_fir(const void* q, const int64_t* sq, const void* k, const int64_t* sk,
+                                  const float* taps, int ntaps, const void* v, const int64_t* sv, const float* tau,
+                                  const void* out, const int64_t* so, const float* out_f32, const void* dout,
+                                  const int64_t* sdo, const float* stat_m, const float* stat_z,
+                                  const int32_t* stat_nmax, const int32_t* stat_arg, void* dq, const int64_t* sdq,
+                                  void* dk, const int64_t* sdk, void* dv, const int64_t* sdv, float* dtau,
+                                  float* dtaps, void* workspace, size_t workspace_bytes, int64_t B, int64_t H,
+                                  int64_t N, int64_t D, float scale, float gamma, int has_gamma, int causal, int dtype,
+                                  int flags, int32_t* status, void* stream) {
+  if (!taps || !sk || !sdk || !dk) return fail(PNFT_EINVAL, "flash bwd fir: null taps, dk or strides");
+  if (ntaps != PNFT_FIR_FUSED_TAPS) return fail(PNFT_EUNSUPPORTED, "flash bwd fir: fused FIR needs %d taps", PNFT_FIR_FUSED_TAPS);
+  if (B < 0 || H < 0 || N < 0 || D < 0) return fail(PNFT_EINVAL, "flash bwd fir: negative size");
+  cudaStream_t st = as_stream(stream);
+  if (B * H * N * D == 0) {
+    if (dtaps && cudaMemsetAsync(dtaps, 0, sizeof(float) * ntaps, st) != cudaSuccess)
+      return check_launch("flash bwd fir: dtaps memset");
+    return pnft_flash_bwd(q, sq, k, sk, v, sv, tau, out, so, out_f32, dout, sdo, stat_m, stat_z, stat_nmax, stat_arg,
+                          dq, sdq, dk, sdk, dv, sdv, dtau, workspace, workspace_bytes, B, H, N, D, scale, gamma,
+                          has_gamma, causal, dtype, flags, status, stream);
+  }
+  FirBwdPlan pl;
+  if (!fir_bwd_plan(sk, sdk, B, H, N, D, &pl))
+    return fail(PNFT_EUNSUPPORTED, "flash bwd fir: k and dk need unit head-dim stride and adjacent (h, d) or (b, h) axes");
+  const size_t need = pnft_flash_bwd_fir_workspace_size(B, H, N, D, flags);
+  if (!workspace || workspace_bytes < need)
+    return fail(PNFT_EINVAL, "flash bwd fir: workspace of %zu bytes < required %zu", workspace_bytes, need);
+  char* ws = static_cast<char*>(workspace);
+  const size_t flash_ws = align256(pnft_flash_bwd_workspace_size(B, H, N, D, flags));
+  void* dkt = ws + flash_ws;                               // d(k~), bf16
+  char* fir_ws = ws + flash_ws + align256((size_t)(B * H * N * D) * 2);
+  int rc = flash_bwd_entry(q, sq, k, sk, v, sv, tau, out, so, out_f32, dout, sdo, stat_m, stat_z, stat_nmax, stat_arg,
+                           dq, sdq, dkt, pl.st, dv, sdv, dtau, workspace, flash_ws, B, H, N, D, scale, gamma,
+                           has_gamma, causal, dtype, flags, status, stream, taps, ntaps);
+  if (rc) return rc;
+  return pnft_fir_bwd(dkt, pl.sg_b, pl.sg_n, 1, taps, ntaps, dk, pl.sdk_b,
+                      pl.sdk_n, 1, dtaps ? k : nullptr, pl.sk_b, pl.sk_n, 1, dtaps, fir_ws,
+                      need - (size_t)(fir_ws - ws), pl.Bf, N, pl.Cf, dtype, stream);
 }

@@ -27,6 +27,10 @@ struct FlashArgs {
   float* dtau;
   int32_t* status;
   uint8_t* tile_flags;  // optional [B*H, nT64, nT64] live-tile record
+  // fused FIR (sm100 kernels only): k is the raw K and the kernels filter each K
+  // tile with these causal taps (fp32[fir_ntaps], index fir_ntaps-1 = lag 0)
+  const float* fir_taps;
+  int fir_ntaps;
   int64_t B, H, N, D;
   float scale, gamma;
   int has_gamma, causal, dtype, flags;

@@ -26,6 +26,7 @@
 
 #include <mutex>
 
+#include "fir_tile.cuh"
 #include "flash.cuh"
 #include "sm100_ptx.cuh"
 
@@ -52,8 +53,15 @@ enum : int {
   B_PFULL = 11,  // [2]
   B_OFULL = 13,
   B_FLAG = 14,  // plain arrive after the o_written flag is stored (release for the flag)
-  B_COUNT = 15
+  B_RAWFULL = 15,   // [2] fused FIR: raw K rows (with halo) landed
+  B_RAWEMPTY = 17,  // [2] fused FIR: raw stage read by the filter warps
+  B_COUNT = 19
 };
+
+// Fused FIR: raw K rows [128 j - FIR_HALO, 128 j + 128) of tile j are staged by TMA
+// and warps 2-3 write K~ = causal_fir(K) rows of the tile into the K stage for the
+// MMA (fir_tile.cuh).
+constexpr int RAW_ROWS = FN + FIR_HALO;
 
 template <int D>
 struct FwdLayout {
@@ -83,6 +91,13 @@ struct FwdLayout {
   static constexpr int END = OFF_REC + (DEFER ? NQW * FM * REC_STRIDE : 0);
   static constexpr int ALLOC = END + 1024;           // slack to align the base to 1024
   static constexpr int SMEM = ALLOC < 116 * 1024 ? 116 * 1024 : ALLOC;  // one CTA per SM (it owns all TMEM)
+  // fused FIR: raw K stages after the rest (1024-aligned for the 128-byte swizzle)
+  static constexpr int RAWGROUP = RAW_ROWS * 128;    // one 64-column group of a raw stage
+  static constexpr int RAWBYTES = (D / 64) * RAWGROUP;
+  static constexpr int NRAW = D == 64 ? 2 : 1;
+  static constexpr int OFF_RAW = (END + 1023) & ~1023;
+  static constexpr int SMEM_FIR = OFF_RAW + NRAW * RAWBYTES + 1024;
+  static_assert(SMEM <= 227 * 1024 && SMEM_FIR <= 227 * 1024, "shared memory budget");
 };
 
 // S buffer s at [128 s, 128 s + 128); warpgroup g's P_hi / P_lo of that tile overwrite
@@ -91,6 +106,8 @@ constexpr uint32_t TM_S = 0, TM_O = 256, TM_COLS = 512;
 
 struct FwdParams {
   CUtensorMap tq, tk, tv;
+  CUtensorMap tkr;    // fused FIR: raw K, RAW_ROWS-row boxes
+  const float* taps;  // fused FIR: fp32[FIR_TAPS], index FIR_TAPS-1 = lag 0
   void* out;
   int64_t so[4];
   float* out32;
@@ -106,7 +123,7 @@ struct FwdParams {
   int has_gamma, causal;
 };
 
-template <int D>
+template <int D, bool FIR>
 __global__ void __launch_bounds__(F_THREADS, 1) flash_fwd_sm100_kernel(const __grid_constant__ FwdParams p) {
   using L = FwdLayout<D>;
   constexpr int DG = D / 64;  // 64-column groups of a row
@@ -128,7 +145,9 @@ __global__ void __launch_bounds__(F_THREADS, 1) flash_fwd_sm100_kernel(const __g
   if (threadIdx.x == 0) {
     mbar_init(bar(B_QFULL), 1);
     for (int i = 0; i < 2; ++i) {
-      mbar_init(bar(B_KFULL + i), 1);
+      mbar_init(bar(B_KFULL + i), FIR ? 2 : 1);  // fused FIR: one arrive per filter warp
+      mbar_init(bar(B_RAWFULL + i), 1);
+      mbar_init(bar(B_RAWEMPTY + i), 2);
       mbar_init(bar(B_KEMPTY + i), 1);
       mbar_init(bar(B_VFULL + i), 1);
       mbar_init(bar(B_VEMPTY + i), 1);
@@ -143,7 +162,7 @@ __global__ void __launch_bounds__(F_THREADS, 1) flash_fwd_sm100_kernel(const __g
   }
   if (warp == 0 && lane == 0) {
     prefetch_tmap(&p.tq);
-    prefetch_tmap(&p.tk);
+    prefetch_tmap(FIR ? &p.tkr : &p.tk);
     prefetch_tmap(&p.tv);
   }
   if (warp == 1) {
@@ -158,6 +177,7 @@ __global__ void __launch_bounds__(F_THREADS, 1) flash_fwd_sm100_kernel(const __g
   const uint32_t sQ = sb0 + L::OFF_Q;
   auto sK = [&](int s) -> uint32_t { return sb0 + L::OFF_K + (uint32_t)s * L::KBYTES; };
   auto sV = [&](int s) -> uint32_t { return sb0 + L::OFF_V + (uint32_t)s * L::VBYTES; };
+  auto sRaw = [&](int s) -> uint32_t { return sb0 + L::OFF_RAW + (uint32_t)s * L::RAWBYTES; };
 
   if (warp == 0) {
     // ------------------------------------------------------------ producer
@@ -166,10 +186,19 @@ __global__ void __launch_bounds__(F_THREADS, 1) flash_fwd_sm100_kernel(const __g
       mbar_arrive_expect_tx(bar(B_QFULL), L::QBYTES);
       for (int g = 0; g < DG; ++g) tma_load_4d(sQ + g * L::GROUP, &p.tq, bar(B_QFULL), 64 * g, q0, hd, b);
       auto issue_k = [&](int j) -> bool {
-        const int s = j & 1;
-        if (!mbar_wait(bar(B_KEMPTY + s), ((j >> 1) & 1) ^ 1, ab)) return false;
-        mbar_arrive_expect_tx(bar(B_KFULL + s), L::KBYTES);
-        for (int g = 0; g < DG; ++g) tma_load_4d(sK(s) + g * L::GROUP, &p.tk, bar(B_KFULL + s), 64 * g, j * FN, hd, b);
+        if constexpr (FIR) {
+          // raw rows [j*FN - RAW_HALO, (j+1)*FN) into a raw stage; the filter warps fill K
+          const int r = j % L::NRAW;
+          if (!mbar_wait(bar(B_RAWEMPTY + r), ((j / L::NRAW) & 1) ^ 1, ab)) return false;
+          mbar_arrive_expect_tx(bar(B_RAWFULL + r), L::RAWBYTES);
+          for (int g = 0; g < DG; ++g)
+            tma_load_4d(sRaw(r) + g * L::RAWGROUP, &p.tkr, bar(B_RAWFULL + r), 64 * g, j * FN - FIR_HALO, hd, b);
+        } else {
+          const int s = j & 1;
+          if (!mbar_wait(bar(B_KEMPTY + s), ((j >> 1) & 1) ^ 1, ab)) return false;
+          mbar_arrive_expect_tx(bar(B_KFULL + s), L::KBYTES);
+          for (int g = 0; g < DG; ++g) tma_load_4d(sK(s) + g * L::GROUP, &p.tk, bar(B_KFULL + s), 64 * g, j * FN, hd, b);
+        }
         k_last = j;
         return true;
       };
@@ -193,7 +222,12 @@ __global__ void __launch_bounds__(F_THREADS, 1) flash_fwd_sm100_kernel(const __g
       }
       // drain: never leave a copy in flight into this CTA's shared memory
       drain_wait(bar(B_QFULL), 0);
-      for (int j = k_last; j >= 0 && j > k_last - 2; --j) drain_wait(bar(B_KFULL + (j & 1)), (j >> 1) & 1);
+      if constexpr (FIR) {
+        for (int j = k_last; j >= 0 && j > k_last - L::NRAW; --j)
+          drain_wait(bar(B_RAWFULL + j % L::NRAW), (j / L::NRAW) & 1);
+      } else {
+        for (int j = k_last; j >= 0 && j > k_last - 2; --j) drain_wait(bar(B_KFULL + (j & 1)), (j >> 1) & 1);
+      }
       for (int j = v_last; j >= 0 && j > v_last - 2; --j) drain_wait(bar(B_VFULL + (j & 1)), (j >> 1) & 1);
     }
   } else if (warp == 1) {
@@ -252,7 +286,29 @@ __global__ void __launch_bounds__(F_THREADS, 1) flash_fwd_sm100_kernel(const __g
       mma_commit(bar(B_OFULL));
       drain_wait(bar(B_OFULL), 0);  // no MMA may still be writing TMEM at teardown
     }
-  } else if (warp >= 4) {
+  } else if (warp < 4) {
+    // ------------------------------------------------------------ fused FIR filter (warps 2-3)
+    if constexpr (FIR) {
+      // 64 threads: column pair ct % 32 of every group, output rows [64 (ct / 32), +64)
+      const int ct = threadIdx.x - 64;
+      float2 h[FIR_TAPS];
+      fir_load_taps(p.taps, h);
+      for (int j = 0; j < ntiles; ++j) {
+        const int r = j % L::NRAW, s = j & 1;
+        if (!warp_wait(bar(B_RAWFULL + r), (j / L::NRAW) & 1, ab)) break;
+        if (!warp_wait(bar(B_KEMPTY + s), ((j >> 1) & 1) ^ 1, ab)) break;  // S of tile j-2 has read stage s
+#pragma unroll
+        for (int g = 0; g < DG; ++g)
+          fir_filter_rows<FN / 2>(sRaw(r) + g * L::RAWGROUP, sK(s) + g * L::GROUP, ct & 31, (ct >> 5) * (FN / 2), h);
+        fence_proxy_async_smem();  // the tensor core reads K through the async proxy
+        __syncwarp();
+        if (lane == 0) {
+          mbar_arrive(bar(B_KFULL + s));
+          mbar_arrive(bar(B_RAWEMPTY + r));
+        }
+      }
+    }
+  } else {
     // ------------------------------------------------------------ elementwise
     const int ew = warp - 4, g = ew >> 2, wq = warp & 3;  // warpgroup g owns key columns [32g, 32g+32)
     const int rl = 32 * wq + lane;  // TMEM lane = local query row
@@ -582,8 +638,16 @@ int flash_fwd_sm100(const FlashArgs& a, cudaStream_t st) {
     kern<<<grid, F_THREADS, smem, st>>>(p);
     return check_launch("flash fwd sm100");
   };
-  if (a.D == 64) return launch(flash_fwd_sm100_kernel<64>, FwdLayout<64>::SMEM);
-  return launch(flash_fwd_sm100_kernel<128>, FwdLayout<128>::SMEM);
+  if (a.fir_taps) {
+    if (a.fir_ntaps != FIR_TAPS) return fail(PNFT_EUNSUPPORTED, "flash fwd sm100: fused FIR needs %d taps", FIR_TAPS);
+    rc = tma_map_bhnd(&p.tkr, a.k, a.sk, a.B, a.H, a.N, a.D, RAW_ROWS);
+    if (rc) return rc;
+    p.taps = a.fir_taps;
+    if (a.D == 64) return launch(flash_fwd_sm100_kernel<64, true>, FwdLayout<64>::SMEM_FIR);
+    return launch(flash_fwd_sm100_kernel<128, true>, FwdLayout<128>::SMEM_FIR);
+  }
+  if (a.D == 64) return launch(flash_fwd_sm100_kernel<64, false>, FwdLayout<64>::SMEM);
+  return launch(flash_fwd_sm100_kernel<128, false>, FwdLayout<128>::SMEM);
 }
 
 }  // namespace pnft

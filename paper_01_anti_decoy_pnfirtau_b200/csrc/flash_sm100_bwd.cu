@@ -36,6 +36,7 @@
 
 #include <type_traits>
 
+#include "fir_tile.cuh"
 #include "flash.cuh"
 #include "sm100_ptx.cuh"
 
@@ -64,7 +65,8 @@ enum : int {
   C_DQEMPTY = 18,  // [2]
   C_DKV = 20,
   C_FLAG = 21,  // plain arrive after dkv_written is stored (release for the flag)
-  C_COUNT = 22
+  C_KRAW = 22,  // fused FIR: raw K rows (with halo) landed
+  C_COUNT = 23
 };
 
 template <int D>
@@ -114,10 +116,19 @@ struct BwdLayout {
     return NSB == 2 ? 128u * (uint32_t)s + 16u * (uint32_t)k : 128u + 32u * (uint32_t)s + 8u * (uint32_t)k;
   }
   static_assert(SMEM <= 227 * 1024, "shared memory budget");
+  // fused FIR: the raw K rows [k0 - FIR_HALO, k0 + BN) are staged in the dS / dQ
+  // staging area, unused until the first tile's elementwise work (which follows
+  // the filtered K through the S MMA)
+  static constexpr int RAWGROUP = (BN + FIR_HALO) * 128;
+  static constexpr int OFF_RAW = OFF_DS;
+  static_assert((D / 64) * RAWGROUP <= OFF_COEF - OFF_DS, "raw K fits the dS / staging area");
+  static_assert(OFF_RAW % 1024 == 0, "swizzle atoms");
 };
 
 struct BwdParams {
   CUtensorMap tk, tv, tq, tdo;
+  CUtensorMap tkr;    // fused FIR: raw K, BN + FIR_HALO rows per box
+  const float* taps;  // fused FIR: fp32[FIR_TAPS], index FIR_TAPS-1 = lag 0
   const float4* coefP;
   const float* tiev;
   const int32_t* argv;
@@ -173,7 +184,7 @@ __device__ __forceinline__ void st_shared_v4(uint32_t addr, uint32_t a, uint32_t
   asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "r"(a), "r"(b), "r"(c), "r"(d) : "memory");
 }
 
-template <int D>
+template <int D, bool FIR>
 __global__ void __launch_bounds__(B_THREADS, 1) flash_bwd_sm100_kernel(const __grid_constant__ BwdParams p) {
   using L = BwdLayout<D>;
   constexpr int DG = D / 64;
@@ -199,7 +210,8 @@ __global__ void __launch_bounds__(B_THREADS, 1) flash_bwd_sm100_kernel(const __g
   auto sdS = [&](int s) -> uint32_t { return sb0 + L::OFF_DS + (uint32_t)s * L::DS_BYTES; };
 
   if (threadIdx.x == 0) {
-    mbar_init(bar(C_KV), 1);
+    mbar_init(bar(C_KV), FIR ? 2 : 1);  // fused FIR: + one arrive once K~ is written
+    mbar_init(bar(C_KRAW), 1);
     mbar_init(bar(C_SDPFULL), 1);
     mbar_init(bar(C_SDPFULL + 1), 1);
     mbar_init(bar(C_SDPEMPTY), 4 * NEW);
@@ -220,7 +232,7 @@ __global__ void __launch_bounds__(B_THREADS, 1) flash_bwd_sm100_kernel(const __g
     fence_barrier_init();
   }
   if (warp == 0 && lane == 0) {
-    prefetch_tmap(&p.tk);
+    prefetch_tmap(FIR ? &p.tkr : &p.tk);
     prefetch_tmap(&p.tv);
     prefetch_tmap(&p.tq);
     prefetch_tmap(&p.tdo);
@@ -237,10 +249,19 @@ __global__ void __launch_bounds__(B_THREADS, 1) flash_bwd_sm100_kernel(const __g
   if (warp == 0) {
     // ------------------------------------------------------------ producer (converged warp, lane 0 issues)
     if (lane == 0) {
-      mbar_arrive_expect_tx(bar(C_KV), 2 * L::KBYTES);
-      for (int g = 0; g < DG; ++g) {
-        tma_load_4d(sK + g * L::KGROUP, &p.tk, bar(C_KV), 64 * g, k0, hd, b);
-        tma_load_4d(sV + g * L::KGROUP, &p.tv, bar(C_KV), 64 * g, k0, hd, b);
+      if constexpr (FIR) {
+        // raw K with its causal halo for the elementwise warps to filter into sK
+        mbar_arrive_expect_tx(bar(C_KRAW), DG * L::RAWGROUP);
+        for (int g = 0; g < DG; ++g)
+          tma_load_4d(sb0 + L::OFF_RAW + g * L::RAWGROUP, &p.tkr, bar(C_KRAW), 64 * g, k0 - FIR_HALO, hd, b);
+        mbar_arrive_expect_tx(bar(C_KV), L::KBYTES);
+        for (int g = 0; g < DG; ++g) tma_load_4d(sV + g * L::KGROUP, &p.tv, bar(C_KV), 64 * g, k0, hd, b);
+      } else {
+        mbar_arrive_expect_tx(bar(C_KV), 2 * L::KBYTES);
+        for (int g = 0; g < DG; ++g) {
+          tma_load_4d(sK + g * L::KGROUP, &p.tk, bar(C_KV), 64 * g, k0, hd, b);
+          tma_load_4d(sV + g * L::KGROUP, &p.tv, bar(C_KV), 64 * g, k0, hd, b);
+        }
       }
     }
     __syncwarp();
@@ -271,6 +292,7 @@ __global__ void __launch_bounds__(B_THREADS, 1) flash_bwd_sm100_kernel(const __g
     }
     if (lane == 0) {
       drain_wait(bar(C_KV), 0);
+      if (FIR) drain_wait(bar(C_KRAW), 0);
       for (int u = t - 1; u >= 0 && u > t - 1 - NQS; --u) drain_wait(bar(C_QDFULL + u % NQS), (u / NQS) & 1);
     }
     __syncwarp();
@@ -393,6 +415,18 @@ __global__ void __launch_bounds__(B_THREADS, 1) flash_bwd_sm100_kernel(const __g
     const int lim = key < p.N ? (p.causal ? key : 0) : 0x7fffffff;  // first valid query of this key
     float2 ds_sum = make_float2(0.f, 0.f);
     bool dead = false;
+    if constexpr (FIR) {
+      // K~ = causal_fir(K) into sK: thread -> (column pair, group, block of rows)
+      constexpr int NB = 128 * NEW / (32 * DG), NR = BN / NB;
+      const int et = threadIdx.x - 128, cp = et & 31, g = (et >> 5) % DG, rb = (et >> 5) / DG;
+      float2 h[FIR_TAPS];
+      fir_load_taps(p.taps, h);
+      dead = !warp_wait(bar(C_KRAW), 0, ab);
+      if (!dead) fir_filter_rows<NR>(sb0 + L::OFF_RAW + g * L::RAWGROUP, sK + g * L::KGROUP, cp, rb * NR, h);
+      fence_proxy_async_smem();  // the tensor core reads K through the async proxy
+      named_bar_sync(3, 128 * NEW);
+      if (et == 0) mbar_arrive(bar(C_KV));
+    }
     int t = 0;
     LiveTiles lt(live, i_first, p.nq64);
     bool multi_tile;
@@ -618,7 +652,13 @@ int flash_bwd_sm100(const FlashArgs& a0, cudaStream_t st) {
   if (rc) return rc;
   BwdParams p;
   memset(&p, 0, sizeof(p));
-  rc = tma_map_bhnd(&p.tk, a.k, a.sk, a.B, a.H, a.N, a.D, BN);
+  if (a.fir_taps) {
+    if (a.fir_ntaps != FIR_TAPS) return fail(PNFT_EUNSUPPORTED, "flash bwd sm100: fused FIR needs %d taps", FIR_TAPS);
+    rc = tma_map_bhnd(&p.tkr, a.k, a.sk, a.B, a.H, a.N, a.D, BN + FIR_HALO);
+    p.taps = a.fir_taps;
+  } else {
+    rc = tma_map_bhnd(&p.tk, a.k, a.sk, a.B, a.H, a.N, a.D, BN);
+  }
   if (!rc) rc = tma_map_bhnd(&p.tv, a.v, a.sv, a.B, a.H, a.N, a.D, BN);
   if (!rc) rc = tma_map_bhnd(&p.tq, a.q, a.sq, a.B, a.H, a.N, a.D, BM);
   if (!rc) rc = tma_map_bhnd(&p.tdo, a.dout, a.sdo, a.B, a.H, a.N, a.D, BM);
@@ -653,8 +693,12 @@ int flash_bwd_sm100(const FlashArgs& a0, cudaStream_t st) {
     kern<<<grid, B_THREADS, smem, st>>>(p);
     return check_launch("flash bwd sm100");
   };
-  rc = a.D == 64 ? launch(flash_bwd_sm100_kernel<64>, BwdLayout<64>::SMEM)
-                 : launch(flash_bwd_sm100_kernel<128>, BwdLayout<128>::SMEM);
+  if (a.fir_taps)
+    rc = a.D == 64 ? launch(flash_bwd_sm100_kernel<64, true>, BwdLayout<64>::SMEM)
+                   : launch(flash_bwd_sm100_kernel<128, true>, BwdLayout<128>::SMEM);
+  else
+    rc = a.D == 64 ? launch(flash_bwd_sm100_kernel<64, false>, BwdLayout<64>::SMEM)
+                   : launch(flash_bwd_sm100_kernel<128, false>, BwdLayout<128>::SMEM);
   if (rc) return rc;
   return flash_bwd_finish(a, st);
 }

@@ -22,7 +22,14 @@ from dataclasses import dataclass
 import torch
 import torch.nn as nn
 
-from .pnfirtau_ops import _flash_bnhd, pn_rows, triton_causal_fir, triton_pn_fir_tau_scores
+from .pnfirtau_ops import (
+    _flash_bnhd,
+    _flash_fir_bnhd,
+    fused_fir_applies,
+    pn_rows,
+    triton_causal_fir,
+    triton_pn_fir_tau_scores,
+)
 
 __all__ = [
     "PnFirConfig",
@@ -167,15 +174,33 @@ class PnFirTauFlashMHA(PnFirTauMHA):
     As in the reference it uses p = 10 and the peak gate regardless of
     ``cfg.p`` / ``cfg.silence_mode`` and applies no attention dropout;
     ``return_weights=True`` takes the row-fused path.
+
+    ``fuse_fir=True`` filters the keys inside the attention kernels' K-tile
+    load (flash_pn_fir_tau_attention_fir) instead of a separate
+    ``triton_causal_fir`` pass, where that path serves the inputs (7 taps,
+    bf16, head dim 64/128); the results are identical (the tile filter is
+    bit-exact), so the choice is purely one of speed.
     """
+
+    def __init__(self, cfg: PnFirConfig, fuse_fir: bool = False):
+        super().__init__(cfg)
+        self.fuse_fir = fuse_fir
 
     def forward(self, x: torch.Tensor, return_weights: bool = False):
         if return_weights:
             return PnFirTauTritonMHA.forward(self, x, return_weights=True)
         cfg = self.cfg
         B, N, _ = x.shape
-        q, k, v = self._qkv_heads(x)
         scale = 1.0 / math.sqrt(self.head_dim)
+        if self.fuse_fir:
+            H, hd = self.n_heads, self.head_dim
+            q_raw, k_raw, v_raw = self.qkv(x).chunk(3, dim=-1)
+            q, k, v = (t.view(B, N, H, hd).transpose(1, 2) for t in (q_raw, k_raw, v_raw))
+            if fused_fir_applies(q, k, v, cfg.fir_k):
+                out = _flash_fir_bnhd(q, k, v, self.score_tau, self.fir_taps, scale, cfg.silence_gamma,
+                                      cfg.causal_mask)
+                return self.out(out.transpose(1, 2).reshape(B, N, -1))
+        q, k, v = self._qkv_heads(x)
         out = _flash_bnhd(q, k, v, self.score_tau, scale, cfg.silence_gamma, cfg.causal_mask)
         out = out.transpose(1, 2).reshape(B, N, -1)
         return self.out(out)

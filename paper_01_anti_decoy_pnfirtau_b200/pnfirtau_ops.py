@@ -388,6 +388,112 @@ def flash_pn_fir_tau_attention(
     return _FlashPnFirTauFn.apply(q, k_tilde, v, score_tau, scale, gamma, causal_mask, "bhnd")
 
 
+class _FlashFirFn(torch.autograd.Function):
+    """Flash attention with the causal FIR on the keys fused into the kernels'
+    K-tile load (pnft_flash_fwd_fir / pnft_flash_bwd_fir): k is the raw key
+    projection; gradients flow to q, k, v, score_tau and, when it requires grad,
+    to the taps."""
+
+    @staticmethod
+    def forward(ctx, q, k, v, score_tau, taps, scale, gamma, causal_mask, out_layout):
+        dev = _require_cuda("flash_pn_fir_tau_attention_fir", q, k, v, score_tau, taps)
+        if not (q.dtype == k.dtype == v.dtype):
+            raise RuntimeError(f"flash_pn_fir_tau_attention_fir: q/k/v dtypes differ ({q.dtype}, {k.dtype}, {v.dtype})")
+        B, H, N, D = q.shape
+        if k.shape != q.shape or v.shape != q.shape:
+            raise RuntimeError(f"flash_pn_fir_tau_attention_fir: q {tuple(q.shape)}, k {tuple(k.shape)}, "
+                               f"v {tuple(v.shape)} must match")
+        if taps.numel() != _lib.FIR_FUSED_TAPS:
+            raise RuntimeError(f"flash_pn_fir_tau_attention_fir: {taps.numel()} taps; the fused filter has "
+                               f"{_lib.FIR_FUSED_TAPS}")
+        if out_layout == "bnhd":
+            out = torch.empty((B, N, H, D), device=dev, dtype=q.dtype).transpose(1, 2)
+        else:
+            out = torch.empty((B, H, N, D), device=dev, dtype=q.dtype)
+        stats = torch.empty((2, B, H, N), device=dev, dtype=torch.float32)
+        nmax = torch.empty((2, B, H, N), device=dev, dtype=torch.int32)
+        tau_f32 = score_tau.detach().to(torch.float32).contiguous()
+        taps_f32 = taps.detach().to(torch.float32).contiguous()
+        has_gamma, gamma_val = _gamma_args(gamma)
+        flags = _flash_flags()
+        needs_grad = any(ctx.needs_input_grad[:5])
+        out32 = torch.empty((B, H, N, D), device=dev, dtype=torch.float32) if needs_grad else None
+        L = _lib.lib()
+        _lib.check(
+            L.pnft_flash_fwd_fir(_ptr(q), _lib.i64x4(q.stride()), _ptr(k), _lib.i64x4(k.stride()), _ptr(taps_f32),
+                                 taps_f32.numel(), _ptr(v), _lib.i64x4(v.stride()), _ptr(tau_f32), _ptr(out),
+                                 _lib.i64x4(out.stride()), _ptr(out32), _ptr(stats[0]), _ptr(stats[1]),
+                                 _ptr(nmax[0]), _ptr(nmax[1]), B, H, N, D, float(scale), gamma_val, has_gamma,
+                                 int(bool(causal_mask)), _dtype_code(q), flags, None, _ptr(_status_word(dev)),
+                                 _stream(dev)),
+            "pnft_flash_fwd_fir",
+        )
+        ctx.save_for_backward(q, k, v, tau_f32, taps_f32, out, out32, stats, nmax)
+        ctx.args = (float(scale), gamma_val, has_gamma, int(bool(causal_mask)), flags)
+        ctx.tau_dtype, ctx.tau_shape = score_tau.dtype, score_tau.shape
+        ctx.taps_dtype, ctx.taps_shape = taps.dtype, taps.shape
+        return out
+
+    @staticmethod
+    def backward(ctx, grad_out):
+        q, k, v, tau_f32, taps_f32, out, out32, stats, nmax = ctx.saved_tensors
+        scale, gamma_val, has_gamma, causal, flags = ctx.args
+        B, H, N, D = q.shape
+        dev = q.device
+        if grad_out.dtype != q.dtype:
+            grad_out = grad_out.to(q.dtype)
+        if grad_out.stride(-1) != 1 or any(s % 8 for s in grad_out.stride()[:3]):
+            grad_out = grad_out.contiguous()
+        dq = torch.empty((B, H, N, D), device=dev, dtype=q.dtype)
+        # dk with k's adjacent axes: (h, d) for the module's [B,N,H*D] view, else (b, h)
+        if H == 1 or k.stride(1) == D:
+            dk = torch.empty((B, N, H, D), device=dev, dtype=k.dtype).transpose(1, 2)
+        else:
+            dk = torch.empty((B, H, N, D), device=dev, dtype=k.dtype)
+        dv = torch.empty((B, H, N, D), device=dev, dtype=v.dtype)
+        dtau = torch.empty((), device=dev, dtype=torch.float32)
+        dtaps = torch.empty(taps_f32.numel(), device=dev, dtype=torch.float32) if ctx.needs_input_grad[4] else None
+        L = _lib.lib()
+        nbytes = L.pnft_flash_bwd_fir_workspace_size(B, H, N, D, flags)
+        ws = torch.empty(max(nbytes, 1), device=dev, dtype=torch.uint8)
+        _lib.check(
+            L.pnft_flash_bwd_fir(_ptr(q), _lib.i64x4(q.stride()), _ptr(k), _lib.i64x4(k.stride()), _ptr(taps_f32),
+                                 taps_f32.numel(), _ptr(v), _lib.i64x4(v.stride()), _ptr(tau_f32), _ptr(out),
+                                 _lib.i64x4(out.stride()), _ptr(out32), _ptr(grad_out),
+                                 _lib.i64x4(grad_out.stride()), _ptr(stats[0]), _ptr(stats[1]), _ptr(nmax[0]),
+                                 _ptr(nmax[1]), _ptr(dq), _lib.i64x4(dq.stride()), _ptr(dk),
+                                 _lib.i64x4(dk.stride()), _ptr(dv), _lib.i64x4(dv.stride()), _ptr(dtau),
+                                 _ptr(dtaps), _ptr(ws), ws.numel(), B, H, N, D, scale, gamma_val, has_gamma, causal,
+                                 _dtype_code(q), flags, _ptr(_status_word(dev)), _stream(dev)),
+            "pnft_flash_bwd_fir",
+        )
+        grad_tau = dtau.to(ctx.tau_dtype).reshape(ctx.tau_shape)
+        grad_taps = dtaps.to(ctx.taps_dtype).reshape(ctx.taps_shape) if dtaps is not None else None
+        return dq, dk, dv, grad_tau, grad_taps, None, None, None, None
+
+
+def flash_pn_fir_tau_attention_fir(
+    q: torch.Tensor,
+    k: torch.Tensor,
+    v: torch.Tensor,
+    score_tau: torch.Tensor,
+    taps: torch.Tensor,
+    scale: float | None = None,
+    gamma: float | None = 0.5,
+    causal_mask: bool = True,
+) -> torch.Tensor:
+    """``flash_pn_fir_tau_attention(q, triton_causal_fir(k, taps), v, ...)`` with
+    the 7-tap causal FIR fused into the attention kernels' K-tile load: each K
+    tile is staged with its 8 preceding rows and filtered in shared memory,
+    bit-identical to ``triton_causal_fir``. ``k`` is the raw key projection
+    ``[B, H, N, D]`` (bf16, head dim 64/128; sm_100a kernels only). Gradients
+    reach ``k`` (through the transposed filter) and ``taps`` when it requires
+    grad. Composition replaced: src/pnfirtau_attention.py:285-316."""
+    if scale is None:
+        scale = 1.0 / math.sqrt(q.shape[-1])
+    return _FlashFirFn.apply(q, k, v, score_tau, taps, scale, gamma, causal_mask, "bhnd")
+
+
 @torch.no_grad()
 def flash_pn_fir_tau_forward_stats(q, k_tilde, v, score_tau, scale=None, gamma=0.5, causal_mask=True,
                                    extra_flags: int = 0):
@@ -423,3 +529,15 @@ def flash_pn_fir_tau_forward_stats(q, k_tilde, v, score_tau, scale=None, gamma=0
 def _flash_bnhd(q, k_tilde, v, score_tau, scale, gamma, causal_mask):
     """Same op; the result's storage is [B,N,H,D] (free transpose back to tokens)."""
     return _FlashPnFirTauFn.apply(q, k_tilde, v, score_tau, scale, gamma, causal_mask, "bnhd")
+
+
+def _flash_fir_bnhd(q, k, v, score_tau, taps, scale, gamma, causal_mask):
+    """flash_pn_fir_tau_attention_fir with the result stored as [B,N,H,D]."""
+    return _FlashFirFn.apply(q, k, v, score_tau, taps, scale, gamma, causal_mask, "bnhd")
+
+
+def fused_fir_applies(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, fir_k: int) -> bool:
+    """Whether flash_pn_fir_tau_attention_fir serves these inputs (7 taps, bf16,
+    head dim 64/128, the sm_100a kernels)."""
+    return (fir_k == _lib.FIR_FUSED_TAPS and q.is_cuda and q.dtype == torch.bfloat16
+            and q.shape[-1] in (64, 128) and flash_kernel_path(q, k, v) == "sm100")

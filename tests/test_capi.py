@@ -107,3 +107,22 @@ def test_rows_rejects_unknown_mode():
     L = _lib.lib()
     rc = L.pnft_rows_fwd(1, 8, 1, 1, 8, 1, 1, 1, 1, 4, 8, 1.0, 10.0, 0.5, 1, 7, 1, _lib.DTYPE_F32, None)
     assert rc == _lib.EINVAL and "silence mode" in _lib.last_error()
+
+
+def test_fused_fir_entry_points_check_arguments():
+    """The fused-FIR entries reject a tap count other than the fused filter's and
+    a null tap pointer on the host, before any device work."""
+    L = _lib.lib()
+    consts = dict(re.findall(r"#define (PNFT_\w+) \(?(-?\w+)\)?", HEADER.read_text()))
+    assert int(consts["PNFT_FIR_FUSED_TAPS"]) == _lib.FIR_FUSED_TAPS == 7
+    s = _lib.i64x4((1, 1, 1, 1))
+    rc = L.pnft_flash_fwd_fir(1, s, 1, s, None, 7, 1, s, 1, 1, s, None, 1, 1, 1, 1, 1, 1, 64, 64, 0.125, 0.5, 1, 1,
+                              _lib.DTYPE_BF16, 0, None, None, None)
+    assert rc == _lib.EINVAL and "taps" in _lib.last_error()
+    rc = L.pnft_flash_bwd_fir(1, s, 1, s, 1, 5, 1, s, 1, 1, s, None, 1, s, 1, 1, 1, 1, 1, s, 1, s, 1, s, 1, None, 1,
+                              1 << 30, 1, 1, 64, 64, 0.125, 0.5, 1, 1, _lib.DTYPE_BF16, 0, None, None)
+    assert rc == _lib.EUNSUPPORTED and "taps" in _lib.last_error()
+    base = L.pnft_flash_bwd_workspace_size(8, 8, 4096, 64, 0)
+    fused = L.pnft_flash_bwd_fir_workspace_size(8, 8, 4096, 64, 0)
+    assert fused >= base + 8 * 8 * 4096 * 64 * 2 and fused % 256 == 0
+    assert L.pnft_flash_bwd_fir_workspace_size(0, 8, 4096, 64, 0) == 0
