@@ -28,37 +28,38 @@ __device__ __forceinline__ void fir_load_taps(const float* taps, float2 (&h)[FIR
   }
 }
 
-// Output rows [r0, r0 + NR) of column pair cp (columns 2cp, 2cp+1) of one group.
-// raw: shared address of the staged group (row i = input row k0 - FIR_HALO + i);
-// dst: shared address of the tile group (row n = output row k0 + n). 32 threads
-// with consecutive cp and the same rows touch one 128-byte row: no bank conflicts.
+// Output rows [r0, r0 + NR) of column pair cp (columns 2cp, 2cp+1) of one group;
+// r0 a multiple of 8. raw: the staged group (row i = input row k0 - FIR_HALO + i);
+// dst: the tile group (row n = output row k0 + n); both shared-memory pointers.
+// 32 threads with consecutive cp and the same rows touch one 128-byte row: no
+// bank conflicts. Fully unrolled: the window rotates by renaming, every row
+// address is a constant offset (r0 is a multiple of the 8-row swizzle period),
+// and plain loads / stores leave the compiler free to run the rows' loads ahead.
 template <int NR>
-__device__ __forceinline__ void fir_filter_rows(uint32_t raw, uint32_t dst, int cp, int r0,
+__device__ __forceinline__ void fir_filter_rows(const uint8_t* raw, uint8_t* dst, int cp, int r0,
                                                 const float2 (&h)[FIR_TAPS]) {
+  static_assert(FIR_HALO % 8 == 0, "row offsets keep the swizzle phase");
   const uint32_t cb = (uint32_t)(cp & 3) * 4u;  // byte inside the 16-byte chunk
   const uint32_t ch = (uint32_t)(cp >> 2);      // 16-byte chunk of the row
-  auto ld = [&](int rr) -> float2 {
-    uint32_t w;
-    asm volatile("ld.shared.b32 %0, [%1];"
-                 : "=r"(w)
-                 : "r"(raw + (uint32_t)rr * 128u + ((ch ^ (uint32_t)(rr & 7)) << 4) + cb));
+  uint32_t col[8];                              // swizzled column offset per row phase
+#pragma unroll
+  for (int i = 0; i < 8; ++i) col[i] = ((ch ^ (uint32_t)i) << 4) + cb;
+  const uint8_t* rb = raw + r0 * 128;
+  uint8_t* db = dst + r0 * 128;
+  auto ld = [&](int rr) -> float2 {  // staged row r0 + rr
+    const uint32_t w = *reinterpret_cast<const uint32_t*>(rb + rr * 128 + col[rr & 7]);
     return make_float2(__uint_as_float(w << 16), __uint_as_float(w & 0xffff0000u));
   };
-  float2 x[FIR_TAPS];  // x[u]: input at lag u of the current output row
+  float2 x[NR + FIR_TAPS - 1];  // x[i] = input row r0 + i - (FIR_TAPS - 1)
 #pragma unroll
-  for (int u = 1; u < FIR_TAPS; ++u) x[u] = ld(r0 + FIR_HALO - u);
-#pragma unroll 4
-  for (int n = r0; n < r0 + NR; ++n) {
-    x[0] = ld(n + FIR_HALO);
-    float2 a = __fmul2_rn(x[0], h[0]);
+  for (int i = 0; i < FIR_TAPS - 1; ++i) x[i] = ld(FIR_HALO - (FIR_TAPS - 1) + i);
 #pragma unroll
-    for (int u = 1; u < FIR_TAPS; ++u) a = __ffma2_rn(x[u], h[u], a);
-    const uint32_t w = pack_bf16x2(a.x, a.y);
-    asm volatile("st.shared.b32 [%0], %1;" ::"r"(dst + (uint32_t)n * 128u + ((ch ^ (uint32_t)(n & 7)) << 4) + cb),
-                 "r"(w)
-                 : "memory");
+  for (int n = 0; n < NR; ++n) {
+    x[n + FIR_TAPS - 1] = ld(n + FIR_HALO);
+    float2 a = __fmul2_rn(x[n + FIR_TAPS - 1], h[0]);
 #pragma unroll
-    for (int u = FIR_TAPS - 1; u > 0; --u) x[u] = x[u - 1];
+    for (int u = 1; u < FIR_TAPS; ++u) a = __ffma2_rn(x[n + FIR_TAPS - 1 - u], h[u], a);
+    *reinterpret_cast<uint32_t*>(db + n * 128 + col[n & 7]) = pack_bf16x2(a.x, a.y);
   }
 }
 

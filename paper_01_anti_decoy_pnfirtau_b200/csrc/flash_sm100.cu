@@ -128,7 +128,8 @@ __global__ void __launch_bounds__(F_THREADS, 1) flash_fwd_sm100_kernel(const __g
   using L = FwdLayout<D>;
   constexpr int DG = D / 64;  // 64-column groups of a row
   extern __shared__ __align__(1024) uint8_t smem_raw[];
-  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  // offset from the __shared__ array itself, so the compiler keeps shared-space accesses
+  uint8_t* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
   const uint32_t sb0 = smem_u32(smem);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   // b*h runs fastest and the query tiles go from the last (longest causal rows)
@@ -299,7 +300,8 @@ __global__ void __launch_bounds__(F_THREADS, 1) flash_fwd_sm100_kernel(const __g
         if (!warp_wait(bar(B_KEMPTY + s), ((j >> 1) & 1) ^ 1, ab)) break;  // S of tile j-2 has read stage s
 #pragma unroll
         for (int g = 0; g < DG; ++g)
-          fir_filter_rows<FN / 2>(sRaw(r) + g * L::RAWGROUP, sK(s) + g * L::GROUP, ct & 31, (ct >> 5) * (FN / 2), h);
+          fir_filter_rows<FN / 2>(smem + L::OFF_RAW + r * L::RAWBYTES + g * L::RAWGROUP,
+                                  smem + L::OFF_K + s * L::KBYTES + g * L::GROUP, ct & 31, (ct >> 5) * (FN / 2), h);
         fence_proxy_async_smem();  // the tensor core reads K through the async proxy
         __syncwarp();
         if (lane == 0) {

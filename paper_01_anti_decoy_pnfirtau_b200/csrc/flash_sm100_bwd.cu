@@ -422,7 +422,7 @@ __global__ void __launch_bounds__(B_THREADS, 1) flash_bwd_sm100_kernel(const __g
       float2 h[FIR_TAPS];
       fir_load_taps(p.taps, h);
       dead = !warp_wait(bar(C_KRAW), 0, ab);
-      if (!dead) fir_filter_rows<NR>(sb0 + L::OFF_RAW + g * L::RAWGROUP, sK + g * L::KGROUP, cp, rb * NR, h);
+      if (!dead) fir_filter_rows<NR>(smem + L::OFF_RAW + g * L::RAWGROUP, smem + L::OFF_K + g * L::KGROUP, cp, rb * NR, h);
       fence_proxy_async_smem();  // the tensor core reads K through the async proxy
       named_bar_sync(3, 128 * NEW);
       if (et == 0) mbar_arrive(bar(C_KV));

@@ -175,14 +175,16 @@ class PnFirTauFlashMHA(PnFirTauMHA):
     ``cfg.p`` / ``cfg.silence_mode`` and applies no attention dropout;
     ``return_weights=True`` takes the row-fused path.
 
-    ``fuse_fir=True`` filters the keys inside the attention kernels' K-tile
-    load (flash_pn_fir_tau_attention_fir) instead of a separate
-    ``triton_causal_fir`` pass, where that path serves the inputs (7 taps,
-    bf16, head dim 64/128); the results are identical (the tile filter is
-    bit-exact), so the choice is purely one of speed.
+    ``fuse_fir`` (default) routes the keys' causal filter through
+    flash_pn_fir_tau_attention_fir where that path serves the inputs (7 taps,
+    bf16, head dim 64/128): the backward filters its key tile inside the
+    attention kernel (no filtered-key tensor is kept for it, no separate
+    filter backward node) and the forward runs one filter pass before the
+    attention kernel. The results equal the unfused path's (the tile filter is
+    bit-exact); ``fuse_fir=False`` keeps the separate ``triton_causal_fir``.
     """
 
-    def __init__(self, cfg: PnFirConfig, fuse_fir: bool = False):
+    def __init__(self, cfg: PnFirConfig, fuse_fir: bool = True):
         super().__init__(cfg)
         self.fuse_fir = fuse_fir
 

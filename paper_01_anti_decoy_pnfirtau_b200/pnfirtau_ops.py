@@ -388,14 +388,31 @@ def flash_pn_fir_tau_attention(
     return _FlashPnFirTauFn.apply(q, k_tilde, v, score_tau, scale, gamma, causal_mask, "bhnd")
 
 
+def _fir_view(t: torch.Tensor):
+    """[B,H,N,D] key tensor as the FIR's [Bf, N, C] (strides, Bf, C): head dims
+    adjacent -> [B, N, H*D]; else b and h adjacent -> [B*H, N, D]."""
+    B, H, N, D = t.shape
+    st = t.stride()
+    if st[3] == 1 and (H == 1 or st[1] == D):
+        return (st[0], st[2], 1), B, H * D
+    if st[3] == 1 and st[0] == H * st[1]:
+        return (st[1], st[2], 1), B * H, D
+    raise RuntimeError(f"flash_pn_fir_tau_attention_fir: key strides {tuple(st)} have neither (h, d) nor (b, h) "
+                       "adjacent")
+
+
 class _FlashFirFn(torch.autograd.Function):
-    """Flash attention with the causal FIR on the keys fused into the kernels'
-    K-tile load (pnft_flash_fwd_fir / pnft_flash_bwd_fir): k is the raw key
-    projection; gradients flow to q, k, v, score_tau and, when it requires grad,
-    to the taps."""
+    """Flash attention on the causally filtered keys k~ = causal_fir(k, taps), k
+    the raw key projection. Backward: pnft_flash_bwd_fir, which filters its K
+    tile in shared memory from k (nothing of k~ is kept) and returns the raw
+    key's gradient and the tap gradient. Forward: by default one standalone
+    filter pass (pnft_fir_fwd) and pnft_flash_fwd on k~; with fused_forward the
+    filter runs in the forward kernel's K-tile load instead (pnft_flash_fwd_fir),
+    which repeats it for every query tile that reads a key tile and is slower.
+    Both forwards give the same k~ bit for bit."""
 
     @staticmethod
-    def forward(ctx, q, k, v, score_tau, taps, scale, gamma, causal_mask, out_layout):
+    def forward(ctx, q, k, v, score_tau, taps, scale, gamma, causal_mask, out_layout, fused_forward=False):
         dev = _require_cuda("flash_pn_fir_tau_attention_fir", q, k, v, score_tau, taps)
         if not (q.dtype == k.dtype == v.dtype):
             raise RuntimeError(f"flash_pn_fir_tau_attention_fir: q/k/v dtypes differ ({q.dtype}, {k.dtype}, {v.dtype})")
@@ -419,15 +436,38 @@ class _FlashFirFn(torch.autograd.Function):
         needs_grad = any(ctx.needs_input_grad[:5])
         out32 = torch.empty((B, H, N, D), device=dev, dtype=torch.float32) if needs_grad else None
         L = _lib.lib()
-        _lib.check(
-            L.pnft_flash_fwd_fir(_ptr(q), _lib.i64x4(q.stride()), _ptr(k), _lib.i64x4(k.stride()), _ptr(taps_f32),
-                                 taps_f32.numel(), _ptr(v), _lib.i64x4(v.stride()), _ptr(tau_f32), _ptr(out),
-                                 _lib.i64x4(out.stride()), _ptr(out32), _ptr(stats[0]), _ptr(stats[1]),
-                                 _ptr(nmax[0]), _ptr(nmax[1]), B, H, N, D, float(scale), gamma_val, has_gamma,
-                                 int(bool(causal_mask)), _dtype_code(q), flags, None, _ptr(_status_word(dev)),
-                                 _stream(dev)),
-            "pnft_flash_fwd_fir",
-        )
+        if fused_forward:
+            _lib.check(
+                L.pnft_flash_fwd_fir(_ptr(q), _lib.i64x4(q.stride()), _ptr(k), _lib.i64x4(k.stride()),
+                                     _ptr(taps_f32), taps_f32.numel(), _ptr(v), _lib.i64x4(v.stride()),
+                                     _ptr(tau_f32), _ptr(out), _lib.i64x4(out.stride()), _ptr(out32),
+                                     _ptr(stats[0]), _ptr(stats[1]), _ptr(nmax[0]), _ptr(nmax[1]), B, H, N, D,
+                                     float(scale), gamma_val, has_gamma, int(bool(causal_mask)), _dtype_code(q),
+                                     flags, None, _ptr(_status_word(dev)), _stream(dev)),
+                "pnft_flash_fwd_fir",
+            )
+        else:
+            (sxb, sxn, sxc), Bf, C = _fir_view(k)
+            # k~ in the layout of k's FIR view, contiguous
+            if C == H * D and (H == 1 or k.stride(1) == D):
+                kt = torch.empty((B, N, H, D), device=dev, dtype=k.dtype).transpose(1, 2)
+                syb, syn = N * H * D, H * D
+            else:
+                kt = torch.empty((B, H, N, D), device=dev, dtype=k.dtype)
+                syb, syn = N * D, D
+            _lib.check(L.pnft_fir_fwd(_ptr(k), sxb, sxn, sxc, _ptr(taps_f32), taps_f32.numel(), _ptr(kt), syb, syn,
+                                      1, Bf, N, C, _dtype_code(k), _stream(dev)), "pnft_fir_fwd")
+            if L.pnft_flash_path(_ptr(q), _lib.i64x4(q.stride()), _ptr(kt), _lib.i64x4(kt.stride()), _ptr(v),
+                                 _lib.i64x4(v.stride()), D, _dtype_code(q), flags) != 1:
+                raise RuntimeError("flash_pn_fir_tau_attention_fir: the sm_100a kernels do not serve these inputs")
+            _lib.check(
+                L.pnft_flash_fwd(_ptr(q), _lib.i64x4(q.stride()), _ptr(kt), _lib.i64x4(kt.stride()), _ptr(v),
+                                 _lib.i64x4(v.stride()), _ptr(tau_f32), _ptr(out), _lib.i64x4(out.stride()),
+                                 _ptr(out32), _ptr(stats[0]), _ptr(stats[1]), _ptr(nmax[0]), _ptr(nmax[1]), B, H, N,
+                                 D, float(scale), gamma_val, has_gamma, int(bool(causal_mask)), _dtype_code(q),
+                                 flags, None, _ptr(_status_word(dev)), _stream(dev)),
+                "pnft_flash_fwd",
+            )
         ctx.save_for_backward(q, k, v, tau_f32, taps_f32, out, out32, stats, nmax)
         ctx.args = (float(scale), gamma_val, has_gamma, int(bool(causal_mask)), flags)
         ctx.tau_dtype, ctx.tau_shape = score_tau.dtype, score_tau.shape
@@ -469,7 +509,7 @@ class _FlashFirFn(torch.autograd.Function):
         )
         grad_tau = dtau.to(ctx.tau_dtype).reshape(ctx.tau_shape)
         grad_taps = dtaps.to(ctx.taps_dtype).reshape(ctx.taps_shape) if dtaps is not None else None
-        return dq, dk, dv, grad_tau, grad_taps, None, None, None, None
+        return dq, dk, dv, grad_tau, grad_taps, None, None, None, None, None
 
 
 def flash_pn_fir_tau_attention_fir(
@@ -481,17 +521,20 @@ def flash_pn_fir_tau_attention_fir(
     scale: float | None = None,
     gamma: float | None = 0.5,
     causal_mask: bool = True,
+    fused_forward: bool = False,
 ) -> torch.Tensor:
     """``flash_pn_fir_tau_attention(q, triton_causal_fir(k, taps), v, ...)`` with
-    the 7-tap causal FIR fused into the attention kernels' K-tile load: each K
-    tile is staged with its 8 preceding rows and filtered in shared memory,
-    bit-identical to ``triton_causal_fir``. ``k`` is the raw key projection
-    ``[B, H, N, D]`` (bf16, head dim 64/128; sm_100a kernels only). Gradients
-    reach ``k`` (through the transposed filter) and ``taps`` when it requires
-    grad. Composition replaced: src/pnfirtau_attention.py:285-316."""
+    the 7-tap causal FIR in the attention kernels' K-tile load: each K tile is
+    staged with its 8 preceding rows and filtered in shared memory, bit-identical
+    to ``triton_causal_fir``. The backward always filters in its kernel (one key
+    tile per CTA); the forward does with ``fused_forward=True``, and otherwise
+    runs one standalone filter pass, which is faster there because every query
+    tile re-reads the key tiles. ``k`` is the raw key projection ``[B, H, N, D]``
+    (bf16, head dim 64/128; sm_100a kernels only). Gradients reach ``k`` and, when
+    it requires grad, ``taps``. Composition replaced: src/pnfirtau_attention.py:285-316."""
     if scale is None:
         scale = 1.0 / math.sqrt(q.shape[-1])
-    return _FlashFirFn.apply(q, k, v, score_tau, taps, scale, gamma, causal_mask, "bhnd")
+    return _FlashFirFn.apply(q, k, v, score_tau, taps, scale, gamma, causal_mask, "bhnd", fused_forward)
 
 
 @torch.no_grad()

@@ -1,8 +1,8 @@
-"""Causal FIR on the keys fused into the tcgen05 kernels' K-tile load
-(flash_pn_fir_tau_attention_fir, pnft_flash_fwd_fir / pnft_flash_bwd_fir)
-against the unfused composition flash(q, triton_causal_fir(k), v) and the fp32
-oracle. The tile filter is bit-exact, so the forward and every gradient but dQ
-(whose cross-CTA accumulation order varies) agree bitwise."""
+"""Causal FIR on the keys in the tcgen05 kernels' K-tile load
+(flash_pn_fir_tau_attention_fir: pnft_flash_bwd_fir always, pnft_flash_fwd_fir
+with fused_forward) against the unfused composition flash(q, triton_causal_fir(k),
+v) and the fp32 oracle. The tile filter is bit-exact, so the forward and every
+gradient but dQ (whose cross-CTA accumulation order varies) agree bitwise."""
 import pytest
 import torch
 
@@ -27,12 +27,12 @@ def _taps(device):
     return O.gaussian_taps(7).to(device)
 
 
-def _run(q, k, v, do, tau, taps, fused):
+def _run(q, k, v, do, tau, taps, fused, fused_forward=False):
     qq, kk, vv = (t.detach().clone().requires_grad_(True) for t in (q, k, v))
     tt = torch.tensor(tau, device=q.device, requires_grad=True)
     hh = taps.detach().clone().requires_grad_(True)
     if fused:
-        out = P.flash_pn_fir_tau_attention_fir(qq, kk, vv, tt, hh)
+        out = P.flash_pn_fir_tau_attention_fir(qq, kk, vv, tt, hh, fused_forward=fused_forward)
     else:
         B, H, N, D = kk.shape
         kt = P.triton_causal_fir(kk.transpose(1, 2).reshape(B, N, H * D), hh).view(B, N, H, D).transpose(1, 2)
@@ -42,14 +42,15 @@ def _run(q, k, v, do, tau, taps, fused):
     return out.detach(), qq.grad, kk.grad, vv.grad, tt.grad, hh.grad
 
 
+@pytest.mark.parametrize("fused_forward", [False, True])
 @pytest.mark.parametrize("D", [64, 128])
 @pytest.mark.parametrize("N,tau", [(128, 0.0), (300, -0.2), (520, 0.3), (70, 0.1)])
-def test_fused_fir_matches_unfused(cuda, D, N, tau):
+def test_fused_fir_matches_unfused(cuda, D, N, tau, fused_forward):
     q, k, v = _module_layout(2, 2, N, D, 11 + N + D, cuda)
     do = torch.randn(q.shape, generator=torch.Generator().manual_seed(N)).to(cuda, torch.bfloat16)
     taps = _taps(cuda)
     assert P.flash_kernel_path(q, k, v) == "sm100"
-    fu = _run(q, k, v, do, tau, taps, fused=True)
+    fu = _run(q, k, v, do, tau, taps, fused=True, fused_forward=fused_forward)
     un = _run(q, k, v, do, tau, taps, fused=False)
     assert torch.equal(fu[0], un[0]), "forward output"
     assert rel_l2(fu[1], un[1]) < 1e-3, ("dq", rel_l2(fu[1], un[1]))
@@ -82,13 +83,14 @@ def test_fused_fir_vs_oracle(cuda, D):
     assert abs(float(ours[4]) - float(tr.grad)) <= 1e-2 * abs(float(tr.grad)) + 1e-6
 
 
-def test_fused_fir_contiguous_keys(cuda):
+@pytest.mark.parametrize("fused_forward", [False, True])
+def test_fused_fir_contiguous_keys(cuda, fused_forward):
     """k as a contiguous [B,H,N,D] tensor (b and h adjacent) also serves."""
     B, H, N, D = 2, 3, 200, 64
     g = torch.Generator().manual_seed(3)
     q, k, v, do = (torch.randn(B, H, N, D, generator=g).to(cuda, torch.bfloat16) for _ in range(4))
     taps = _taps(cuda)
-    fu = _run(q, k, v, do, 0.1, taps, fused=True)
+    fu = _run(q, k, v, do, 0.1, taps, fused=True, fused_forward=fused_forward)
     un = _run(q, k, v, do, 0.1, taps, fused=False)
     assert torch.equal(fu[0], un[0])
     assert torch.equal(fu[2], un[2]) and torch.equal(fu[3], un[3])
@@ -97,8 +99,8 @@ def test_fused_fir_contiguous_keys(cuda):
 def test_module_fuse_fir_is_identical(cuda):
     cfg = P.PnFirConfig(d_model=256, n_heads=4)
     torch.manual_seed(0)
-    m0 = P.PnFirTauFlashMHA(cfg).to(cuda)
-    m1 = P.PnFirTauFlashMHA(cfg, fuse_fir=True).to(cuda)
+    m0 = P.PnFirTauFlashMHA(cfg, fuse_fir=False).to(cuda)
+    m1 = P.PnFirTauFlashMHA(cfg).to(cuda)
     m1.load_state_dict(m0.state_dict())
     x = torch.randn(2, 384, 256, device=cuda)
     outs, grads = [], []
