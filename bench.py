@@ -473,17 +473,28 @@ def bench_reference(args, dist_: Dist) -> dict | None:
     }
 
 
+def _claim_stdout():
+    """Point file descriptor 1 at stderr for the run (NCCL and other native code
+    print banners to stdout) and return a writer on the original stdout, which
+    then carries exactly the one JSON line."""
+    sys.stdout.flush()
+    out = os.fdopen(os.dup(1), "w")
+    os.dup2(2, 1)
+    return out
+
+
 def main():
+    out = _claim_stdout()
     args = parse_args()
     dist_ = Dist()
     if args.impl == "reference":
         res = bench_reference(args, dist_)
         if res is not None:
-            print(json.dumps(res), flush=True)
+            print(json.dumps(res), file=out, flush=True)
         return
     res = bench_ours(args, dist_)
     if dist_.rank == 0:
-        print(json.dumps(res), flush=True)
+        print(json.dumps(res), file=out, flush=True)
     dist_.close()
 
 
