@@ -12,6 +12,7 @@ from dataclasses import dataclass
 
 import torch
 import torch.nn as nn
+import torch.nn.functional as F
 
 from .pnfirtau_attention import PnFirConfig, PnFirTauFlashMHA, PnFirTauMHA, PnFirTauTritonMHA
 
@@ -67,23 +68,38 @@ class PnFirLM(nn.Module):
         self.head = nn.Linear(cfg.d_model, cfg.vocab, bias=False)
         self.head.weight = self.embed.weight
 
-    def forward(self, idx: torch.Tensor) -> torch.Tensor:
+    def forward(self, idx: torch.Tensor, for_loss: bool = False) -> torch.Tensor:
+        """Logits ``[B, N, vocab]``. ``for_loss``: the logits the next-token loss
+        scores, ``[B, N-1, vocab_pad]`` for positions 0..N-2, with the vocabulary
+        padded to a multiple of 64 (the padded logits are -inf, so they add nothing
+        to a softmax): the head GEMM then has 16-byte aligned rows and no slice
+        copy of the logits is needed."""
         B, N = idx.shape
         pos = torch.arange(N, device=idx.device).unsqueeze(0)
         h = self.drop(self.embed(idx) + self.pos(pos))
         for blk in self.blocks:
             h = blk(h)
-        return self.head(self.ln_f(h))
+        h = self.ln_f(h)
+        if not for_loss:
+            return self.head(h)
+        V = self.cfg.vocab
+        Vp = (V + 63) // 64 * 64
+        w = F.pad(self.head.weight, (0, 0, 0, Vp - V))
+        logits = F.linear(h[:, :-1], w)
+        if Vp > V:
+            logits[..., V:] = float("-inf")
+        return logits
 
     def param_count(self) -> int:
         return sum(p.numel() for p in {id(p): p for p in self.parameters()}.values())
 
 
 def lm_loss(model: nn.Module, idx: torch.Tensor) -> torch.Tensor:
-    """Next-token cross-entropy: logits of all N positions, scored on the
-    shifted ids (exp4_wikitext2_lm.py:714-719)."""
-    logits = model(idx)
-    return nn.functional.cross_entropy(logits[:, :-1].reshape(-1, logits.size(-1)), idx[:, 1:].reshape(-1))
+    """Next-token cross-entropy of positions 0..N-2 scored on the shifted ids
+    (exp4_wikitext2_lm.py:714-719, which slices the logits of all N positions:
+    the same loss)."""
+    logits = model(idx, for_loss=True)
+    return nn.functional.cross_entropy(logits.reshape(-1, logits.size(-1)), idx[:, 1:].reshape(-1))
 
 
 def train_step(model: nn.Module, opt: torch.optim.Optimizer, idx: torch.Tensor, clip: float = 1.0) -> torch.Tensor:
