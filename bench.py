@@ -128,7 +128,7 @@ class ClockSampler:
         0x0000000000000100: "display_clock_setting",
     }
 
-    def __init__(self, device: torch.device, period: float = 0.02):
+    def __init__(self, device: torch.device, period: float = 0.005):
         self.period = period
         self.samples: list[tuple[float, int]] = []
         self.max_mhz = None
