@@ -1,19 +1,24 @@
 // sm_100a flash pn_fir_tau kernels: TMA -> shared memory, tcgen05 MMAs with
 // TMEM accumulators, warp-specialised pipelines. bf16 inputs, head dim 64/128.
 //
-// Forward, one CTA per (128 query rows, b*h), 640 threads:
+// Forward, one CTA per (128 query rows, b*h), 320 threads, two CTAs per SM (each
+// holds 256 of the 512 TMEM columns; the two CTAs' tile phases are independent,
+// so one CTA's loads, hand-offs and MMAs overlap the other's elementwise work):
 //   warp 0      TMA producer: Q once; K and V tile j+1 while tile j is computed.
-//   warp 1      MMA issuer and TMEM owner: S_j = Q K_j^T (SS, M=N=128) into one
-//               of two S buffers; O += P_j V_j (TS: P read from TMEM) for the live
-//               32-key quarters only.
-//   warps 4-19  four elementwise warpgroups; warpgroup g owns key columns
-//               [32g, 32g+32) of every tile, thread = TMEM lane = query row:
+//   warp 1      MMA issuer and TMEM owner: S_j = Q K_j^T (SS, M=128, N=64) into
+//               one of two S buffers; O += P_j V_j (TS: P read from TMEM) for the
+//               live 32-key column blocks only.
+//   warps 2-9   two elementwise groups of four warps (every group covers the four
+//               TMEM lane quadrants, warp % 4); group g owns key columns
+//               [32g, 32g+32) of every 64-key tile, thread = TMEM lane = query row:
 //               s = S*scale - tau (packed f32x2 FMA, rounded once), u = max(s, 0),
 //               row max via 3-input max, per-warp silent vote, u^10 by repeated
 //               squaring (no exp), running peak / tie count / argmax / mass, and
 //               P = u^10 split into two bf16 terms P_hi + P_lo written back over
 //               the tile's own S columns in TMEM for the two PV MMAs.
-// TMEM: S/P buffers [0,128) and [128,256), O [256, 256+D).
+// TMEM (256 columns per CTA): S/P buffers [0,64) and [64,128), O [128, 128+D).
+// With the fused FIR, warps 2-3 filter the K tiles (fir_tile.cuh), the
+// elementwise warps are 4-11 and the CTA runs alone on its SM.
 // Epilogue: O * gate/(mass + 1e-12) with gate = peak/(peak+gamma), stats M, Z,
 // Nmax, argmax.
 // Semantics follow src/triton_pnfirtau.py:313-443 (the reference skips 64x64
@@ -37,10 +42,13 @@ using namespace sm100;
 namespace {
 
 constexpr int FM = 128;  // query rows per CTA (TMEM lanes)
-constexpr int FN = 128;  // keys per tile
-constexpr int FQ = 32;                  // key columns per elementwise warpgroup
-constexpr int NQW = FN / FQ;            // elementwise warpgroups (4)
-constexpr int F_THREADS = 128 * (1 + NQW);
+constexpr int FN = 64;   // keys per tile
+constexpr int FQ = 32;                  // key columns per elementwise group
+constexpr int NQW = FN / FQ;            // elementwise groups of four warps (2)
+// warp 0 producer, warp 1 MMA issuer, elementwise warps from EW0 on (with the
+// fused FIR, warps 2-3 filter K and the elementwise warps start at 4)
+template <bool FIR> constexpr int ew0() { return FIR ? 4 : 2; }
+template <bool FIR> constexpr int f_threads() { return 32 * ew0<FIR>() + 128 * NQW; }
 
 // barrier slots
 enum : int {
@@ -65,7 +73,8 @@ constexpr int RAW_ROWS = FN + FIR_HALO;
 
 template <int D>
 struct FwdLayout {
-  static constexpr int GROUP = FM * 128;            // bytes of one 64-column (128 B) group of a 128-row tile
+  static constexpr int GROUP = FM * 128;            // bytes of one 64-column (128 B) group of a Q tile
+  static constexpr int KGROUP = FN * 128;           // same for a K / V tile
   static constexpr int QBYTES = FM * D * 2;
   static constexpr int KBYTES = FN * D * 2;
   static constexpr int VBYTES = FN * D * 2;
@@ -76,21 +85,22 @@ struct FwdLayout {
   static constexpr int OFF_TMEM = OFF_BAR + B_COUNT * 8;
   static constexpr int OFF_ABORT = OFF_TMEM + 4;
   static constexpr int OFF_OWR = OFF_ABORT + 4;
-  // u8 [2 buf][4 quarters][4 warps]: one word per quarter, nonzero when any warp saw a live row
+  // u8 [2 buf][NQW column groups][4 warps]: one word per group, nonzero when any warp saw a live row
   static constexpr int OFF_VPART = OFF_OWR + 8;
-  static constexpr int OFF_STATS = OFF_VPART + 2 * NQW * 4;  // float [4 quarters][4][128]: peak, mass, count, argmax
-  // float4 per row (16-byte aligned for the vector loads): running peaks of the four quarters
+  static constexpr int OFF_STATS = OFF_VPART + 2 * NQW * 4;  // float [NQW][4][128]: peak, mass, count, argmax
+  // float4 per row (16-byte aligned for the vector loads): running peaks of the column groups
+  // (slots past NQW stay zero)
   static constexpr int OFF_RPK = (OFF_STATS + NQW * 4 * FM * 4 + 15) & ~15;
   static_assert(OFF_RPK % 16 == 0, "float4 rows need 16-byte alignment");
   // d=64 only (d=128 has no room): per elementwise lane the 32 s-values of the tile
-  // that set its quarter's peak, rows 144 B apart (conflict-free 16-byte stores)
+  // that set its column block's peak, rows 144 B apart (conflict-free 16-byte stores)
   static constexpr bool DEFER = D == 64;
   static constexpr int REC_STRIDE = 144;
-  static constexpr int OFF_REC = OFF_RPK + FM * NQW * 4;
+  static constexpr int OFF_REC = OFF_RPK + FM * 16;
   static_assert(OFF_REC % 16 == 0, "16-byte rows");
   static constexpr int END = OFF_REC + (DEFER ? NQW * FM * REC_STRIDE : 0);
   static constexpr int ALLOC = END + 1024;           // slack to align the base to 1024
-  static constexpr int SMEM = ALLOC < 116 * 1024 ? 116 * 1024 : ALLOC;  // one CTA per SM (it owns all TMEM)
+  static constexpr int SMEM = ALLOC;  // two CTAs per SM, 256 TMEM columns each
   // fused FIR: raw K stages after the rest (1024-aligned for the 128-byte swizzle)
   static constexpr int RAWGROUP = RAW_ROWS * 128;    // one 64-column group of a raw stage
   static constexpr int RAWBYTES = (D / 64) * RAWGROUP;
@@ -100,9 +110,10 @@ struct FwdLayout {
   static_assert(SMEM <= 227 * 1024 && SMEM_FIR <= 227 * 1024, "shared memory budget");
 };
 
-// S buffer s at [128 s, 128 s + 128); warpgroup g's P_hi / P_lo of that tile overwrite
-// its own S columns [128 s + 64 g, +32) / [+32, +32) once they are in registers.
-constexpr uint32_t TM_S = 0, TM_O = 256, TM_COLS = 512;
+// S buffer s at [FN s, FN s + FN); group g's P_hi / P_lo of that tile overwrite its
+// own S columns [FN s + 32 g, +16) / [+16, +16) once they are in registers.
+constexpr uint32_t TM_S = 0, TM_O = 2 * FN, TM_COLS = 256;
+static_assert(TM_O + 128 <= TM_COLS, "TMEM budget (d <= 128)");
 
 struct FwdParams {
   CUtensorMap tq, tk, tv;
@@ -118,13 +129,13 @@ struct FwdParams {
   uint8_t* tile_flags;
   const float* tau;
   int32_t* status;
-  int H, N, nq;
+  int H, N, nq, nk;
   float scale, gamma;
   int has_gamma, causal;
 };
 
 template <int D, bool FIR>
-__global__ void __launch_bounds__(F_THREADS, 1) flash_fwd_sm100_kernel(const __grid_constant__ FwdParams p) {
+__global__ void __launch_bounds__(f_threads<FIR>(), FIR ? 1 : 2) flash_fwd_sm100_kernel(const __grid_constant__ FwdParams p) {
   using L = FwdLayout<D>;
   constexpr int DG = D / 64;  // 64-column groups of a row
   extern __shared__ __align__(1024) uint8_t smem_raw[];
@@ -137,7 +148,7 @@ __global__ void __launch_bounds__(F_THREADS, 1) flash_fwd_sm100_kernel(const __g
   const int qt = p.nq - 1 - (int)blockIdx.y;
   const int bh = blockIdx.x, b = bh / p.H, hd = bh % p.H;
   const int q0 = qt * FM;
-  const int ntiles = p.causal ? qt + 1 : p.nq;
+  const int ntiles = p.causal ? min(p.nk, (q0 + FM + FN - 1) / FN) : p.nk;
   auto bar = [&](int i) -> uint32_t { return sb0 + L::OFF_BAR + 8u * (uint32_t)i; };
   volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + L::OFF_ABORT);
   volatile uint8_t* vpart = smem + L::OFF_VPART;
@@ -170,7 +181,7 @@ __global__ void __launch_bounds__(F_THREADS, 1) flash_fwd_sm100_kernel(const __g
     tmem_alloc(sb0 + L::OFF_TMEM, TM_COLS);
     tmem_relinquish();
   }
-  for (int i = threadIdx.x; i < FM * NQW; i += F_THREADS) reinterpret_cast<float*>(smem + L::OFF_RPK)[i] = 0.f;
+  for (int i = threadIdx.x; i < FM * 4; i += blockDim.x) reinterpret_cast<float*>(smem + L::OFF_RPK)[i] = 0.f;
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
@@ -198,7 +209,7 @@ __global__ void __launch_bounds__(F_THREADS, 1) flash_fwd_sm100_kernel(const __g
           const int s = j & 1;
           if (!mbar_wait(bar(B_KEMPTY + s), ((j >> 1) & 1) ^ 1, ab)) return false;
           mbar_arrive_expect_tx(bar(B_KFULL + s), L::KBYTES);
-          for (int g = 0; g < DG; ++g) tma_load_4d(sK(s) + g * L::GROUP, &p.tk, bar(B_KFULL + s), 64 * g, j * FN, hd, b);
+          for (int g = 0; g < DG; ++g) tma_load_4d(sK(s) + g * L::KGROUP, &p.tk, bar(B_KFULL + s), 64 * g, j * FN, hd, b);
         }
         k_last = j;
         return true;
@@ -210,9 +221,9 @@ __global__ void __launch_bounds__(F_THREADS, 1) flash_fwd_sm100_kernel(const __g
         const int s = j & 1;
         if (!mbar_wait(bar(B_VEMPTY + s), ((j >> 1) & 1) ^ 1, ab)) return false;
         mbar_arrive_expect_tx(bar(B_VFULL + s), L::VBYTES);
-        for (int hh = 0; hh < 2; ++hh)
+        for (int hh = 0; hh < FN / 64; ++hh)
           for (int g = 0; g < DG; ++g)
-            tma_load_4d(sV(s) + g * L::GROUP + hh * (L::GROUP / 2), &p.tv, bar(B_VFULL + s), 64 * g,
+            tma_load_4d(sV(s) + g * L::KGROUP + hh * 64 * 128, &p.tv, bar(B_VFULL + s), 64 * g,
                         j * FN + 64 * hh, hd, b);
         v_last = j;
         return true;
@@ -245,8 +256,8 @@ __global__ void __launch_bounds__(F_THREADS, 1) flash_fwd_sm100_kernel(const __g
         tc_fence_after();
 #pragma unroll
         for (int kk = 0; kk < D / 16; ++kk) {
-          const uint32_t off = (kk >> 2) * L::GROUP + (kk & 3) * 32;
-          mma_ss(tmem + TM_S + 128u * s, sw128_desc(sQ + off, 16), sw128_desc(sK(s) + off, 16), ID_S,
+          const uint32_t off = (kk >> 2) * L::GROUP + (kk & 3) * 32, koff = (kk >> 2) * L::KGROUP + (kk & 3) * 32;
+          mma_ss(tmem + TM_S + (uint32_t)FN * s, sw128_desc(sQ + off, 16), sw128_desc(sK(s) + koff, 16), ID_S,
                  kk > 0);
         }
         mma_commit(bar(B_SFULL + s));
@@ -259,13 +270,13 @@ __global__ void __launch_bounds__(F_THREADS, 1) flash_fwd_sm100_kernel(const __g
         if (!mbar_wait(bar(B_VFULL + s), (j >> 1) & 1, ab)) return false;
         tc_fence_after();
         for (int g = 0; g < NQW; ++g) {
-          // the four warps' votes of this quarter, published before their PFULL arrives
+          // the four warps' votes of this column block, published before their PFULL arrives
           if (!reinterpret_cast<volatile const uint32_t*>(vpart)[s * NQW + g]) continue;  // silent: P is zero
 #pragma unroll
           for (int kq = 0; kq < FQ / 16; ++kq) {
             const int kk = g * (FQ / 16) + kq;  // 16 keys per MMA
-            const uint32_t a_hi = tmem + TM_S + 128u * s + (uint32_t)FQ * g + 8u * kq;
-            const uint32_t bdesc = sw128_desc(sV(s) + kk * 2048, L::GROUP);
+            const uint32_t a_hi = tmem + TM_S + (uint32_t)FN * s + (uint32_t)FQ * g + 8u * kq;
+            const uint32_t bdesc = sw128_desc(sV(s) + kk * 2048, L::KGROUP);
             mma_ts(tmem + TM_O, a_hi, bdesc, ID_O, o_acc);             // O += P_hi V
             mma_ts(tmem + TM_O, a_hi + FQ / 2, bdesc, ID_O, 1u);       // O += P_lo V
             o_acc = 1;
@@ -287,7 +298,7 @@ __global__ void __launch_bounds__(F_THREADS, 1) flash_fwd_sm100_kernel(const __g
       mma_commit(bar(B_OFULL));
       drain_wait(bar(B_OFULL), 0);  // no MMA may still be writing TMEM at teardown
     }
-  } else if (warp < 4) {
+  } else if (warp < ew0<FIR>()) {
     // ------------------------------------------------------------ fused FIR filter (warps 2-3)
     if constexpr (FIR) {
       // 64 threads: column pair ct % 32 of every group, output rows [64 (ct / 32), +64)
@@ -301,7 +312,7 @@ __global__ void __launch_bounds__(F_THREADS, 1) flash_fwd_sm100_kernel(const __g
 #pragma unroll
         for (int g = 0; g < DG; ++g)
           fir_filter_rows<FN / 2>(smem + L::OFF_RAW + r * L::RAWBYTES + g * L::RAWGROUP,
-                                  smem + L::OFF_K + s * L::KBYTES + g * L::GROUP, ct & 31, (ct >> 5) * (FN / 2), h);
+                                  smem + L::OFF_K + s * L::KBYTES + g * L::KGROUP, ct & 31, (ct >> 5) * (FN / 2), h);
         fence_proxy_async_smem();  // the tensor core reads K through the async proxy
         __syncwarp();
         if (lane == 0) {
@@ -312,7 +323,7 @@ __global__ void __launch_bounds__(F_THREADS, 1) flash_fwd_sm100_kernel(const __g
     }
   } else {
     // ------------------------------------------------------------ elementwise
-    const int ew = warp - 4, g = ew >> 2, wq = warp & 3;  // warpgroup g owns key columns [32g, 32g+32)
+    const int ew = warp - ew0<FIR>(), g = ew >> 2, wq = warp & 3;  // group g owns key columns [32g, 32g+32)
     const int rl = 32 * wq + lane;  // TMEM lane = local query row
     const int row = q0 + rl;
     const uint32_t lane_off = (uint32_t)(32 * wq) << 16;
@@ -324,22 +335,22 @@ __global__ void __launch_bounds__(F_THREADS, 1) flash_fwd_sm100_kernel(const __g
     const float2 sc2 = make_float2(0.5f * p.scale, 0.5f * p.scale), nt2 = make_float2(-0.5f * tau, -0.5f * tau);
     const int nT64 = (p.N + 63) >> 6;
     float peak = 0.f, cnt = 0.f;
-    int arg = -1;  // first key attaining the running peak in this quarter
+    int arg = -1;  // first key attaining the running peak in this column block
     // deferred search (d=64): the tile that set the peak is saved; `arg` holds its
     // first key and `cnt` counts only the maxima of later tiles equal to the peak
     float* rec = reinterpret_cast<float*>(smem + L::OFF_REC + (g * FM + rl) * L::REC_STRIDE);
-    // running peaks of this row's four quarters; a quarter whose tile maximum is
+    // running peaks of this row's column groups; a group whose tile maximum is
     // below the row's best so far can never hold the row maximum, so it skips the
     // per-column search (the estimate may lag: that only costs extra searches)
     float4* rpk = reinterpret_cast<float4*>(smem + L::OFF_RPK) + rl;  // zeroed before the first __syncthreads
     float2 ms[2] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f)};  // mass partial sums
     // `dead` (warp-uniform) turns the rest of the loop into no-ops after an
-    // abort, while every warp still passes the warpgroup's named barriers.
+    // abort, while every warp still passes the named barriers.
     bool dead = false;
     for (int j = 0; j < ntiles; ++j) {
       const int s = j & 1;
       if (!dead) dead = !warp_wait(bar(B_SFULL + s), (j >> 1) & 1, ab);
-      const uint32_t scol = tmem + lane_off + TM_S + 128u * s + (uint32_t)FQ * g;
+      const uint32_t scol = tmem + lane_off + TM_S + (uint32_t)FN * s + (uint32_t)FQ * g;
       uint32_t r[32];
       if (!dead) {
         tc_fence_after();
@@ -364,8 +375,8 @@ __global__ void __launch_bounds__(F_THREADS, 1) flash_fwd_sm100_kernel(const __g
       for (int c = 3; c < 31; c += 2) m = max3(m, x[c], x[c + 1]);
       m = fmaxf(m, x[31]);
       // silent vote of this warp's 32 rows; the MMA issuer ORs the four warps of
-      // the quarter after PFULL completes (no barrier between the warps). A silent
-      // warp writes zeros: another warp's rows may keep the quarter live.
+      // the column block after PFULL completes (no barrier between the warps). A silent
+      // warp writes zeros: another warp's rows may keep the column block live.
       const unsigned live_w = __any_sync(0xffffffffu, m > 0.f);
       if (lane == 0) {
         vpart[(s * NQW + g) * 4 + wq] = live_w ? 1 : 0;
@@ -375,7 +386,7 @@ __global__ void __launch_bounds__(F_THREADS, 1) flash_fwd_sm100_kernel(const __g
         }
       }
       if (live_w && !dead) {
-        const float mu = m > 0.f ? m : 0.f;  // row max of u/2 over this quarter of the tile
+        const float mu = m > 0.f ? m : 0.f;  // row max of u/2 over this column block of the tile
         const float4 rp4 = *rpk;
         const float row_best = fmaxf(fmaxf(rp4.x, rp4.y), fmaxf(rp4.z, rp4.w));
         if (mu > 0.f && mu >= fmaxf(peak, row_best)) {
@@ -402,7 +413,7 @@ __global__ void __launch_bounds__(F_THREADS, 1) flash_fwd_sm100_kernel(const __g
         // backward's <dO,O>/gate, stays fp32-accurate; the tau gradient is a small
         // residual of cancelling per-row sums and needs that accuracy
         // Two halves of 16 columns, each stored as soon as it is packed (fewer live
-        // registers): P_hi / P_lo over this warpgroup's own S columns
+        // registers): P_hi / P_lo over this group's own S columns
         // [32g + 8hh, +8) / [32g + 16 + 8hh, +8).
         const float2 neg1 = make_float2(-1.f, -1.f);
 #pragma unroll
@@ -438,7 +449,7 @@ __global__ void __launch_bounds__(F_THREADS, 1) flash_fwd_sm100_kernel(const __g
       if (lane == 0) mbar_arrive(bar(B_PFULL + s));
     }
     if (L::DEFER && peak > 0.f) {
-      // search of the saved tile: its maximum equals the quarter's peak
+      // search of the saved tile: its maximum equals the column block's peak
       uint32_t mk = 0u;
 #pragma unroll
       for (int k = 0; k < 8; ++k) {
@@ -451,7 +462,7 @@ __global__ void __launch_bounds__(F_THREADS, 1) flash_fwd_sm100_kernel(const __g
       cnt += (float)__popc(mk);
       arg += __ffs(mk) - 1;
     }
-    // ---- epilogue: merge the four column quarters of every row, scale O, store
+    // ---- epilogue: merge the column groups of every row, scale O, store
     float* st = reinterpret_cast<float*>(smem + L::OFF_STATS);
     const float mass_q = (ms[0].x + ms[0].y) + (ms[1].x + ms[1].y);
     st[(g * 4 + 0) * FM + rl] = peak;
@@ -465,8 +476,8 @@ __global__ void __launch_bounds__(F_THREADS, 1) flash_fwd_sm100_kernel(const __g
       pk = fmaxf(pk, st[(q * 4 + 0) * FM + rl]);
       mass += st[(q * 4 + 1) * FM + rl];
     }
-    // first key of the row maximum: each quarter kept its earliest key (an earlier
-    // tile wins a tie), so the smallest key over the quarters holding the maximum
+    // first key of the row maximum: each column block kept its earliest key (an earlier
+    // tile wins a tie), so the smallest key over the column blocks holding the maximum
     float nm = 0.f;
     int amax = -1;
     if (pk > 0.f) {
@@ -490,7 +501,7 @@ __global__ void __launch_bounds__(F_THREADS, 1) flash_fwd_sm100_kernel(const __g
     __nv_bfloat16* O = static_cast<__nv_bfloat16*>(p.out) + (int64_t)b * p.so[0] + (int64_t)hd * p.so[1] +
                        (int64_t)row * p.so[2];
 #pragma unroll
-    for (int cb = 0; cb < D / NQW; cb += 16) {  // warpgroup g writes head dims [g*D/4, (g+1)*D/4)
+    for (int cb = 0; cb < D / NQW; cb += 16) {  // group g writes head dims [g*D/NQW, (g+1)*D/NQW)
       const int d0 = g * (D / NQW) + cb;
       uint32_t r[16];
       if (o_written) {
@@ -613,7 +624,7 @@ int flash_fwd_sm100(const FlashArgs& a, cudaStream_t st) {
   memset(&p, 0, sizeof(p));
   int rc = tma_map_bhnd(&p.tq, a.q, a.sq, a.B, a.H, a.N, a.D, FM);
   if (!rc) rc = tma_map_bhnd(&p.tk, a.k, a.sk, a.B, a.H, a.N, a.D, FN);
-  if (!rc) rc = tma_map_bhnd(&p.tv, a.v, a.sv, a.B, a.H, a.N, a.D, FN / 2);
+  if (!rc) rc = tma_map_bhnd(&p.tv, a.v, a.sv, a.B, a.H, a.N, a.D, 64);
   if (rc) return rc;
   p.out = a.out;
   for (int i = 0; i < 4; ++i) p.so[i] = a.so[i];
@@ -628,6 +639,7 @@ int flash_fwd_sm100(const FlashArgs& a, cudaStream_t st) {
   p.H = (int)a.H;
   p.N = (int)a.N;
   p.nq = (int)((a.N + FM - 1) / FM);
+  p.nk = (int)((a.N + FN - 1) / FN);
   p.scale = a.scale;
   p.gamma = a.gamma;
   p.has_gamma = a.has_gamma;
@@ -637,7 +649,7 @@ int flash_fwd_sm100(const FlashArgs& a, cudaStream_t st) {
   auto launch = [&](auto kern, int smem) -> int {
     if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess)
       return check_launch("flash fwd sm100: smem attribute", 0);
-    kern<<<grid, F_THREADS, smem, st>>>(p);
+    kern<<<grid, a.fir_taps ? f_threads<true>() : f_threads<false>(), smem, st>>>(p);
     return check_launch("flash fwd sm100");
   };
   if (a.fir_taps) {
