@@ -409,7 +409,8 @@ __global__ void __launch_bounds__(f_threads<FIR>(), FIR ? 1 : 2) flash_fwd_sm100
           peak = mu;
           reinterpret_cast<float*>(rpk)[g] = peak;
         }
-        // P = u^10 as P_hi + P_lo (two bf16 terms, ~2^-17 relative): O, and with it the
+        // P = u^10 as P_hi + P_lo (two bf16 terms: P_hi truncated, P_lo = P - P_hi exact
+        // then rounded, ~2^-17 relative): O, and with it the
         // backward's <dO,O>/gate, stays fp32-accurate; the tau gradient is a small
         // residual of cancelling per-row sums and needs that accuracy
         // Two halves of 16 columns, each stored as soon as it is packed (fewer live
@@ -427,8 +428,10 @@ __global__ void __launch_bounds__(f_threads<FIR>(), FIR ? 1 : 2) flash_fwd_sm100
             const float2 u2 = __fmul2_rn(u, u), u4 = __fmul2_rn(u2, u2);
             const float2 pw = __fmul2_rn(__fmul2_rn(u4, u4), u2);
             ms[c & 1] = __fadd2_rn(ms[c & 1], pw);
-            hi[cc] = pack_bf16x2(pw.x, pw.y);
-            const float2 hf = make_float2(__uint_as_float(hi[cc] << 16), __uint_as_float(hi[cc] & 0xffff0000u));
+            // P_hi = P truncated to bf16 (its low 16 bits cleared), packed by one byte permute
+            const uint32_t bx = __float_as_uint(pw.x), by = __float_as_uint(pw.y);
+            hi[cc] = __byte_perm(bx, by, 0x7632);
+            const float2 hf = make_float2(__uint_as_float(bx & 0xffff0000u), __uint_as_float(by & 0xffff0000u));
             const float2 lf = __ffma2_rn(hf, neg1, pw);  // exact: pw - hi
             lo[cc] = pack_bf16x2(lf.x, lf.y);
           }
