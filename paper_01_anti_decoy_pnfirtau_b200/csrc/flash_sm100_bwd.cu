@@ -77,6 +77,9 @@ struct BwdLayout {
   static constexpr int KBYTES = BN * D * 2;
   static constexpr int QBYTES = BM * D * 2;
   static constexpr int NDQ = D == 64 ? 2 : 1;   // dQ buffers in TMEM
+  // D=64: dQ^T of two consecutive tiles in one MMA sequence (N = 128 queries from two
+  // adjacent dS tiles), accumulated in the NDQ * 64 columns as one buffer
+  static constexpr bool DQ_PAIR = D == 64;
   static constexpr int NSTG = D == 64 ? 2 : 1;  // dQ staging tiles in smem
   static constexpr int STG_BYTES = BM * D * 4;
   static constexpr int DS_BYTES = BN * BM * 2;
@@ -301,6 +304,7 @@ __global__ void __launch_bounds__(B_THREADS, 1) flash_bwd_sm100_kernel(const __g
     constexpr uint32_t ID_S = idesc_f16(BN, BM, 1, 0, 0);   // S^T, dP^T: K-major A and B
     constexpr uint32_t ID_G = idesc_f16(BN, D, 1, 0, 1);    // dV (A in TMEM), dK (A K-major); B MN-major
     constexpr uint32_t ID_DQ = idesc_f16(D, BM, 1, 1, 1);   // dQ^T: M = head dims
+    constexpr uint32_t ID_DQ2 = idesc_f16(D, 2 * BM, 1, 1, 1);  // dQ^T of a tile pair (N = 128)
     // Descriptors of k-step 0; a k-step moves +32 B inside a 128-byte K-major row
     // (+2 in descriptor units, +GROUP bytes across 64-column groups) or +16 rows
     // (2048 B, +128) of an MN-major tile.
@@ -346,6 +350,26 @@ __global__ void __launch_bounds__(B_THREADS, 1) flash_bwd_sm100_kernel(const __g
       __syncwarp();
       return true;
     };
+    // dQ^T of tiles u and u+1 (u even; `two` false for a last tile alone): the
+    // dS tiles u % NDS and u % NDS + 1 are adjacent, one 64-query atom apart, so the
+    // MN-major descriptor of tile u spans both (its atom stride is the dS tile size)
+    auto dq_pair = [&](int u, bool two) -> bool {
+      const int ds = u % L::NDS;
+      if (!warp_wait(bar(C_DQEMPTY), ((u >> 1) & 1) ^ 1, ab)) return false;
+      tc_fence_after();
+      if (elect_one()) {
+        const uint32_t id = two ? ID_DQ2 : ID_DQ;
+#pragma unroll
+        for (int kk = 0; kk < BN / 16; ++kk)
+          mma_ss(tmem + L::TM_DQ, dKmn + kk * 128, dSmn + ds * DSSTEP + kk * 128, id, kk > 0);
+        mma_commit(bar(C_DQFULL));
+        mma_commit(bar(C_PDSEMPTY + ds));
+        if (two) mma_commit(bar(C_PDSEMPTY + ds + 1));
+      }
+      __syncwarp();
+      return true;
+    };
+    static_assert(!L::DQ_PAIR || (L::NDS % 2 == 0 && L::DS_BYTES == L::KGROUP), "tile pairs in adjacent dS tiles");
     auto dq = [&](int u) -> bool {
       const int ds = u % L::NDS, bq = u % L::NDQ;
       if (!warp_wait(bar(C_DQEMPTY + bq), ((u / L::NDQ) & 1) ^ 1, ab)) return false;
@@ -383,7 +407,14 @@ __global__ void __launch_bounds__(B_THREADS, 1) flash_bwd_sm100_kernel(const __g
           if (!(ok = issue_sdp(j + 2))) break;
           t = j + 3;
         }
-        if (!(ok = dq(j))) break;
+        if constexpr (L::DQ_PAIR) {
+          if ((j & 1) && !(ok = dq_pair(j - 1, true))) break;
+        } else {
+          if (!(ok = dq(j))) break;
+        }
+      }
+      if constexpr (L::DQ_PAIR) {
+        if (ok && (T & 1)) ok = dq_pair(T - 1, false);
       }
     } else {
       // one S/dP buffer: S/dP of tile j once every warp has read tile j-1's, then
@@ -587,9 +618,55 @@ __global__ void __launch_bounds__(B_THREADS, 1) flash_bwd_sm100_kernel(const __g
     const uint32_t lane_off = (uint32_t)(32 * wq) << 16;
     const bool leader = warp == W_DRAIN && lane == 0;
     bool dead = false;
-    int t = 0;
     LiveTiles lt(live, i_first, p.nq64);
     bool mt;
+    if constexpr (L::DQ_PAIR) {
+      // tile pairs: dQ^T columns [0,64) = tile A's queries, [64,128) = tile B's;
+      // head dim 16*wq + l in lane l < 16 of quadrant wq (M=64 layout)
+      static_assert(L::NSTG == 2, "one staging tile per tile of a pair");
+      const bool holds = lane < 16;
+      const int d = 16 * wq + lane;
+      for (int pr = 0;; ++pr) {
+        const int ia = lt.next(&mt);
+        if (ia < 0) break;
+        const int ib = lt.next(&mt);  // -1: tile A is the last one
+        const bool two = ib >= 0;
+        if (!dead) dead = !warp_wait(bar(C_DQFULL), pr & 1, ab);
+        if (leader) bulk_wait_read<0>();  // the previous pair's reduces have read both staging tiles
+        named_bar_sync(4, 128);
+        if (!dead) tc_fence_after();
+#pragma unroll
+        for (int h4 = 0; h4 < 4; ++h4) {  // 32 query columns at a time
+          if (h4 >= 2 && !two) break;
+          uint32_t r[32];
+          if (!dead) tmem_load32(tmem + lane_off + L::TM_DQ + 32u * h4, r);
+          float* stg = reinterpret_cast<float*>(smem + L::OFF_STG + (h4 >> 1) * L::STG_BYTES);  // [64 q][D]
+          if (holds && !dead) {
+#pragma unroll
+            for (int q = 0; q < 32; ++q) stg[(32 * (h4 & 1) + q) * D + d] = __uint_as_float(r[q]);
+          }
+        }
+        if (!dead) {
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(bar(C_DQEMPTY));
+        }
+        fence_proxy_async_smem();
+        named_bar_sync(4, 128);
+        if (leader && !dead) {
+          const int qa = ia * BM;
+          bulk_reduce_add_f32(p.dq_acc + ((int64_t)bh * p.N + qa) * D, smem_u32(smem + L::OFF_STG),
+                              (uint32_t)(min(BM, p.N - qa) * D * 4));
+          if (two) {
+            const int qb2 = ib * BM;
+            bulk_reduce_add_f32(p.dq_acc + ((int64_t)bh * p.N + qb2) * D, smem_u32(smem + L::OFF_STG + L::STG_BYTES),
+                                (uint32_t)(min(BM, p.N - qb2) * D * 4));
+          }
+          bulk_commit();
+        }
+      }
+    } else {
+    int t = 0;
     for (int i; (i = lt.next(&mt)) >= 0;) {
       const int bq = t % L::NDQ, sg = t % L::NSTG;
       const int q0 = i * BM;
@@ -626,6 +703,7 @@ __global__ void __launch_bounds__(B_THREADS, 1) flash_bwd_sm100_kernel(const __g
         bulk_commit();
       }
       ++t;
+    }
     }
     if (leader) bulk_wait_all();
   }
