@@ -19,6 +19,8 @@
 //
 // S is recomputed in the backward by the same `tile_dot` routine (same FMA
 // order), so u == peak identifies exactly the forward's maxima.
+#include <type_traits>
+
 #include "flash.cuh"
 
 namespace pnft {
@@ -204,6 +206,10 @@ __global__ void __launch_bounds__(256) flash_bwd_prep_kernel(FlashArgs a) {
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, sub = lane >> 3, sl = lane & 7;
   const int64_t bh = blockIdx.y, b = bh / a.H, h = bh % a.H;
   const int64_t nt = (a.N + 63) / 64, npad = nt * 64;
+  // bf16 dO: 16-byte loads, lane sl reads head dims [8sl + 64k, +8) of dO and the fp32 O
+  const bool vec = std::is_same<T, __nv_bfloat16>::value && a.out32 && (a.D % 64) == 0 && a.sdo[3] == 1 && (a.sdo[2] % 8) == 0 &&
+                   (a.sdo[1] % 8) == 0 && (a.sdo[0] % 8) == 0 && (reinterpret_cast<uintptr_t>(a.dout) & 15) == 0 &&
+                   (reinterpret_cast<uintptr_t>(a.out32) & 15) == 0;
   int live = 0, multi = 0;
 #pragma unroll
   for (int pass = 0; pass < 2; ++pass) {
@@ -213,7 +219,20 @@ __global__ void __launch_bounds__(256) flash_bwd_prep_kernel(FlashArgs a) {
     const T* O = static_cast<const T*>(a.out_c) + b * a.so[0] + h * a.so[1] + (ok ? n : 0) * a.so[2];
     const T* dO = static_cast<const T*>(a.dout) + b * a.sdo[0] + h * a.sdo[1] + (ok ? n : 0) * a.sdo[2];
     float dot = 0.f;
-    if (ok) {
+    if (ok && vec) {
+      for (int e0 = 8 * sl; e0 < a.D; e0 += 64) {
+        const uint4 w = __ldg(reinterpret_cast<const uint4*>(dO + e0));
+        const float4* o4 = reinterpret_cast<const float4*>(a.out32 + r * a.D + e0);
+        const float4 o0 = __ldg(o4), o1 = __ldg(o4 + 1);
+        const uint32_t ws[4] = {w.x, w.y, w.z, w.w};
+        const float os[8] = {o0.x, o0.y, o0.z, o0.w, o1.x, o1.y, o1.z, o1.w};
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          dot = fmaf(__uint_as_float(ws[i] << 16), os[2 * i], dot);
+          dot = fmaf(__uint_as_float(ws[i] & 0xffff0000u), os[2 * i + 1], dot);
+        }
+      }
+    } else if (ok) {
       if (a.out32) {
         const float* O32 = a.out32 + r * a.D;
         for (int e = sl; e < a.D; e += 8) dot = fmaf(to_f32<T>(dO[e * a.sdo[3]]), O32[e], dot);
@@ -431,6 +450,39 @@ __global__ void __launch_bounds__(GTHREADS) flash_bwd_generic_kernel(FlashArgs a
 }
 
 template <typename T>
+__device__ __forceinline__ uint32_t pack2(float lo, float hi) {
+  static_assert(sizeof(T) == 2, "16-bit element type");
+  const T l = from_f32<T>(lo), u = from_f32<T>(hi);
+  uint16_t bl, bu;
+  memcpy(&bl, &l, 2);
+  memcpy(&bu, &u, 2);
+  return (uint32_t)bl | ((uint32_t)bu << 16);
+}
+
+// dQ = dq_scale * dq_acc for head dims 64 / 128 (SH = log2(D / 8)), unit inner
+// stride, 16-byte aligned rows: grid (rows * D / 8 / 256, B * H), one 16-byte store
+// per thread, no 64-bit divisions.
+template <typename T, int SH>
+__global__ void __launch_bounds__(256) dq_cast_rows_kernel(FlashArgs a) {
+  const int bh = blockIdx.y, b = bh / (int)a.H, h = bh - b * (int)a.H;
+  const uint32_t li = blockIdx.x * 256u + threadIdx.x;
+  const int64_t n = li >> SH;
+  if (n >= a.N) return;
+  constexpr int D = 8 << SH;
+  const int c = (int)(li & ((1u << SH) - 1)) * 8;
+  const float4* src = reinterpret_cast<const float4*>(a.dq_acc + ((int64_t)bh * a.N + n) * D + c);
+  float4 f0 = __ldcs(src), f1 = __ldcs(src + 1);
+  const float fs = a.dq_scale;
+  uint4 w;
+  w.x = pack2<T>(fs * f0.x, fs * f0.y);
+  w.y = pack2<T>(fs * f0.z, fs * f0.w);
+  w.z = pack2<T>(fs * f1.x, fs * f1.y);
+  w.w = pack2<T>(fs * f1.z, fs * f1.w);
+  T* dst = static_cast<T*>(a.dq) + b * a.sdq[0] + h * a.sdq[1] + n * a.sdq[2] + c;
+  *reinterpret_cast<uint4*>(dst) = w;
+}
+
+template <typename T>
 __global__ void __launch_bounds__(256) dq_cast_kernel(FlashArgs a) {
   T* dq = static_cast<T*>(a.dq);
   const float fs = a.dq_scale;
@@ -542,7 +594,20 @@ int flash_bwd_prep(const FlashArgs& a, cudaStream_t st) {
 }
 
 int flash_bwd_finish(const FlashArgs& a, cudaStream_t st) {
+  const bool rows = (a.D == 64 || a.D == 128) && a.sdq[3] == 1 && (a.sdq[2] % 8) == 0 && (a.sdq[1] % 8) == 0 &&
+                    (a.sdq[0] % 8) == 0 && (reinterpret_cast<uintptr_t>(a.dq) % 16) == 0 && a.B * a.H <= 65535 &&
+                    a.N * (a.D / 8) < ((int64_t)1 << 31);
   PNFT_DISPATCH_DTYPE(a.dtype, T, {
+    if constexpr (sizeof(T) == 2) {
+      if (rows) {
+        const dim3 grid((unsigned)((a.N * (a.D / 8) + 255) / 256), (unsigned)(a.B * a.H));
+        if (a.D == 64) dq_cast_rows_kernel<T, 3><<<grid, 256, 0, st>>>(a);
+        else dq_cast_rows_kernel<T, 4><<<grid, 256, 0, st>>>(a);
+        int rc = check_launch("flash bwd dq cast");
+        if (rc) return rc;
+        return pnft_sum_f32(a.dtau_part, a.n_dtau_part, a.dtau, st);
+      }
+    }
     const int64_t items = a.B * a.H * a.N * (a.D % 8 == 0 ? a.D / 8 : a.D);
     dq_cast_kernel<T><<<grid_cap(items, 256), 256, 0, st>>>(a);
   });
