@@ -2,8 +2,8 @@
 //
 // One CTA per (128 keys, b*h), KV-parallel over the 64-query tiles at or below
 // the causal diagonal whose rows are not all silent (per-tile flags from the
-// prep kernel). 768 threads:
-//   warp 0       TMA producer: K, V once; per query tile Q, dO (3 stages for
+// prep kernel). 512 threads:
+//   warp 0       TMA producer: K, V once; per query tile Q, dO (4 stages for
 //                D=64, 2 for D=128) and the tile's per-row coefficient records.
 //   warp 1       MMA issuer + TMEM owner (a converged warp; one elected lane
 //                issues, descriptors are precomputed bases plus constant
@@ -13,8 +13,8 @@
 //                  dV += P^T dO   (TS: P^T bf16 from TMEM)
 //                  dK += dS^T Q   (SS: dS^T bf16 from shared memory)
 //                  dQ^T = K^T dS^T (SS, M = head dims), into TMEM
-//   warps 4-19   elementwise, thread = TMEM lane = key; warpgroup g owns query
-//                columns [16g, 16g+16). Each thread pulls its whole S/dP slice
+//   warps 4-11   elementwise, thread = TMEM lane = key; warpgroup g owns query
+//                columns [32g, 32g+32). Each thread pulls its whole S/dP slice
 //                into registers and releases TMEM at once, then computes
 //                u = relu(S*scale - tau), W = c1 u^10 (-> P^T in TMEM) and
 //                dS' = c1 u^9 (dP - D) + [key == argmax] tie/10 (-> smem,
@@ -24,7 +24,7 @@
 //                on tiles that cross the diagonal or a sequence end; the gate
 //                term is one patched entry per row (value tests only on tiles
 //                holding a row with several maxima).
-//   warps 20-23  dQ drain: TMEM -> fp32 staging tile in smem -> one
+//   warps 12-15  dQ drain: TMEM -> fp32 staging tile in smem -> one
 //                cp.reduce.async.bulk add into the fp32 dQ accumulator.
 // Finally the elementwise warps write dK, dV (bf16) from TMEM.
 // TMEM columns: S [0,64) dP [64,128) P^T x2 [128,192) dV [192,192+D)
@@ -48,30 +48,32 @@ namespace {
 
 constexpr int BN = 128;  // keys per CTA (TMEM lanes)
 constexpr int BM = 64;   // queries per tile
-constexpr int NEW = 4;                       // elementwise warpgroups
+// two elementwise warpgroups of 32 query columns per warp: half the per-tile
+// bookkeeping of four groups of 16 per score element, and 128 registers per thread
+constexpr int NEW = 2;                       // elementwise warpgroups
 constexpr int CW = BM / NEW;                 // query columns per elementwise warp
 constexpr int W_DRAIN = 4 + 4 * NEW;         // first dQ drain warp
 constexpr int B_THREADS = 32 * (W_DRAIN + 4);
 
 enum : int {
   C_KV = 0,
-  C_QDFULL = 1,    // [3]
-  C_QDEMPTY = 4,   // [3]
-  C_SDPFULL = 7,   // [2] (one per S/dP buffer)
-  C_SDPEMPTY = 9,  // single-buffer layout only
-  C_PDSFULL = 10,  // [2]
-  C_PDSEMPTY = 12, // [4] (one per dS buffer)
-  C_DQFULL = 16,   // [2]
-  C_DQEMPTY = 18,  // [2]
-  C_DKV = 20,
-  C_FLAG = 21,  // plain arrive after dkv_written is stored (release for the flag)
-  C_KRAW = 22,  // fused FIR: raw K rows (with halo) landed
-  C_COUNT = 23
+  C_QDFULL = 1,    // [4]
+  C_QDEMPTY = 5,   // [4]
+  C_SDPFULL = 9,   // [2] (one per S/dP buffer)
+  C_SDPEMPTY = 11, // single-buffer layout only
+  C_PDSFULL = 12,  // [2]
+  C_PDSEMPTY = 14, // [4] (one per dS buffer)
+  C_DQFULL = 18,   // [2]
+  C_DQEMPTY = 20,  // [2]
+  C_DKV = 22,
+  C_FLAG = 23,  // plain arrive after dkv_written is stored (release for the flag)
+  C_KRAW = 24,  // fused FIR: raw K rows (with halo) landed
+  C_COUNT = 25
 };
 
 template <int D>
 struct BwdLayout {
-  static constexpr int NQS = D == 64 ? 3 : 2;    // Q / dO / coefficient stages
+  static constexpr int NQS = D == 64 ? 4 : 2;    // Q / dO / coefficient stages
   static constexpr int KGROUP = BN * 128;  // one 64-column group of the K / V tile
   static constexpr int QGROUP = BM * 128;  // one 64-column group of a Q / dO tile
   static constexpr int KBYTES = BN * D * 2;
@@ -104,8 +106,8 @@ struct BwdLayout {
   static constexpr int END = OFF_RED + 4 * 4 * NEW;
   static constexpr int SMEM = END + 1024;
   // TMEM. D=64: two S/dP buffers [128b, 128b+128) (S at +0, dP at +64); a warp
-  // writes its packed P^T over the first 8 of its own 16 S columns once they are
-  // in registers, so buffer b is free again once dV of its tile has been issued
+  // writes the packed P^T of each 16-query group over the first 8 of that group's S
+  // columns (its own columns) once they are in registers, so buffer b is free again once dV of its tile has been issued
   // (MMAs of one thread run in order). dV [256,320) dK [320,384) dQ^T x2 [384,512).
   // D=128: one S/dP buffer [0,128), P^T x2 [128,192), dV [192,320), dK [320,448),
   // dQ^T [448,512).
@@ -473,8 +475,12 @@ __global__ void __launch_bounds__(B_THREADS, 1) flash_bwd_sm100_kernel(const __g
       uint32_t rs[CW], rp[CW];
       if (!dead) {
         tc_fence_after();
-        tmem_load16x2(tmem + lane_off + L::tm_s(sb) + (uint32_t)(CW * hh), rs,
-                      tmem + lane_off + L::tm_dp(sb) + (uint32_t)(CW * hh), rp);
+        if constexpr (CW == 32)
+          tmem_load32x2(tmem + lane_off + L::tm_s(sb) + (uint32_t)(CW * hh), rs,
+                        tmem + lane_off + L::tm_dp(sb) + (uint32_t)(CW * hh), rp);
+        else
+          tmem_load16x2(tmem + lane_off + L::tm_s(sb) + (uint32_t)(CW * hh), rs,
+                        tmem + lane_off + L::tm_dp(sb) + (uint32_t)(CW * hh), rp);
         if constexpr (L::NSB == 1) {
           tc_fence_before();
           __syncwarp();
@@ -516,7 +522,9 @@ __global__ void __launch_bounds__(B_THREADS, 1) flash_bwd_sm100_kernel(const __g
             pw_pk[c2] = pack_bf16x2(w.x, w.y);
             ds_pk[c2] = pack_bf16x2(ds.x, ds.y);
           }
-          tmem_st8(tmem + lane_off + L::tm_p(s, hh), pw_pk);
+#pragma unroll
+          for (int k = 0; k < CW / 16; ++k)
+            tmem_st8(tmem + lane_off + L::tm_p(s, (CW / 16) * hh + k), *reinterpret_cast<const uint32_t(*)[8]>(pw_pk + 8 * k));
 #pragma unroll
           for (int cc = 0; cc < CW / 8; ++cc) {
             const uint32_t chunk = (CW / 8) * hh + cc;  // 16-byte chunk of the 128-byte key row
@@ -524,7 +532,7 @@ __global__ void __launch_bounds__(B_THREADS, 1) flash_bwd_sm100_kernel(const __g
                          ds_pk[4 * cc + 2], ds_pk[4 * cc + 3]);
           }
         };
-        static_assert(CW == 16, "one tmem_st8 of packed P^T and two 16-byte dS chunks per warp");
+        static_assert(CW == 16 || CW == 32, "16 or 32 query columns per warp");
         using T_ = std::true_type;
         using F_ = std::false_type;
         const bool edge = (p.causal && qb < kb + 31) || qb + CW > p.N || kb + 32 > p.N;
