@@ -210,6 +210,15 @@ __global__ void __launch_bounds__(256) flash_bwd_prep_kernel(FlashArgs a) {
   const bool vec = std::is_same<T, __nv_bfloat16>::value && a.out32 && (a.D % 64) == 0 && a.sdo[3] == 1 && (a.sdo[2] % 8) == 0 &&
                    (a.sdo[1] % 8) == 0 && (a.sdo[0] % 8) == 0 && (reinterpret_cast<uintptr_t>(a.dout) & 15) == 0 &&
                    (reinterpret_cast<uintptr_t>(a.out32) & 15) == 0;
+  {  // this block's rows of the fp32 dQ accumulator start at zero (the backward adds into them)
+    const int64_t n0 = (int64_t)blockIdx.x * 64, cnt = (min((int64_t)64, a.N - n0)) * a.D;
+    float* z = a.dq_acc + (bh * a.N + n0) * a.D;
+    if ((reinterpret_cast<uintptr_t>(z) & 15) == 0 && (cnt & 3) == 0) {
+      for (int64_t i = threadIdx.x; i < cnt / 4; i += blockDim.x) reinterpret_cast<float4*>(z)[i] = make_float4(0.f, 0.f, 0.f, 0.f);
+    } else {
+      for (int64_t i = threadIdx.x; i < cnt; i += blockDim.x) z[i] = 0.f;
+    }
+  }
   int live = 0, multi = 0;
 #pragma unroll
   for (int pass = 0; pass < 2; ++pass) {
@@ -449,6 +458,21 @@ __global__ void __launch_bounds__(GTHREADS) flash_bwd_generic_kernel(FlashArgs a
   if (tid == 0) a.dtau_part[bh * gridDim.x + kt] = -t / a.scale;
 }
 
+// dtau = fixed-order fp64 sum of the backward's tau partials, by one block of 256
+// threads (block (0,0) of the dQ cast, which runs after the backward kernel)
+__device__ __forceinline__ void tau_partials_sum(const FlashArgs& a) {
+  __shared__ double sm[256];
+  double v = 0.0;
+  for (int64_t i = threadIdx.x; i < a.n_dtau_part; i += 256) v += (double)a.dtau_part[i];
+  sm[threadIdx.x] = v;
+  __syncthreads();
+  for (int w = 128; w > 0; w >>= 1) {
+    if ((int)threadIdx.x < w) sm[threadIdx.x] += sm[threadIdx.x + w];
+    __syncthreads();
+  }
+  if (threadIdx.x == 0) a.dtau[0] = (float)sm[0];
+}
+
 template <typename T>
 __device__ __forceinline__ uint32_t pack2(float lo, float hi) {
   static_assert(sizeof(T) == 2, "16-bit element type");
@@ -464,6 +488,7 @@ __device__ __forceinline__ uint32_t pack2(float lo, float hi) {
 // per thread, no 64-bit divisions.
 template <typename T, int SH>
 __global__ void __launch_bounds__(256) dq_cast_rows_kernel(FlashArgs a) {
+  if (blockIdx.x == 0 && blockIdx.y == 0) tau_partials_sum(a);
   const int bh = blockIdx.y, b = bh / (int)a.H, h = bh - b * (int)a.H;
   const uint32_t li = blockIdx.x * 256u + threadIdx.x;
   const int64_t n = li >> SH;
@@ -484,6 +509,7 @@ __global__ void __launch_bounds__(256) dq_cast_rows_kernel(FlashArgs a) {
 
 template <typename T>
 __global__ void __launch_bounds__(256) dq_cast_kernel(FlashArgs a) {
+  if (blockIdx.x == 0) tau_partials_sum(a);
   T* dq = static_cast<T*>(a.dq);
   const float fs = a.dq_scale;
   const bool vec = (a.D % 8) == 0 && a.sdq[3] == 1 && (a.sdq[2] % 8) == 0 && (a.sdq[1] % 8) == 0 &&
@@ -585,8 +611,6 @@ int flash_fwd_generic(const FlashArgs& a, cudaStream_t st) {
 }
 
 int flash_bwd_prep(const FlashArgs& a, cudaStream_t st) {
-  if (cudaMemsetAsync(a.dq_acc, 0, (size_t)(a.B * a.H * a.N * a.D) * sizeof(float), st) != cudaSuccess)
-    return check_launch("flash bwd: dq accumulator memset");
   PNFT_DISPATCH_DTYPE(a.dtype, T, {
     flash_bwd_prep_kernel<T><<<dim3((unsigned)((a.N + 63) / 64), (unsigned)(a.B * a.H)), 256, 0, st>>>(a);
   });
@@ -603,17 +627,13 @@ int flash_bwd_finish(const FlashArgs& a, cudaStream_t st) {
         const dim3 grid((unsigned)((a.N * (a.D / 8) + 255) / 256), (unsigned)(a.B * a.H));
         if (a.D == 64) dq_cast_rows_kernel<T, 3><<<grid, 256, 0, st>>>(a);
         else dq_cast_rows_kernel<T, 4><<<grid, 256, 0, st>>>(a);
-        int rc = check_launch("flash bwd dq cast");
-        if (rc) return rc;
-        return pnft_sum_f32(a.dtau_part, a.n_dtau_part, a.dtau, st);
+        return check_launch("flash bwd dq cast + tau sum");
       }
     }
     const int64_t items = a.B * a.H * a.N * (a.D % 8 == 0 ? a.D / 8 : a.D);
     dq_cast_kernel<T><<<grid_cap(items, 256), 256, 0, st>>>(a);
   });
-  int rc = check_launch("flash bwd dq cast");
-  if (rc) return rc;
-  return pnft_sum_f32(a.dtau_part, a.n_dtau_part, a.dtau, st);
+  return check_launch("flash bwd dq cast + tau sum");
 }
 
 int flash_bwd_generic(const FlashArgs& a0, cudaStream_t st) {
