@@ -63,6 +63,8 @@ def parse_args():
     ap.add_argument("--lm-steps", type=int, default=10)
     ap.add_argument("--no-lm", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--e2e-chunks", type=int, default=8,
+                    help="pipeline chunks of the e2e step (whole heads each; 1 = one call per step)")
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--cpu-seconds", type=float, default=12.0)
     ap.add_argument("--generic", action="store_true", help="force the generic SIMT kernels")
@@ -376,22 +378,73 @@ def bench_ours(args, dist_: Dist) -> dict:
 
 def bench_e2e(args, dist_: Dist, w: dict, dev, flops: float, P) -> dict:
     """Same op through the public API with pinned host inputs and host outputs:
-    every step copies q,k,v,dO host->device and out,dq,dk,dv,dtau device->host."""
-    from paper_01_anti_decoy_pnfirtau_b200.sharding import sharded_flash_pn_fir_tau_attention
+    every step copies q,k,v,dO host->device and out,dq,dk,dv,dtau device->host.
+
+    The step is pipelined over chunks of whole heads (--e2e-chunks, default 8: one
+    batch element each for config 3; one call of the public API per chunk), as a caller streaming host data would run it: the
+    host->device copies of chunk i+1, the attention fwd+bwd of chunk i and the
+    device->host copies of chunk i-1 run on three streams, so the two PCIe
+    directions and the kernels overlap. Every byte of the serial version is still
+    copied every step; dtau is the sum over chunks (all-reduced over ranks)."""
+    from paper_01_anti_decoy_pnfirtau_b200.pnfirtau_ops import flash_pn_fir_tau_attention
 
     hq, hk, hv, hdo = (t.detach().cpu().pin_memory() for t in make_inputs(w, args.seed + 7, dev))
     outs = [torch.empty_like(hq).pin_memory() for _ in range(4)]
     htau = torch.empty((), dtype=torch.float32).pin_memory()
     tau = torch.tensor(args.tau, device=dev, requires_grad=True)
+    # chunks of whole heads: (b, h0, h1) blocks, each contiguous in the host buffers
+    B, H = hq.shape[0], hq.shape[1]
+    want = max(1, args.e2e_chunks)
+    if want <= B:  # whole batch elements
+        bounds = [(B * i // want, B * (i + 1) // want, 0, H) for i in range(want)]
+    else:  # every batch element split into head groups
+        hsplit = min(H, (want + B - 1) // B)
+        bounds = [(b, b + 1, H * j // hsplit, H * (j + 1) // hsplit) for b in range(B) for j in range(hsplit)]
+    nchunk = len(bounds)
+    gq_, gk_, gv_, gdo_ = (torch.empty(t.shape, device=dev, dtype=t.dtype) for t in (hq, hk, hv, hdo))  # device inputs
+    s_in, s_cmp, s_out = torch.cuda.Stream(dev), torch.cuda.Stream(dev), torch.cuda.Stream(dev)
+    done_cmp = [None] * nchunk  # compute of chunk i finished reading its device inputs (previous step)
 
     def step():
-        q, k, v, do = (t.to(dev, non_blocking=True) for t in (hq, hk, hv, hdo))
-        q.requires_grad_(True), k.requires_grad_(True), v.requires_grad_(True)
-        out = sharded_flash_pn_fir_tau_attention(q, k, v, tau)
-        dq, dk, dv, dtau = torch.autograd.grad(out, (q, k, v, tau), do)
-        for h, d in zip(outs, (out, dq, dk, dv)):
-            h.copy_(d, non_blocking=True)
-        htau.copy_(dtau, non_blocking=True)
+        main = torch.cuda.current_stream(dev)
+        start = torch.cuda.Event()
+        start.record(main)
+        s_in.wait_event(start)
+        total = None
+        for i, (b0, b1, h0, h1) in enumerate(bounds):
+            sl = (slice(b0, b1), slice(h0, h1))
+            with torch.cuda.stream(s_in):
+                if done_cmp[i] is not None:
+                    s_in.wait_event(done_cmp[i])
+                for d, h in zip((gq_, gk_, gv_, gdo_), (hq, hk, hv, hdo)):
+                    d[sl].copy_(h[sl], non_blocking=True)
+                landed = torch.cuda.Event()
+                landed.record(s_in)
+            with torch.cuda.stream(s_cmp):
+                s_cmp.wait_event(landed)
+                q, k, v = (t[sl].detach().requires_grad_(True) for t in (gq_, gk_, gv_))
+                out = flash_pn_fir_tau_attention(q, k, v, tau)
+                gq, gk, gv, gt = torch.autograd.grad(out, (q, k, v, tau), gdo_[sl])
+                total = gt if total is None else total + gt
+                ev = torch.cuda.Event()
+                ev.record(s_cmp)
+                done_cmp[i] = ev
+            with torch.cuda.stream(s_out):
+                s_out.wait_event(ev)
+                for h, d in zip(outs, (out, gq, gk, gv)):
+                    d.record_stream(s_out)
+                    h[sl].copy_(d, non_blocking=True)
+        with torch.cuda.stream(s_cmp):
+            if dist_.world > 1:
+                import torch.distributed as tdist
+                tdist.all_reduce(total)
+            total.record_stream(s_out)
+            fin = torch.cuda.Event()
+            fin.record(s_cmp)
+        with torch.cuda.stream(s_out):
+            s_out.wait_event(fin)
+            htau.copy_(total, non_blocking=True)
+        main.wait_stream(s_out)
 
     for _ in range(max(2, min(args.warmup, 3))):
         step()
@@ -410,7 +463,9 @@ def bench_e2e(args, dist_: Dist, w: dict, dev, flops: float, P) -> dict:
     d2h = sum(t.numel() * t.element_size() for t in outs) + htau.element_size()
     return {"value": round(dist_.world * flops * steps / (ms / 1e3) / 1e12, 3), "unit": "TFLOP/s",
             "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h, "ms_per_step": round(ms / steps, 4),
-            "steps": steps, "api": "flash_pn_fir_tau_attention + torch.autograd.grad, pinned host buffers"}
+            "steps": steps, "chunks": nchunk,
+            "api": "flash_pn_fir_tau_attention + torch.autograd.grad per batch chunk, pinned host buffers, "
+                   "H2D / compute / D2H on three streams"}
 
 
 def bench_lm(args, dist_: Dist, dev) -> dict:
