@@ -1,16 +1,17 @@
 // sm_100a flash pn_fir_tau kernels: TMA -> shared memory, tcgen05 MMAs with
 // TMEM accumulators, warp-specialised pipelines. bf16 inputs, head dim 64/128.
 //
-// Forward, one CTA per (128 query rows, b*h), 320 threads, two CTAs per SM (each
+// Forward, one CTA per (128 query rows, b*h), 192 threads, two CTAs per SM (each
 // holds 256 of the 512 TMEM columns; the two CTAs' tile phases are independent,
 // so one CTA's loads, hand-offs and MMAs overlap the other's elementwise work):
 //   warp 0      TMA producer: Q once; K and V tile j+1 while tile j is computed.
 //   warp 1      MMA issuer and TMEM owner: S_j = Q K_j^T (SS, M=128, N=64) into
 //               one of two S buffers; O += P_j V_j (TS: P read from TMEM) for the
-//               live 32-key column blocks only.
-//   warps 2-9   two elementwise groups of four warps (every group covers the four
-//               TMEM lane quadrants, warp % 4); group g owns key columns
-//               [32g, 32g+32) of every 64-key tile, thread = TMEM lane = query row:
+//               live 64-key tiles only.
+//   warps 2-5   one elementwise group of four warps (covering the four TMEM lane
+//               quadrants, warp % 4) owning all 64 key columns of every tile (per
+//               warp and tile the bookkeeping is amortised over 64 columns, half
+//               the per-element cost of two groups of 32), thread = TMEM lane = query row:
 //               s = S*scale - tau (packed f32x2 FMA, rounded once), u = max(s, 0),
 //               row max via 3-input max, per-warp silent vote, u^10 by repeated
 //               squaring (no exp), running peak / tie count / argmax / mass, and
@@ -18,11 +19,11 @@
 //               the tile's own S columns in TMEM for the two PV MMAs.
 // TMEM (256 columns per CTA): S/P buffers [0,64) and [64,128), O [128, 128+D).
 // With the fused FIR, warps 2-3 filter the K tiles (fir_tile.cuh), the
-// elementwise warps are 4-11 and the CTA runs alone on its SM.
+// elementwise warps are 4-7 and the CTA runs alone on its SM.
 // Epilogue: O * gate/(mass + 1e-12) with gate = peak/(peak+gamma), stats M, Z,
 // Nmax, argmax.
 // Semantics follow src/triton_pnfirtau.py:313-443 (the reference skips 64x64
-// tiles; here the skip unit is 128 query rows x 32 keys, and the optional
+// tiles; here the skip unit is 128 query rows x 64 keys, and the optional
 // tile_flags record reports the 64x64 decisions of the same u values).
 //
 // Every mbarrier wait is bounded (sm100_ptx.cuh): on timeout the CTA sets the
@@ -43,8 +44,8 @@ namespace {
 
 constexpr int FM = 128;  // query rows per CTA (TMEM lanes)
 constexpr int FN = 64;   // keys per tile
-constexpr int FQ = 32;                  // key columns per elementwise group
-constexpr int NQW = FN / FQ;            // elementwise groups of four warps (2)
+constexpr int FQ = 64;                  // key columns per elementwise group
+constexpr int NQW = FN / FQ;            // elementwise groups of four warps
 // warp 0 producer, warp 1 MMA issuer, elementwise warps from EW0 on (with the
 // fused FIR, warps 2-3 filter K and the elementwise warps start at 4)
 template <bool FIR> constexpr int ew0() { return FIR ? 4 : 2; }
@@ -92,10 +93,11 @@ struct FwdLayout {
   // (slots past NQW stay zero)
   static constexpr int OFF_RPK = (OFF_STATS + NQW * 4 * FM * 4 + 15) & ~15;
   static_assert(OFF_RPK % 16 == 0, "float4 rows need 16-byte alignment");
-  // d=64 only (d=128 has no room): per elementwise lane the 32 s-values of the tile
-  // that set its column block's peak, rows 144 B apart (conflict-free 16-byte stores)
+  // d=64 only (d=128 has no room): per elementwise lane the FQ s-values of the tile
+  // that set its column block's peak, rows FQ*4 + 16 B apart (an odd number of 16-byte
+  // units: conflict-free 16-byte stores)
   static constexpr bool DEFER = D == 64;
-  static constexpr int REC_STRIDE = 144;
+  static constexpr int REC_STRIDE = FQ * 4 + 16;
   static constexpr int OFF_REC = OFF_RPK + FM * 16;
   static_assert(OFF_REC % 16 == 0, "16-byte rows");
   static constexpr int END = OFF_REC + (DEFER ? NQW * FM * REC_STRIDE : 0);
@@ -323,7 +325,7 @@ __global__ void __launch_bounds__(f_threads<FIR>(), FIR ? 1 : 2) flash_fwd_sm100
     }
   } else {
     // ------------------------------------------------------------ elementwise
-    const int ew = warp - ew0<FIR>(), g = ew >> 2, wq = warp & 3;  // group g owns key columns [32g, 32g+32)
+    const int ew = warp - ew0<FIR>(), g = ew >> 2, wq = warp & 3;  // group g owns key columns [FQ g, FQ g + FQ)
     const int rl = 32 * wq + lane;  // TMEM lane = local query row
     const int row = q0 + rl;
     const uint32_t lane_off = (uint32_t)(32 * wq) << 16;
@@ -351,29 +353,31 @@ __global__ void __launch_bounds__(f_threads<FIR>(), FIR ? 1 : 2) flash_fwd_sm100
       const int s = j & 1;
       if (!dead) dead = !warp_wait(bar(B_SFULL + s), (j >> 1) & 1, ab);
       const uint32_t scol = tmem + lane_off + TM_S + (uint32_t)FN * s + (uint32_t)FQ * g;
-      uint32_t r[32];
+      static_assert(FQ == 32 || FQ == 64, "32 or 64 key columns per warp");
+      uint32_t r[FQ / 32][32];
       if (!dead) {
         tc_fence_after();
-        tmem_load32(scol, r);
+        if constexpr (FQ == 64) tmem_load32x2(scol, r[0], scol + 32, r[FQ / 32 - 1]);
+        else tmem_load32(scol, r[0]);
       }
-      float x[32];
+      float x[FQ];
 #pragma unroll
-      for (int c = 0; c < 32; c += 2) {
-        const float2 a = __ffma2_rn(make_float2(__uint_as_float(r[c]), __uint_as_float(r[c + 1])), sc2, nt2);
+      for (int c = 0; c < FQ; c += 2) {
+        const float2 a = __ffma2_rn(make_float2(__uint_as_float(r[c >> 5][c & 31]), __uint_as_float(r[c >> 5][(c & 31) + 1])), sc2, nt2);
         x[c] = a.x;
         x[c + 1] = a.y;
       }
       const int kb = j * FN + FQ * g;
       int lim = row < p.N ? (p.causal ? row : p.N - 1) - kb : -1;  // last valid column offset
       if (dead) lim = -1;                                                // after an abort: silent
-      if (lim < 31) {
+      if (lim < FQ - 1) {
 #pragma unroll
-        for (int c = 0; c < 32; ++c) x[c] = c > lim ? -1.f : x[c];
+        for (int c = 0; c < FQ; ++c) x[c] = c > lim ? -1.f : x[c];
       }
       float m = max3(x[0], x[1], x[2]);
 #pragma unroll
-      for (int c = 3; c < 31; c += 2) m = max3(m, x[c], x[c + 1]);
-      m = fmaxf(m, x[31]);
+      for (int c = 3; c < FQ - 1; c += 2) m = max3(m, x[c], x[c + 1]);
+      m = fmaxf(m, x[FQ - 1]);
       // silent vote of this warp's 32 rows; the MMA issuer ORs the four warps of
       // the column block after PFULL completes (no barrier between the warps). A silent
       // warp writes zeros: another warp's rows may keep the column block live.
@@ -393,17 +397,17 @@ __global__ void __launch_bounds__(f_threads<FIR>(), FIR ? 1 : 2) flash_fwd_sm100
           if (L::DEFER && mu > peak) {
             // new peak: save the tile's values, search them once after the loop
 #pragma unroll
-            for (int k = 0; k < 8; ++k)
+            for (int k = 0; k < FQ / 4; ++k)
               reinterpret_cast<float4*>(rec)[k] = make_float4(x[4 * k], x[4 * k + 1], x[4 * k + 2], x[4 * k + 3]);
             arg = kb;
             cnt = 0.f;
           } else {
             // columns attaining the maximum as a bit mask: count and first key
-            uint32_t mk = 0u;
+            unsigned long long mk = 0ull;
 #pragma unroll
-            for (int i = 0; i < 32; ++i) mk |= x[i] == m ? 1u << i : 0u;
-            const float c = (float)__popc(mk);
-            if (mu > peak) arg = kb + __ffs(mk) - 1;  // equal to an earlier tile's peak: keep the earlier key
+            for (int i = 0; i < FQ; ++i) mk |= x[i] == m ? 1ull << i : 0ull;
+            const float c = (float)__popcll(mk);
+            if (mu > peak) arg = kb + __ffsll((long long)mk) - 1;  // equal to an earlier tile's peak: keep the earlier key
             cnt = mu > peak ? c : cnt + c;
           }
           peak = mu;
@@ -413,12 +417,12 @@ __global__ void __launch_bounds__(f_threads<FIR>(), FIR ? 1 : 2) flash_fwd_sm100
         // then rounded, ~2^-17 relative): O, and with it the
         // backward's <dO,O>/gate, stays fp32-accurate; the tau gradient is a small
         // residual of cancelling per-row sums and needs that accuracy
-        // Two halves of 16 columns, each stored as soon as it is packed (fewer live
+        // Quarters of 16 columns, each stored as soon as it is packed (fewer live
         // registers): P_hi / P_lo over this group's own S columns
-        // [32g + 8hh, +8) / [32g + 16 + 8hh, +8).
+        // [FQ g + 8hh, +8) / [FQ g + FQ/2 + 8hh, +8).
         const float2 neg1 = make_float2(-1.f, -1.f);
 #pragma unroll
-        for (int hh = 0; hh < 2; ++hh) {
+        for (int hh = 0; hh < FQ / 16; ++hh) {
           uint32_t hi[8], lo[8];
 #pragma unroll
           for (int cc = 0; cc < 8; ++cc) {
@@ -443,8 +447,8 @@ __global__ void __launch_bounds__(f_threads<FIR>(), FIR ? 1 : 2) flash_fwd_sm100
         uint32_t zr[16];
 #pragma unroll
         for (int c = 0; c < 16; ++c) zr[c] = 0u;
-        tmem_st16(scol, zr);
-        tmem_st16(scol + FQ / 2, zr);
+#pragma unroll
+        for (int c = 0; c < FQ; c += 16) tmem_st16(scol + c, zr);
         tmem_wait_st();
       }
       tc_fence_before();
@@ -453,17 +457,16 @@ __global__ void __launch_bounds__(f_threads<FIR>(), FIR ? 1 : 2) flash_fwd_sm100
     }
     if (L::DEFER && peak > 0.f) {
       // search of the saved tile: its maximum equals the column block's peak
-      uint32_t mk = 0u;
+      unsigned long long mk = 0ull;
 #pragma unroll
-      for (int k = 0; k < 8; ++k) {
+      for (int k = 0; k < FQ / 4; ++k) {
         const float4 v4 = reinterpret_cast<const float4*>(rec)[k];
-        mk |= (v4.x == peak ? 1u : 0u) << (4 * k);
-        mk |= (v4.y == peak ? 2u : 0u) << (4 * k);
-        mk |= (v4.z == peak ? 4u : 0u) << (4 * k);
-        mk |= (v4.w == peak ? 8u : 0u) << (4 * k);
+        mk |= (unsigned long long)((v4.x == peak ? 1u : 0u) | (v4.y == peak ? 2u : 0u) | (v4.z == peak ? 4u : 0u) |
+                                   (v4.w == peak ? 8u : 0u))
+              << (4 * k);
       }
-      cnt += (float)__popc(mk);
-      arg += __ffs(mk) - 1;
+      cnt += (float)__popcll(mk);
+      arg += __ffsll((long long)mk) - 1;
     }
     // ---- epilogue: merge the column groups of every row, scale O, store
     float* st = reinterpret_cast<float*>(smem + L::OFF_STATS);
