@@ -63,6 +63,7 @@ def parse_args():
     ap.add_argument("--lm-steps", type=int, default=10)
     ap.add_argument("--no-lm", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--no-fir", action="store_true")
     ap.add_argument("--e2e-chunks", type=int, default=8,
                     help="pipeline chunks of the e2e step (whole heads each; 1 = one call per step)")
     ap.add_argument("--no-cpu", action="store_true")
@@ -368,6 +369,8 @@ def bench_ours(args, dist_: Dist) -> dict:
         result["e2e"] = bench_e2e(args, dist_, w, dev, flops, P)
     if not args.no_lm:
         result["lm"] = bench_lm(args, dist_, dev)
+    if not args.no_fir:
+        result["fir"] = bench_fir(args, dist_, dev)
     if dist_.rank == 0 and dist_.world == 1 and not args.no_cpu:
         tf, cores, n, el = cpu_oracle_sample(w, args.cpu_seconds, args.seed)
         result["cpu_baseline"] = {"value": round(tf, 6), "unit": "TFLOP/s", "cores": cores, "kind": "port",
@@ -466,6 +469,41 @@ def bench_e2e(args, dist_: Dist, w: dict, dev, flops: float, P) -> dict:
             "steps": steps, "chunks": nchunk,
             "api": "flash_pn_fir_tau_attention + torch.autograd.grad per batch chunk, pinned host buffers, "
                    "H2D / compute / D2H on three streams"}
+
+
+def bench_fir(args, dist_: Dist, dev, iters: int = 20) -> dict:
+    """Standalone causal FIR (triton_causal_fir, 7 Gaussian taps, bf16) as achieved
+    HBM GB/s: bytes = one read of x + one write of y per pass (the 6-row halo
+    re-reads are not counted). Shapes: the LM's keys [32, 512, 256] and the keys
+    of config 5 viewed as [8, 16384, 16*128]. Buffers rotate so the inputs of
+    consecutive passes together exceed the 126 MiB L2 (every pass reads DRAM)."""
+    from paper_01_anti_decoy_pnfirtau_b200.pnfirtau_attention import causal_gaussian_taps
+    from paper_01_anti_decoy_pnfirtau_b200.pnfirtau_ops import triton_causal_fir
+
+    peak = measured_peaks().get("hbm_gbs")
+    taps = causal_gaussian_taps(7, device=dev)
+    g = torch.Generator(device=dev).manual_seed(args.seed + 11)
+    res = {}
+    for name, shape in (("lm_k_32x512x256", (32, 512, 256)), ("c5_k_8x16384x2048", (8, 16384, 2048))):
+        nbytes = 2 * shape[0] * shape[1] * shape[2]
+        nbuf = max(1, -(-2 * L2_BYTES // nbytes))
+        xs = [torch.randn(shape, generator=g, device=dev).to(torch.bfloat16) for _ in range(nbuf)]
+        for i in range(3):
+            triton_causal_fir(xs[i % nbuf], taps)
+        torch.cuda.synchronize()
+        s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s.record()
+        for i in range(iters):
+            triton_causal_fir(xs[i % nbuf], taps)
+        e.record()
+        torch.cuda.synchronize()
+        ms = s.elapsed_time(e) / iters
+        gbs = 2 * nbytes / (ms / 1e3) / 1e9
+        res[name] = {"ms": round(ms, 4), "bytes_per_pass": 2 * nbytes, "GB/s": round(gbs, 1),
+                     "frac_of_hbm": round(gbs / peak, 3) if peak else None}
+        del xs
+    res["peak_GB/s"] = peak
+    return res
 
 
 def bench_lm(args, dist_: Dist, dev) -> dict:

@@ -1,9 +1,11 @@
 // Depthwise causal FIR along the sequence axis of x[B,N,C] (and its transpose
 // and tap gradient). HBM-bound: every element is read once and written once;
 // threads own 16-byte channel vectors so a warp moves 512 contiguous bytes per
-// row, and each thread walks FIR_TN consecutive rows keeping the K-1 previous
-// rows in registers (the halo rows are re-read from L1/L2, never from DRAM
-// twice in practice because neighbouring row chunks run in the same block).
+// row, and each thread walks a run of consecutive rows (8, or 32 when the problem
+// still fills every SM twice over) keeping the K-1 previous rows in registers
+// (the halo rows are re-read from L1/L2, never from DRAM twice in practice). A run
+// that lies inside the sequence loads eight rows at a time before using them, so
+// each thread keeps eight 16-byte loads in flight.
 //
 // Semantics follow the reference kernels src/triton_pnfirtau.py:40-135:
 //   fwd  y[b,n,c]  = sum_{u=0}^{K-1} taps[K-1-u] * x[b,n-u,c]   (x[<0] = 0)
@@ -61,7 +63,7 @@ struct FirGeom {
 
 // Sliding-window kernel with compile-time tap count. DIR = +1: causal fwd
 // (window over past rows), DIR = -1: transpose (window over future rows).
-template <typename T, int VEC, int K, int DIR>
+template <typename T, int VEC, int K, int DIR, int TN = FIR_TN>
 __global__ void __launch_bounds__(FIR_THREADS) fir_sliding_kernel(FirGeom g, const float* __restrict__ taps) {
   const T* __restrict__ x = static_cast<const T*>(g.in);
   T* __restrict__ y = static_cast<T*>(g.out);
@@ -69,7 +71,7 @@ __global__ void __launch_bounds__(FIR_THREADS) fir_sliding_kernel(FirGeom g, con
 #pragma unroll
   for (int u = 0; u < K; ++u) h[u] = __ldg(taps + (K - 1 - u));
   const int64_t CV = (g.C + VEC - 1) / VEC;
-  const int64_t chunks = (g.N + FIR_TN - 1) / FIR_TN;
+  const int64_t chunks = (g.N + TN - 1) / TN;
   const int64_t items = g.B * chunks * CV;
   for (int64_t it = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; it < items;
        it += (int64_t)gridDim.x * blockDim.x) {
@@ -81,8 +83,8 @@ __global__ void __launch_bounds__(FIR_THREADS) fir_sliding_kernel(FirGeom g, con
     const T* xb = x + b * g.sib + c0 * g.sic;
     T* yb = y + b * g.sob + c0 * g.soc;
     float win[K][VEC];
-    const int64_t n_first = chunk * FIR_TN;
-    const int64_t n_last = min(n_first + FIR_TN, g.N) - 1;
+    const int64_t n_first = chunk * TN;
+    const int64_t n_last = min(n_first + TN, g.N) - 1;
     if (DIR > 0) {
       // win[u] = x[n-u]; prime lags 1..K-1 for n = n_first
 #pragma unroll
@@ -96,8 +98,37 @@ __global__ void __launch_bounds__(FIR_THREADS) fir_sliding_kernel(FirGeom g, con
           for (int v = 0; v < VEC; ++v) win[u][v] = 0.f;
         }
       }
+      if (VEC * sizeof(T) == 16 && TN % 8 == 0 && n_first + TN <= g.N) {
+        // whole chunk inside the sequence: eight rows' loads issued before their use
 #pragma unroll
-      for (int t = 0; t < FIR_TN; ++t) {
+        for (int t0 = 0; t0 < TN; t0 += 8) {
+          uint4 raw[8];
+#pragma unroll
+          for (int t = 0; t < 8; ++t) raw[t] = __ldg(reinterpret_cast<const uint4*>(xb + (n_first + t0 + t) * g.sin));
+#pragma unroll
+          for (int t = 0; t < 8; ++t) {
+            const T* e = reinterpret_cast<const T*>(&raw[t]);
+#pragma unroll
+            for (int v = 0; v < VEC; ++v) win[0][v] = to_f32<T>(e[v]);
+            float acc[VEC];
+#pragma unroll
+            for (int v = 0; v < VEC; ++v) {
+              float a = win[0][v] * h[0];
+#pragma unroll
+              for (int u = 1; u < K; ++u) a = fmaf(win[u][v], h[u], a);
+              acc[v] = a;
+            }
+            st_vec<T, VEC>(yb + (n_first + t0 + t) * g.son, acc);
+#pragma unroll
+            for (int u = K - 1; u > 0; --u)
+#pragma unroll
+              for (int v = 0; v < VEC; ++v) win[u][v] = win[u - 1][v];
+          }
+        }
+        continue;
+      }
+#pragma unroll
+      for (int t = 0; t < TN; ++t) {
         const int64_t n = n_first + t;
         if (n <= n_last) {
           if constexpr (VEC > 1) ld_vec<T, VEC>(xb + n * g.sin, win[0]);
@@ -131,8 +162,37 @@ __global__ void __launch_bounds__(FIR_THREADS) fir_sliding_kernel(FirGeom g, con
           for (int v = 0; v < VEC; ++v) win[u][v] = 0.f;
         }
       }
+      if (VEC * sizeof(T) == 16 && TN % 8 == 0 && n_first + TN <= g.N) {
+        // whole chunk inside the sequence: eight rows' loads issued before their use
 #pragma unroll
-      for (int t = FIR_TN - 1; t >= 0; --t) {
+        for (int t0 = TN - 8; t0 >= 0; t0 -= 8) {
+          uint4 raw[8];
+#pragma unroll
+          for (int t = 0; t < 8; ++t) raw[t] = __ldg(reinterpret_cast<const uint4*>(xb + (n_first + t0 + t) * g.sin));
+#pragma unroll
+          for (int t = 7; t >= 0; --t) {
+            const T* e = reinterpret_cast<const T*>(&raw[t]);
+#pragma unroll
+            for (int v = 0; v < VEC; ++v) win[0][v] = to_f32<T>(e[v]);
+            float acc[VEC];
+#pragma unroll
+            for (int v = 0; v < VEC; ++v) {
+              float a = win[0][v] * h[0];
+#pragma unroll
+              for (int u = 1; u < K; ++u) a = fmaf(win[u][v], h[u], a);
+              acc[v] = a;
+            }
+            st_vec<T, VEC>(yb + (n_first + t0 + t) * g.son, acc);
+#pragma unroll
+            for (int u = K - 1; u > 0; --u)
+#pragma unroll
+              for (int v = 0; v < VEC; ++v) win[u][v] = win[u - 1][v];
+          }
+        }
+        continue;
+      }
+#pragma unroll
+      for (int t = TN - 1; t >= 0; --t) {
         const int64_t n = n_first + t;
         if (n <= n_last) {
           if constexpr (VEC > 1) ld_vec<T, VEC>(xb + n * g.sin, win[0]);
@@ -232,7 +292,14 @@ static int fir_launch(const FirGeom& g, const float* taps, int K, cudaStream_t s
     const int64_t chunks = (g.N + FIR_TN - 1) / FIR_TN;
     if (vec_ok<T>(g)) {
       const int64_t items = g.B * chunks * (g.C / VEC);
-      fir_sliding_kernel<T, VEC, 7, DIR><<<grid_for(items), FIR_THREADS, 0, st>>>(g, taps);
+      // long runs of rows per thread (6-row halo and index math amortised over 32
+      // rows) once that still leaves two 256-thread blocks per SM of a B200
+      if (items / (32 / FIR_TN) >= 2 * 148 * FIR_THREADS) {
+        const int64_t items32 = g.B * ((g.N + 31) / 32) * (g.C / VEC);
+        fir_sliding_kernel<T, VEC, 7, DIR, 32><<<grid_for(items32), FIR_THREADS, 0, st>>>(g, taps);
+      } else {
+        fir_sliding_kernel<T, VEC, 7, DIR><<<grid_for(items), FIR_THREADS, 0, st>>>(g, taps);
+      }
     } else {
       const int64_t items = g.B * chunks * g.C;
       fir_sliding_kernel<T, 1, 7, DIR><<<grid_for(items), FIR_THREADS, 0, st>>>(g, taps);

@@ -617,22 +617,27 @@ int flash_bwd_prep(const FlashArgs& a, cudaStream_t st) {
   return check_launch("flash bwd prep");
 }
 
-int flash_bwd_finish(const FlashArgs& a, cudaStream_t st) {
-  const bool rows = (a.D == 64 || a.D == 128) && a.sdq[3] == 1 && (a.sdq[2] % 8) == 0 && (a.sdq[1] % 8) == 0 &&
-                    (a.sdq[0] % 8) == 0 && (reinterpret_cast<uintptr_t>(a.dq) % 16) == 0 && a.B * a.H <= 65535 &&
-                    a.N * (a.D / 8) < ((int64_t)1 << 31);
-  PNFT_DISPATCH_DTYPE(a.dtype, T, {
-    if constexpr (sizeof(T) == 2) {
-      if (rows) {
-        const dim3 grid((unsigned)((a.N * (a.D / 8) + 255) / 256), (unsigned)(a.B * a.H));
-        if (a.D == 64) dq_cast_rows_kernel<T, 3><<<grid, 256, 0, st>>>(a);
-        else dq_cast_rows_kernel<T, 4><<<grid, 256, 0, st>>>(a);
-        return check_launch("flash bwd dq cast + tau sum");
-      }
+// the dQ cast (and tau sum) in element type T: the row kernel for 16-bit types with
+// head dim 64 / 128 and 16-byte aligned rows, else the grid-stride kernel
+template <typename T>
+static void dq_cast_launch(const FlashArgs& a, cudaStream_t st) {
+  if constexpr (sizeof(T) == 2) {
+    const bool rows = (a.D == 64 || a.D == 128) && a.sdq[3] == 1 && (a.sdq[2] % 8) == 0 && (a.sdq[1] % 8) == 0 &&
+                      (a.sdq[0] % 8) == 0 && (reinterpret_cast<uintptr_t>(a.dq) % 16) == 0 && a.B * a.H <= 65535 &&
+                      a.N * (a.D / 8) < ((int64_t)1 << 31);
+    if (rows) {
+      const dim3 grid((unsigned)((a.N * (a.D / 8) + 255) / 256), (unsigned)(a.B * a.H));
+      if (a.D == 64) dq_cast_rows_kernel<T, 3><<<grid, 256, 0, st>>>(a);
+      else dq_cast_rows_kernel<T, 4><<<grid, 256, 0, st>>>(a);
+      return;
     }
-    const int64_t items = a.B * a.H * a.N * (a.D % 8 == 0 ? a.D / 8 : a.D);
-    dq_cast_kernel<T><<<grid_cap(items, 256), 256, 0, st>>>(a);
-  });
+  }
+  const int64_t items = a.B * a.H * a.N * (a.D % 8 == 0 ? a.D / 8 : a.D);
+  dq_cast_kernel<T><<<grid_cap(items, 256), 256, 0, st>>>(a);
+}
+
+int flash_bwd_finish(const FlashArgs& a, cudaStream_t st) {
+  PNFT_DISPATCH_DTYPE(a.dtype, T, { dq_cast_launch<T>(a, st); });
   return check_launch("flash bwd dq cast + tau sum");
 }
 
