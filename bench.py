@@ -534,10 +534,64 @@ def bench_lm(args, dist_: Dist, dev) -> dict:
     torch.cuda.synchronize()
     ms = dist_.max(s.elapsed_time(e), dev)
     ms_step = ms / args.lm_steps
-    return {"tokens_per_s": round(dist_.world * B * N / (ms_step / 1e3), 1), "ms_per_step": round(ms_step, 3),
-            "steps": args.lm_steps, "global_batch": B * dist_.world, "seq_len": N, "params": nparams,
-            "loss": round(float(loss), 4), "model": "6-layer Pre-LN pn_fir_tau LM, D256 H4 MLP4x V33278, bf16 autocast, AdamW",
-            "parallelism": f"ddp{dist_.world}" if dist_.world > 1 else "single GPU"}
+    res = {"tokens_per_s": round(dist_.world * B * N / (ms_step / 1e3), 1), "ms_per_step": round(ms_step, 3),
+           "steps": args.lm_steps, "global_batch": B * dist_.world, "seq_len": N, "params": nparams,
+           "loss": round(float(loss), 4), "model": "6-layer Pre-LN pn_fir_tau LM, D256 H4 MLP4x V33278, bf16 autocast, AdamW",
+           "parallelism": f"ddp{dist_.world}" if dist_.world > 1 else "single GPU"}
+    if not dist_.active:
+        try:
+            res.update(bench_lm_graph(args, dev, cfg, batches))
+        except Exception as exc:  # report, keep the eager number
+            res["graph"] = f"capture failed: {type(exc).__name__}: {exc}"[:200]
+    return res
+
+
+def bench_lm_graph(args, dev, cfg, batches) -> dict:
+    """The same training step captured once in a CUDA graph and replayed (the
+    reference's exp4c technique for the launch-bound 6-layer stack): loss,
+    backward, clip_grad_norm_ and AdamW(capturable=True) in one graph; each step
+    copies its batch into the captured input. Single GPU (DDP stays eager)."""
+    from paper_01_anti_decoy_pnfirtau_b200.lm import PnFirLM, lm_loss
+
+    torch.manual_seed(args.seed)
+    model = PnFirLM(cfg).to(dev)
+    opt = torch.optim.AdamW(model.parameters(), lr=3e-4, betas=(0.9, 0.95), weight_decay=0.1, capturable=True)
+    static_idx = batches[0].clone()
+
+    def step():
+        with torch.autocast(device_type="cuda", dtype=torch.bfloat16, cache_enabled=False):
+            loss = lm_loss(model, static_idx)
+        loss.backward()
+        torch.nn.utils.clip_grad_norm_(model.parameters(), 1.0)
+        opt.step()
+        return loss.detach()
+
+    side = torch.cuda.Stream(dev)
+    side.wait_stream(torch.cuda.current_stream(dev))
+    with torch.cuda.stream(side):
+        for _ in range(3):
+            opt.zero_grad(set_to_none=True)
+            step()
+    torch.cuda.current_stream(dev).wait_stream(side)
+    graph = torch.cuda.CUDAGraph()
+    opt.zero_grad(set_to_none=True)
+    with torch.cuda.graph(graph):
+        static_loss = step()
+    for i in range(3):
+        static_idx.copy_(batches[i % len(batches)])
+        graph.replay()
+    torch.cuda.synchronize()
+    s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    s.record()
+    for i in range(args.lm_steps):
+        static_idx.copy_(batches[i % len(batches)])
+        graph.replay()
+    e.record()
+    torch.cuda.synchronize()
+    ms_step = s.elapsed_time(e) / args.lm_steps
+    B, N = static_idx.shape
+    return {"tokens_per_s_graph": round(B * N / (ms_step / 1e3), 1), "ms_per_step_graph": round(ms_step, 3),
+            "loss_graph": round(float(static_loss), 4)}
 
 
 # ---------------------------------------------------------------------------
