@@ -374,10 +374,18 @@ __global__ void __launch_bounds__(f_threads<FIR>(), FIR ? 1 : 2) flash_fwd_sm100
 #pragma unroll
         for (int c = 0; c < FQ; ++c) x[c] = c > lim ? -1.f : x[c];
       }
-      float m = max3(x[0], x[1], x[2]);
+      // row maximum as four independent 3-input max chains of FQ/4 columns (dependency
+      // depth ~FQ/8 + 2 instead of FQ/2)
+      constexpr int MQ = FQ / 4;
+      float mc[4];
 #pragma unroll
-      for (int c = 3; c < FQ - 1; c += 2) m = max3(m, x[c], x[c + 1]);
-      m = fmaxf(m, x[FQ - 1]);
+      for (int k = 0; k < 4; ++k) {
+        mc[k] = max3(x[k * MQ], x[k * MQ + 1], x[k * MQ + 2]);
+#pragma unroll
+        for (int c = 3; c + 1 < MQ; c += 2) mc[k] = max3(mc[k], x[k * MQ + c], x[k * MQ + c + 1]);
+        if constexpr (MQ % 2 == 0) mc[k] = fmaxf(mc[k], x[k * MQ + MQ - 1]);
+      }
+      const float m = max3(mc[0], mc[1], fmaxf(mc[2], mc[3]));
       // silent vote of this warp's 32 rows; the MMA issuer ORs the four warps of
       // the column block after PFULL completes (no barrier between the warps). A silent
       // warp writes zeros: another warp's rows may keep the column block live.
