@@ -91,3 +91,31 @@ def test_fir_single_tap_is_identity(cuda):
 def test_fir_empty(cuda):
     x = torch.randn(0, 9, 8, device=cuda)
     assert P.triton_causal_fir(x, P.causal_gaussian_taps(7, cuda)).shape == (0, 9, 8)
+
+
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
+def test_fir_long_runs(cuda, dtype):
+    """Shapes large enough for the 32-row runs per thread (at least two blocks per
+    SM of a B200), with N not a multiple of 32: the last run of every sequence
+    takes the per-row bounded path, the others the eight-rows-in-flight path;
+    forward, transpose (dx) and tap gradient."""
+    B, N, C = 4, 4100, 2048
+    g = torch.Generator(device="cpu").manual_seed(7)
+    x = torch.randn(B, N, C, generator=g).to(device=cuda, dtype=dtype)
+    taps = P.causal_gaussian_taps(7, cuda)
+    gy = torch.randn(B, N, C, generator=g).to(device=cuda, dtype=dtype)
+    xr = x.detach().clone().requires_grad_(True)
+    tr = taps.clone().requires_grad_(True)
+    y = P.triton_causal_fir(xr, tr)
+    y.backward(gy)
+    ref_y = O.causal_fir(x.double(), taps.double())
+    ref_gx = O.causal_fir_transpose(gy.double(), taps.double())
+    ref_dt = O.causal_fir_dtaps(gy.double(), x.double(), 7)
+    if dtype == torch.float32:
+        assert rel_max(y, ref_y) < 1e-6
+        assert rel_max(xr.grad, ref_gx) < 1e-6
+        assert rel_max(tr.grad, ref_dt) < 1e-5
+    else:
+        assert rel_l2(y, ref_y) < 1e-2 and rel_max(y, ref_y) < 1e-2
+        assert rel_l2(xr.grad, ref_gx) < 1e-2
+        assert rel_l2(tr.grad, ref_dt) < 1e-2
