@@ -1,0 +1,51 @@
+"""bench.py's one-line JSON contract: the keys the round-end driver reads, for the
+reference arm (host cores, runs here) and for this repository's arm (GPU)."""
+import json
+import subprocess
+import sys
+
+import pytest
+
+from conftest import REPO
+
+BASE_KEYS = {"metric", "value", "unit", "n_gpus", "steps", "warmup", "ms_per_step", "higher_is_better",
+             "scaling", "vs_baseline", "dtype", "data", "config"}
+
+
+def _run_bench(args, timeout):
+    r = subprocess.run([sys.executable, "bench.py", *args], cwd=REPO, capture_output=True, text=True, timeout=timeout)
+    assert r.returncode == 0, r.stderr[-2000:]
+    lines = [l for l in r.stdout.splitlines() if l.strip()]
+    assert len(lines) == 1, r.stdout[-2000:]  # exactly one JSON line on stdout
+    return json.loads(lines[0])
+
+
+def test_profile_traffic_lines():
+    import bench
+
+    for key in ("flash_bwd:c3", "flash_fwd:c3"):
+        t = bench.profile_traffic(key)
+        assert t is not None and t > 1e8, key
+
+
+def test_reference_arm_json_contract():
+    d = _run_bench(["--impl", "reference", "--steps", "1", "--warmup", "1"], timeout=600)
+    assert BASE_KEYS <= set(d), BASE_KEYS - set(d)
+    assert d["impl"] == "reference"
+    assert d["config"]["workload"].startswith("c3")
+    cb = d["cpu_baseline"]
+    assert cb["kind"] in ("port", "reference") and cb["cores"] >= 1 and cb["value"] == d["value"]
+    assert d["e2e"] == {"value": d["value"], "unit": d["unit"], "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}
+
+
+@pytest.mark.gpu
+def test_bench_json_contract_gpu():
+    d = _run_bench(["--steps", "3", "--warmup", "3", "--no-lm", "--no-cpu", "--lm-steps", "1"], timeout=900)
+    assert BASE_KEYS <= set(d), BASE_KEYS - set(d)
+    assert d["config"]["kernel_path"] == "sm100" and d["value"] > 0
+    rf = d["roofline"]
+    assert rf["bound"] in ("hbm", "tensor") and rf["peak"] > 0 and 0 < rf["frac"] == pytest.approx(rf["achieved"] / rf["peak"], rel=1e-2)
+    e2e = d["e2e"]
+    assert e2e["h2d_bytes_per_step"] == 4 * 8 * 8 * 4096 * 64 * 2 and e2e["d2h_bytes_per_step"] == 4 * 8 * 8 * 4096 * 64 * 2 + 4
+    assert d["gpu_launches"] > 0 and "sm_mhz" in d["clocks"] and "reasons" in d["clocks"]
+    assert d["fir"]["c5_k_8x16384x2048"]["GB/s"] > 0
