@@ -13,11 +13,17 @@ the SM clocks seen during the timed region.
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
     torchrun --nproc-per-node N bench.py --gpus N ...     (one rank per GPU)
 
+Also: config 3's tau sweep {-0.5, 0, +0.5} with the silent-tile skips the
+kernels took, and config 5 (B8 H16 N16384 d128) with its 128 heads sharded
+over the ranks.
+
 Multi-GPU: every rank runs its own config-3-sized shard of batch x heads
 (weak scaling, no collective on the operator's data path); the shared tau
-gradient is summed across ranks with one fp32 all-reduce per step, and the LM
-uses DDP over NCCL. ``--impl reference`` times the CPU oracle (the reference's
-eager algorithm restated in oracle/) on rank 0 only.
+gradient is summed across ranks with one fp64 all-reduce per backward on a side
+stream (TauGradReducer: no step waits for the other ranks; the sum is collected
+at the end of the timed region), and the LM uses DDP over NCCL.
+``--impl reference`` times the reference's eager algorithm on the host cores
+on rank 0 only.
 """
 from __future__ import annotations
 
@@ -64,6 +70,10 @@ def parse_args():
     ap.add_argument("--no-lm", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-fir", action="store_true")
+    ap.add_argument("--no-sweep", action="store_true", help="skip the config-3 tau sweep")
+    ap.add_argument("--no-c5", action="store_true", help="skip the config-5 measurement")
+    ap.add_argument("--sweep-steps", type=int, default=10)
+    ap.add_argument("--c5-steps", type=int, default=4)
     ap.add_argument("--e2e-chunks", type=int, default=8,
                     help="pipeline chunks of the e2e step (whole heads each; 1 = one call per step)")
     ap.add_argument("--no-cpu", action="store_true")
@@ -222,6 +232,15 @@ def profile_traffic(kernel_key: str) -> float | None:
     return None
 
 
+def profile_traffic_source(kernel_key: str) -> str | None:
+    """Which committed ncu summary the traffic figure comes from (it is a recorded
+    capture, not measured in this run)."""
+    for p in sorted((ROOT / "profiles").glob("*.md")):
+        if re.search(rf"traffic_bytes_per_launch\[{re.escape(kernel_key)}\]", p.read_text()):
+            return f"recorded ncu capture, profiles/{p.name} (not measured in this run)"
+    return None
+
+
 # ---------------------------------------------------------------------------
 # workload
 # ---------------------------------------------------------------------------
@@ -285,7 +304,7 @@ def cpu_oracle_sample(w: dict, seconds: float, seed: int, steps: int | None = No
 def bench_ours(args, dist_: Dist) -> dict:
     import paper_01_anti_decoy_pnfirtau_b200 as P
     from paper_01_anti_decoy_pnfirtau_b200 import _lib, pnfirtau_ops
-    from paper_01_anti_decoy_pnfirtau_b200.sharding import sharded_flash_pn_fir_tau_attention
+    from paper_01_anti_decoy_pnfirtau_b200.sharding import TauGradReducer, sharded_flash_pn_fir_tau_attention
 
     dev = torch.device("cuda", dist_.local_rank)
     torch.cuda.set_device(dev)
@@ -298,25 +317,31 @@ def bench_ours(args, dist_: Dist) -> dict:
     leaves = [t.requires_grad_(True) for t in (q, k, v)]
     path = P.flash_kernel_path(q, k, v)
     flops = flops_fwd_bwd(w)
+    # tau's gradient: this rank's partial is summed over the ranks in fp64 on a side
+    # stream (TauGradReducer), so no step waits for the other ranks; the sum is
+    # collected once, by the consumer of tau's gradient, at the end of the timed region
+    reducer = TauGradReducer()
 
     def step(evs=None):
         if evs is not None:
             evs[0].record()
-        # this rank's B*H shard; tau's gradient is summed over the ranks (fp64)
-        out = sharded_flash_pn_fir_tau_attention(*leaves, tau)
+        # this rank's B*H shard
+        out = sharded_flash_pn_fir_tau_attention(*leaves, tau, reducer=reducer)
         if evs is not None:
             evs[1].record()
-        grads = torch.autograd.grad(out, (*leaves, tau), do)
+        grads = torch.autograd.grad(out, (*leaves, tau), do, allow_unused=True)
         if evs is not None:
             evs[2].record()
         return out, grads
 
     for _ in range(args.warmup):
         step()
+    reducer.result()
     torch.cuda.synchronize()
     P.check_device_status(dev)
     evs = [[torch.cuda.Event(enable_timing=True) for _ in range(3)] for _ in range(args.steps)]
     start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    steps_done = torch.cuda.Event(enable_timing=True)
     dist_.barrier()
     torch.cuda.synchronize()
     n0 = _lib.launch_count()
@@ -324,6 +349,8 @@ def bench_ours(args, dist_: Dist) -> dict:
         start.record()
         for i in range(args.steps):
             step(evs[i])
+        steps_done.record()
+        dtau_sum = reducer.result()  # the tau-gradient consumer waits for the last all-reduce
         end.record()
         torch.cuda.synchronize()
     launches = _lib.launch_count() - n0
@@ -333,6 +360,7 @@ def bench_ours(args, dist_: Dist) -> dict:
     ms = dist_.max(ms_local, dev)
     fwd_ms = statistics.mean(e[0].elapsed_time(e[1]) for e in evs)
     bwd_ms = statistics.mean(e[1].elapsed_time(e[2]) for e in evs)
+    collective_wait_ms = steps_done.elapsed_time(end)
     ms_per_step = ms / args.steps
     value = dist_.world * flops * args.steps / (ms / 1e3) / 1e12
     peaks = measured_peaks()
@@ -344,9 +372,11 @@ def bench_ours(args, dist_: Dist) -> dict:
         kname, kflops, kms = "flash_fwd", 2.0 * B * H * N * N * D, fwd_ms
     achieved = kflops / (kms / 1e3) / 1e12
     traffic = profile_traffic(f"{kname}:{args.workload}")
+    traffic_src = profile_traffic_source(f"{kname}:{args.workload}")
     roofline = {
         "bound": "tensor", "kernel": kname, "achieved": round(achieved, 2), "peak": peaks["bf16_tflops"],
         "unit": "TFLOP/s", "frac": round(achieved / peaks["bf16_tflops"], 4), "traffic": traffic,
+        "traffic_source": traffic_src,
         "peak_source": f"{peaks['source']} bf16 burst (sustained {peaks['bf16_tflops_sustained']})",
         "flops_per_launch": kflops, "ms_per_launch": round(kms, 4),
         "note": "flash_bwd time includes its per-row prep, dQ cast and tau-sum launches",
@@ -362,9 +392,18 @@ def bench_ours(args, dist_: Dist) -> dict:
                    "flops_per_step_per_gpu": flops},
         "pct_of_peak": round(100.0 * value / dist_.world / peaks["bf16_tflops"], 2),
         "fwd_ms": round(fwd_ms, 4), "bwd_ms": round(bwd_ms, 4),
+        "tau_grad": {"allreduce": "fp64 on a side stream per backward (no per-step rank lock-step)" if dist_.active
+                     else "single GPU: no collective", "pushes": reducer.pushes,
+                     "exposed_wait_ms": round(collective_wait_ms, 4),
+                     "value": float(dtau_sum) if dtau_sum is not None else None},
         "roofline": roofline, "gpu_launches": int(launches), "clocks": clocks.summary(),
     }
 
+    del q, k, v, do, leaves
+    if not args.no_sweep and args.workload == "c3":
+        result["tau_sweep"] = bench_tau_sweep(args, dist_, w, dev)
+    if not args.no_c5 and args.workload == "c3":
+        result["c5"] = bench_c5(args, dist_, dev)
     if not args.no_e2e:
         result["e2e"] = bench_e2e(args, dist_, w, dev, flops, P)
     if not args.no_lm:
@@ -377,6 +416,119 @@ def bench_ours(args, dist_: Dist) -> dict:
                                   "sample": f"{n} (b,h) slices of [1,1,{N},{D}] fp32 fwd+bwd in {el:.1f} s "
                                             f"(oracle/pnfirtau_oracle.py, torch CPU eager)"}
     return result
+
+
+def _time_fwd_bwd(q, k, v, do, tau, steps: int, warmup: int, reducer):
+    """(total ms, mean fwd ms, mean bwd ms) of `steps` fwd+bwd calls of this rank's
+    shard through the public API; tau's gradient through `reducer`."""
+    from paper_01_anti_decoy_pnfirtau_b200.sharding import sharded_flash_pn_fir_tau_attention
+
+    leaves = [t.detach().requires_grad_(True) for t in (q, k, v)]
+
+    def one(ev=None):
+        if ev is not None:
+            ev[0].record()
+        out = sharded_flash_pn_fir_tau_attention(*leaves, tau, reducer=reducer)
+        if ev is not None:
+            ev[1].record()
+        torch.autograd.grad(out, (*leaves, tau), do, allow_unused=True)
+        if ev is not None:
+            ev[2].record()
+
+    for _ in range(warmup):
+        one()
+    reducer.result()
+    evs = [[torch.cuda.Event(enable_timing=True) for _ in range(3)] for _ in range(steps)]
+    s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize()
+    s.record()
+    for i in range(steps):
+        one(evs[i])
+    reducer.result()
+    e.record()
+    torch.cuda.synchronize()
+    return (s.elapsed_time(e), statistics.mean(x[0].elapsed_time(x[1]) for x in evs),
+            statistics.mean(x[1].elapsed_time(x[2]) for x in evs))
+
+
+def bench_tau_sweep(args, dist_: Dist, w: dict, dev) -> dict:
+    """Config 3's tau sweep {-0.5, 0, +0.5} on the same inputs (50% of the 64-row
+    query blocks scaled by 0.05): fwd+bwd time and algorithmic TFLOP/s (silent
+    tiles still counted), with the skip decisions the kernels took, read back from
+    the forward's per-64x64-tile record:
+      tiles_silent_frac   causal 64x64 tiles with no u > 0: their elementwise work
+                          (u^10, P) is skipped (per 32-row warp) and they are the
+                          reference's silent tiles (exp4b definition; the tests
+                          check the decisions against the oracle on every head);
+      pv_skipped_frac     causal 64x64 tiles whose PV MMA was not issued: the
+                          forward's PV unit is 128 query rows x 64 keys, skipped
+                          when both of its 64-row halves are silent;
+      bwd_qtiles_skipped_frac  64-row query tiles with every row silent, which the
+                          backward skips entirely (the reference's `max(peak) > 0`)."""
+    from paper_01_anti_decoy_pnfirtau_b200 import TauGradReducer
+    from paper_01_anti_decoy_pnfirtau_b200.pnfirtau_ops import flash_pn_fir_tau_forward_stats
+
+    q, k, v, do = make_inputs(w, args.seed + 1000 * dist_.rank, dev)
+    B, H, N, D = w["B"], w["H"], w["N"], w["D"]
+    flops = flops_fwd_bwd(w)
+    nT = (N + 63) // 64
+    causal = torch.tril(torch.ones(nT, nT, dtype=torch.bool, device=dev))
+    out = {}
+    for tau0 in (-0.5, 0.0, 0.5):
+        tau = torch.tensor(tau0, device=dev, requires_grad=True)
+        ms, fwd, bwd = _time_fwd_bwd(q, k, v, do, tau, args.sweep_steps, 3, TauGradReducer())
+        ms = dist_.max(ms, dev)
+        _, M, _, _, live = flash_pn_fir_tau_forward_stats(q, k, v, tau.detach())
+        ncausal = float(causal.sum()) * B * H
+        silent = (~live) & causal
+        # PV unit = query tiles (2p, 2p+1): skipped iff both halves are silent
+        lp = torch.nn.functional.pad(live, (0, 0, 0, nT % 2))
+        pair_live = (lp[:, :, 0::2] | lp[:, :, 1::2]).repeat_interleave(2, dim=2)[:, :, :nT]
+        pv_skip = (~pair_live) & causal
+        qt_dead = ~(torch.nn.functional.pad(M, (0, nT * 64 - N)).reshape(B, H, nT, 64) > 0).any(-1)
+        out[f"{tau0:+.1f}"] = {
+            "tau": tau0, "ms_per_step": round(ms / args.sweep_steps, 4),
+            "value": round(dist_.world * flops * args.sweep_steps / (ms / 1e3) / 1e12, 2), "unit": "TFLOP/s",
+            "fwd_ms": round(fwd, 4), "bwd_ms": round(bwd, 4),
+            "tiles_silent_frac": round(float(silent.sum()) / ncausal, 4),
+            "pv_skipped_frac": round(float(pv_skip.sum()) / ncausal, 4),
+            "bwd_qtiles_skipped_frac": round(float(qt_dead.float().mean()), 4),
+            "rows_silent_frac": round(float((M <= 0).float().mean()), 4),
+        }
+    out["note"] = ("algorithmic FLOPs 7*B*H*N^2*d per step at every tau (skipped tiles counted); this rank's "
+                   "shard; fractions over causal 64x64 tiles")
+    return out
+
+
+def bench_c5(args, dist_: Dist, dev) -> dict:
+    """Config 5 (B8 H16 N16384 d128 bf16, fwd+bwd) with batch x heads sharded
+    over the ranks (strong scaling of the fixed 128 heads): each rank runs its
+    contiguous block of heads; reported value = total FLOPs / max-over-ranks time."""
+    from paper_01_anti_decoy_pnfirtau_b200 import TauGradReducer, bh_range
+
+    w = WORKLOADS["c5"]
+    B, H, N, D = w["B"], w["H"], w["N"], w["D"]
+    lo, hi = bh_range(B, H, dist_.rank, dist_.world)
+    ws = dict(w, B=1, H=hi - lo)
+    q, k, v, do = make_inputs(ws, args.seed + 50 + lo, dev)
+    tau = torch.tensor(0.0, device=dev, requires_grad=True)
+    ms, fwd, bwd = _time_fwd_bwd(q, k, v, do, tau, args.c5_steps, 2, TauGradReducer())
+    ms = dist_.max(ms, dev)
+    total = flops_fwd_bwd(w)
+    mine = flops_fwd_bwd(ws)
+    peaks = measured_peaks()
+    bwd_tf = 5.0 * ws["B"] * ws["H"] * N * N * D / (bwd / 1e3) / 1e12
+    return {
+        "workload": w["desc"], "heads_per_rank": hi - lo, "steps": args.c5_steps, "scaling": "strong",
+        "ms_per_step": round(ms / args.c5_steps, 3),
+        "value": round(total * args.c5_steps / (ms / 1e3) / 1e12, 2), "unit": "TFLOP/s",
+        "fwd_ms": round(fwd, 3), "bwd_ms": round(bwd, 3),
+        "roofline": {"bound": "tensor", "kernel": "flash_bwd", "achieved": round(bwd_tf, 2),
+                     "peak": peaks["bf16_tflops"], "unit": "TFLOP/s", "frac": round(bwd_tf / peaks["bf16_tflops"], 4),
+                     "flops_per_launch": 5.0 * ws["B"] * ws["H"] * N * N * D, "ms_per_launch": round(bwd, 3)},
+        "rank0_fwd_tflops": round(2.0 * ws["B"] * ws["H"] * N * N * D / (fwd / 1e3) / 1e12, 2),
+        "flops_per_step_per_rank": mine,
+    }
 
 
 def bench_e2e(args, dist_: Dist, w: dict, dev, flops: float, P) -> dict:
@@ -406,6 +558,9 @@ def bench_e2e(args, dist_: Dist, w: dict, dev, flops: float, P) -> dict:
     nchunk = len(bounds)
     gq_, gk_, gv_, gdo_ = (torch.empty(t.shape, device=dev, dtype=t.dtype) for t in (hq, hk, hv, hdo))  # device inputs
     s_in, s_cmp, s_out = torch.cuda.Stream(dev), torch.cuda.Stream(dev), torch.cuda.Stream(dev)
+    from paper_01_anti_decoy_pnfirtau_b200 import TauGradReducer
+
+    reducer = TauGradReducer()
     done_cmp = [None] * nchunk  # compute of chunk i finished reading its device inputs (previous step)
 
     def step():
@@ -438,15 +593,15 @@ def bench_e2e(args, dist_: Dist, w: dict, dev, flops: float, P) -> dict:
                     d.record_stream(s_out)
                     h[sl].copy_(d, non_blocking=True)
         with torch.cuda.stream(s_cmp):
-            if dist_.world > 1:
-                import torch.distributed as tdist
-                tdist.all_reduce(total)
             total.record_stream(s_out)
+            if dist_.world > 1:
+                reducer.push(total)  # fp64 all-reduce on the reducer's side stream
             fin = torch.cuda.Event()
             fin.record(s_cmp)
         with torch.cuda.stream(s_out):
             s_out.wait_event(fin)
-            htau.copy_(total, non_blocking=True)
+            summed = reducer.result() if dist_.world > 1 else total  # s_out waits for the all-reduce
+            htau.copy_(summed, non_blocking=True)
         main.wait_stream(s_out)
 
     for _ in range(max(2, min(args.warmup, 3))):

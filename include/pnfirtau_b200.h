@@ -14,8 +14,8 @@
  * PNFT_E* code for invalid arguments or a CUDA launch error. The message of
  * the last failure on the calling thread is available from pnft_last_error().
  * Kernels that wait on hardware barriers write a positive PNFT_DEV_* code to
- * the caller's `status` word instead of hanging; the host reads it when it
- * next synchronises.
+ * the caller's `status` word instead of hanging (device memory, read after a
+ * synchronisation, or mapped pinned host memory, see pnft_mapped_status_ptr).
  *
  * Reference interface replaced (paths inside the reference project):
  *   src/triton_pnfirtau.py  - Triton kernels + autograd wrappers
@@ -61,6 +61,12 @@ extern "C" {
 #define PNFT_FLASH_FORCE_GENERIC 0x1 /* use the SIMT kernel even where tcgen05 applies */
 #define PNFT_FLASH_DETERMINISTIC 0x2 /* reserved: ordered dQ accumulation             */
 #define PNFT_FLASH_PREFER_SM100 0x4  /* tcgen05 kernels wherever their shape rules allow */
+/* Test-only: the tcgen05 kernels' elementwise warps make their first pipeline
+ * wait on a barrier that nothing arrives on, so every CTA takes the timeout path
+ * after the 1 s limit (status word set to PNFT_DEV_WAIT_TIMEOUT, the other roles
+ * unwind, copies drain, TMEM is freed). The outputs of such a call are invalid.
+ * No effect on the generic kernels. */
+#define PNFT_FLASH_TEST_STALL 0x100
 
 /* Tap count of the FIR fused into the flash kernels (pnft_flash_fwd_fir): the
  * module's causal filter on the keys, PnFirConfig.fir_k = 7
@@ -82,6 +88,13 @@ PNFT_API const char* pnft_last_error(void);
  * of this library run on it). */
 PNFT_API int pnft_query_caps(int device, int* cc_major, int* cc_minor, int* sm_count,
                     int* smem_optin_bytes, int* has_sm100a);
+
+/* Device address of a status word in pinned host memory (cudaHostAlloc /
+ * cudaMallocHost, which unified addressing maps into every device): the
+ * kernels' `status` argument may be that address, so a failure they report is
+ * visible to the host by reading the word, with no copy and no synchronisation.
+ * Returns PNFT_EINVAL if host_word is not such memory. Host pointers in and out. */
+PNFT_API int pnft_mapped_status_ptr(void* host_word, void** device_ptr);
 
 /* ------------------------------------------------------------------------- */
 /* Depthwise causal FIR along N of x[B,N,C]                                   */
@@ -189,8 +202,9 @@ PNFT_API int pnft_sum_f32(const float* x, int64_t n, float* out, void* stream);
  * 64x64 tile it processed as live (some u > 0) and leaves skipped silent
  * tiles and tiles above the causal diagonal at 0 - the silent-tile decisions
  * of experiments/exp4b_mha6_instrumentation.py:91-111.
- * status: device int32 word, set to PNFT_DEV_* if a pipeline wait times out
- * (never cleared by the library).
+ * status: int32 word the device can write (device memory, or mapped pinned host
+ * memory, see pnft_mapped_status_ptr; may be NULL), set to PNFT_DEV_* if a
+ * pipeline wait times out (never cleared by the library).
  * Replaces: src/triton_pnfirtau.py:313-443 (_flash_pn_fir_tau_fwd_kernel) and
  * _FlashPnFirTauFn.forward (:814-898). */
 PNFT_API int pnft_flash_fwd(const void* q, const int64_t* sq, const void* k, const int64_t* sk,

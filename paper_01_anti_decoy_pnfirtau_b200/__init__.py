@@ -22,7 +22,14 @@ from .pnfirtau_ops import (
     triton_causal_fir,
     triton_pn_fir_tau_scores,
 )
-from .sharding import bh_range, shard_bh, share_tau, sharded_flash_pn_fir_tau_attention, unshard_bh
+from .sharding import (
+    TauGradReducer,
+    bh_range,
+    shard_bh,
+    share_tau,
+    sharded_flash_pn_fir_tau_attention,
+    unshard_bh,
+)
 
 __all__ = [
     "PnFirConfig",
@@ -44,4 +51,5 @@ __all__ = [
     "unshard_bh",
     "share_tau",
     "sharded_flash_pn_fir_tau_attention",
+    "TauGradReducer",
 ]

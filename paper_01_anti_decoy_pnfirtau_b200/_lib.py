@@ -17,6 +17,7 @@ OK, EINVAL, EUNSUPPORTED, ECUDA = 0, -1, -2, -3
 DEV_OK, DEV_WAIT_TIMEOUT = 0, 1
 SILENCE_PEAK, SILENCE_MASS_RELU, SILENCE_MASS_POW = 0, 1, 2
 FLASH_FORCE_GENERIC, FLASH_DETERMINISTIC, FLASH_PREFER_SM100 = 0x1, 0x2, 0x4
+FLASH_TEST_STALL = 0x100  # test-only: the tcgen05 kernels take their timeout path
 FIR_FUSED_TAPS = 7  # PNFT_FIR_FUSED_TAPS
 
 _I64x4 = c_int64 * 4
@@ -28,6 +29,7 @@ SIGNATURES: dict[str, tuple] = {
     "pnft_launch_count": (ctypes.c_uint64, []),
     "pnft_last_error": (ctypes.c_char_p, []),
     "pnft_query_caps": (c_int, [c_int, POINTER(c_int), POINTER(c_int), POINTER(c_int), POINTER(c_int), POINTER(c_int)]),
+    "pnft_mapped_status_ptr": (c_int, [_P, POINTER(c_void_p)]),
     "pnft_fir_fwd": (
         c_int,
         [_P, c_int64, c_int64, c_int64, _P, c_int, _P, c_int64, c_int64, c_int64, c_int64, c_int64, c_int64, c_int, _P],

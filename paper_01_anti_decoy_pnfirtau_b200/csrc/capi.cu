@@ -63,6 +63,20 @@ extern "C" int pnft_query_caps(int device, int* cc_major, int* cc_minor, int* sm
   return PNFT_OK;
 }
 
+extern "C" int pnft_mapped_status_ptr(void* host_word, void** device_ptr) {
+  if (!host_word || !device_ptr) return fail(PNFT_EINVAL, "mapped_status_ptr: null pointer");
+  *device_ptr = nullptr;
+  void* d = nullptr;
+  const cudaError_t e = cudaHostGetDevicePointer(&d, host_word, 0);
+  if (e != cudaSuccess) {
+    (void)cudaGetLastError();  // not sticky: clear it for the caller's next launch check
+    return fail(PNFT_EINVAL, "mapped_status_ptr: %s (the word must be pinned host memory mapped into the device)",
+                cudaGetErrorString(e));
+  }
+  *device_ptr = d;
+  return PNFT_OK;
+}
+
 static int fill_common(FlashArgs& a, const void* q, const int64_t* sq, const void* k, const int64_t* sk,
                        const void* v, const int64_t* sv, const float* tau, int64_t B, int64_t H, int64_t N,
                        int64_t D, float scale, float gamma, int has_gamma, int causal, int dtype, int flags,

@@ -64,7 +64,8 @@ enum : int {
   B_FLAG = 14,  // plain arrive after the o_written flag is stored (release for the flag)
   B_RAWFULL = 15,   // [2] fused FIR: raw K rows (with halo) landed
   B_RAWEMPTY = 17,  // [2] fused FIR: raw stage read by the filter warps
-  B_COUNT = 19
+  B_STALL = 19,     // test-only: a barrier nothing arrives on (PNFT_FLASH_TEST_STALL)
+  B_COUNT = 20
 };
 
 // Fused FIR: raw K rows [128 j - FIR_HALO, 128 j + 128) of tile j are staged by TMA
@@ -134,6 +135,7 @@ struct FwdParams {
   int H, N, nq, nk;
   float scale, gamma;
   int has_gamma, causal;
+  int stall;  // PNFT_FLASH_TEST_STALL: the elementwise warps first wait on B_STALL
 };
 
 template <int D, bool FIR>
@@ -170,6 +172,7 @@ __global__ void __launch_bounds__(f_threads<FIR>(), FIR ? 1 : 2) flash_fwd_sm100
     }
     mbar_init(bar(B_OFULL), 1);
     mbar_init(bar(B_FLAG), 1);
+    mbar_init(bar(B_STALL), 1);
     *abort_flag = 0;
     *reinterpret_cast<volatile int*>(smem + L::OFF_OWR) = 0;
     fence_barrier_init();
@@ -349,9 +352,12 @@ __global__ void __launch_bounds__(f_threads<FIR>(), FIR ? 1 : 2) flash_fwd_sm100
     // `dead` (warp-uniform) turns the rest of the loop into no-ops after an
     // abort, while every warp still passes the named barriers.
     bool dead = false;
+    // test-only (p.stall): the first wait is on B_STALL, which nothing completes,
+    // so the warps run it out and unwind like any timed-out wait
+    const uint32_t bar_s0 = p.stall ? bar(B_STALL) : bar(B_SFULL);
     for (int j = 0; j < ntiles; ++j) {
       const int s = j & 1;
-      if (!dead) dead = !warp_wait(bar(B_SFULL + s), (j >> 1) & 1, ab);
+      if (!dead) dead = !warp_wait(j == 0 ? bar_s0 : bar(B_SFULL + s), (j >> 1) & 1, ab);
       const uint32_t scol = tmem + lane_off + TM_S + (uint32_t)FN * s + (uint32_t)FQ * g;
       static_assert(FQ == 32 || FQ == 64, "32 or 64 key columns per warp");
       uint32_t r[FQ / 32][32];
@@ -658,6 +664,7 @@ int flash_fwd_sm100(const FlashArgs& a, cudaStream_t st) {
   p.gamma = a.gamma;
   p.has_gamma = a.has_gamma;
   p.causal = a.causal;
+  p.stall = (a.flags & PNFT_FLASH_TEST_STALL) ? 1 : 0;
   if (p.nq > 65535) return fail(PNFT_EUNSUPPORTED, "flash fwd sm100: N = %lld needs more than 65535 query tiles", (long long)a.N);
   const dim3 grid((unsigned)(a.B * a.H), (unsigned)p.nq);
   auto launch = [&](auto kern, int smem) -> int {

@@ -68,7 +68,8 @@ enum : int {
   C_DKV = 22,
   C_FLAG = 23,  // plain arrive after dkv_written is stored (release for the flag)
   C_KRAW = 24,  // fused FIR: raw K rows (with halo) landed
-  C_COUNT = 25
+  C_STALL = 25, // test-only: a barrier nothing arrives on (PNFT_FLASH_TEST_STALL)
+  C_COUNT = 26
 };
 
 template <int D>
@@ -151,6 +152,7 @@ struct BwdParams {
   int H, N, nq64, nkt;
   float scale;
   int causal;
+  int stall;  // PNFT_FLASH_TEST_STALL: the elementwise warps first wait on C_STALL
 };
 
 // Warp-cooperative walk over the query tiles [i0, n) whose live bit is set: 32
@@ -232,6 +234,7 @@ __global__ void __launch_bounds__(B_THREADS, 1) flash_bwd_sm100_kernel(const __g
     }
     mbar_init(bar(C_DKV), 1);
     mbar_init(bar(C_FLAG), 1);
+    mbar_init(bar(C_STALL), 1);
     *abort_flag = 0;
     *dkv_written = 0;
     fence_barrier_init();
@@ -454,7 +457,7 @@ __global__ void __launch_bounds__(B_THREADS, 1) flash_bwd_sm100_kernel(const __g
       const int et = threadIdx.x - 128, cp = et & 31, g = (et >> 5) % DG, rb = (et >> 5) / DG;
       float2 h[FIR_TAPS];
       fir_load_taps(p.taps, h);
-      dead = !warp_wait(bar(C_KRAW), 0, ab);
+      if (!dead) dead = !warp_wait(bar(C_KRAW), 0, ab);
       if (!dead) fir_filter_rows<NR>(smem + L::OFF_RAW + g * L::RAWGROUP, smem + L::OFF_K + g * L::KGROUP, cp, rb * NR, h);
       fence_proxy_async_smem();  // the tensor core reads K through the async proxy
       named_bar_sync(3, 128 * NEW);
@@ -469,9 +472,11 @@ __global__ void __launch_bounds__(B_THREADS, 1) flash_bwd_sm100_kernel(const __g
       // S/dP of this tile, its coefficient records, and a free dS buffer (d=128:
       // also a free P^T buffer; d=64 writes P^T over its own S columns)
       const int sb = t % L::NSB;
+      // test-only (p.stall): the first tile waits on C_STALL, which nothing
+      // completes, so the warps run the wait out and unwind like any timeout
       if (!dead)
-        dead = !warp_wait3(bar(C_SDPFULL + sb), (t / L::NSB) & 1, bar(C_QDFULL + qs), (t / NQS) & 1,
-                           bar(C_PDSEMPTY + ds), ((t / L::NDS) & 1) ^ 1, ab);
+        dead = !warp_wait3(t == 0 && p.stall ? bar(C_STALL) : bar(C_SDPFULL + sb), (t / L::NSB) & 1,
+                           bar(C_QDFULL + qs), (t / NQS) & 1, bar(C_PDSEMPTY + ds), ((t / L::NDS) & 1) ^ 1, ab);
       uint32_t rs[CW], rp[CW];
       if (!dead) {
         tc_fence_after();
@@ -771,6 +776,7 @@ int flash_bwd_sm100(const FlashArgs& a0, cudaStream_t st) {
   p.nkt = nkt;
   p.scale = a.scale;
   p.causal = a.causal;
+  p.stall = (a.flags & PNFT_FLASH_TEST_STALL) ? 1 : 0;
   if (nkt > 65535) return fail(PNFT_EUNSUPPORTED, "flash bwd sm100: N = %lld needs more than 65535 key tiles", (long long)a.N);
   const dim3 grid((unsigned)(a.B * a.H), (unsigned)nkt);
   auto launch = [&](auto kern, int smem) -> int {

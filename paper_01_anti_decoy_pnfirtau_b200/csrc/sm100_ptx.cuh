@@ -48,11 +48,18 @@ __device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
   return ok != 0;
 }
 
+// Records a device-side failure in the caller's status word: a system-scope
+// store, so the word may live in device memory or in pinned host memory mapped
+// into the device's address space (the host then sees it without a copy).
+__device__ __forceinline__ void report_status(int32_t* status, int32_t code) {
+  if (status) asm volatile("st.relaxed.sys.global.s32 [%0], %1;" ::"l"(status), "r"(code) : "memory");
+}
+
 // Shared abort word of a CTA: the first role whose wait times out sets it, so
 // every other role stops waiting on work that will never arrive.
 struct Abort {
   volatile int* flag;   // shared memory
-  int32_t* status;      // global status word (may be null)
+  int32_t* status;      // status word (device or mapped host memory; may be null)
 };
 
 // Bounded wait on the phase with the given parity; false if the CTA aborted.
@@ -66,7 +73,7 @@ __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, const A
     if (*ab.flag) return false;
     if (globaltimer() - t0 > kWaitTimeoutNs) {
       *ab.flag = 1;
-      if (ab.status) atomicExch(ab.status, PNFT_DEV_WAIT_TIMEOUT);
+      report_status(ab.status, PNFT_DEV_WAIT_TIMEOUT);
       return false;
     }
   }
@@ -87,7 +94,7 @@ __device__ __forceinline__ bool warp_wait(uint32_t bar, uint32_t parity, const A
     if (__any_sync(kAll, globaltimer() - t0 > kWaitTimeoutNs)) {
       if ((threadIdx.x & 31) == 0) {
         *ab.flag = 1;
-        if (ab.status) atomicExch(ab.status, PNFT_DEV_WAIT_TIMEOUT);
+        report_status(ab.status, PNFT_DEV_WAIT_TIMEOUT);
       }
       __syncwarp();
       return false;
@@ -110,7 +117,7 @@ __device__ __forceinline__ bool warp_wait3(uint32_t b0, uint32_t p0, uint32_t b1
     if (__any_sync(kAll, globaltimer() - t0 > kWaitTimeoutNs)) {
       if ((threadIdx.x & 31) == 0) {
         *ab.flag = 1;
-        if (ab.status) atomicExch(ab.status, PNFT_DEV_WAIT_TIMEOUT);
+        report_status(ab.status, PNFT_DEV_WAIT_TIMEOUT);
       }
       __syncwarp();
       return false;

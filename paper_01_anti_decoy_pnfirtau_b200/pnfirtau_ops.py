@@ -66,30 +66,84 @@ def _ptr(t: torch.Tensor | None) -> int | None:
     return None if t is None else t.data_ptr()
 
 
-_status: dict[int, torch.Tensor] = {}
+class _StatusWord:
+    """Per-device int32 word the tcgen05 kernels set to a PNFT_DEV_* code when a
+    pipeline wait times out (their outputs are then invalid). It lives in pinned
+    host memory mapped into the device, so the host sees a code as soon as the
+    kernel writes it, with no copy and no synchronisation: every flash call
+    first checks the word and raises if an earlier kernel on the device reported
+    a failure. Where the mapping is unavailable the word is device memory, read
+    only by check_device_status()."""
+
+    def __init__(self, idx: int):
+        import ctypes
+
+        self.host = torch.zeros(1, dtype=torch.int32).pin_memory()
+        out = ctypes.c_void_p()
+        with torch.cuda.device(idx):
+            rc = _lib.lib().pnft_mapped_status_ptr(self.host.data_ptr(), ctypes.byref(out))
+        if rc == _lib.OK and out.value:
+            self.dev = None
+            self.ptr = int(out.value)
+        else:
+            self.host = None
+            self.dev = torch.zeros(1, dtype=torch.int32, device=torch.device("cuda", idx))
+            self.ptr = self.dev.data_ptr()
+
+    def peek(self) -> int:
+        """The code seen so far without synchronising (0 when only device memory holds it)."""
+        return int(self.host[0]) if self.host is not None else _lib.DEV_OK
+
+    def read(self) -> int:
+        return int(self.host[0]) if self.host is not None else int(self.dev.item())
+
+    def reset(self) -> None:
+        (self.host if self.host is not None else self.dev).zero_()
 
 
-def _status_word(dev: torch.device) -> torch.Tensor:
-    """Per-device int32 word where pipelined kernels report a timed-out wait."""
+_status: dict[int, _StatusWord] = {}
+
+
+def _status_entry(dev: torch.device) -> _StatusWord:
     idx = dev.index if dev.index is not None else torch.cuda.current_device()
-    t = _status.get(idx)
-    if t is None:
-        t = torch.zeros(1, dtype=torch.int32, device=torch.device("cuda", idx))
-        _status[idx] = t
-    return t
+    w = _status.get(idx)
+    if w is None:
+        w = _status[idx] = _StatusWord(idx)
+    return w
+
+
+def _status_ptr(dev: torch.device) -> int:
+    """Device address of `dev`'s status word, for the kernels' `status` argument."""
+    return _status_entry(dev).ptr
+
+
+def _raise(v: int, dev, when: str) -> None:
+    raise RuntimeError(f"pn_fir_tau kernel on {dev} reported device status {v} {when} (pipeline wait timed out; "
+                       "the outputs of that call are invalid)")
+
+
+def _check_pending(dev: torch.device) -> None:
+    """Raises (and clears the word) if a kernel launched earlier on `dev` has
+    reported a failure; costs one host read, no synchronisation."""
+    w = _status_entry(dev)
+    v = w.peek()
+    if v != _lib.DEV_OK:
+        w.reset()
+        _raise(v, dev, "in an earlier call")
 
 
 def check_device_status(device: torch.device | int | None = None, reset: bool = True) -> None:
-    """Synchronise and raise if a kernel on ``device`` reported a device-side error."""
+    """Synchronise ``device`` and raise if a kernel on it reported a device-side error."""
     if device is None:
         device = torch.cuda.current_device()
     dev = torch.device("cuda", device) if isinstance(device, int) else torch.device(device)
-    w = _status_word(dev)
-    v = int(w.item())
+    torch.cuda.synchronize(dev)
+    w = _status_entry(dev)
+    v = w.read()
     if v != _lib.DEV_OK:
         if reset:
-            w.zero_()
-        raise RuntimeError(f"pn_fir_tau kernel reported device status {v} (pipeline wait timed out)")
+            w.reset()
+        _raise(v, dev, "")
 
 
 def _taps_f32(taps: torch.Tensor, dev: torch.device) -> torch.Tensor:
@@ -271,10 +325,13 @@ def triton_pn_fir_tau_scores(
 
 
 def _flash_flags() -> int:
-    return _lib.FLASH_FORCE_GENERIC if _FORCE_GENERIC else 0
+    return (_lib.FLASH_FORCE_GENERIC if _FORCE_GENERIC else 0) | _TEST_FLAGS
 
 
 _FORCE_GENERIC = False
+# Test-only PNFT_FLASH_* bits OR-ed into every flash call (forward and backward),
+# e.g. FLASH_TEST_STALL to exercise the kernels' timeout path.
+_TEST_FLAGS = 0
 
 
 def flash_kernel_path(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor) -> str:
@@ -297,6 +354,7 @@ class _FlashPnFirTauFn(torch.autograd.Function):
     @staticmethod
     def forward(ctx, q, k, v, score_tau, scale, gamma, causal_mask, out_layout):
         dev = _require_cuda("flash_pn_fir_tau_attention", q, k, v, score_tau)
+        _check_pending(dev)
         if not (q.dtype == k.dtype == v.dtype):
             raise RuntimeError(f"flash_pn_fir_tau_attention: q/k/v dtypes differ ({q.dtype}, {k.dtype}, {v.dtype})")
         B, H, N, D = q.shape
@@ -328,7 +386,7 @@ class _FlashPnFirTauFn(torch.autograd.Function):
                              _ptr(out32), _ptr(stats[0]), _ptr(stats[1]), _ptr(nmax[0]), _ptr(nmax[1]), B, H, N,
                              D, float(scale), gamma_val, has_gamma, int(bool(causal_mask)), _dtype_code(q), flags,
                              None,
-                             _ptr(_status_word(dev)), _stream(dev)),
+                             _status_ptr(dev), _stream(dev)),
             "pnft_flash_fwd",
         )
         ctx.save_for_backward(q, k, v, tau_f32, out, out32, stats, nmax)
@@ -341,8 +399,10 @@ class _FlashPnFirTauFn(torch.autograd.Function):
     def backward(ctx, grad_out):
         q, k, v, tau_f32, out, out32, stats, nmax = ctx.saved_tensors
         scale, gamma_val, has_gamma, causal, flags = ctx.args
+        flags |= _TEST_FLAGS
         B, H, N, D = q.shape
         dev = q.device
+        _check_pending(dev)
         if grad_out.dtype != q.dtype:
             grad_out = grad_out.to(q.dtype)
         if grad_out.stride(-1) != 1 or any(s % 8 for s in grad_out.stride()[:3]):
@@ -362,7 +422,7 @@ class _FlashPnFirTauFn(torch.autograd.Function):
                              _ptr(dk), _lib.i64x4(dk.stride()),
                              _ptr(dv), _lib.i64x4(dv.stride()), _ptr(dtau), _ptr(ws), ws.numel(), B, H, N, D,
                              scale, gamma_val, has_gamma, causal, _dtype_code(q), flags,
-                             _ptr(_status_word(dev)), _stream(dev)),
+                             _status_ptr(dev), _stream(dev)),
             "pnft_flash_bwd",
         )
         grad_tau = dtau.to(ctx.tau_dtype).reshape(ctx.tau_shape)
@@ -414,6 +474,7 @@ class _FlashFirFn(torch.autograd.Function):
     @staticmethod
     def forward(ctx, q, k, v, score_tau, taps, scale, gamma, causal_mask, out_layout, fused_forward=False):
         dev = _require_cuda("flash_pn_fir_tau_attention_fir", q, k, v, score_tau, taps)
+        _check_pending(dev)
         if not (q.dtype == k.dtype == v.dtype):
             raise RuntimeError(f"flash_pn_fir_tau_attention_fir: q/k/v dtypes differ ({q.dtype}, {k.dtype}, {v.dtype})")
         B, H, N, D = q.shape
@@ -443,7 +504,7 @@ class _FlashFirFn(torch.autograd.Function):
                                      _ptr(tau_f32), _ptr(out), _lib.i64x4(out.stride()), _ptr(out32),
                                      _ptr(stats[0]), _ptr(stats[1]), _ptr(nmax[0]), _ptr(nmax[1]), B, H, N, D,
                                      float(scale), gamma_val, has_gamma, int(bool(causal_mask)), _dtype_code(q),
-                                     flags, None, _ptr(_status_word(dev)), _stream(dev)),
+                                     flags, None, _status_ptr(dev), _stream(dev)),
                 "pnft_flash_fwd_fir",
             )
         else:
@@ -465,7 +526,7 @@ class _FlashFirFn(torch.autograd.Function):
                                  _lib.i64x4(v.stride()), _ptr(tau_f32), _ptr(out), _lib.i64x4(out.stride()),
                                  _ptr(out32), _ptr(stats[0]), _ptr(stats[1]), _ptr(nmax[0]), _ptr(nmax[1]), B, H, N,
                                  D, float(scale), gamma_val, has_gamma, int(bool(causal_mask)), _dtype_code(q),
-                                 flags, None, _ptr(_status_word(dev)), _stream(dev)),
+                                 flags, None, _status_ptr(dev), _stream(dev)),
                 "pnft_flash_fwd",
             )
         ctx.save_for_backward(q, k, v, tau_f32, taps_f32, out, out32, stats, nmax)
@@ -478,8 +539,10 @@ class _FlashFirFn(torch.autograd.Function):
     def backward(ctx, grad_out):
         q, k, v, tau_f32, taps_f32, out, out32, stats, nmax = ctx.saved_tensors
         scale, gamma_val, has_gamma, causal, flags = ctx.args
+        flags |= _TEST_FLAGS
         B, H, N, D = q.shape
         dev = q.device
+        _check_pending(dev)
         if grad_out.dtype != q.dtype:
             grad_out = grad_out.to(q.dtype)
         if grad_out.stride(-1) != 1 or any(s % 8 for s in grad_out.stride()[:3]):
@@ -504,7 +567,7 @@ class _FlashFirFn(torch.autograd.Function):
                                  _ptr(nmax[1]), _ptr(dq), _lib.i64x4(dq.stride()), _ptr(dk),
                                  _lib.i64x4(dk.stride()), _ptr(dv), _lib.i64x4(dv.stride()), _ptr(dtau),
                                  _ptr(dtaps), _ptr(ws), ws.numel(), B, H, N, D, scale, gamma_val, has_gamma, causal,
-                                 _dtype_code(q), flags, _ptr(_status_word(dev)), _stream(dev)),
+                                 _dtype_code(q), flags, _status_ptr(dev), _stream(dev)),
             "pnft_flash_bwd_fir",
         )
         grad_tau = dtau.to(ctx.tau_dtype).reshape(ctx.tau_shape)
@@ -547,6 +610,7 @@ def flash_pn_fir_tau_forward_stats(q, k_tilde, v, score_tau, scale=None, gamma=0
     64x64 tile the kernel processed as live. ``extra_flags`` are PNFT_FLASH_*
     bits (e.g. to select a kernel family for a comparison)."""
     dev = _require_cuda("flash_pn_fir_tau_forward_stats", q, k_tilde, v, score_tau)
+    _check_pending(dev)
     if scale is None:
         scale = 1.0 / math.sqrt(q.shape[-1])
     B, H, N, D = q.shape
@@ -563,7 +627,7 @@ def flash_pn_fir_tau_forward_stats(q, k_tilde, v, score_tau, scale=None, gamma=0
                          _lib.i64x4(v.stride()), _ptr(tau_f32), _ptr(out), _lib.i64x4(out.stride()), None,
                          _ptr(stats[0]), _ptr(stats[1]), _ptr(nmax[0]), _ptr(nmax[1]), B, H, N, D, float(scale),
                          gamma_val, has_gamma, int(bool(causal_mask)), _dtype_code(q), _flash_flags() | extra_flags,
-                         _ptr(tiles), _ptr(_status_word(dev)), _stream(dev)),
+                         _ptr(tiles), _status_ptr(dev), _stream(dev)),
         "pnft_flash_fwd",
     )
     return out, stats[0], stats[1], nmax[0], tiles.bool()

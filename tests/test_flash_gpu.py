@@ -171,34 +171,3 @@ def test_flash_exact_ties(cuda):
     _, _, _, Nmax, _ = flash_pn_fir_tau_forward_stats(q, k, v, torch.tensor(0.0, device=cuda))
     assert int(Nmax[0, 0, 40]) == 3
     assert_close_lowp(ours, ref, tol=2e-5, dtau_tol=2e-4)
-
-
-@pytest.mark.slow
-def test_flash_config3_full_size(cuda):
-    """BASELINE config 3 at full size (B8 H8 N4096 d64 bf16, 50% quiet query
-    blocks): size-independent checks over every head plus exact per-head parity
-    of the outputs, gradients and tau gradient against fp32 eager."""
-    B, H, N, D = 8, 8, 4096, 64
-    q, k, v, do = _qkv(B, H, N, D, 2024, torch.bfloat16, cuda, quiet_frac=0.5)
-    tau = 0.5
-    out, dq, dk, dv, dtau = run_ours(q, k, v, tau, do)
-    for t in (out, dq, dk, dv):
-        assert torch.isfinite(t).all()
-    _, M, _, _, tiles = flash_pn_fir_tau_forward_stats(q, k, v, torch.tensor(tau, device=cuda))
-    dtau_ref = 0.0
-    for bh in range(B * H):
-        b, h = divmod(bh, H)
-        sl = (slice(b, b + 1), slice(h, h + 1))
-        ref = run_oracle(q[sl], k[sl], v[sl], tau, do[sl])
-        dtau_ref += float(ref[4])
-        if bh % 16 == 0:
-            for name, a, r in zip(("out", "dq", "dk", "dv"), (out[sl], dq[sl], dk[sl], dv[sl]), ref[:4]):
-                assert rel_l2(a, r) < BF16_TOL, (bh, name)
-            ref_tiles, _, _ = O.tile_silence(q[sl].float(), k[sl].float(), tau)
-            peak_ref, _, _ = O.row_stats(q[sl].float(), k[sl].float(), torch.tensor(tau, device=cuda))
-            near = peak_ref.abs() < 1e-3
-            assert torch.equal((M[sl] > 0)[~near], (peak_ref > 0)[~near])
-            nT = ref_tiles.shape[-1]
-            near_t = near.reshape(1, 1, nT, 64).any(-1)[..., None].expand_as(ref_tiles)
-            assert not torch.any((tiles[sl] != ref_tiles) & ~near_t)
-    assert abs(float(dtau) - dtau_ref) <= BF16_TOL * abs(dtau_ref) + 1e-6

@@ -1,0 +1,154 @@
+"""Parity at the full sizes of BASELINE configs 3 and 5, through the public API.
+
+Config 3: B8 H8 N4096 d64 bf16, half of the 64-row query blocks scaled by 0.05,
+tau in {-0.5, 0, +0.5}. Gate masks (peak > 0) and the 64x64 silent-tile
+decisions are compared with the exp4b oracle on EVERY head; out/dq/dk/dv against
+the fp32 eager oracle per (b,h) on every eighth head; dtau against the sum of the
+oracle's per-head dtau over every head.
+
+Config 5: B8 H16 N16384 d128 bf16 (the long-context shape: 32-bit TMA row
+coordinates up to 16383, 128 key tiles per head, a 1 GiB fp32 dQ accumulator, 16384
+tau partials), plain and with the causal FIR on the raw keys fused into the
+kernels. out/dq/dk/dv per (b,h) on four sampled heads; dtau (and, fused, the tap
+gradient) against the oracle summed over all 128 heads.
+
+Tolerances (north star): bf16 outputs and gradients within 1e-2 relative L2 of
+the fp32 eager run on the same rounded inputs; dtau / dtaps within 1e-2
+relative; decisions identical except rows whose peak is within 1e-3 of the
+threshold.
+"""
+import pytest
+import torch
+
+import paper_01_anti_decoy_pnfirtau_b200 as P
+from conftest import rel_l2
+from oracle import pnfirtau_oracle as O
+from paper_01_anti_decoy_pnfirtau_b200.pnfirtau_ops import check_device_status, flash_pn_fir_tau_forward_stats
+
+pytestmark = [pytest.mark.gpu, pytest.mark.slow]
+
+TOL = 1e-2
+
+
+def _gen(B, H, N, D, seed, device, quiet_frac=0.0):
+    """Seeded q, k, v, dO ~ N(0,1) drawn on the device (config 5 holds 268 M
+    elements per tensor), rounded to bf16; with quiet_frac a seeded fraction of
+    the 64-row query blocks of every head is scaled by 0.05."""
+    g = torch.Generator(device=device).manual_seed(seed)
+    q = torch.randn(B, H, N, D, generator=g, device=device)
+    if quiet_frac:
+        nb = (N + 63) // 64
+        quiet = torch.rand(B, H, nb, generator=g, device=device) < quiet_frac
+        q = q * torch.where(quiet, 0.05, 1.0).repeat_interleave(64, dim=-1)[..., :N, None]
+    k = torch.randn(B, H, N, D, generator=g, device=device)
+    v = torch.randn(B, H, N, D, generator=g, device=device)
+    do = torch.randn(B, H, N, D, generator=g, device=device)
+    return tuple(t.to(torch.bfloat16) for t in (q, k, v, do))
+
+
+def _ours(q, k, v, do, tau, taps=None):
+    qq, kk, vv = (t.detach().requires_grad_(True) for t in (q, k, v))
+    tt = torch.tensor(tau, device=q.device, requires_grad=True)
+    hh = None
+    if taps is None:
+        out = P.flash_pn_fir_tau_attention(qq, kk, vv, tt)
+    else:
+        hh = taps.detach().clone().requires_grad_(True)
+        out = P.flash_pn_fir_tau_attention_fir(qq, kk, vv, tt, hh)
+    out.backward(do)
+    torch.cuda.synchronize()
+    check_device_status(q.device)
+    return out.detach(), qq.grad, kk.grad, vv.grad, float(tt.grad), (hh.grad if hh is not None else None)
+
+
+def _oracle_slice(q, k, v, do, tau, taps=None):
+    """fp32 eager run of one (b,h) slice; with taps the slice's raw keys are
+    filtered by the oracle's causal FIR (gradients reach k and the taps)."""
+    qr, kr, vr = (t.float().requires_grad_(True) for t in (q, k, v))
+    tr = torch.tensor(tau, device=q.device, requires_grad=True)
+    hr = None
+    kt = kr
+    if taps is not None:
+        hr = taps.float().clone().requires_grad_(True)
+        N, D = kr.shape[-2:]
+        kt = O.causal_fir(kr.reshape(1, N, D), hr).reshape(kr.shape)
+    out = O.pn_fir_tau_attention(qr, kt, vr, tr)
+    out.backward(do.float())
+    return out.detach(), qr.grad, kr.grad, vr.grad, float(tr.grad), (hr.grad if hr is not None else None)
+
+
+def _sl(bh, H):
+    b, h = divmod(bh, H)
+    return (slice(b, b + 1), slice(h, h + 1))
+
+
+@pytest.mark.parametrize("tau", [-0.5, 0.0, 0.5])
+def test_config3_full_size(cuda, tau):
+    B, H, N, D = 8, 8, 4096, 64
+    q, k, v, do = _gen(B, H, N, D, 2024, cuda, quiet_frac=0.5)
+    ours = _ours(q, k, v, do, tau)
+    for t in ours[:4]:
+        assert torch.isfinite(t).all()
+    t = torch.tensor(tau, device=cuda)
+    _, M, _, _, tiles = flash_pn_fir_tau_forward_stats(q, k, v, t)
+    check_device_status(cuda)
+    dtau_ref = 0.0
+    n_tiles = n_silent = 0
+    for bh in range(B * H):
+        sl = _sl(bh, H)
+        # decisions on every head
+        ref_tiles, _, peak_ref = O.tile_silence(q[sl].float(), k[sl].float(), tau)
+        near = peak_ref.abs() < 1e-3
+        assert torch.equal((M[sl] > 0)[~near], (peak_ref > 0)[~near]), ("gate", bh)
+        nT = ref_tiles.shape[-1]
+        near_t = near.reshape(1, 1, nT, 64).any(-1)[..., None].expand_as(ref_tiles)
+        assert not torch.any((tiles[sl] != ref_tiles) & ~near_t), ("tiles", bh)
+        causal = torch.tril(torch.ones(nT, nT, dtype=torch.bool, device=cuda))
+        n_tiles += int(causal.sum())
+        n_silent += int((~ref_tiles[0, 0] & causal).sum())
+        # gradients: dtau on every head, the tensors on every eighth
+        ref = _oracle_slice(q[sl], k[sl], v[sl], do[sl], tau)
+        dtau_ref += ref[4]
+        if bh % 8 == 0:
+            for name, a, r in zip(("out", "dq", "dk", "dv"), (ours[0][sl], ours[1][sl], ours[2][sl], ours[3][sl]),
+                                  ref[:4]):
+                err = rel_l2(a, r)
+                assert err < TOL, (bh, name, err)
+    assert abs(ours[4] - dtau_ref) <= TOL * abs(dtau_ref) + 1e-6, (ours[4], dtau_ref)
+    if tau == 0.5:  # the survey's regime: about half of the causal tiles are silent
+        assert 0.3 < n_silent / n_tiles < 0.7, n_silent / n_tiles
+    else:
+        assert n_silent == 0
+
+
+C5 = (8, 16, 16384, 128)
+C5_HEADS = (0, 45, 90, 127)
+
+
+@pytest.mark.parametrize("fused_fir", [False, True], ids=["plain", "fused_fir"])
+def test_config5_full_size(cuda, fused_fir):
+    B, H, N, D = C5
+    q, k, v, do = _gen(B, H, N, D, 5005, cuda)
+    taps = O.gaussian_taps(7).to(cuda) if fused_fir else None
+    assert P.flash_kernel_path(q, k, v) == "sm100"
+    ours = _ours(q, k, v, do, 0.0, taps)
+    for t in ours[:4]:
+        assert torch.isfinite(t).all()
+    dtau_ref = 0.0
+    dtaps_ref = torch.zeros(7, dtype=torch.float64, device=cuda)
+    for bh in range(B * H):
+        sl = _sl(bh, H)
+        ref = _oracle_slice(q[sl], k[sl], v[sl], do[sl], 0.0, taps)
+        dtau_ref += ref[4]
+        if fused_fir:
+            dtaps_ref += ref[5].double()
+        if bh in C5_HEADS:
+            for name, a, r in zip(("out", "dq", "dk", "dv"), (ours[0][sl], ours[1][sl], ours[2][sl], ours[3][sl]),
+                                  ref[:4]):
+                err = rel_l2(a, r)
+                assert err < TOL, (bh, name, err)
+        del ref
+    assert abs(ours[4] - dtau_ref) <= TOL * abs(dtau_ref) + 1e-6, (ours[4], dtau_ref)
+    if fused_fir:
+        err = rel_l2(ours[5], dtaps_ref)
+        assert err < TOL, ("dtaps", err, ours[5].tolist(), dtaps_ref.tolist())

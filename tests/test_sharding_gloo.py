@@ -17,6 +17,7 @@ import torch.multiprocessing as mp
 
 from oracle import pnfirtau_oracle as O
 from paper_01_anti_decoy_pnfirtau_b200.sharding import (
+    TauGradReducer,
     bh_range,
     shard_bh,
     share_tau,
@@ -72,7 +73,7 @@ def _inputs(B, H, N, D, seed):
     return q, k, v, do
 
 
-def _worker(rank, world, port, B, H, N, D, tau0, result_q):
+def _worker(rank, world, port, B, H, N, D, tau0, result_q, deferred=False):
     os.environ["MASTER_ADDR"] = "127.0.0.1"
     os.environ["MASTER_PORT"] = str(port)
     import torch.distributed as dist
@@ -84,20 +85,34 @@ def _worker(rank, world, port, B, H, N, D, tau0, result_q):
         q, k, v, do = _inputs(B, H, N, D, seed=7)
         ql, kl, vl, dol = (shard_bh(t, rank, world).clone().requires_grad_(True) for t in (q, k, v, do))
         tau = torch.tensor(tau0, dtype=torch.float64, requires_grad=True)
-        out = sharded_flash_pn_fir_tau_attention(ql, kl, vl, tau, None, 0.5, True, attention=_oracle_attention)
+        reducer = TauGradReducer() if deferred else None
+        out = sharded_flash_pn_fir_tau_attention(ql, kl, vl, tau, None, 0.5, True, attention=_oracle_attention,
+                                                 reducer=reducer)
         out.backward(dol.detach())
+        if deferred:
+            assert tau.grad is None  # nothing reaches tau until the reducer is finalised
+            # a second backward accumulates a second partial sum in the reducer
+            out2 = sharded_flash_pn_fir_tau_attention(ql.detach(), kl.detach(), vl.detach(), tau, None, 0.5, True,
+                                                      attention=_oracle_attention, reducer=reducer)
+            out2.backward(dol.detach())
+            assert reducer.pushes == 2
+            reducer.accumulate_into(tau)
+            assert reducer.result() is None
+            tau.grad /= 2
         result_q.put((rank, out.detach(), ql.grad, kl.grad, vl.grad, tau.grad.item()))
     finally:
         dist.destroy_process_group()
 
 
+@pytest.mark.parametrize("deferred", [False, True], ids=["inline", "reducer"])
 @pytest.mark.parametrize("world", [2])
-def test_two_rank_gloo_matches_single_process(world):
+def test_two_rank_gloo_matches_single_process(world, deferred):
     B, H, N, D, tau0 = 2, 3, 40, 8, 0.1
     ctx = mp.get_context("spawn")
     result_q = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_worker, args=(r, world, port, B, H, N, D, tau0, result_q)) for r in range(world)]
+    procs = [ctx.Process(target=_worker, args=(r, world, port, B, H, N, D, tau0, result_q, deferred))
+             for r in range(world)]
     for p in procs:
         p.start()
     results = {}
