@@ -9,8 +9,10 @@ oracle's per-head dtau over every head.
 Config 5: B8 H16 N16384 d128 bf16 (the long-context shape: 32-bit TMA row
 coordinates up to 16383, 128 key tiles per head, a 1 GiB fp32 dQ accumulator, 16384
 tau partials), plain and with the causal FIR on the raw keys fused into the
-kernels. out/dq/dk/dv per (b,h) on four sampled heads; dtau (and, fused, the tap
-gradient) against the oracle summed over all 128 heads.
+kernels (the oracle then filters in fp32 and rounds the filtered keys to bf16,
+as the reference's bf16 path and the fused kernels do). out/dq/dk/dv per (b,h)
+on four sampled heads; dtau (and, fused, the tap gradient) against the oracle
+summed over all 128 heads.
 
 Tolerances (north star): bf16 outputs and gradients within 1e-2 relative L2 of
 the fp32 eager run on the same rounded inputs; dtau / dtaps within 1e-2
@@ -71,10 +73,18 @@ def _oracle_slice(q, k, v, do, tau, taps=None):
     if taps is not None:
         hr = taps.float().clone().requires_grad_(True)
         N, D = kr.shape[-2:]
-        kt = O.causal_fir(kr.reshape(1, N, D), hr).reshape(kr.shape)
+        kt = _bf16_round(O.causal_fir(kr.reshape(1, N, D), hr).reshape(kr.shape))
     out = O.pn_fir_tau_attention(qr, kt, vr, tr)
     out.backward(do.float())
     return out.detach(), qr.grad, kr.grad, vr.grad, float(tr.grad), (hr.grad if hr is not None else None)
+
+
+def _bf16_round(x):
+    """x rounded to bf16 in value, with an identity gradient: the reference's
+    bf16 module path returns the filtered keys of triton_causal_fir in the
+    input dtype (src/triton_pnfirtau.py:629-658), and the fused kernels round
+    them the same way before the QK^T MMA."""
+    return x + (x.to(torch.bfloat16).float() - x).detach()
 
 
 def _sl(bh, H):

@@ -1,8 +1,8 @@
 """The bounded pipeline waits of the tcgen05 kernels, run out on purpose.
 
-With the test-only flag PNFT_FLASH_TEST_STALL the elementwise warps first wait
-on an mbarrier that nothing arrives on, with a 2 ms limit. That is the failure
-path of every pipeline wait: the warp sets the CTA's abort word and the status
+With the test-only flag PNFT_FLASH_TEST_STALL the elementwise warps make their
+first pipeline wait on an mbarrier that nothing arrives on, so it runs out after
+the kernels' 1 s limit. That is the failure path of every pipeline wait: the warp sets the CTA's abort word and the status
 word, the producer and MMA roles stop at their next wait, the producer lets its
 own TMA copies land, the MMA issuer waits for its MMAs, TMEM is freed and the
 kernel returns. Nothing faults, traps or spins without a limit; the test checks
@@ -45,8 +45,11 @@ def _oracle(q, k, v, do, tau, fused_fir=False):
     tr = torch.tensor(tau, device=q.device, requires_grad=True)
     kt = kr
     if fused_fir:
+        # filtered in fp32, rounded to bf16 as the fused kernels (and the reference's
+        # bf16 path) do; identity gradient through the rounding
         B, H, N, D = kr.shape
         kt = O.causal_fir(kr.transpose(1, 2).reshape(B, N, H * D), O.gaussian_taps(7).to(q.device))
+        kt = kt + (kt.to(torch.bfloat16).float() - kt).detach()
         kt = kt.view(B, N, H, D).transpose(1, 2)
     out = O.pn_fir_tau_attention(qr, kt, vr, tr)
     out.backward(do.float())
