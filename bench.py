@@ -72,6 +72,8 @@ def parse_args():
     ap.add_argument("--no-fir", action="store_true")
     ap.add_argument("--no-sweep", action="store_true", help="skip the config-3 tau sweep")
     ap.add_argument("--no-c5", action="store_true", help="skip the config-5 measurement")
+    ap.add_argument("--no-triton", action="store_true",
+                    help="reference arm: skip timing the reference's Triton kernels on the GPU")
     ap.add_argument("--sweep-steps", type=int, default=10)
     ap.add_argument("--c5-steps", type=int, default=4)
     ap.add_argument("--e2e-chunks", type=int, default=8,
@@ -267,21 +269,55 @@ def flops_fwd_bwd(w: dict) -> float:
     return 7.0 * w["B"] * w["H"] * w["N"] ** 2 * w["D"]
 
 
-def cpu_oracle_sample(w: dict, seconds: float, seed: int, steps: int | None = None):
-    """Times the CPU oracle (fp32 eager algorithm) on whole (b,h) slices of the
-    workload; returns (TFLOP/s, threads, slices, seconds)."""
-    from oracle import pnfirtau_oracle as O
+def reference_package():
+    """The reference's own package (src.triton_pnfirtau, src.pnfirtau_attention)
+    as staged unchanged into oracle/_ref by oracle/stage_ref.py, or None when it
+    was not staged. Used only by the CPU-baseline legs and the reference arm."""
+    from oracle import stage_ref
 
+    d = stage_ref.staged()
+    if d is None:
+        return None
+    if str(d) not in sys.path:
+        sys.path.insert(0, str(d))
+    import src.pnfirtau_attention as A
+    import src.triton_pnfirtau as R
+
+    return R, A
+
+
+def cpu_oracle_sample(w: dict, seconds: float, seed: int, steps: int | None = None):
+    """Times the reference's CPU path of the operator on whole (b,h) slices of
+    the workload, fp32 fwd+bwd: raw = q k^T, the reference's own
+    triton_pn_fir_tau_scores (on CPU tensors it runs its eager fallback,
+    power_norm_peak_gate, src/triton_pnfirtau.py:797-811), then @ v. Without the
+    staged reference package, the oracle's restatement of the same algorithm.
+    Returns (TFLOP/s, threads, slices, seconds, kind, what)."""
     torch.set_num_threads(len(os.sched_getaffinity(0)))
     N, D = w["N"], w["D"]
+    scale = 1.0 / math.sqrt(D)
     flops_slice = 7.0 * N * N * D
     g = torch.Generator().manual_seed(seed)
+    ref = reference_package()
+    if ref is not None:
+        R = ref[0]
+        kind, what = "reference", "the reference's own triton_pn_fir_tau_scores CPU path (oracle/_ref, unchanged)"
+
+        def attn(q, k, v, tau):
+            return torch.matmul(R.triton_pn_fir_tau_scores(torch.matmul(q, k.transpose(-2, -1)), tau, scale), v)
+    else:
+        from oracle import pnfirtau_oracle as O
+
+        kind, what = "port", "oracle/pnfirtau_oracle.py, the reference's eager algorithm restated"
+
+        def attn(q, k, v, tau):
+            return O.pn_fir_tau_attention(q, k, v, tau, scale)
 
     def one():
         q, k, v, do = (torch.randn(1, 1, N, D, generator=g) for _ in range(4))
         q.requires_grad_(True), k.requires_grad_(True), v.requires_grad_(True)
         tau = torch.tensor(0.0, requires_grad=True)
-        out = O.pn_fir_tau_attention(q, k, v, tau)
+        out = attn(q, k, v, tau)
         torch.autograd.grad(out, (q, k, v, tau), do)
 
     one()  # warm-up
@@ -293,7 +329,63 @@ def cpu_oracle_sample(w: dict, seconds: float, seed: int, steps: int | None = No
         el = time.perf_counter() - t0
         if (steps is not None and n >= steps) or (steps is None and el >= seconds):
             break
-    return flops_slice * n / el / 1e12, torch.get_num_threads(), n, el
+    return flops_slice * n / el / 1e12, torch.get_num_threads(), n, el, kind, what
+
+
+def reference_triton_b200(args, w: dict) -> dict:
+    """The reference's own Triton Flash kernels (flash_pn_fir_tau_attention,
+    src/triton_pnfirtau.py:971-983, unchanged, from oracle/_ref) timed fwd+bwd on
+    one B200 on this workload's shape and inputs, at the config-3 tau sweep
+    {-0.5, 0, +0.5} (the first value is the headline tau). CUDA events, after
+    Triton's JIT warm-up."""
+    if not torch.cuda.is_available():
+        return {"unavailable": "no CUDA device in this process"}
+    ref = reference_package()
+    if ref is None:
+        return {"unavailable": "the reference package was not staged into oracle/_ref (oracle/stage_ref.py)"}
+    R = ref[0]
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    q, k, v, do = make_inputs(w, args.seed, dev)
+    leaves = [t.detach().requires_grad_(True) for t in (q, k, v)]
+    flops = flops_fwd_bwd(w)
+    res = {"impl": "src/triton_pnfirtau.py flash_pn_fir_tau_attention (reference Triton, unchanged)",
+           "triton": __import__("triton").__version__}
+    taus = [args.tau] + [t for t in (-0.5, 0.0, 0.5) if t != args.tau]
+    try:
+        for tau0 in taus:
+            tau = torch.tensor(tau0, device=dev, requires_grad=True)
+
+            def one(ev=None):
+                if ev is not None:
+                    ev[0].record()
+                out = R.flash_pn_fir_tau_attention(*leaves, tau)
+                if ev is not None:
+                    ev[1].record()
+                torch.autograd.grad(out, (*leaves, tau), do)
+                if ev is not None:
+                    ev[2].record()
+
+            for _ in range(max(3, args.warmup)):
+                one()
+            torch.cuda.synchronize()
+            steps = max(5, min(args.steps, 20))
+            evs = [[torch.cuda.Event(enable_timing=True) for _ in range(3)] for _ in range(steps)]
+            s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            s.record()
+            for i in range(steps):
+                one(evs[i])
+            e.record()
+            torch.cuda.synchronize()
+            ms = s.elapsed_time(e) / steps
+            res[f"{tau0:+.1f}"] = {
+                "tau": tau0, "ms_per_step": round(ms, 4), "value": round(flops / (ms / 1e3) / 1e12, 2),
+                "unit": "TFLOP/s", "steps": steps,
+                "fwd_ms": round(statistics.mean(x[0].elapsed_time(x[1]) for x in evs), 4),
+                "bwd_ms": round(statistics.mean(x[1].elapsed_time(x[2]) for x in evs), 4)}
+    except Exception as exc:  # the reference's kernels may not compile or run on this GPU: report why
+        res["unavailable"] = f"{type(exc).__name__}: {exc}"[:400]
+    return res
 
 
 # ---------------------------------------------------------------------------
@@ -402,6 +494,8 @@ def bench_ours(args, dist_: Dist) -> dict:
     del q, k, v, do, leaves
     if not args.no_sweep and args.workload == "c3":
         result["tau_sweep"] = bench_tau_sweep(args, dist_, w, dev)
+    if not args.no_sweep:
+        result["deterministic"] = bench_deterministic(args, dist_, w, dev)
     if not args.no_c5 and args.workload == "c3":
         result["c5"] = bench_c5(args, dist_, dev)
     if not args.no_e2e:
@@ -411,14 +505,14 @@ def bench_ours(args, dist_: Dist) -> dict:
     if not args.no_fir:
         result["fir"] = bench_fir(args, dist_, dev)
     if dist_.rank == 0 and dist_.world == 1 and not args.no_cpu:
-        tf, cores, n, el = cpu_oracle_sample(w, args.cpu_seconds, args.seed)
-        result["cpu_baseline"] = {"value": round(tf, 6), "unit": "TFLOP/s", "cores": cores, "kind": "port",
+        tf, cores, n, el, kind, what = cpu_oracle_sample(w, args.cpu_seconds, args.seed)
+        result["cpu_baseline"] = {"value": round(tf, 6), "unit": "TFLOP/s", "cores": cores, "kind": kind,
                                   "sample": f"{n} (b,h) slices of [1,1,{N},{D}] fp32 fwd+bwd in {el:.1f} s "
-                                            f"(oracle/pnfirtau_oracle.py, torch CPU eager)"}
+                                            f"({what}, torch CPU eager)"}
     return result
 
 
-def _time_fwd_bwd(q, k, v, do, tau, steps: int, warmup: int, reducer):
+def _time_fwd_bwd(q, k, v, do, tau, steps: int, warmup: int, reducer, attention=None):
     """(total ms, mean fwd ms, mean bwd ms) of `steps` fwd+bwd calls of this rank's
     shard through the public API; tau's gradient through `reducer`."""
     from paper_01_anti_decoy_pnfirtau_b200.sharding import sharded_flash_pn_fir_tau_attention
@@ -428,7 +522,7 @@ def _time_fwd_bwd(q, k, v, do, tau, steps: int, warmup: int, reducer):
     def one(ev=None):
         if ev is not None:
             ev[0].record()
-        out = sharded_flash_pn_fir_tau_attention(*leaves, tau, reducer=reducer)
+        out = sharded_flash_pn_fir_tau_attention(*leaves, tau, reducer=reducer, attention=attention)
         if ev is not None:
             ev[1].record()
         torch.autograd.grad(out, (*leaves, tau), do, allow_unused=True)
@@ -498,6 +592,25 @@ def bench_tau_sweep(args, dist_: Dist, w: dict, dev) -> dict:
     out["note"] = ("algorithmic FLOPs 7*B*H*N^2*d per step at every tau (skipped tiles counted); this rank's "
                    "shard; fractions over causal 64x64 tiles")
     return out
+
+
+def bench_deterministic(args, dist_: Dist, w: dict, dev) -> dict:
+    """The same fwd+bwd with the ordered (bitwise reproducible) dQ accumulation
+    (flash_pn_fir_tau_attention(..., deterministic=True))."""
+    import functools
+
+    from paper_01_anti_decoy_pnfirtau_b200 import TauGradReducer
+    from paper_01_anti_decoy_pnfirtau_b200.pnfirtau_ops import flash_pn_fir_tau_attention
+
+    q, k, v, do = make_inputs(w, args.seed + 1000 * dist_.rank, dev)
+    tau = torch.tensor(args.tau, device=dev, requires_grad=True)
+    attn = functools.partial(flash_pn_fir_tau_attention, deterministic=True)
+    ms, fwd, bwd = _time_fwd_bwd(q, k, v, do, tau, args.sweep_steps, 3, TauGradReducer(), attention=attn)
+    ms = dist_.max(ms, dev)
+    return {"ms_per_step": round(ms / args.sweep_steps, 4),
+            "value": round(dist_.world * flops_fwd_bwd(w) * args.sweep_steps / (ms / 1e3) / 1e12, 2),
+            "unit": "TFLOP/s", "fwd_ms": round(fwd, 4), "bwd_ms": round(bwd, 4), "tau": args.tau,
+            "note": "dQ contributions added in key order (turn counters): bitwise reproducible gradients"}
 
 
 def bench_c5(args, dist_: Dist, dev) -> dict:
@@ -755,24 +868,29 @@ def bench_lm_graph(args, dev, cfg, batches) -> dict:
 
 
 def bench_reference(args, dist_: Dist) -> dict | None:
+    """The reference arm: the reference's own CPU path of the operator on the
+    host cores (see cpu_oracle_sample; one whole (b,h) slice per step), rank 0
+    only. Alongside, as `triton_b200`, the reference's own Triton Flash kernels
+    timed on GPU 0 (reference_triton_b200)."""
     if dist_.rank != 0:
         return None
     w = WORKLOADS[args.workload]
-    from oracle import pnfirtau_oracle as O  # noqa: F401  (imported for its CPU eager path)
-
     for _ in range(args.warmup):
         cpu_oracle_sample(w, 0.0, args.seed, steps=1)
-    tf, cores, n, el = cpu_oracle_sample(w, 0.0, args.seed, steps=args.steps)
+    tf, cores, n, el, kind, what = cpu_oracle_sample(w, 0.0, args.seed, steps=args.steps)
     sample = (f"each step = one (b,h) slice [1,1,{w['N']},{w['D']}] fp32 fwd+bwd of the {args.workload} workload "
-              f"(oracle/pnfirtau_oracle.py: the reference's eager torch algorithm), {cores} threads")
-    return {
+              f"({what}), {cores} threads")
+    res = {
         "impl": "reference", "metric": METRIC, "value": round(tf, 6), "unit": "TFLOP/s", "n_gpus": dist_.world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(1e3 * el / n, 3), "higher_is_better": True,
         "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
         "config": {"workload": f"{args.workload}: {w['desc']}", "B": w["B"], "H": w["H"], "N": w["N"], "d": w["D"]},
-        "cpu_baseline": {"value": round(tf, 6), "unit": "TFLOP/s", "cores": cores, "kind": "port", "sample": sample},
+        "cpu_baseline": {"value": round(tf, 6), "unit": "TFLOP/s", "cores": cores, "kind": kind, "sample": sample},
         "e2e": {"value": round(tf, 6), "unit": "TFLOP/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
+    if not args.no_triton:
+        res["triton_b200"] = reference_triton_b200(args, w)
+    return res
 
 
 def _claim_stdout():

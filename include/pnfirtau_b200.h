@@ -59,7 +59,11 @@ extern "C" {
 
 /* flags of the flash entry points */
 #define PNFT_FLASH_FORCE_GENERIC 0x1 /* use the SIMT kernel even where tcgen05 applies */
-#define PNFT_FLASH_DETERMINISTIC 0x2 /* reserved: ordered dQ accumulation             */
+/* Ordered dQ accumulation: the backward adds the dQ contributions of the key
+ * tiles of each 64-row query tile in key order (per-tile turn counters in the
+ * workspace, work taken in ticket order), so dq is bitwise reproducible run to
+ * run; dk, dv, dtau and the FIR's dk / dtaps always are. Slower backward. */
+#define PNFT_FLASH_DETERMINISTIC 0x2
 #define PNFT_FLASH_PREFER_SM100 0x4  /* tcgen05 kernels wherever their shape rules allow */
 /* Test-only: the tcgen05 kernels' elementwise warps make their first pipeline
  * wait on a barrier that nothing arrives on, so every CTA takes the timeout path

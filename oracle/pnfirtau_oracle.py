@@ -164,6 +164,26 @@ def mha_forward(x: torch.Tensor, qkv_weight: torch.Tensor, out_weight: torch.Ten
     return F.linear(out, out_weight, out_bias)
 
 
+def smfir_forward(x: torch.Tensor, qkv_weight: torch.Tensor, out_weight: torch.Tensor, fir_taps: torch.Tensor,
+                  n_heads: int, causal: bool = True, qkv_bias=None, out_bias=None):
+    """SmFirMHA.forward without dropout (src/pnfirtau_attention.py:152-192):
+    softmax attention on causally filtered keys, the future masked to -1e4.
+    Returns (out, weights)."""
+    B, N, Dm = x.shape
+    H, hd = n_heads, Dm // n_heads
+    qkv = F.linear(x, qkv_weight, qkv_bias).reshape(B, N, 3, H, hd)
+    q, k, v = qkv.unbind(2)
+    k = causal_fir(k.reshape(B, N, H * hd), fir_taps).view(B, N, H, hd)
+    q, k, v = q.transpose(1, 2), k.transpose(1, 2), v.transpose(1, 2)
+    att = torch.matmul(q, k.transpose(-2, -1)) * (1.0 / math.sqrt(hd))
+    if causal:
+        mask = torch.triu(torch.ones(N, N, dtype=torch.bool, device=x.device), diagonal=1)
+        att = att.masked_fill(mask, -1e4)
+    w = torch.softmax(att, dim=-1)
+    out = torch.matmul(w, v).transpose(1, 2).reshape(B, N, -1)
+    return F.linear(out, out_weight, out_bias), w
+
+
 # ---------------------------------------------------------------------------
 # silent-tile oracle (experiments/exp4b_mha6_instrumentation.py:80-128)
 # ---------------------------------------------------------------------------

@@ -9,6 +9,7 @@ from .pnfirtau_attention import (
     PnFirTauFlashMHA,
     PnFirTauMHA,
     PnFirTauTritonMHA,
+    SmFirMHA,
     causal_fir,
     causal_gaussian_taps,
     power_norm_peak_gate,
@@ -36,6 +37,7 @@ __all__ = [
     "PnFirTauMHA",
     "PnFirTauTritonMHA",
     "PnFirTauFlashMHA",
+    "SmFirMHA",
     "causal_fir",
     "causal_gaussian_taps",
     "power_norm_peak_gate",

@@ -207,6 +207,8 @@ static int flash_bwd_entry(const void* q, const int64_t* sq, const void* k, cons
   }
   a.live64 = reinterpret_cast<int32_t*>(ws + w.off_live);
   a.dtau_part = reinterpret_cast<float*>(ws + w.off_part);
+  a.dq_sem = reinterpret_cast<int32_t*>(ws + w.off_sem);
+  a.dq_ticket = a.dq_sem + (B * H) * ((N + 63) / 64);
   a.dq_scale = 1.f;
   if (use_sm100(a)) return flash_bwd_sm100(a, st);
   if (fir_taps) return fail(PNFT_EUNSUPPORTED, "flash bwd: the fused FIR runs on the sm_100a kernels only");

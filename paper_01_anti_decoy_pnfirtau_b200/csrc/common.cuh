@@ -39,6 +39,42 @@ __device__ __forceinline__ __nv_bfloat16 from_f32<__nv_bfloat16>(float v) { retu
 template <>
 __device__ __forceinline__ __half from_f32<__half>(float v) { return __float2half_rn(v); }
 
+// ---- ordered (deterministic) accumulation: per-tile turn counters ----
+// A counter per accumulator tile counts the contributions already added; the
+// contributor with rank `turn` adds after the counter reaches `turn`, so the
+// additions (and their fp32 rounding) happen in one fixed order on every run.
+__device__ __forceinline__ int ld_acquire_gpu(const int32_t* p) {
+  int v;
+  asm volatile("ld.acquire.gpu.global.s32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+__device__ __forceinline__ uint64_t global_ns() {
+  uint64_t t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+// Bounded wait for *sem >= turn (1 s). On timeout the caller's status word gets
+// PNFT_DEV_WAIT_TIMEOUT (and *abort_flag, when given, is set) and the wait gives
+// up: the order is then lost but nothing hangs. Also gives up at once when
+// *abort_flag is set by another role of the CTA.
+__device__ __forceinline__ bool turn_wait(const int32_t* sem, int turn, int32_t* status, volatile int* abort_flag) {
+  if (ld_acquire_gpu(sem) >= turn) return true;
+  const uint64_t t0 = global_ns();
+  while (true) {
+#pragma unroll 1
+    for (int i = 0; i < 16; ++i) {
+      if (ld_acquire_gpu(sem) >= turn) return true;
+      __nanosleep(64);
+    }
+    if (abort_flag && *abort_flag) return false;
+    if (global_ns() - t0 > 1000000000ull) {
+      if (abort_flag) *abort_flag = 1;
+      if (status) asm volatile("st.relaxed.sys.global.s32 [%0], %1;" ::"l"(status), "r"(PNFT_DEV_WAIT_TIMEOUT) : "memory");
+      return false;
+    }
+  }
+}
+
 // ---- reductions over the low `width` lanes groups of a warp ----
 template <int WIDTH>
 __device__ __forceinline__ float group_max(float v) {

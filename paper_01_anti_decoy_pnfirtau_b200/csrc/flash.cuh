@@ -45,6 +45,10 @@ struct FlashArgs {
   int32_t* live64;     // [B*H, ceil(N/64)]: bit 0 any row live (peak > 0), bit 1 any row with Nmax > 1
   float* dtau_part;    // per (bh, key tile) partial of -sum du
   int64_t n_dtau_part;
+  // deterministic mode (PNFT_FLASH_DETERMINISTIC): per (bh, 64-row query tile) turn
+  // counters of the dQ accumulator and the work-ticket counter, zeroed by the prep kernel
+  int32_t* dq_sem;     // [B*H, ceil(N/64)]
+  int32_t* dq_ticket;  // [1]
   float dq_scale;      // factor the dQ cast applies to the fp32 accumulator
 };
 
@@ -76,7 +80,7 @@ __host__ __device__ __forceinline__ int64_t rec_rows(int64_t N) { return (N + 63
 
 // Workspace layout shared by both kernel families (256-byte aligned sections).
 struct BwdWorkspace {
-  size_t off_dq, off_coef, off_live, off_part, total;
+  size_t off_dq, off_coef, off_live, off_part, off_sem, total;
 };
 BwdWorkspace bwd_workspace_layout(int64_t B, int64_t H, int64_t N, int64_t D);
 

@@ -284,7 +284,11 @@ __global__ void __launch_bounds__(256) flash_bwd_prep_kernel(FlashArgs a) {
   }
   live = __syncthreads_or(live);
   multi = __syncthreads_or(multi);
-  if (threadIdx.x == 0) a.live64[bh * nt + blockIdx.x] = (live ? kLiveRow : 0) | (multi ? kMultiTie : 0);
+  if (threadIdx.x == 0) {
+    a.live64[bh * nt + blockIdx.x] = (live ? kLiveRow : 0) | (multi ? kMultiTie : 0);
+    a.dq_sem[bh * nt + blockIdx.x] = 0;  // no dQ contribution added yet (deterministic mode)
+    if (bh == 0 && blockIdx.x == 0) *a.dq_ticket = 0;
+  }
 }
 
 template <typename T, int DP>
@@ -303,10 +307,34 @@ __global__ void __launch_bounds__(GTHREADS) flash_bwd_generic_kernel(FlashArgs a
   int* sArg = reinterpret_cast<int*>(sTie + GB);            // argmax key of the row
   float* sPc = reinterpret_cast<float*>(sArg + GB);         // peak for the value test (NaN: unused)
   const int tid = threadIdx.x, rg = tid >> 4, cg = tid & 15;
-  const int64_t kt = blockIdx.x, k0 = kt * GB;
-  const int64_t bh = blockIdx.y, b = bh / a.H, h = bh % a.H;
+  // deterministic mode: key blocks add their dQ contributions to each query tile in
+  // key order (turn counters); blocks take their (key block, b*h) from a ticket in
+  // grid order, so a block only ever waits for blocks that started before it
+  const bool det = (a.flags & PNFT_FLASH_DETERMINISTIC) != 0;
+  int64_t kt_ = blockIdx.x, bh_ = blockIdx.y;
+  if (det) {
+    __shared__ int s_ticket;
+    if (tid == 0) s_ticket = atomicAdd(a.dq_ticket, 1);
+    __syncthreads();
+    kt_ = s_ticket % (int)gridDim.x;
+    bh_ = s_ticket / (int)gridDim.x;
+  }
+  const int64_t kt = kt_, k0 = kt * GB;
+  const int64_t bh = bh_, b = bh / a.H, h = bh % a.H;
   const int D = (int)a.D;
   const int64_t N = a.N;
+  int32_t* sem_bh = a.dq_sem + bh * ((N + GB - 1) / GB);
+  // this block's turn on query tile q0 (det mode): wait for the lower key blocks,
+  // optionally add (plain read-modify-write through L2), pass the turn on
+  auto det_turn_wait = [&](int64_t q0) {
+    if (tid == 0) turn_wait(sem_bh + q0 / GB, (int)kt, a.status, nullptr);
+    __syncthreads();
+  };
+  auto det_turn_pass = [&](int64_t q0) {
+    __threadfence();
+    __syncthreads();
+    if (tid == 0) atomicAdd(sem_bh + q0 / GB, 1);
+  };
   const T* Q = static_cast<const T*>(a.q) + b * a.sq[0] + h * a.sq[1];
   const T* K = static_cast<const T*>(a.k) + b * a.sk[0] + h * a.sk[1];
   const T* V = static_cast<const T*>(a.v) + b * a.sv[0] + h * a.sv[1];
@@ -342,7 +370,13 @@ __global__ void __launch_bounds__(GTHREADS) flash_bwd_generic_kernel(FlashArgs a
       sPc[tid] = pcmp;
       live_row = arg >= 0;
     }
-    if (!__syncthreads_or(live_row)) continue;  // every query row of the block is silent
+    if (!__syncthreads_or(live_row)) {  // every query row of the block is silent
+      if (det) {
+        det_turn_wait(q0);
+        det_turn_pass(q0);
+      }
+      continue;
+    }
     load_tile<T, DP>(sQ, Q, a.sq[2], a.sq[3], q0, N, D);
     __syncthreads();
     float u[4][4];
@@ -360,7 +394,13 @@ __global__ void __launch_bounds__(GTHREADS) flash_bwd_generic_kernel(FlashArgs a
         live |= u[ii][jj] > 0.f;
       }
     }
-    if (!__syncthreads_or(live)) continue;  // silent tile
+    if (!__syncthreads_or(live)) {  // silent tile
+      if (det) {
+        det_turn_wait(q0);
+        det_turn_pass(q0);
+      }
+      continue;
+    }
     load_tile<T, DP>(sdO, dO, a.sdo[2], a.sdo[3], q0, N, D);
     __syncthreads();
     float dp[4][4];
@@ -427,6 +467,7 @@ __global__ void __launch_bounds__(GTHREADS) flash_bwd_generic_kernel(FlashArgs a
 #pragma unroll
         for (int jj = 0; jj < NJ; ++jj) dq[ii][jj] = fmaf(s[ii], kv[jj], dq[ii][jj]);
     }
+    if (det) det_turn_wait(q0);
 #pragma unroll
     for (int ii = 0; ii < 4; ++ii) {
       const int64_t row = q0 + rg + 16 * ii;
@@ -434,9 +475,14 @@ __global__ void __launch_bounds__(GTHREADS) flash_bwd_generic_kernel(FlashArgs a
 #pragma unroll
       for (int jj = 0; jj < NJ; ++jj) {
         const int e = cg + 16 * jj;
-        if (e < D) atomicAdd(dQa + row * a.D + e, dq[ii][jj]);
+        if (e < D) {
+          float* dst = dQa + row * a.D + e;
+          if (det) __stcg(dst, __ldcg(dst) + dq[ii][jj]);
+          else atomicAdd(dst, dq[ii][jj]);
+        }
       }
     }
+    if (det) det_turn_pass(q0);
   }
   T* dK = static_cast<T*>(a.dk) + b * a.sdk[0] + h * a.sdk[1];
   T* dV = static_cast<T*>(a.dv) + b * a.sdv[0] + h * a.sdv[1];
@@ -562,7 +608,8 @@ BwdWorkspace bwd_workspace_layout(int64_t B, int64_t H, int64_t N, int64_t D) {
   // coefP (two floats per row), tiev, argv, pcmpv: recs records each
   w.off_live = w.off_coef + up(recs * (sizeof(float2) + sizeof(float) + sizeof(int32_t) + sizeof(float)));
   w.off_part = w.off_live + up(ntiles64 * sizeof(int32_t));
-  w.total = w.off_part + up(ntiles64 * sizeof(float));
+  w.off_sem = w.off_part + up(ntiles64 * sizeof(float));
+  w.total = w.off_sem + up((ntiles64 + 1) * sizeof(int32_t));  // turn counters + work ticket
   return w;
 }
 

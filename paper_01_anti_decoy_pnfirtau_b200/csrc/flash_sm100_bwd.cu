@@ -25,7 +25,10 @@
 //                term is one patched entry per row (value tests only on tiles
 //                holding a row with several maxima).
 //   warps 12-15  dQ drain: TMEM -> fp32 staging tile in smem -> one
-//                cp.reduce.async.bulk add into the fp32 dQ accumulator.
+//                cp.reduce.async.bulk add into the fp32 dQ accumulator (in
+//                deterministic mode: a read-modify-write of the tile once the
+//                lower key tiles of the head have added theirs, so the fp32
+//                additions happen in key order on every run).
 // Finally the elementwise warps write dK, dV (bf16) from TMEM.
 // TMEM columns: S [0,64) dP [64,128) P^T x2 [128,192) dV [192,192+D)
 //               dK [192+D,192+2D) dQ^T (x2 for D=64) [192+2D, 512).
@@ -104,7 +107,8 @@ struct BwdLayout {
   static constexpr int OFF_ABORT = OFF_TMEM + 4;
   static constexpr int OFF_DKVW = OFF_ABORT + 4;
   static constexpr int OFF_RED = OFF_DKVW + 8;  // one float per elementwise warp
-  static constexpr int END = OFF_RED + 4 * 4 * NEW;
+  static constexpr int OFF_TKT = OFF_RED + 4 * 4 * NEW;  // deterministic mode: this CTA's work ticket
+  static constexpr int END = OFF_TKT + 16;
   static constexpr int SMEM = END + 1024;
   // TMEM. D=64: two S/dP buffers [128b, 128b+128) (S at +0, dP at +64); a warp
   // writes the packed P^T of each 16-query group over the first 8 of that group's S
@@ -153,6 +157,11 @@ struct BwdParams {
   float scale;
   int causal;
   int stall;  // PNFT_FLASH_TEST_STALL: the elementwise warps first wait on C_STALL
+  // PNFT_FLASH_DETERMINISTIC: work items in ticket order; the dQ drain adds each tile
+  // into the accumulator after the lower key tiles of its head (turn counters)
+  int det;
+  int32_t* sem;     // [B*H, nq64]
+  int32_t* ticket;  // [1]
 };
 
 // Warp-cooperative walk over the query tiles [i0, n) whose live bit is set: 32
@@ -202,8 +211,18 @@ __global__ void __launch_bounds__(B_THREADS, 1) flash_bwd_sm100_kernel(const __g
   const uint32_t sb0 = smem_u32(smem);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   // b*h runs fastest and key tile 0 (the most causal query tiles) comes first:
-  // the grid starts with its longest CTAs, so none starts late
-  const int kt = blockIdx.y, bh = blockIdx.x, b = bh / p.H, hd = bh % p.H;
+  // the grid starts with its longest CTAs, so none starts late. Deterministic mode
+  // takes the same order from a work ticket, so every CTA whose dQ additions a CTA
+  // waits for (the lower key tiles of its head) started before it.
+  int kt_ = blockIdx.y, bh_ = blockIdx.x;
+  if (p.det) {
+    volatile int* tk = reinterpret_cast<volatile int*>(smem + L::OFF_TKT);
+    if (threadIdx.x == 0) *tk = atomicAdd(p.ticket, 1);
+    __syncthreads();
+    bh_ = *tk % (int)gridDim.x;
+    kt_ = *tk / (int)gridDim.x;
+  }
+  const int kt = kt_, bh = bh_, b = bh / p.H, hd = bh % p.H;
   const int k0 = kt * BN;
   const int i_first = p.causal ? k0 / BM : 0;
   const int32_t* live = p.live64 + (int64_t)bh * p.nq64;
@@ -631,6 +650,31 @@ __global__ void __launch_bounds__(B_THREADS, 1) flash_bwd_sm100_kernel(const __g
     const uint32_t lane_off = (uint32_t)(32 * wq) << 16;
     const bool leader = warp == W_DRAIN && lane == 0;
     bool dead = false;
+    // deterministic mode: add the staged fp32 tile of query tile i (rows of 64 x D,
+    // the accumulator's own layout) once the lower key tiles of this head have added
+    // theirs, then pass the turn on; all 128 drain threads
+    const int dt = threadIdx.x - 32 * W_DRAIN;
+    auto ordered_add = [&](int i, const float* stg, int rows) {
+      int32_t* sem = p.sem + (int64_t)bh * p.nq64 + i;
+      if (leader) turn_wait(sem, kt, p.status, abort_flag);
+      named_bar_sync(4, 128);
+      if (!dead) {
+        float4* dst = reinterpret_cast<float4*>(p.dq_acc + ((int64_t)bh * p.N + (int64_t)i * BM) * D);
+        const float4* src = reinterpret_cast<const float4*>(stg);
+        for (int e = dt; e < rows * (D / 4); e += 128) {
+          float4 a = __ldcg(dst + e);
+          const float4 b4 = src[e];
+          a.x += b4.x;
+          a.y += b4.y;
+          a.z += b4.z;
+          a.w += b4.w;
+          __stcg(dst + e, a);
+        }
+      }
+      __threadfence();
+      named_bar_sync(4, 128);
+      if (leader) atomicAdd(sem, 1);
+    };
     LiveTiles lt(live, i_first, p.nq64);
     bool mt;
     if constexpr (L::DQ_PAIR) {
@@ -666,7 +710,10 @@ __global__ void __launch_bounds__(B_THREADS, 1) flash_bwd_sm100_kernel(const __g
         }
         fence_proxy_async_smem();
         named_bar_sync(4, 128);
-        if (leader && !dead) {
+        if (p.det) {
+          ordered_add(ia, reinterpret_cast<const float*>(smem + L::OFF_STG), min(BM, p.N - ia * BM));
+          if (two) ordered_add(ib, reinterpret_cast<const float*>(smem + L::OFF_STG + L::STG_BYTES), min(BM, p.N - ib * BM));
+        } else if (leader && !dead) {
           const int qa = ia * BM;
           bulk_reduce_add_f32(p.dq_acc + ((int64_t)bh * p.N + qa) * D, smem_u32(smem + L::OFF_STG),
                               (uint32_t)(min(BM, p.N - qa) * D * 4));
@@ -710,7 +757,9 @@ __global__ void __launch_bounds__(B_THREADS, 1) flash_bwd_sm100_kernel(const __g
       }
       fence_proxy_async_smem();
       named_bar_sync(4, 128);
-      if (leader && !dead) {
+      if (p.det) {
+        ordered_add(i, stg, min(BM, p.N - q0));
+      } else if (leader && !dead) {
         const int rows = min(BM, p.N - q0);
         bulk_reduce_add_f32(p.dq_acc + ((int64_t)bh * p.N + q0) * D, smem_u32(stg), (uint32_t)(rows * D * 4));
         bulk_commit();
@@ -777,6 +826,9 @@ int flash_bwd_sm100(const FlashArgs& a0, cudaStream_t st) {
   p.scale = a.scale;
   p.causal = a.causal;
   p.stall = (a.flags & PNFT_FLASH_TEST_STALL) ? 1 : 0;
+  p.det = (a.flags & PNFT_FLASH_DETERMINISTIC) ? 1 : 0;
+  p.sem = a.dq_sem;
+  p.ticket = a.dq_ticket;
   if (nkt > 65535) return fail(PNFT_EUNSUPPORTED, "flash bwd sm100: N = %lld needs more than 65535 key tiles", (long long)a.N);
   const dim3 grid((unsigned)(a.B * a.H), (unsigned)nkt);
   auto launch = [&](auto kern, int smem) -> int {

@@ -21,6 +21,7 @@ from dataclasses import dataclass
 
 import torch
 import torch.nn as nn
+import torch.nn.functional as F
 
 from .pnfirtau_ops import (
     _flash_bnhd,
@@ -39,6 +40,7 @@ __all__ = [
     "PnFirTauMHA",
     "PnFirTauTritonMHA",
     "PnFirTauFlashMHA",
+    "SmFirMHA",
 ]
 
 
@@ -206,3 +208,51 @@ class PnFirTauFlashMHA(PnFirTauMHA):
         out = _flash_bnhd(q, k, v, self.score_tau, scale, cfg.silence_gamma, cfg.causal_mask)
         out = out.transpose(1, 2).reshape(B, N, -1)
         return self.out(out)
+
+
+class SmFirMHA(nn.Module):
+    """Softmax attention on causally filtered keys (src/pnfirtau_attention.py:152-192).
+
+    The keys' causal FIR runs on this library's FIR kernel (triton_causal_fir,
+    the same kernel the pn_fir_tau modules use, with its tap gradient); only the
+    normaliser differs from PnFirTauMHA. Scores, the causal mask (-1e4 on the
+    future, as the reference; equal to -inf under softmax since every row keeps
+    its diagonal), softmax, dropout and PV are PyTorch's: fused
+    scaled_dot_product_attention when no weights are returned, explicit matmul +
+    softmax when ``return_weights=True``. Parameter and buffer names (``qkv``,
+    ``out``, ``fir_taps``) match the reference. CUDA only, like the other modules.
+    """
+
+    def __init__(self, cfg: PnFirConfig):
+        super().__init__()
+        assert cfg.d_model % cfg.n_heads == 0
+        self.cfg = cfg
+        self.n_heads = cfg.n_heads
+        self.head_dim = cfg.d_model // cfg.n_heads
+        self.qkv = nn.Linear(cfg.d_model, 3 * cfg.d_model, bias=cfg.bias)
+        self.out = nn.Linear(cfg.d_model, cfg.d_model, bias=cfg.bias)
+        self.drop = nn.Dropout(cfg.dropout)
+        taps = causal_gaussian_taps(cfg.fir_k, torch.device("cpu"), torch.float32, cfg.fir_sigma_frac)
+        self.register_buffer("fir_taps", taps, persistent=True)
+
+    def forward(self, x: torch.Tensor, return_weights: bool = False):
+        B, N, _ = x.shape
+        H, hd = self.n_heads, self.head_dim
+        q_raw, k_raw, v_raw = self.qkv(x).chunk(3, dim=-1)
+        k = triton_causal_fir(k_raw, self.fir_taps).view(B, N, H, hd).transpose(1, 2)
+        q = q_raw.view(B, N, H, hd).transpose(1, 2)
+        v = v_raw.view(B, N, H, hd).transpose(1, 2)
+        if return_weights:
+            att = torch.matmul(q, k.transpose(-2, -1)) * (1.0 / math.sqrt(hd))
+            if self.cfg.causal_mask:
+                causal = torch.triu(torch.ones(N, N, device=x.device, dtype=torch.bool), diagonal=1)
+                att = att.masked_fill(causal, -1e4)
+            w = self.drop(F.softmax(att, dim=-1))
+            out = torch.matmul(w, v)
+        else:
+            out = F.scaled_dot_product_attention(q, k, v, dropout_p=self.drop.p if self.training else 0.0,
+                                                 is_causal=self.cfg.causal_mask)
+        out = self.out(out.transpose(1, 2).reshape(B, N, -1))
+        if return_weights:
+            return out, w
+        return out

@@ -324,8 +324,13 @@ def triton_pn_fir_tau_scores(
 # ---------------------------------------------------------------------------
 
 
-def _flash_flags() -> int:
-    return (_lib.FLASH_FORCE_GENERIC if _FORCE_GENERIC else 0) | _TEST_FLAGS
+def _flash_flags(deterministic: bool | None = None) -> int:
+    """PNFT_FLASH_* bits of a flash call. deterministic=None follows
+    torch.are_deterministic_algorithms_enabled()."""
+    if deterministic is None:
+        deterministic = torch.are_deterministic_algorithms_enabled()
+    return ((_lib.FLASH_FORCE_GENERIC if _FORCE_GENERIC else 0) | (_lib.FLASH_DETERMINISTIC if deterministic else 0)
+            | _TEST_FLAGS)
 
 
 _FORCE_GENERIC = False
@@ -352,7 +357,7 @@ class _FlashPnFirTauFn(torch.autograd.Function):
     """
 
     @staticmethod
-    def forward(ctx, q, k, v, score_tau, scale, gamma, causal_mask, out_layout):
+    def forward(ctx, q, k, v, score_tau, scale, gamma, causal_mask, out_layout, deterministic=None):
         dev = _require_cuda("flash_pn_fir_tau_attention", q, k, v, score_tau)
         _check_pending(dev)
         if not (q.dtype == k.dtype == v.dtype):
@@ -368,7 +373,7 @@ class _FlashPnFirTauFn(torch.autograd.Function):
         nmax = torch.empty((2, B, H, N), device=dev, dtype=torch.int32)    # tie count, argmax key
         tau_f32 = score_tau.detach().to(torch.float32).contiguous()
         has_gamma, gamma_val = _gamma_args(gamma)
-        flags = _flash_flags()
+        flags = _flash_flags(deterministic)
         # fp32 copy of O for the backward's per-row <dO,O>/gate (see pnft_flash_fwd)
         needs_grad = any(ctx.needs_input_grad[:4])
         out32 = None
@@ -426,7 +431,7 @@ class _FlashPnFirTauFn(torch.autograd.Function):
             "pnft_flash_bwd",
         )
         grad_tau = dtau.to(ctx.tau_dtype).reshape(ctx.tau_shape)
-        return dq, dk, dv, grad_tau, None, None, None, None
+        return dq, dk, dv, grad_tau, None, None, None, None, None
 
 
 def flash_pn_fir_tau_attention(
@@ -437,15 +442,23 @@ def flash_pn_fir_tau_attention(
     scale: float | None = None,
     gamma: float | None = 0.5,
     causal_mask: bool = True,
+    *,
+    deterministic: bool | None = None,
 ) -> torch.Tensor:
     """FlashAttention-style O(N)-memory tiled attention for ``pn_fir_tau`` (p = 10).
 
     Reference: src/triton_pnfirtau.py:971-983. ``scale`` defaults to
     1/sqrt(head_dim). Returns ``[B, H, N, D]`` in q's dtype.
+
+    ``deterministic`` (keyword only, an addition to the reference's signature):
+    the backward adds the dQ contributions of the key tiles in a fixed order,
+    so every gradient is bitwise reproducible run to run (dK, dV and dtau always
+    are); None follows ``torch.use_deterministic_algorithms``. The reference's
+    backward accumulates dQ with atomics (src/triton_pnfirtau.py:596-602).
     """
     if scale is None:
         scale = 1.0 / math.sqrt(q.shape[-1])
-    return _FlashPnFirTauFn.apply(q, k_tilde, v, score_tau, scale, gamma, causal_mask, "bhnd")
+    return _FlashPnFirTauFn.apply(q, k_tilde, v, score_tau, scale, gamma, causal_mask, "bhnd", deterministic)
 
 
 def _fir_view(t: torch.Tensor):
@@ -472,7 +485,8 @@ class _FlashFirFn(torch.autograd.Function):
     Both forwards give the same k~ bit for bit."""
 
     @staticmethod
-    def forward(ctx, q, k, v, score_tau, taps, scale, gamma, causal_mask, out_layout, fused_forward=False):
+    def forward(ctx, q, k, v, score_tau, taps, scale, gamma, causal_mask, out_layout, fused_forward=False,
+                deterministic=None):
         dev = _require_cuda("flash_pn_fir_tau_attention_fir", q, k, v, score_tau, taps)
         _check_pending(dev)
         if not (q.dtype == k.dtype == v.dtype):
@@ -493,7 +507,7 @@ class _FlashFirFn(torch.autograd.Function):
         tau_f32 = score_tau.detach().to(torch.float32).contiguous()
         taps_f32 = taps.detach().to(torch.float32).contiguous()
         has_gamma, gamma_val = _gamma_args(gamma)
-        flags = _flash_flags()
+        flags = _flash_flags(deterministic)
         needs_grad = any(ctx.needs_input_grad[:5])
         out32 = torch.empty((B, H, N, D), device=dev, dtype=torch.float32) if needs_grad else None
         L = _lib.lib()
@@ -572,7 +586,7 @@ class _FlashFirFn(torch.autograd.Function):
         )
         grad_tau = dtau.to(ctx.tau_dtype).reshape(ctx.tau_shape)
         grad_taps = dtaps.to(ctx.taps_dtype).reshape(ctx.taps_shape) if dtaps is not None else None
-        return dq, dk, dv, grad_tau, grad_taps, None, None, None, None, None
+        return dq, dk, dv, grad_tau, grad_taps, None, None, None, None, None, None
 
 
 def flash_pn_fir_tau_attention_fir(
@@ -585,6 +599,8 @@ def flash_pn_fir_tau_attention_fir(
     gamma: float | None = 0.5,
     causal_mask: bool = True,
     fused_forward: bool = False,
+    *,
+    deterministic: bool | None = None,
 ) -> torch.Tensor:
     """``flash_pn_fir_tau_attention(q, triton_causal_fir(k, taps), v, ...)`` with
     the 7-tap causal FIR in the attention kernels' K-tile load: each K tile is
@@ -594,10 +610,11 @@ def flash_pn_fir_tau_attention_fir(
     runs one standalone filter pass, which is faster there because every query
     tile re-reads the key tiles. ``k`` is the raw key projection ``[B, H, N, D]``
     (bf16, head dim 64/128; sm_100a kernels only). Gradients reach ``k`` and, when
-    it requires grad, ``taps``. Composition replaced: src/pnfirtau_attention.py:285-316."""
+    it requires grad, ``taps``. ``deterministic`` as in flash_pn_fir_tau_attention.
+    Composition replaced: src/pnfirtau_attention.py:285-316."""
     if scale is None:
         scale = 1.0 / math.sqrt(q.shape[-1])
-    return _FlashFirFn.apply(q, k, v, score_tau, taps, scale, gamma, causal_mask, "bhnd", fused_forward)
+    return _FlashFirFn.apply(q, k, v, score_tau, taps, scale, gamma, causal_mask, "bhnd", fused_forward, deterministic)
 
 
 @torch.no_grad()

@@ -4,7 +4,7 @@ code in src/pnfirtau_attention.py) on seeded inputs on the CPU in fp32.
 
 Run from the repository root, with the reference checkout importable:
 
-    python tests/golden/make_golden.py /path/to/reference
+    python tests/golden/make_golden.py /path/to/reference [fixture names ...]
 
 Only this script touches the reference; the fixtures it writes (small .pt
 files) travel with the tests. The reference's Triton/Flash functions need a
@@ -145,6 +145,31 @@ def gen_mha(ref):
     torch.save(cases, OUT / "mha.pt")
 
 
+def gen_smfir(ref):
+    """SmFirMHA (softmax attention on the causally filtered keys,
+    src/pnfirtau_attention.py:152-192) forward+backward."""
+    cases = {}
+    for name, (B, N, Dm, H, seed, causal) in {
+        "b4n48d64h4": (4, 48, 64, 4, 7, True),
+        "b2n33d32h2_noncausal": (2, 33, 32, 2, 8, False),
+    }.items():
+        torch.manual_seed(seed)
+        cfg = ref.PnFirConfig(d_model=Dm, n_heads=H, causal_mask=causal)
+        m = ref.SmFirMHA(cfg)
+        x = torch.randn(B, N, Dm)
+        xr = x.clone().requires_grad_(True)
+        y, w = m(xr, return_weights=True)
+        dy = torch.randn_like(y)
+        y.backward(dy)
+        cases[name] = {
+            "d_model": Dm, "n_heads": H, "causal": causal, "x": x, "dy": dy,
+            "state_dict": {k: v.clone() for k, v in m.state_dict().items()},
+            "out": y.detach(), "weights": w.detach(), "dx": xr.grad,
+            "grads": {n: p.grad.clone() for n, p in m.named_parameters()},
+        }
+    torch.save(cases, OUT / "smfir.pt")
+
+
 def gen_tiles(ref):
     """exp4b's silent-tile definition (experiments/exp4b_mha6_instrumentation.py:91-111)
     evaluated with the reference's own reshape/permute expression."""
@@ -174,18 +199,18 @@ def gen_tiles(ref):
     torch.save(out, OUT / "tiles.pt")
 
 
+GENERATORS = {"taps": gen_taps, "fir": gen_fir, "pngate": gen_pngate, "attention": gen_attention, "mha": gen_mha,
+              "smfir": gen_smfir, "tiles": gen_tiles}
+
+
 def main():
     root = sys.argv[1] if len(sys.argv) > 1 else None
     if root is None:
-        raise SystemExit("usage: make_golden.py <reference checkout root>")
+        raise SystemExit("usage: make_golden.py <reference checkout root> [fixture names ...]")
     ref = _import_reference(root)
     torch.set_num_threads(1)
-    gen_taps(ref)
-    gen_fir(ref)
-    gen_pngate(ref)
-    gen_attention(ref)
-    gen_mha(ref)
-    gen_tiles(ref)
+    for name in sys.argv[2:] or list(GENERATORS):
+        GENERATORS[name](ref)
     print("golden fixtures written to", OUT)
 
 

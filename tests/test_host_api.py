@@ -21,7 +21,10 @@ def test_config_defaults_match_reference():
 
 def test_public_signatures_match_reference():
     s = inspect.signature(P.flash_pn_fir_tau_attention)
-    assert list(s.parameters) == ["q", "k_tilde", "v", "score_tau", "scale", "gamma", "causal_mask"]
+    # the reference's positional parameters, in order; additions are keyword-only
+    positional = [n for n, q in s.parameters.items() if q.kind is not inspect.Parameter.KEYWORD_ONLY]
+    assert positional == ["q", "k_tilde", "v", "score_tau", "scale", "gamma", "causal_mask"]
+    assert [n for n in s.parameters if n not in positional] == ["deterministic"]
     assert s.parameters["scale"].default is None and s.parameters["gamma"].default == 0.5
     assert s.parameters["causal_mask"].default is True
     s = inspect.signature(P.triton_pn_fir_tau_scores)

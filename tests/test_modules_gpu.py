@@ -131,3 +131,37 @@ def test_bf16_autocast_module(cuda):
     y16, dx16 = eager(True)
     assert rel_l2(y.float(), y32) <= max(2e-2, 1.25 * rel_l2(y16, y32))
     assert rel_l2(x.grad, dx32) <= max(2e-2, 1.25 * rel_l2(dx16, dx32))
+
+
+@pytest.mark.parametrize("return_weights", [False, True])
+@pytest.mark.parametrize("case", ["b4n48d64h4", "b2n33d32h2_noncausal"])
+def test_smfir_golden_fp32(cuda, golden, case, return_weights):
+    """SmFirMHA (softmax on the FIR-filtered keys, the FIR on this library's
+    kernel) against the reference's golden forward/backward, fp32."""
+    c = golden("smfir")[case]
+    m = P.SmFirMHA(P.PnFirConfig(d_model=c["d_model"], n_heads=c["n_heads"], causal_mask=c["causal"])).to(cuda)
+    m.load_state_dict(c["state_dict"])
+    x = c["x"].to(cuda).requires_grad_(True)
+    if return_weights:
+        y, w = m(x, return_weights=True)
+        assert rel_max(w, c["weights"]) < 1e-5
+    else:
+        y = m(x)
+    y.backward(c["dy"].to(cuda))
+    assert rel_max(y, c["out"]) < 1e-5
+    assert rel_max(x.grad, c["dx"]) < 5e-5
+    for n, p in m.named_parameters():
+        assert rel_max(p.grad, c["grads"][n]) < 5e-5, n
+
+
+def test_smfir_bf16_autocast_lm_shape(cuda):
+    """The LM's attention shape (d_model 256, 4 heads of 64, seq 512) under bf16
+    autocast against the fp32 oracle with the same parameters."""
+    torch.manual_seed(3)
+    m = P.SmFirMHA(P.PnFirConfig(d_model=256, n_heads=4)).to(cuda)
+    x = torch.randn(4, 512, 256, device=cuda)
+    with torch.autocast("cuda", dtype=torch.bfloat16):
+        y = m(x)
+    sd = m.state_dict()
+    yr, _ = O.smfir_forward(x, sd["qkv.weight"], sd["out.weight"], sd["fir_taps"], 4)
+    assert rel_l2(y.float(), yr) < 1e-2

@@ -106,3 +106,17 @@ def test_row_stats_consistent_with_weights(golden):
     # rows sum to gate * mass / (mass + 1e-12): below the gate only when u^10 is tiny
     assert torch.allclose(w.sum(-1), gate * (1 - 1e-12 / z), rtol=1e-5, atol=1e-6)
     assert torch.all((nmax == 0) == (peak == 0))
+
+
+@pytest.mark.parametrize("case", ["b4n48d64h4", "b2n33d32h2_noncausal"])
+def test_smfir_matches_reference(golden, case):
+    c = golden("smfir")[case]
+    sd = {k: v.clone().requires_grad_(k != "fir_taps") for k, v in c["state_dict"].items()}
+    x = c["x"].clone().requires_grad_(True)
+    y, w = O.smfir_forward(x, sd["qkv.weight"], sd["out.weight"], sd["fir_taps"], c["n_heads"], c["causal"])
+    y.backward(c["dy"])
+    assert rel_max(y, c["out"]) < TIGHT
+    assert rel_max(w, c["weights"]) < TIGHT
+    assert rel_max(x.grad, c["dx"]) < 1e-5
+    for n in ("qkv.weight", "out.weight"):
+        assert rel_max(sd[n].grad, c["grads"][n]) < 1e-5, n
