@@ -53,6 +53,12 @@ __device__ __forceinline__ uint64_t global_ns() {
   asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
   return t;
 }
+// Passes the turn on: a release increment at gpu scope. Called by one thread
+// after a barrier with the threads whose writes it publishes (the release is
+// cumulative over the writes the barrier made visible to it).
+__device__ __forceinline__ void turn_pass(int32_t* sem) {
+  asm volatile("red.release.gpu.global.add.s32 [%0], 1;" ::"l"(sem) : "memory");
+}
 // Bounded wait for *sem >= turn (1 s). On timeout the caller's status word gets
 // PNFT_DEV_WAIT_TIMEOUT (and *abort_flag, when given, is set) and the wait gives
 // up: the order is then lost but nothing hangs. Also gives up at once when

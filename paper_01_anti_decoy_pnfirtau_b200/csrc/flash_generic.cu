@@ -331,9 +331,8 @@ __global__ void __launch_bounds__(GTHREADS) flash_bwd_generic_kernel(FlashArgs a
     __syncthreads();
   };
   auto det_turn_pass = [&](int64_t q0) {
-    __threadfence();
     __syncthreads();
-    if (tid == 0) atomicAdd(sem_bh + q0 / GB, 1);
+    if (tid == 0) turn_pass(sem_bh + q0 / GB);
   };
   const T* Q = static_cast<const T*>(a.q) + b * a.sq[0] + h * a.sq[1];
   const T* K = static_cast<const T*>(a.k) + b * a.sk[0] + h * a.sk[1];
@@ -350,7 +349,12 @@ __global__ void __launch_bounds__(GTHREADS) flash_bwd_generic_kernel(FlashArgs a
     for (int jj = 0; jj < NJ; ++jj) dk[ii][jj] = dv[ii][jj] = 0.f;
   float dtau = 0.f;
   const int64_t lo = a.causal ? k0 : 0;
-  for (int64_t q0 = lo; q0 < N; q0 += GB) {
+  // query tiles in ascending order; deterministic mode walks them downwards, so the
+  // blocks of a head reach a query tile at about the same time and the key-ordered
+  // dQ additions seldom wait
+  const int64_t nqt = (N - lo + GB - 1) / GB;
+  for (int64_t it = 0; it < nqt; ++it) {
+    const int64_t q0 = lo + (det ? nqt - 1 - it : it) * GB;
     __syncthreads();
     int live_row = 0;
     if (tid < GB) {

@@ -167,32 +167,38 @@ struct BwdParams {
 // Warp-cooperative walk over the query tiles [i0, n) whose live bit is set: 32
 // flags per ballot, the next 32 already loaded (one flag per lane), so moving
 // from tile to tile never waits on global memory. All 32 lanes call next().
+// Ascending by default; descending (from n-1 down to i0) in deterministic mode,
+// where every CTA of a head then reaches a given query tile at about the same
+// step, so the key-ordered dQ additions seldom wait.
 struct LiveTiles {
   const int32_t* f;
-  int n, base;
+  int n, i0, base;  // ascending: chunk [base, base+32); descending: chunk [base-31, base]
+  bool desc;
   uint32_t live, multi;
-  int32_t ahead;  // this lane's flag of tile base + 32 + lane
-  __device__ __forceinline__ LiveTiles(const int32_t* flags, int i0, int n_) : f(flags), n(n_), base(i0) {
+  int32_t ahead;  // this lane's flag of the next chunk
+  __device__ __forceinline__ int32_t flag(int j) const { return j >= i0 && j < n ? f[j] : 0; }
+  __device__ __forceinline__ LiveTiles(const int32_t* flags, int i0_, int n_, bool desc_ = false)
+      : f(flags), n(n_), i0(i0_), base(desc_ ? n_ - 1 : i0_), desc(desc_) {
     const int lane = threadIdx.x & 31;
-    const int32_t cur = i0 + lane < n ? f[i0 + lane] : 0;
-    ahead = i0 + 32 + lane < n ? f[i0 + 32 + lane] : 0;
+    const int32_t cur = flag(desc ? base - lane : base + lane);
+    ahead = flag(desc ? base - 32 - lane : base + 32 + lane);
     live = __ballot_sync(0xffffffffu, cur & kLiveRow);
     multi = __ballot_sync(0xffffffffu, cur & kMultiTie);
   }
   // Next live tile, -1 past the end; *is_multi: the tile holds a row with several maxima.
   __device__ __forceinline__ int next(bool* is_multi) {
     while (!live) {
-      if (base + 32 >= n) return -1;
-      base += 32;
+      if (desc ? base - 32 < i0 : base + 32 >= n) return -1;
+      base += desc ? -32 : 32;
       live = __ballot_sync(0xffffffffu, ahead & kLiveRow);
       multi = __ballot_sync(0xffffffffu, ahead & kMultiTie);
-      const int j = base + 32 + (int)(threadIdx.x & 31);
-      ahead = j < n ? f[j] : 0;
+      const int lane = (int)(threadIdx.x & 31);
+      ahead = flag(desc ? base - 32 - lane : base + 32 + lane);
     }
     const int bit = __ffs(live) - 1;
     live &= live - 1;
     *is_multi = (multi >> bit) & 1u;
-    return base + bit;
+    return desc ? base - bit : base + bit;
   }
 };
 
@@ -292,7 +298,7 @@ __global__ void __launch_bounds__(B_THREADS, 1) flash_bwd_sm100_kernel(const __g
       }
     }
     __syncwarp();
-    LiveTiles lt(live, i_first, p.nq64);
+    LiveTiles lt(live, i_first, p.nq64, p.det != 0);
     int t = 0;
     bool ok = true, mt;
     for (int i; ok && (i = lt.next(&mt)) >= 0;) {
@@ -411,7 +417,7 @@ __global__ void __launch_bounds__(B_THREADS, 1) flash_bwd_sm100_kernel(const __g
     };
     int t = 0;  // tiles whose S / dP are issued
     bool ok = warp_wait(bar(C_KV), 0, ab), mt;
-    LiveTiles lt(live, i_first, p.nq64);
+    LiveTiles lt(live, i_first, p.nq64, p.det != 0);
     if constexpr (NSB == 2) {
       // S/dP run two tiles ahead: per step j, dV/dK of tile j, then S/dP of tile
       // j+2 (into tile j's buffer, behind dV(j) in the MMA pipe), then dQ of tile j.
@@ -483,7 +489,7 @@ __global__ void __launch_bounds__(B_THREADS, 1) flash_bwd_sm100_kernel(const __g
       if (et == 0) mbar_arrive(bar(C_KV));
     }
     int t = 0;
-    LiveTiles lt(live, i_first, p.nq64);
+    LiveTiles lt(live, i_first, p.nq64, p.det != 0);
     bool multi_tile;
     for (int i; (i = lt.next(&multi_tile)) >= 0;) {
       const int s = t & 1, qs = t % NQS, ds = t % L::NDS;
@@ -671,11 +677,10 @@ __global__ void __launch_bounds__(B_THREADS, 1) flash_bwd_sm100_kernel(const __g
           __stcg(dst + e, a);
         }
       }
-      __threadfence();
       named_bar_sync(4, 128);
-      if (leader) atomicAdd(sem, 1);
+      if (leader) turn_pass(sem);
     };
-    LiveTiles lt(live, i_first, p.nq64);
+    LiveTiles lt(live, i_first, p.nq64, p.det != 0);
     bool mt;
     if constexpr (L::DQ_PAIR) {
       // tile pairs: dQ^T columns [0,64) = tile A's queries, [64,128) = tile B's;

@@ -1,10 +1,10 @@
 """Deterministic backward (PNFT_FLASH_DETERMINISTIC, ``deterministic=True`` or
 ``torch.use_deterministic_algorithms(True)``): the key tiles add their dQ
 contributions to each query tile in key order, so two runs give bitwise-equal
-gradients. dk, dv, dtau and the output do not depend on that order and equal the
-default (atomic-order) backward bit for bit; dq equals it within fp32 rounding of
-the accumulation order; everything stays within the north-star tolerance of the
-fp32 oracle. The reference's backward accumulates dQ with atomics
+gradients. The output equals the default path's bit for bit; the gradients equal
+the default (atomic-order) backward's within fp32 rounding of the accumulation
+orders (the deterministic walk visits the query tiles top down); everything
+stays within the north-star tolerance of the fp32 oracle. The reference's backward accumulates dQ with atomics
 (src/triton_pnfirtau.py:596-602) although its docstring promises a deterministic
 backward (:15-17)."""
 import pytest
@@ -79,11 +79,11 @@ def test_deterministic_backward(cuda, case):
     for n, x, y in zip(names, a, b):
         assert torch.equal(x, y), f"{n} differs between two deterministic runs"
     c = _run(q, k, v, do, tau, False, fir, causal)
-    for n, x, y in zip(names, a, c):
-        if n == "dq":
-            assert rel_l2(x, y) < 2e-3, (n, rel_l2(x, y))
-        else:
-            assert torch.equal(x, y), f"{n} depends on the dQ accumulation order"
+    assert torch.equal(a[0], c[0]), "the forward does not depend on the backward's mode"
+    for n, x, y in zip(names[1:], a[1:], c[1:]):
+        # the deterministic walk visits query tiles in the opposite order, so the
+        # fp32 accumulations of dQ (and of dK, dV, dtau) round differently
+        assert rel_l2(x, y) < 2e-3, (n, rel_l2(x, y))
     ref = _oracle(q, k, v, do, tau, fir, causal)
     tol = 2e-5 if dtype == torch.float32 else 1e-2
     for n, x, r in zip(names[:4], a[:4], ref[:4]):
