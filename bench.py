@@ -100,7 +100,15 @@ class Dist:
         if self.active:
             import torch.distributed as dist
 
-            dist.init_process_group(backend, timeout=timedelta(seconds=180))
+            opts = None
+            if backend == "nccl":
+                # NCCL's kernels on a high-priority stream: the per-backward tau
+                # all-reduce then takes the next free SM slot instead of queueing
+                # behind the attention kernels that fill every SM
+                opts = dist.ProcessGroupNCCL.Options()
+                opts.is_high_priority_stream = True
+            dist.init_process_group(backend, timeout=timedelta(seconds=180), pg_options=opts,
+                                    device_id=torch.device("cuda", self.local_rank) if backend == "nccl" else None)
 
     def barrier(self):
         if self.active:
@@ -744,7 +752,12 @@ def bench_fir(args, dist_: Dist, dev, iters: int = 20) -> dict:
     HBM GB/s: bytes = one read of x + one write of y per pass (the 6-row halo
     re-reads are not counted). Shapes: the LM's keys [32, 512, 256] and the keys
     of config 5 viewed as [8, 16384, 16*128]. Buffers rotate so the inputs of
-    consecutive passes together exceed the 126 MiB L2 (every pass reads DRAM)."""
+    consecutive passes together exceed the 126 MiB L2 (every pass reads DRAM).
+    Three figures per shape: `GB/s` through the public API call by call (at the
+    LM shape this is bound by the host's per-call overhead), `device_GB/s` from
+    a CUDA graph of the same calls replayed (kernel time, no host overhead), and
+    `dtaps_GB/s`, the tap gradient alone (torch.autograd.grad of the output with
+    respect to the taps: one read of gy and one of x per pass)."""
     from paper_01_anti_decoy_pnfirtau_b200.pnfirtau_attention import causal_gaussian_taps
     from paper_01_anti_decoy_pnfirtau_b200.pnfirtau_ops import triton_causal_fir
 
@@ -752,25 +765,67 @@ def bench_fir(args, dist_: Dist, dev, iters: int = 20) -> dict:
     taps = causal_gaussian_taps(7, device=dev)
     g = torch.Generator(device=dev).manual_seed(args.seed + 11)
     res = {}
+
+    def timed(fn, n):
+        s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        torch.cuda.synchronize()
+        s.record()
+        fn(n)
+        e.record()
+        torch.cuda.synchronize()
+        return s.elapsed_time(e) / n
+
     for name, shape in (("lm_k_32x512x256", (32, 512, 256)), ("c5_k_8x16384x2048", (8, 16384, 2048))):
         nbytes = 2 * shape[0] * shape[1] * shape[2]
         nbuf = max(1, -(-2 * L2_BYTES // nbytes))
         xs = [torch.randn(shape, generator=g, device=dev).to(torch.bfloat16) for _ in range(nbuf)]
         for i in range(3):
             triton_causal_fir(xs[i % nbuf], taps)
-        torch.cuda.synchronize()
-        s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        s.record()
-        for i in range(iters):
-            triton_causal_fir(xs[i % nbuf], taps)
-        e.record()
-        torch.cuda.synchronize()
-        ms = s.elapsed_time(e) / iters
+
+        def calls(n):
+            for i in range(n):
+                triton_causal_fir(xs[i % nbuf], taps)
+
+        ms = timed(calls, iters)
+        # the same calls captured once in a CUDA graph and replayed: device time per call
+        ncap = 2 * nbuf if nbytes < L2_BYTES else nbuf
+        side = torch.cuda.Stream(dev)
+        side.wait_stream(torch.cuda.current_stream(dev))
+        with torch.cuda.stream(side):
+            calls(ncap)
+        torch.cuda.current_stream(dev).wait_stream(side)
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph):
+            calls(ncap)
+        graph.replay()
+        reps = max(1, iters // ncap)
+        ms_dev = timed(lambda n: [graph.replay() for _ in range(reps)], 1) / (reps * ncap)
+        del graph
+        # tap gradient alone (gx not requested)
+        th = taps.clone().requires_grad_(True)
+        gys = [torch.randn(shape, generator=g, device=dev).to(torch.bfloat16) for _ in range(nbuf)]
+
+        def dtaps_calls(n):
+            for i in range(n):
+                y = triton_causal_fir(xs[i % nbuf], th)
+                torch.autograd.grad(y, th, gys[i % nbuf])
+
+        dtaps_calls(2)
+        ms_fwd_dt = timed(dtaps_calls, iters)  # includes the forward pass
+        ms_dt = max(ms_fwd_dt - ms, 1e-6)
         gbs = 2 * nbytes / (ms / 1e3) / 1e9
+        gbs_dev = 2 * nbytes / (ms_dev / 1e3) / 1e9
+        gbs_dt = 2 * nbytes / (ms_dt / 1e3) / 1e9
         res[name] = {"ms": round(ms, 4), "bytes_per_pass": 2 * nbytes, "GB/s": round(gbs, 1),
-                     "frac_of_hbm": round(gbs / peak, 3) if peak else None}
-        del xs
+                     "frac_of_hbm": round(gbs / peak, 3) if peak else None,
+                     "device_ms": round(ms_dev, 4), "device_GB/s": round(gbs_dev, 1),
+                     "device_frac_of_hbm": round(gbs_dev / peak, 3) if peak else None,
+                     "dtaps_ms": round(ms_dt, 4), "dtaps_GB/s": round(gbs_dt, 1),
+                     "dtaps_frac_of_hbm": round(gbs_dt / peak, 3) if peak else None}
+        del xs, gys
     res["peak_GB/s"] = peak
+    res["note"] = ("device_* from a replayed CUDA graph of the calls; dtaps_* = (forward + tap-gradient call) "
+                   "minus the forward call, 2 reads of B*N*C bf16 per pass")
     return res
 
 

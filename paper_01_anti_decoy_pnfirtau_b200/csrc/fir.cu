@@ -16,6 +16,7 @@
 #include <stdarg.h>
 #include <stdio.h>
 
+#include <algorithm>
 #include <mutex>
 
 #include "common.cuh"
@@ -65,6 +66,7 @@ struct FirGeom {
 // (window over past rows), DIR = -1: transpose (window over future rows).
 template <typename T, int VEC, int K, int DIR, int TN = FIR_TN>
 __global__ void __launch_bounds__(FIR_THREADS) fir_sliding_kernel(FirGeom g, const float* __restrict__ taps) {
+  constexpr int BATCH = TN < 8 ? TN : 8;  // row loads in flight per thread on the fast path
   const T* __restrict__ x = static_cast<const T*>(g.in);
   T* __restrict__ y = static_cast<T*>(g.out);
   float h[K];  // h[u] multiplies the input at lag u
@@ -98,15 +100,15 @@ __global__ void __launch_bounds__(FIR_THREADS) fir_sliding_kernel(FirGeom g, con
           for (int v = 0; v < VEC; ++v) win[u][v] = 0.f;
         }
       }
-      if (VEC * sizeof(T) == 16 && TN % 8 == 0 && n_first + TN <= g.N) {
-        // whole chunk inside the sequence: eight rows' loads issued before their use
+      if (VEC * sizeof(T) == 16 && TN % BATCH == 0 && n_first + TN <= g.N) {
+        // whole chunk inside the sequence: BATCH rows' loads issued before their use
 #pragma unroll
-        for (int t0 = 0; t0 < TN; t0 += 8) {
-          uint4 raw[8];
+        for (int t0 = 0; t0 < TN; t0 += BATCH) {
+          uint4 raw[BATCH];
 #pragma unroll
-          for (int t = 0; t < 8; ++t) raw[t] = __ldg(reinterpret_cast<const uint4*>(xb + (n_first + t0 + t) * g.sin));
+          for (int t = 0; t < BATCH; ++t) raw[t] = __ldg(reinterpret_cast<const uint4*>(xb + (n_first + t0 + t) * g.sin));
 #pragma unroll
-          for (int t = 0; t < 8; ++t) {
+          for (int t = 0; t < BATCH; ++t) {
             const T* e = reinterpret_cast<const T*>(&raw[t]);
 #pragma unroll
             for (int v = 0; v < VEC; ++v) win[0][v] = to_f32<T>(e[v]);
@@ -162,15 +164,15 @@ __global__ void __launch_bounds__(FIR_THREADS) fir_sliding_kernel(FirGeom g, con
           for (int v = 0; v < VEC; ++v) win[u][v] = 0.f;
         }
       }
-      if (VEC * sizeof(T) == 16 && TN % 8 == 0 && n_first + TN <= g.N) {
-        // whole chunk inside the sequence: eight rows' loads issued before their use
+      if (VEC * sizeof(T) == 16 && TN % BATCH == 0 && n_first + TN <= g.N) {
+        // whole chunk inside the sequence: BATCH rows' loads issued before their use
 #pragma unroll
-        for (int t0 = TN - 8; t0 >= 0; t0 -= 8) {
-          uint4 raw[8];
+        for (int t0 = TN - BATCH; t0 >= 0; t0 -= BATCH) {
+          uint4 raw[BATCH];
 #pragma unroll
-          for (int t = 0; t < 8; ++t) raw[t] = __ldg(reinterpret_cast<const uint4*>(xb + (n_first + t0 + t) * g.sin));
+          for (int t = 0; t < BATCH; ++t) raw[t] = __ldg(reinterpret_cast<const uint4*>(xb + (n_first + t0 + t) * g.sin));
 #pragma unroll
-          for (int t = 7; t >= 0; --t) {
+          for (int t = BATCH - 1; t >= 0; --t) {
             const T* e = reinterpret_cast<const T*>(&raw[t]);
 #pragma unroll
             for (int v = 0; v < VEC; ++v) win[0][v] = to_f32<T>(e[v]);
@@ -261,6 +263,88 @@ __global__ void __launch_bounds__(FIR_THREADS) fir_dtaps_partial_kernel(
   if (threadIdx.x == 0) partial[(int64_t)u * gridDim.x + blockIdx.x] = s;
 }
 
+// Tap gradient in one pass over gy and x (16-byte channel vectors, unit channel
+// stride): a thread owns VEC channels of a run of TN rows, keeps x[n-K+1..n] in a
+// register window and adds gy[n,c] * x[n-u,c] to acc[u] for every lag u at once,
+// so gy and x are read once (plus the K-1 halo rows of each run, from L1/L2)
+// instead of once per lag. Grid-stride over (b, run, channel vector) with a fixed
+// grid; partial[u][block] = the block's sum for lag u (reduced in fp64 in block
+// order by fir_dtaps_final_kernel, so the result is deterministic).
+template <typename T, int VEC, int K, int TN>
+__global__ void __launch_bounds__(FIR_THREADS) fir_dtaps_sliding_kernel(
+    const T* __restrict__ gy, int64_t sgb, int64_t sgn, const T* __restrict__ x, int64_t sxb, int64_t sxn,
+    int64_t B, int64_t N, int64_t C, float* __restrict__ partial) {
+  __shared__ float red[K][FIR_THREADS / 32];
+  float acc[K];
+#pragma unroll
+  for (int u = 0; u < K; ++u) acc[u] = 0.f;
+  const int64_t CV = C / VEC, chunks = (N + TN - 1) / TN, items = B * chunks * CV;
+  for (int64_t it = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; it < items;
+       it += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t cv = it % CV, rest = it / CV, chunk = rest % chunks, b = rest / chunks;
+    const T* xb = x + b * sxb + cv * VEC;
+    const T* gb = gy + b * sgb + cv * VEC;
+    const int64_t n0 = chunk * TN;
+    float win[K][VEC];  // win[u] = x[n-u]
+#pragma unroll
+    for (int u = 1; u < K; ++u) {
+      if (n0 - u >= 0) {
+        ld_vec<T, VEC>(xb + (n0 - u) * sxn, win[u]);
+      } else {
+#pragma unroll
+        for (int v = 0; v < VEC; ++v) win[u][v] = 0.f;
+      }
+    }
+    const int rows = (int)min((int64_t)TN, N - n0);
+    auto step = [&](const uint4& xr, const uint4& gr) {
+      float gv[VEC];
+      const T* xe = reinterpret_cast<const T*>(&xr);
+      const T* ge = reinterpret_cast<const T*>(&gr);
+#pragma unroll
+      for (int v = 0; v < VEC; ++v) {
+        win[0][v] = to_f32<T>(xe[v]);
+        gv[v] = to_f32<T>(ge[v]);
+      }
+#pragma unroll
+      for (int u = 0; u < K; ++u)
+#pragma unroll
+        for (int v = 0; v < VEC; ++v) acc[u] = fmaf(gv[v], win[u][v], acc[u]);
+#pragma unroll
+      for (int u = K - 1; u > 0; --u)
+#pragma unroll
+        for (int v = 0; v < VEC; ++v) win[u][v] = win[u - 1][v];
+    };
+    if (rows == TN) {
+      // whole run inside the sequence: every row of x and gy requested before use
+      uint4 xr[TN], gr[TN];
+#pragma unroll
+      for (int t = 0; t < TN; ++t) {
+        xr[t] = __ldg(reinterpret_cast<const uint4*>(xb + (n0 + t) * sxn));
+        gr[t] = __ldg(reinterpret_cast<const uint4*>(gb + (n0 + t) * sgn));
+      }
+#pragma unroll
+      for (int t = 0; t < TN; ++t) step(xr[t], gr[t]);
+    } else {
+      for (int t = 0; t < rows; ++t)
+        step(__ldg(reinterpret_cast<const uint4*>(xb + (n0 + t) * sxn)),
+             __ldg(reinterpret_cast<const uint4*>(gb + (n0 + t) * sgn)));
+    }
+  }
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+#pragma unroll
+  for (int u = 0; u < K; ++u) {
+    const float s = group_sum<32>(acc[u]);
+    if (lane == 0) red[u][warp] = s;
+  }
+  __syncthreads();
+  if (threadIdx.x < K) {
+    float s = 0.f;
+#pragma unroll
+    for (int w = 0; w < FIR_THREADS / 32; ++w) s += red[threadIdx.x][w];
+    partial[(int64_t)threadIdx.x * gridDim.x + blockIdx.x] = s;
+  }
+}
+
 // dtaps[K-1-u] = fp64 sum over the partials of lag u, in block order.
 __global__ void fir_dtaps_final_kernel(const float* __restrict__ partial, int nblk, int K, float* __restrict__ dtaps) {
   const int u = threadIdx.x;
@@ -293,10 +377,15 @@ static int fir_launch(const FirGeom& g, const float* taps, int K, cudaStream_t s
     if (vec_ok<T>(g)) {
       const int64_t items = g.B * chunks * (g.C / VEC);
       // long runs of rows per thread (6-row halo and index math amortised over 32
-      // rows) once that still leaves two 256-thread blocks per SM of a B200
+      // rows) once that still leaves two 256-thread blocks per SM of a B200; short
+      // runs of 4 rows when 8-row runs would give under four blocks per SM (small
+      // inputs are bound by load round trips, not bytes: twice the threads in flight)
       if (items / (32 / FIR_TN) >= 2 * 148 * FIR_THREADS) {
         const int64_t items32 = g.B * ((g.N + 31) / 32) * (g.C / VEC);
         fir_sliding_kernel<T, VEC, 7, DIR, 32><<<grid_for(items32), FIR_THREADS, 0, st>>>(g, taps);
+      } else if (items < 4 * 148 * FIR_THREADS) {
+        const int64_t items4 = g.B * ((g.N + 3) / 4) * (g.C / VEC);
+        fir_sliding_kernel<T, VEC, 7, DIR, 4><<<grid_for(items4), FIR_THREADS, 0, st>>>(g, taps);
       } else {
         fir_sliding_kernel<T, VEC, 7, DIR><<<grid_for(items), FIR_THREADS, 0, st>>>(g, taps);
       }
@@ -315,6 +404,31 @@ static int64_t dtaps_blocks(int64_t B, int64_t N, int64_t C) {
   if (g < 1) g = 1;
   if (g > FIR_DTAPS_MAX_BLOCKS) g = FIR_DTAPS_MAX_BLOCKS;
   return g;
+}
+
+// Tap-gradient partials: the one-pass sliding kernel for 7 taps on 16-byte
+// aligned rows with unit channel stride, else the per-lag kernel. Returns the
+// number of blocks (<= dtaps_blocks(B, N, C)) whose partials partial[u][block]
+// the final reduction sums.
+template <typename T>
+static int dtaps_partials(const T* gy, int64_t sgb, int64_t sgn, int64_t sgc, const T* x, int64_t sxb, int64_t sxn,
+                          int64_t sxc, int64_t B, int64_t N, int64_t C, int K, float* part, cudaStream_t st) {
+  constexpr int VEC = 16 / sizeof(T);
+  constexpr int TN = 8;
+  const int nmax = (int)dtaps_blocks(B, N, C);
+  const bool vec = K == 7 && sgc == 1 && sxc == 1 && C % VEC == 0 && sgn % VEC == 0 && sgb % VEC == 0 &&
+                   sxn % VEC == 0 && sxb % VEC == 0 && reinterpret_cast<uintptr_t>(gy) % 16 == 0 &&
+                   reinterpret_cast<uintptr_t>(x) % 16 == 0;
+  if (vec) {
+    const int64_t items = B * ((N + TN - 1) / TN) * (C / VEC);
+    int nblk = (int)std::min<int64_t>(nmax, (items + FIR_THREADS - 1) / FIR_THREADS);
+    if (nblk < 1) nblk = 1;
+    fir_dtaps_sliding_kernel<T, VEC, 7, TN><<<nblk, FIR_THREADS, 0, st>>>(gy, sgb, sgn, x, sxb, sxn, B, N, C, part);
+    return nblk;
+  }
+  fir_dtaps_partial_kernel<T><<<dim3(nmax, K), FIR_THREADS, 0, st>>>(gy, sgb, sgn, sgc, x, sxb, sxn, sxc, B, N, C,
+                                                                    part);
+  return nmax;
 }
 
 // Scratch of pnft_fir_bwd_noalloc: the per-block, per-lag partial sums of the tap
@@ -392,11 +506,11 @@ extern "C" int pnft_fir_bwd(const void* gy, int64_t sgb, int64_t sgn, int64_t sg
       const size_t need = pnft_fir_bwd_workspace_size(B, N, C, ntaps);
       if (!workspace || workspace_bytes < need)
         return fail(PNFT_EINVAL, "fir bwd: workspace of %zu bytes < required %zu", workspace_bytes, need);
-      const int nblk = (int)dtaps_blocks(B, N, C);
+      int nblk = 0;
       float* part = static_cast<float*>(workspace);
       PNFT_DISPATCH_DTYPE(dtype, T, {
-        fir_dtaps_partial_kernel<T><<<dim3(nblk, ntaps), FIR_THREADS, 0, st>>>(
-            static_cast<const T*>(gy), sgb, sgn, sgc, static_cast<const T*>(x), s0b, s0n, s0c, B, N, C, part);
+        nblk = dtaps_partials<T>(static_cast<const T*>(gy), sgb, sgn, sgc, static_cast<const T*>(x), s0b, s0n, s0c,
+                                 B, N, C, ntaps, part, st);
       });
       fir_dtaps_final_kernel<<<1, FIR_MAX_TAPS, 0, st>>>(part, nblk, ntaps, dtaps);
       rc = check_launch("fir dtaps", 2);
@@ -433,10 +547,10 @@ extern "C" int pnft_fir_bwd_noalloc(const void* gy, int64_t sgb, int64_t sgn, in
   float* part = nullptr;
   rc = dtaps_scratch_ptr(&part);
   if (rc) return rc;
-  const int nblk = (int)dtaps_blocks(B, N, C);  // <= FIR_DTAPS_MAX_BLOCKS by construction
+  int nblk = 0;  // <= dtaps_blocks(B, N, C) <= FIR_DTAPS_MAX_BLOCKS by construction
   PNFT_DISPATCH_DTYPE(dtype, T, {
-    fir_dtaps_partial_kernel<T><<<dim3(nblk, ntaps), FIR_THREADS, 0, st>>>(
-        static_cast<const T*>(gy), sgb, sgn, sgc, static_cast<const T*>(x), s0b, s0n, s0c, B, N, C, part);
+    nblk = dtaps_partials<T>(static_cast<const T*>(gy), sgb, sgn, sgc, static_cast<const T*>(x), s0b, s0n, s0c, B, N,
+                             C, ntaps, part, st);
   });
   fir_dtaps_final_kernel<<<1, FIR_MAX_TAPS, 0, st>>>(part, nblk, ntaps, dtaps);
   rc = check_launch("fir dtaps noalloc", 2);

@@ -58,7 +58,10 @@ class TauGradReducer:
     to :meth:`push`, which converts it to fp64 and all-reduces it on a side stream
     of the gradient's device (the compute stream only records an event): the
     collective overlaps the next kernels instead of putting every rank in
-    lock-step once per backward. The partial sums of successive backwards
+    lock-step once per backward (the side stream has high priority; with NCCL
+    on a high-priority stream too, the collective's kernel takes the next free SM
+    slot instead of queueing behind long compute kernels). The partial sums of
+    successive backwards
     accumulate here until the consumer of tau's gradient calls :meth:`result`
     (its current stream then waits for the side stream) or :meth:`accumulate_into`
     (which adds the sum to ``tau.grad``), as data-parallel training finalises its
@@ -85,7 +88,7 @@ class TauGradReducer:
         cur = torch.cuda.current_stream(g.device)
         side = self._streams.get(g.device)
         if side is None:
-            side = self._streams[g.device] = torch.cuda.Stream(g.device)
+            side = self._streams[g.device] = torch.cuda.Stream(g.device, priority=-1)
         side.wait_stream(cur)
         with torch.cuda.stream(side):
             t = g.detach().to(torch.float64)
