@@ -95,6 +95,30 @@ bool flash_sm100_supported(const FlashArgs& a);
 int flash_fwd_sm100(const FlashArgs& a, cudaStream_t st);
 int flash_bwd_sm100(const FlashArgs& a, cudaStream_t st);
 
+// CTA order of the tcgen05 kernels: work item w (a CTA's linear block index, or
+// its ticket) -> head bh and tile index t. Heads are taken in groups of G: inside a
+// group the tile index runs slowest and the head fastest (the longest tiles of the
+// group first), and the groups follow one another, so the per-head data that the
+// CTAs in flight re-read (K/V in the forward; Q, dO and the dQ accumulator in the
+// backward) stays within L2 on long sequences. G >= number of heads is the plain
+// order: tile slowest, head fastest.
+__device__ __forceinline__ void work_item(int w, int BH, int nT, int G, int* bh, int* t) {
+  const int full = BH / G * G;  // heads in complete groups
+  if (w < full * nT) {
+    const int gsz = G * nT, g = w / gsz, r = w - g * gsz;
+    *t = r / G;
+    *bh = g * G + r % G;
+  } else {
+    const int r = w - full * nT, last = BH - full;
+    *t = r / last;
+    *bh = full + r % last;
+  }
+}
+// Heads per group for a per-head working set of `head_bytes`: the groups in flight
+// re-read about 80 MB (the 126 MB L2 keeps streamed tiles too). PNFT_HEAD_GROUP in
+// the environment (a positive head count) overrides the choice.
+int head_group(int64_t BH, int64_t head_bytes);
+
 // Host helpers shared by the sm_100a kernels: a 4-D TMA map {D, N, H, B} over a
 // bf16 [B,H,N,D] view with element strides s (box {64, rows}, 128-byte swizzle),
 // the stride/alignment rule such a map needs, and the device check.

@@ -28,8 +28,10 @@
 //
 // Every mbarrier wait is bounded (sm100_ptx.cuh): on timeout the CTA sets the
 // caller's status word, drains its own TMA/MMA work and frees TMEM.
+#include <stdlib.h>
 #include <string.h>
 
+#include <algorithm>
 #include <mutex>
 
 #include "fir_tile.cuh"
@@ -136,6 +138,7 @@ struct FwdParams {
   float scale, gamma;
   int has_gamma, causal;
   int stall;  // PNFT_FLASH_TEST_STALL: the elementwise warps first wait on B_STALL
+  int hgroup;  // heads per group of the CTA order (work_item)
 };
 
 template <int D, bool FIR>
@@ -149,8 +152,10 @@ __global__ void __launch_bounds__(f_threads<FIR>(), FIR ? 1 : 2) flash_fwd_sm100
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   // b*h runs fastest and the query tiles go from the last (longest causal rows)
   // down: the grid starts with its longest CTAs, so none starts late
-  const int qt = p.nq - 1 - (int)blockIdx.y;
-  const int bh = blockIdx.x, b = bh / p.H, hd = bh % p.H;
+  int bh, qt;
+  work_item((int)(blockIdx.y * gridDim.x + blockIdx.x), (int)gridDim.x, p.nq, p.hgroup, &bh, &qt);
+  qt = p.nq - 1 - qt;
+  const int b = bh / p.H, hd = bh % p.H;
   const int q0 = qt * FM;
   const int ntiles = p.causal ? min(p.nk, (q0 + FM + FN - 1) / FN) : p.nk;
   auto bar = [&](int i) -> uint32_t { return sb0 + L::OFF_BAR + 8u * (uint32_t)i; };
@@ -620,6 +625,16 @@ bool tma_ok_bhnd(const void* ptr, const int64_t* s) {
   return true;
 }
 
+int head_group(int64_t BH, int64_t head_bytes) {
+  if (const char* e = getenv("PNFT_HEAD_GROUP")) {
+    const long g = strtol(e, nullptr, 10);
+    if (g > 0) return (int)std::min<int64_t>(g, BH);
+  }
+  const int64_t budget = (int64_t)80 << 20;
+  const int64_t g = std::max<int64_t>(1, budget / std::max<int64_t>(head_bytes, 1));
+  return (int)std::min<int64_t>(g, BH);
+}
+
 bool device_is_sm100() {
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess) return false;
@@ -665,6 +680,7 @@ int flash_fwd_sm100(const FlashArgs& a, cudaStream_t st) {
   p.has_gamma = a.has_gamma;
   p.causal = a.causal;
   p.stall = (a.flags & PNFT_FLASH_TEST_STALL) ? 1 : 0;
+  p.hgroup = head_group(a.B * a.H, a.N * a.D * 4);  // K and V of a head, re-read by its query tiles
   if (p.nq > 65535) return fail(PNFT_EUNSUPPORTED, "flash fwd sm100: N = %lld needs more than 65535 query tiles", (long long)a.N);
   const dim3 grid((unsigned)(a.B * a.H), (unsigned)p.nq);
   auto launch = [&](auto kern, int smem) -> int {

@@ -162,6 +162,7 @@ struct BwdParams {
   int det;
   int32_t* sem;     // [B*H, nq64]
   int32_t* ticket;  // [1]
+  int hgroup;       // heads per group of the CTA order (work_item)
 };
 
 // Warp-cooperative walk over the query tiles [i0, n) whose live bit is set: 32
@@ -220,14 +221,16 @@ __global__ void __launch_bounds__(B_THREADS, 1) flash_bwd_sm100_kernel(const __g
   // the grid starts with its longest CTAs, so none starts late. Deterministic mode
   // takes the same order from a work ticket, so every CTA whose dQ additions a CTA
   // waits for (the lower key tiles of its head) started before it.
-  int kt_ = blockIdx.y, bh_ = blockIdx.x;
+  int kt_, bh_, w = (int)(blockIdx.y * gridDim.x + blockIdx.x);
   if (p.det) {
     volatile int* tk = reinterpret_cast<volatile int*>(smem + L::OFF_TKT);
     if (threadIdx.x == 0) *tk = atomicAdd(p.ticket, 1);
     __syncthreads();
-    bh_ = *tk % (int)gridDim.x;
-    kt_ = *tk / (int)gridDim.x;
+    w = *tk;
   }
+  // heads in groups sized to L2 (work_item): in deterministic mode the lower key
+  // tiles of a head still come earlier in the order, within its group
+  work_item(w, (int)gridDim.x, p.nkt, p.hgroup, &bh_, &kt_);
   const int kt = kt_, bh = bh_, b = bh / p.H, hd = bh % p.H;
   const int k0 = kt * BN;
   const int i_first = p.causal ? k0 / BM : 0;
@@ -832,6 +835,8 @@ int flash_bwd_sm100(const FlashArgs& a0, cudaStream_t st) {
   p.causal = a.causal;
   p.stall = (a.flags & PNFT_FLASH_TEST_STALL) ? 1 : 0;
   p.det = (a.flags & PNFT_FLASH_DETERMINISTIC) ? 1 : 0;
+  // Q, dO (bf16) and the fp32 dQ accumulator of a head, re-read by its key tiles
+  p.hgroup = head_group(a.B * a.H, a.N * a.D * 8);
   p.sem = a.dq_sem;
   p.ticket = a.dq_ticket;
   if (nkt > 65535) return fail(PNFT_EUNSUPPORTED, "flash bwd sm100: N = %lld needs more than 65535 key tiles", (long long)a.N);
