@@ -646,7 +646,9 @@ def bench_c5(args, dist_: Dist, dev) -> dict:
         "fwd_ms": round(fwd, 3), "bwd_ms": round(bwd, 3),
         "roofline": {"bound": "tensor", "kernel": "flash_bwd", "achieved": round(bwd_tf, 2),
                      "peak": peaks["bf16_tflops"], "unit": "TFLOP/s", "frac": round(bwd_tf / peaks["bf16_tflops"], 4),
-                     "flops_per_launch": 5.0 * ws["B"] * ws["H"] * N * N * D, "ms_per_launch": round(bwd, 3)},
+                     "flops_per_launch": 5.0 * ws["B"] * ws["H"] * N * N * D, "ms_per_launch": round(bwd, 3),
+                     "traffic": (profile_traffic("flash_bwd:c5") or 0) * (hi - lo) / (B * H) or None,
+                     "traffic_source": profile_traffic_source("flash_bwd:c5")},
         "rank0_fwd_tflops": round(2.0 * ws["B"] * ws["H"] * N * N * D / (fwd / 1e3) / 1e12, 2),
         "flops_per_step_per_rank": mine,
     }
