@@ -471,22 +471,39 @@ __global__ void __launch_bounds__(GTHREADS) flash_bwd_generic_kernel(FlashArgs a
 #pragma unroll
         for (int jj = 0; jj < NJ; ++jj) dq[ii][jj] = fmaf(s[ii], kv[jj], dq[ii][jj]);
     }
-    if (det) det_turn_wait(q0);
+    if (det) {
+      // this block's turn: every load of its dQ elements issued before the first add
+      det_turn_wait(q0);
+      float old[4][NJ];
 #pragma unroll
-    for (int ii = 0; ii < 4; ++ii) {
-      const int64_t row = q0 + rg + 16 * ii;
-      if (row >= N) continue;
+      for (int ii = 0; ii < 4; ++ii)
 #pragma unroll
-      for (int jj = 0; jj < NJ; ++jj) {
-        const int e = cg + 16 * jj;
-        if (e < D) {
-          float* dst = dQa + row * a.D + e;
-          if (det) __stcg(dst, __ldcg(dst) + dq[ii][jj]);
-          else atomicAdd(dst, dq[ii][jj]);
+        for (int jj = 0; jj < NJ; ++jj) {
+          const int64_t row = q0 + rg + 16 * ii;
+          const int e = cg + 16 * jj;
+          old[ii][jj] = (row < N && e < D) ? __ldcg(dQa + row * a.D + e) : 0.f;
+        }
+#pragma unroll
+      for (int ii = 0; ii < 4; ++ii)
+#pragma unroll
+        for (int jj = 0; jj < NJ; ++jj) {
+          const int64_t row = q0 + rg + 16 * ii;
+          const int e = cg + 16 * jj;
+          if (row < N && e < D) __stcg(dQa + row * a.D + e, old[ii][jj] + dq[ii][jj]);
+        }
+      det_turn_pass(q0);
+    } else {
+#pragma unroll
+      for (int ii = 0; ii < 4; ++ii) {
+        const int64_t row = q0 + rg + 16 * ii;
+        if (row >= N) continue;
+#pragma unroll
+        for (int jj = 0; jj < NJ; ++jj) {
+          const int e = cg + 16 * jj;
+          if (e < D) atomicAdd(dQa + row * a.D + e, dq[ii][jj]);
         }
       }
     }
-    if (det) det_turn_pass(q0);
   }
   T* dK = static_cast<T*>(a.dk) + b * a.sdk[0] + h * a.sdk[1];
   T* dV = static_cast<T*>(a.dv) + b * a.sdv[0] + h * a.sdv[1];

@@ -659,29 +659,62 @@ __global__ void __launch_bounds__(B_THREADS, 1) flash_bwd_sm100_kernel(const __g
     const uint32_t lane_off = (uint32_t)(32 * wq) << 16;
     const bool leader = warp == W_DRAIN && lane == 0;
     bool dead = false;
-    // deterministic mode: add the staged fp32 tile of query tile i (rows of 64 x D,
-    // the accumulator's own layout) once the lower key tiles of this head have added
-    // theirs, then pass the turn on; all 128 drain threads
+    // deterministic mode: add the staged fp32 tiles of query tiles ia and (if ib >= 0)
+    // ib (rows of 64 x D, the accumulator's own layout) once the lower key tiles of
+    // this head have added theirs, then pass both turns on; all 128 drain threads.
+    // Both tiles' turns are awaited together and all their loads issued before the
+    // first add, so a pair costs one turn wait and one L2 round trip.
     const int dt = threadIdx.x - 32 * W_DRAIN;
-    auto ordered_add = [&](int i, const float* stg, int rows) {
-      int32_t* sem = p.sem + (int64_t)bh * p.nq64 + i;
-      if (leader) turn_wait(sem, kt, p.status, abort_flag);
+    auto ordered_add = [&](int ia, const float* stga, int ib, const float* stgb) {
+      int32_t* sema = p.sem + (int64_t)bh * p.nq64 + ia;
+      int32_t* semb = ib >= 0 ? p.sem + (int64_t)bh * p.nq64 + ib : nullptr;
+      if (leader) {
+        turn_wait(sema, kt, p.status, abort_flag);
+        if (semb) turn_wait(semb, kt, p.status, abort_flag);
+      }
       named_bar_sync(4, 128);
       if (!dead) {
-        float4* dst = reinterpret_cast<float4*>(p.dq_acc + ((int64_t)bh * p.N + (int64_t)i * BM) * D);
-        const float4* src = reinterpret_cast<const float4*>(stg);
-        for (int e = dt; e < rows * (D / 4); e += 128) {
-          float4 a = __ldcg(dst + e);
-          const float4 b4 = src[e];
-          a.x += b4.x;
-          a.y += b4.y;
-          a.z += b4.z;
-          a.w += b4.w;
-          __stcg(dst + e, a);
+        // loads of up to 8 float4 per thread (both tiles of a pair at d = 64, half a
+        // tile at d = 128) issued before their adds
+        constexpr int PER = BM * D / 4 / 128;   // float4 per drain thread and tile
+        constexpr int NT = L::DQ_PAIR ? 2 : 1;  // tiles per drain step
+        constexpr int CH = PER * NT > 8 ? 8 : PER * NT;
+        auto addr = [&](int c, int* e, int* t) {  // c-th float4 of this thread -> tile, element
+          *t = c / PER;
+          *e = dt + 128 * (c % PER);
+        };
+#pragma unroll
+        for (int c0 = 0; c0 < PER * NT; c0 += CH) {
+          float4 a[CH];
+#pragma unroll
+          for (int k = 0; k < CH; ++k) {
+            int e, t;
+            addr(c0 + k, &e, &t);
+            const int i = t == 0 ? ia : ib;
+            if (i >= 0 && e < min(BM, p.N - i * BM) * (D / 4))
+              a[k] = __ldcg(reinterpret_cast<const float4*>(p.dq_acc + ((int64_t)bh * p.N + (int64_t)i * BM) * D) + e);
+          }
+#pragma unroll
+          for (int k = 0; k < CH; ++k) {
+            int e, t;
+            addr(c0 + k, &e, &t);
+            const int i = t == 0 ? ia : ib;
+            if (i >= 0 && e < min(BM, p.N - i * BM) * (D / 4)) {
+              const float4 b4 = reinterpret_cast<const float4*>(t == 0 ? stga : stgb)[e];
+              a[k].x += b4.x;
+              a[k].y += b4.y;
+              a[k].z += b4.z;
+              a[k].w += b4.w;
+              __stcg(reinterpret_cast<float4*>(p.dq_acc + ((int64_t)bh * p.N + (int64_t)i * BM) * D) + e, a[k]);
+            }
+          }
         }
       }
       named_bar_sync(4, 128);
-      if (leader) turn_pass(sem);
+      if (leader) {
+        turn_pass(sema);
+        if (semb) turn_pass(semb);
+      }
     };
     LiveTiles lt(live, i_first, p.nq64, p.det != 0);
     bool mt;
@@ -719,8 +752,8 @@ __global__ void __launch_bounds__(B_THREADS, 1) flash_bwd_sm100_kernel(const __g
         fence_proxy_async_smem();
         named_bar_sync(4, 128);
         if (p.det) {
-          ordered_add(ia, reinterpret_cast<const float*>(smem + L::OFF_STG), min(BM, p.N - ia * BM));
-          if (two) ordered_add(ib, reinterpret_cast<const float*>(smem + L::OFF_STG + L::STG_BYTES), min(BM, p.N - ib * BM));
+          ordered_add(ia, reinterpret_cast<const float*>(smem + L::OFF_STG), two ? ib : -1,
+                      reinterpret_cast<const float*>(smem + L::OFF_STG + L::STG_BYTES));
         } else if (leader && !dead) {
           const int qa = ia * BM;
           bulk_reduce_add_f32(p.dq_acc + ((int64_t)bh * p.N + qa) * D, smem_u32(smem + L::OFF_STG),
@@ -766,7 +799,7 @@ __global__ void __launch_bounds__(B_THREADS, 1) flash_bwd_sm100_kernel(const __g
       fence_proxy_async_smem();
       named_bar_sync(4, 128);
       if (p.det) {
-        ordered_add(i, stg, min(BM, p.N - q0));
+        ordered_add(i, stg, -1, nullptr);
       } else if (leader && !dead) {
         const int rows = min(BM, p.N - q0);
         bulk_reduce_add_f32(p.dq_acc + ((int64_t)bh * p.N + q0) * D, smem_u32(stg), (uint32_t)(rows * D * 4));

@@ -72,6 +72,27 @@ def test_noalloc_matches_workspace_entry_point_twice(cuda, dtype):
         assert _rel(dt, dt_ref) <= 1e-6
 
 
+@pytest.mark.parametrize("ntaps", [7, 5])
+def test_noalloc_tap_gradient_only(cuda, ntaps):
+    """gx = NULL: the tap gradient alone, with the 7-tap one-pass kernel and with
+    the per-lag kernel that other tap counts use; two calls in a row."""
+    L = _lib.lib()
+    for B, N, C, seed in ((4, 300, 64, 4), (1, 19, 16, 5)):
+        gy, x, taps = _case(B, N, C, torch.bfloat16, seed, cuda)
+        taps = taps[:ntaps] / taps[:ntaps].sum()
+        dt_ref = torch.empty(ntaps, device=cuda)
+        ws = torch.empty(max(L.pnft_fir_bwd_workspace_size(B, N, C, ntaps), 1), device=cuda, dtype=torch.uint8)
+        _lib.check(L.pnft_fir_bwd(gy.data_ptr(), *gy.stride(), taps.data_ptr(), ntaps, None, 0, 0, 0, x.data_ptr(),
+                                  *x.stride(), dt_ref.data_ptr(), ws.data_ptr(), ws.numel(), B, N, C, _lib.DTYPE_BF16,
+                                  torch.cuda.current_stream().cuda_stream), "pnft_fir_bwd")
+        dt = torch.empty(ntaps, device=cuda)
+        _lib.check(L.pnft_fir_bwd_noalloc(gy.data_ptr(), *gy.stride(), taps.data_ptr(), ntaps, None, 0, 0, 0,
+                                          x.data_ptr(), *x.stride(), dt.data_ptr(), B, N, C, _lib.DTYPE_BF16,
+                                          torch.cuda.current_stream().cuda_stream), "pnft_fir_bwd_noalloc")
+        torch.cuda.synchronize()
+        assert _rel(dt, dt_ref) <= 1e-6
+
+
 def test_noalloc_rejects_too_many_taps(cuda):
     L = _lib.lib()
     gy, x, _ = _case(1, 8, 8, torch.float32, 3, cuda)
