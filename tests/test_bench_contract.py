@@ -48,4 +48,28 @@ def test_bench_json_contract_gpu():
     e2e = d["e2e"]
     assert e2e["h2d_bytes_per_step"] == 4 * 8 * 8 * 4096 * 64 * 2 and e2e["d2h_bytes_per_step"] == 4 * 8 * 8 * 4096 * 64 * 2 + 4
     assert d["gpu_launches"] > 0 and "sm_mhz" in d["clocks"] and "reasons" in d["clocks"]
-    assert d["fir"]["c5_k_8x16384x2048"]["GB/s"] > 0
+    assert d["fir"]["c5_k_8x16384x2048"]["GB/s"] > 0 and d["fir"]["lm_k_32x512x256"]["device_GB/s"] > 0
+    assert rf["traffic"] > 1e8 and "profiles/" in rf["traffic_source"]
+    # config 3's tau sweep: silence only at +0.5, where about half the causal tiles skip
+    sw = d["tau_sweep"]
+    assert set(sw) >= {"-0.5", "+0.0", "+0.5"}
+    assert sw["-0.5"]["tiles_silent_frac"] == 0.0 and 0.3 < sw["+0.5"]["tiles_silent_frac"] < 0.7
+    assert sw["+0.5"]["ms_per_step"] < sw["+0.0"]["ms_per_step"]
+    assert d["deterministic"]["value"] > 0
+    c5 = d["c5"]
+    assert c5["heads_per_rank"] == 128 and c5["value"] > 0 and c5["roofline"]["frac"] > 0
+
+
+@pytest.mark.gpu
+def test_reference_arm_times_reference_triton_on_gpu():
+    """On a GPU the reference arm also times the reference's own Triton Flash kernels
+    (staged unchanged in oracle/_ref) at the config-3 tau sweep."""
+    from oracle import stage_ref
+
+    if stage_ref.staged() is None:
+        pytest.skip("the reference package was not staged into oracle/_ref (no reference checkout at build time)")
+    d = _run_bench(["--impl", "reference", "--steps", "2", "--warmup", "1"], timeout=900)
+    t = d["triton_b200"]
+    assert "unavailable" not in t, t
+    for k in ("+0.0", "-0.5", "+0.5"):
+        assert t[k]["value"] > 0 and t[k]["ms_per_step"] > 0
