@@ -1,8 +1,8 @@
 // Depthwise causal FIR along the sequence axis of x[B,N,C] (and its transpose
 // and tap gradient). HBM-bound: every element is read once and written once;
 // threads own 16-byte channel vectors so a warp moves 512 contiguous bytes per
-// row, and each thread walks a run of consecutive rows (8, or 32 when the problem
-// still fills every SM twice over) keeping the K-1 previous rows in registers
+// row, and each thread walks a run of consecutive rows (32, 16 or 8: the longest
+// that still fills every SM) keeping the K-1 previous rows in registers
 // (the halo rows are re-read from L1/L2, never from DRAM twice in practice). A run
 // that lies inside the sequence loads eight rows at a time before using them, so
 // each thread keeps eight 16-byte loads in flight.
@@ -345,13 +345,21 @@ __global__ void __launch_bounds__(FIR_THREADS) fir_dtaps_sliding_kernel(
   }
 }
 
-// dtaps[K-1-u] = fp64 sum over the partials of lag u, in block order.
+// dtaps[K-1-u] = fp64 sum over the partials of lag u: one warp per lag, lane l adds
+// blocks l, l+32, ... in order, then a fixed butterfly across the lanes, so the
+// rounding is the same on every run.
 __global__ void fir_dtaps_final_kernel(const float* __restrict__ partial, int nblk, int K, float* __restrict__ dtaps) {
-  const int u = threadIdx.x;
+  const int u = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5), lane = threadIdx.x & 31;
   if (u >= K) return;
   double s = 0.0;
-  for (int i = 0; i < nblk; ++i) s += (double)partial[(int64_t)u * nblk + i];
-  dtaps[K - 1 - u] = (float)s;
+  for (int i = lane; i < nblk; i += 32) s += (double)partial[(int64_t)u * nblk + i];
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+  if (lane == 0) dtaps[K - 1 - u] = (float)s;
+}
+static void dtaps_final(const float* part, int nblk, int K, float* dtaps, cudaStream_t st) {
+  constexpr int WARPS = 8;
+  fir_dtaps_final_kernel<<<(K + WARPS - 1) / WARPS, 32 * WARPS, 0, st>>>(part, nblk, K, dtaps);
 }
 
 static int grid_for(int64_t items) {
@@ -375,19 +383,19 @@ static int fir_launch(const FirGeom& g, const float* taps, int K, cudaStream_t s
   if (K == 7) {
     const int64_t chunks = (g.N + FIR_TN - 1) / FIR_TN;
     if (vec_ok<T>(g)) {
-      const int64_t items = g.B * chunks * (g.C / VEC);
-      // long runs of rows per thread (6-row halo and index math amortised over 32
-      // rows) once that still leaves two 256-thread blocks per SM of a B200; short
-      // runs of 4 rows when 8-row runs would give under four blocks per SM (small
-      // inputs are bound by load round trips, not bytes: twice the threads in flight)
-      if (items / (32 / FIR_TN) >= 2 * 148 * FIR_THREADS) {
-        const int64_t items32 = g.B * ((g.N + 31) / 32) * (g.C / VEC);
+      // the longest run of rows per thread (the 6-row halo, the index math and the
+      // load round trips amortised over 32, 16 or 8 rows) that still gives at least
+      // 1.5 blocks of 256 threads per SM of a B200 (measured: 32-row runs 14.7 us
+      // against 24.0 us for 8-row runs on [8, 4096, 512]; on [32, 512, 256], where
+      // longer runs leave SMs idle, 8-row runs 7.5 us against 9.6 us for 4-row runs)
+      const int64_t CV = g.C / VEC, enough = 148 * FIR_THREADS * 3 / 2;
+      const int64_t items32 = g.B * ((g.N + 31) / 32) * CV, items16 = g.B * ((g.N + 15) / 16) * CV;
+      if (items32 >= enough) {
         fir_sliding_kernel<T, VEC, 7, DIR, 32><<<grid_for(items32), FIR_THREADS, 0, st>>>(g, taps);
-      } else if (items < 4 * 148 * FIR_THREADS) {
-        const int64_t items4 = g.B * ((g.N + 3) / 4) * (g.C / VEC);
-        fir_sliding_kernel<T, VEC, 7, DIR, 4><<<grid_for(items4), FIR_THREADS, 0, st>>>(g, taps);
+      } else if (items16 >= enough) {
+        fir_sliding_kernel<T, VEC, 7, DIR, 16><<<grid_for(items16), FIR_THREADS, 0, st>>>(g, taps);
       } else {
-        fir_sliding_kernel<T, VEC, 7, DIR><<<grid_for(items), FIR_THREADS, 0, st>>>(g, taps);
+        fir_sliding_kernel<T, VEC, 7, DIR><<<grid_for(g.B * chunks * CV), FIR_THREADS, 0, st>>>(g, taps);
       }
     } else {
       const int64_t items = g.B * chunks * g.C;
@@ -512,7 +520,7 @@ extern "C" int pnft_fir_bwd(const void* gy, int64_t sgb, int64_t sgn, int64_t sg
         nblk = dtaps_partials<T>(static_cast<const T*>(gy), sgb, sgn, sgc, static_cast<const T*>(x), s0b, s0n, s0c,
                                  B, N, C, ntaps, part, st);
       });
-      fir_dtaps_final_kernel<<<1, FIR_MAX_TAPS, 0, st>>>(part, nblk, ntaps, dtaps);
+      dtaps_final(part, nblk, ntaps, dtaps, st);
       rc = check_launch("fir dtaps", 2);
       if (rc) return rc;
     }
@@ -552,7 +560,7 @@ extern "C" int pnft_fir_bwd_noalloc(const void* gy, int64_t sgb, int64_t sgn, in
     nblk = dtaps_partials<T>(static_cast<const T*>(gy), sgb, sgn, sgc, static_cast<const T*>(x), s0b, s0n, s0c, B, N,
                              C, ntaps, part, st);
   });
-  fir_dtaps_final_kernel<<<1, FIR_MAX_TAPS, 0, st>>>(part, nblk, ntaps, dtaps);
+  dtaps_final(part, nblk, ntaps, dtaps, st);
   rc = check_launch("fir dtaps noalloc", 2);
   if (rc) return rc;
   if (gx) {
