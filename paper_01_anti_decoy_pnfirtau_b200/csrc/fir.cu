@@ -88,6 +88,45 @@ __global__ void __launch_bounds__(FIR_THREADS) fir_sliding_kernel(FirGeom g, con
     const int64_t n_first = chunk * TN;
     const int64_t n_last = min(n_first + TN, g.N) - 1;
     if (DIR > 0) {
+      if (VEC * sizeof(T) == 16 && TN % BATCH == 0 && n_first >= K - 1 && n_first + TN <= g.N) {
+        // interior run: the K-1 halo rows and the first BATCH rows requested together
+        uint4 hr[K - 1], raw[BATCH];
+#pragma unroll
+        for (int u = 1; u < K; ++u) hr[u - 1] = __ldg(reinterpret_cast<const uint4*>(xb + (n_first - u) * g.sin));
+#pragma unroll
+        for (int t0 = 0; t0 < TN; t0 += BATCH) {
+#pragma unroll
+          for (int t = 0; t < BATCH; ++t) raw[t] = __ldg(reinterpret_cast<const uint4*>(xb + (n_first + t0 + t) * g.sin));
+          if (t0 == 0) {
+#pragma unroll
+            for (int u = 1; u < K; ++u) {
+              const T* e = reinterpret_cast<const T*>(&hr[u - 1]);
+#pragma unroll
+              for (int v = 0; v < VEC; ++v) win[u][v] = to_f32<T>(e[v]);
+            }
+          }
+#pragma unroll
+          for (int t = 0; t < BATCH; ++t) {
+            const T* e = reinterpret_cast<const T*>(&raw[t]);
+#pragma unroll
+            for (int v = 0; v < VEC; ++v) win[0][v] = to_f32<T>(e[v]);
+            float acc[VEC];
+#pragma unroll
+            for (int v = 0; v < VEC; ++v) {
+              float a = win[0][v] * h[0];
+#pragma unroll
+              for (int u = 1; u < K; ++u) a = fmaf(win[u][v], h[u], a);
+              acc[v] = a;
+            }
+            st_vec<T, VEC>(yb + (n_first + t0 + t) * g.son, acc);
+#pragma unroll
+            for (int u = K - 1; u > 0; --u)
+#pragma unroll
+              for (int v = 0; v < VEC; ++v) win[u][v] = win[u - 1][v];
+          }
+        }
+        continue;
+      }
       // win[u] = x[n-u]; prime lags 1..K-1 for n = n_first
 #pragma unroll
       for (int u = 1; u < K; ++u) {
@@ -152,6 +191,45 @@ __global__ void __launch_bounds__(FIR_THREADS) fir_sliding_kernel(FirGeom g, con
         }
       }
     } else {
+      if (VEC * sizeof(T) == 16 && TN % BATCH == 0 && n_last + K - 1 < g.N && n_first + TN <= g.N) {
+        // interior run: the K-1 halo rows and the last BATCH rows requested together
+        uint4 hr[K - 1], raw[BATCH];
+#pragma unroll
+        for (int u = 1; u < K; ++u) hr[u - 1] = __ldg(reinterpret_cast<const uint4*>(xb + (n_last + u) * g.sin));
+#pragma unroll
+        for (int t0 = TN - BATCH; t0 >= 0; t0 -= BATCH) {
+#pragma unroll
+          for (int t = 0; t < BATCH; ++t) raw[t] = __ldg(reinterpret_cast<const uint4*>(xb + (n_first + t0 + t) * g.sin));
+          if (t0 == TN - BATCH) {
+#pragma unroll
+            for (int u = 1; u < K; ++u) {
+              const T* e = reinterpret_cast<const T*>(&hr[u - 1]);
+#pragma unroll
+              for (int v = 0; v < VEC; ++v) win[u][v] = to_f32<T>(e[v]);
+            }
+          }
+#pragma unroll
+          for (int t = BATCH - 1; t >= 0; --t) {
+            const T* e = reinterpret_cast<const T*>(&raw[t]);
+#pragma unroll
+            for (int v = 0; v < VEC; ++v) win[0][v] = to_f32<T>(e[v]);
+            float acc[VEC];
+#pragma unroll
+            for (int v = 0; v < VEC; ++v) {
+              float a = win[0][v] * h[0];
+#pragma unroll
+              for (int u = 1; u < K; ++u) a = fmaf(win[u][v], h[u], a);
+              acc[v] = a;
+            }
+            st_vec<T, VEC>(yb + (n_first + t0 + t) * g.son, acc);
+#pragma unroll
+            for (int u = K - 1; u > 0; --u)
+#pragma unroll
+              for (int v = 0; v < VEC; ++v) win[u][v] = win[u - 1][v];
+          }
+        }
+        continue;
+      }
       // win[u] = gy[n+u]; prime lags 1..K-1 for n = n_last
 #pragma unroll
       for (int u = 1; u < K; ++u) {
@@ -286,15 +364,6 @@ __global__ void __launch_bounds__(FIR_THREADS) fir_dtaps_sliding_kernel(
     const T* gb = gy + b * sgb + cv * VEC;
     const int64_t n0 = chunk * TN;
     float win[K][VEC];  // win[u] = x[n-u]
-#pragma unroll
-    for (int u = 1; u < K; ++u) {
-      if (n0 - u >= 0) {
-        ld_vec<T, VEC>(xb + (n0 - u) * sxn, win[u]);
-      } else {
-#pragma unroll
-        for (int v = 0; v < VEC; ++v) win[u][v] = 0.f;
-      }
-    }
     const int rows = (int)min((int64_t)TN, N - n0);
     auto step = [&](const uint4& xr, const uint4& gr) {
       float gv[VEC];
@@ -314,17 +383,34 @@ __global__ void __launch_bounds__(FIR_THREADS) fir_dtaps_sliding_kernel(
 #pragma unroll
         for (int v = 0; v < VEC; ++v) win[u][v] = win[u - 1][v];
     };
-    if (rows == TN) {
-      // whole run inside the sequence: every row of x and gy requested before use
-      uint4 xr[TN], gr[TN];
+    if (rows == TN && n0 >= K - 1) {
+      // interior run: the halo rows of x and every row of x and gy requested before use
+      uint4 hr[K - 1], xr[TN], gr[TN];
+#pragma unroll
+      for (int u = 1; u < K; ++u) hr[u - 1] = __ldg(reinterpret_cast<const uint4*>(xb + (n0 - u) * sxn));
 #pragma unroll
       for (int t = 0; t < TN; ++t) {
         xr[t] = __ldg(reinterpret_cast<const uint4*>(xb + (n0 + t) * sxn));
         gr[t] = __ldg(reinterpret_cast<const uint4*>(gb + (n0 + t) * sgn));
       }
 #pragma unroll
+      for (int u = 1; u < K; ++u) {
+        const T* e = reinterpret_cast<const T*>(&hr[u - 1]);
+#pragma unroll
+        for (int v = 0; v < VEC; ++v) win[u][v] = to_f32<T>(e[v]);
+      }
+#pragma unroll
       for (int t = 0; t < TN; ++t) step(xr[t], gr[t]);
     } else {
+#pragma unroll
+      for (int u = 1; u < K; ++u) {
+        if (n0 - u >= 0) {
+          ld_vec<T, VEC>(xb + (n0 - u) * sxn, win[u]);
+        } else {
+#pragma unroll
+          for (int v = 0; v < VEC; ++v) win[u][v] = 0.f;
+        }
+      }
       for (int t = 0; t < rows; ++t)
         step(__ldg(reinterpret_cast<const uint4*>(xb + (n0 + t) * sxn)),
              __ldg(reinterpret_cast<const uint4*>(gb + (n0 + t) * sgn)));
