@@ -862,6 +862,7 @@ def bench_lm(args, dist_: Dist, dev) -> dict:
     res = {"tokens_per_s": round(dist_.world * B * N / (ms_step / 1e3), 1), "ms_per_step": round(ms_step, 3),
            "steps": args.lm_steps, "global_batch": B * dist_.world, "seq_len": N, "params": nparams,
            "loss": round(float(loss), 4), "model": "6-layer Pre-LN pn_fir_tau LM, D256 H4 MLP4x V33278, bf16 autocast, AdamW",
+           "step_ops": "library LayerNorm and one-pass head cross-entropy kernels, fused AdamW",
            "parallelism": f"ddp{dist_.world}" if dist_.world > 1 else "single GPU"}
     if not dist_.active:
         try:
@@ -876,11 +877,11 @@ def bench_lm_graph(args, dev, cfg, batches) -> dict:
     reference's exp4c technique for the launch-bound 6-layer stack): loss,
     backward, clip_grad_norm_ and AdamW(capturable=True) in one graph; each step
     copies its batch into the captured input. Single GPU (DDP stays eager)."""
-    from paper_01_anti_decoy_pnfirtau_b200.lm import PnFirLM, lm_loss
+    from paper_01_anti_decoy_pnfirtau_b200.lm import PnFirLM, lm_loss, make_optimizer
 
     torch.manual_seed(args.seed)
     model = PnFirLM(cfg).to(dev)
-    opt = torch.optim.AdamW(model.parameters(), lr=3e-4, betas=(0.9, 0.95), weight_decay=0.1, capturable=True)
+    opt = make_optimizer(model, capturable=True)
     static_idx = batches[0].clone()
 
     def step():

@@ -51,6 +51,7 @@ extern "C" {
 /* device-reported status codes (written to the caller's status word) */
 #define PNFT_DEV_OK 0
 #define PNFT_DEV_WAIT_TIMEOUT 1 /* a pipeline mbarrier wait hit its bound */
+#define PNFT_DEV_BAD_INDEX 2    /* pnft_lm_xent: a target outside [0, V) (not ignore_index) */
 
 /* silence modes of power_norm_peak_gate (src/pnfirtau_attention.py:108-116) */
 #define PNFT_SILENCE_PEAK 0
@@ -281,6 +282,94 @@ PNFT_API size_t pnft_flash_bwd_fir_workspace_size(int64_t B, int64_t H, int64_t 
  * arguments: 1 = sm_100a tcgen05/TMA kernels, 0 = generic SIMT kernels. */
 PNFT_API int pnft_flash_path(const void* q, const int64_t* sq, const void* k, const int64_t* sk,
                     const void* v, const int64_t* sv, int64_t D, int dtype, int flags);
+
+/* ---------------------------------------------------------------------------
+ * LM training step around the operator (the caller in the reference's
+ * language-model experiments, experiments/exp4_wikitext2_lm.py).
+ * ------------------------------------------------------------------------- */
+
+/* Next-token cross-entropy of the LM head, loss and logit gradient in one pass.
+ * logits: bf16 [M, ld] row-major; columns [V, ld) are padding and excluded.
+ * On return `logits` holds the gradient s * (softmax(row) - onehot(target)) for
+ * columns < V and 0 for the padding, with s = grad_scale * (*grad_scale_dev if
+ * grad_scale_dev is not NULL; a device float, e.g. 1/number of counted rows);
+ * row_loss[m] (fp32) = logsumexp(row m) - row m[target m]. Rows whose target
+ * equals ignore_index get loss 0 and gradient 0. A target outside [0, V) that is
+ * not ignore_index gives that row a NaN loss, no one-hot term, and sets the
+ * status word to PNFT_DEV_BAD_INDEX. targets: int64 [M].
+ * Replaces: nn.functional.cross_entropy(logits, targets) (mean reduction,
+ * ignore_index) and its autograd backward (experiments/exp4_wikitext2_lm.py:714-719). */
+PNFT_API int pnft_lm_xent(void* logits, int64_t ld, const int64_t* targets, int64_t ignore_index, float* row_loss,
+                 int64_t M, int64_t V, float grad_scale, const float* grad_scale_dev, int32_t* status,
+                 void* stream);
+
+/* LayerNorm over the last C elements of M rows (row strides sx / sy in
+ * elements, unit column stride): y = (x - mean) * rstd * gamma + beta with
+ * rstd = 1/sqrt(var + eps) (biased variance); gamma / beta may be NULL (1 / 0).
+ * Writes mean[M] and rstd[M] (fp32) for the backward. x and y are float32 or
+ * bfloat16 (x_dtype / y_dtype: PNFT_DTYPE_*), arithmetic in fp32.
+ * Replaces: nn.LayerNorm.forward in the Pre-LN blocks
+ * (experiments/exp4_wikitext2_lm.py:183-200, 203-247). */
+PNFT_API int pnft_layernorm_fwd(const void* x, int64_t sx, const float* gamma, const float* beta, float eps, void* y,
+                       int64_t sy, float* mean, float* rstd, int64_t M, int64_t C, int x_dtype, int y_dtype,
+                       void* stream);
+
+/* Backward of pnft_layernorm_fwd: dx (the type of x, row stride sdx) and, when
+ * dgamma / dbeta are not NULL, the parameter gradients (fp32 [C]) summed over
+ * the rows in a fixed order (bitwise reproducible). dy is float32 or bfloat16.
+ * workspace: pnft_layernorm_bwd_workspace_size(M, C) bytes when dgamma or
+ * dbeta is requested (else may be NULL).
+ * Replaces: the autograd backward of nn.LayerNorm (same call sites). */
+PNFT_API int pnft_layernorm_bwd(const void* dy, int64_t sdy, const void* x, int64_t sx, const float* gamma,
+                       const float* mean, const float* rstd, void* dx, int64_t sdx, float* dgamma, float* dbeta,
+                       void* workspace, size_t workspace_bytes, int64_t M, int64_t C, int dy_dtype, int x_dtype,
+                       void* stream);
+
+PNFT_API size_t pnft_layernorm_bwd_workspace_size(int64_t M, int64_t C);
+
+/* Residual add fused with the LayerNorm that follows it (the Pre-LN block's
+ * `x + branch(...)` then `ln(x)`): s = x + r in x's type (r: r_dtype, float32 or
+ * bfloat16; strides sr / ss), then y = LN(s) as pnft_layernorm_fwd. With r NULL
+ * this is pnft_layernorm_fwd (s unused).
+ * Replaces: the residual adds and nn.LayerNorm calls of the Pre-LN blocks
+ * (experiments/exp4_wikitext2_lm.py:183-200) and the final ln_f (:203-247). */
+PNFT_API int pnft_add_layernorm_fwd(const void* x, int64_t sx, const void* r, int64_t sr, int r_dtype, void* s,
+                           int64_t ss, const float* gamma, const float* beta, float eps, void* y, int64_t sy,
+                           float* mean, float* rstd, int64_t M, int64_t C, int x_dtype, int y_dtype, void* stream);
+
+/* Backward of pnft_add_layernorm_fwd. x is the LayerNorm input (s of the
+ * forward). dx (x's type, may be NULL) = gs + LN'(dy), with gs (x's type, may
+ * be NULL) the gradient already flowing into s from the residual path; dr (may
+ * be NULL, dr_dtype) receives the same values (the gradient of the residual
+ * branch r); at least one of dx / dr. dgamma / dbeta / workspace as
+ * pnft_layernorm_bwd.
+ * Replaces: the autograd backward of the same composition, including the
+ * residual gradient accumulation and the cast of the branch's gradient. */
+PNFT_API int pnft_add_layernorm_bwd(const void* dy, int64_t sdy, const void* gs, int64_t sgs, const void* x,
+                           int64_t sx, const float* gamma, const float* mean, const float* rstd, void* dx,
+                           int64_t sdx, void* dr, int64_t sdr, int dr_dtype, float* dgamma, float* dbeta,
+                           void* workspace, size_t workspace_bytes, int64_t M, int64_t C, int dy_dtype,
+                           int x_dtype, void* stream);
+
+/* Bias gradient of a Linear layer: out[c] = sum over the M rows of g[r, c]
+ * (fp32, summed in a fixed order for a given GPU). g: float32 or bfloat16,
+ * row stride sg. workspace: pnft_colsum_workspace_size(M, C) bytes.
+ * Replaces: grad_output.sum(0) in the backward of the MLP's nn.Linear layers
+ * (experiments/exp4_wikitext2_lm.py:183-200). */
+PNFT_API int pnft_colsum(const void* g, int64_t sg, float* out, void* workspace, size_t workspace_bytes, int64_t M,
+                int64_t C, int dtype, void* stream);
+
+PNFT_API size_t pnft_colsum_workspace_size(int64_t M, int64_t C);
+
+/* Backward of the MLP's exact (erf) GELU fused with the first Linear's bias
+ * gradient: da[r, c] = dh[r, c] * GELU'(a[r, c]) (written in `dtype`), and
+ * db[c] = sum over rows of da[r, c] as stored (fp32, fixed order). a is the
+ * GELU input. workspace: pnft_colsum_workspace_size(M, C) bytes.
+ * Replaces: nn.GELU's backward and grad_output.sum(0) of the first nn.Linear
+ * (same call sites). */
+PNFT_API int pnft_gelu_bwd_colsum(const void* dh, int64_t sdh, const void* a, int64_t sa, void* da, int64_t sda,
+                         float* db, void* workspace, size_t workspace_bytes, int64_t M, int64_t C, int dtype,
+                         void* stream);
 
 #ifdef __cplusplus
 }

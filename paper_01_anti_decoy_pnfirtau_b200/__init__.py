@@ -4,6 +4,7 @@ reference's Python API (mcfax-arch/paper_01_anti_decoy_pnfirtau, ``src/``).
 Exports the reference's eager names (src/__init__.py) plus the fused-op
 entry points of src/triton_pnfirtau.py.
 """
+from .lm_ops import LayerNorm, head_cross_entropy, layer_norm
 from .pnfirtau_attention import (
     PnFirConfig,
     PnFirTauFlashMHA,
@@ -54,4 +55,7 @@ __all__ = [
     "share_tau",
     "sharded_flash_pn_fir_tau_attention",
     "TauGradReducer",
+    "LayerNorm",
+    "layer_norm",
+    "head_cross_entropy",
 ]

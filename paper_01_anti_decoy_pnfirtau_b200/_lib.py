@@ -14,7 +14,7 @@ LIB_PATH = Path(__file__).resolve().parent / "libpnfirtau_b200.so"
 
 DTYPE_F32, DTYPE_BF16, DTYPE_F16 = 0, 1, 2
 OK, EINVAL, EUNSUPPORTED, ECUDA = 0, -1, -2, -3
-DEV_OK, DEV_WAIT_TIMEOUT = 0, 1
+DEV_OK, DEV_WAIT_TIMEOUT, DEV_BAD_INDEX = 0, 1, 2
 SILENCE_PEAK, SILENCE_MASS_RELU, SILENCE_MASS_POW = 0, 1, 2
 FLASH_FORCE_GENERIC, FLASH_DETERMINISTIC, FLASH_PREFER_SM100 = 0x1, 0x2, 0x4
 FLASH_TEST_STALL = 0x100  # test-only: the tcgen05 kernels take their timeout path
@@ -81,6 +81,28 @@ SIGNATURES: dict[str, tuple] = {
     ),
     "pnft_flash_bwd_fir_workspace_size": (c_size_t, [c_int64, c_int64, c_int64, c_int64, c_int]),
     "pnft_flash_path": (c_int, [_P, _I64x4, _P, _I64x4, _P, _I64x4, c_int64, c_int, c_int]),
+    "pnft_lm_xent": (c_int, [_P, c_int64, _P, c_int64, _P, c_int64, c_int64, c_float, _P, _P, _P]),
+    "pnft_layernorm_fwd": (
+        c_int, [_P, c_int64, _P, _P, c_float, _P, c_int64, _P, _P, c_int64, c_int64, c_int, c_int, _P]),
+    "pnft_layernorm_bwd": (
+        c_int,
+        [_P, c_int64, _P, c_int64, _P, _P, _P, _P, c_int64, _P, _P, _P, c_size_t, c_int64, c_int64, c_int, c_int, _P],
+    ),
+    "pnft_layernorm_bwd_workspace_size": (c_size_t, [c_int64, c_int64]),
+    "pnft_add_layernorm_fwd": (
+        c_int,
+        [_P, c_int64, _P, c_int64, c_int, _P, c_int64, _P, _P, c_float, _P, c_int64, _P, _P, c_int64, c_int64, c_int,
+         c_int, _P],
+    ),
+    "pnft_add_layernorm_bwd": (
+        c_int,
+        [_P, c_int64, _P, c_int64, _P, c_int64, _P, _P, _P, _P, c_int64, _P, c_int64, c_int, _P, _P, _P, c_size_t,
+         c_int64, c_int64, c_int, c_int, _P],
+    ),
+    "pnft_colsum": (c_int, [_P, c_int64, _P, _P, c_size_t, c_int64, c_int64, c_int, _P]),
+    "pnft_colsum_workspace_size": (c_size_t, [c_int64, c_int64]),
+    "pnft_gelu_bwd_colsum": (
+        c_int, [_P, c_int64, _P, c_int64, _P, c_int64, _P, _P, c_size_t, c_int64, c_int64, c_int, _P]),
 }
 
 _lock = threading.Lock()

@@ -5,6 +5,14 @@ experiments/exp4f_scaleout.py:260-271 for the D=256 / N=512 shape).
 
 Token embedding + learned positions -> n_layers x Block(x + attn(ln1 x);
 x + ffn(ln2 x)) -> ln_f -> head tied to the embedding.
+
+With ``fused_step_ops`` (default) the step's non-attention work runs on this
+library's kernels (lm_ops): each residual add fused with the LayerNorm after
+it (output written in the autocast dtype), the MLP's GELU backward fused with
+its bias gradients, and the head's loss and logit gradient in one pass over the
+logits. With ``fused_step_ops=False`` the blocks are nn.LayerNorm, nn.Linear,
+nn.GELU and F.cross_entropy. Parameters and state_dict keys are the same either
+way.
 """
 from __future__ import annotations
 
@@ -14,6 +22,7 @@ import torch
 import torch.nn as nn
 import torch.nn.functional as F
 
+from .lm_ops import LayerNorm, add_layer_norm, head_cross_entropy, mlp_gelu
 from .pnfirtau_attention import PnFirConfig, PnFirTauFlashMHA, PnFirTauMHA, PnFirTauTritonMHA
 
 _VARIANTS = {"pn_fir_tau": PnFirTauMHA, "pn_fir_tau_triton": PnFirTauTritonMHA, "pn_fir_tau_flash": PnFirTauFlashMHA}
@@ -37,11 +46,11 @@ class LMConfig:
 class Block(nn.Module):
     """exp4_wikitext2_lm.py:183-200."""
 
-    def __init__(self, d_model: int, attn: nn.Module, dropout: float, d_ff: int):
+    def __init__(self, d_model: int, attn: nn.Module, dropout: float, d_ff: int, norm=nn.LayerNorm):
         super().__init__()
-        self.ln1 = nn.LayerNorm(d_model)
+        self.ln1 = norm(d_model)
         self.attn = attn
-        self.ln2 = nn.LayerNorm(d_model)
+        self.ln2 = norm(d_model)
         self.ffn = nn.Sequential(nn.Linear(d_model, d_ff), nn.GELU(), nn.Linear(d_ff, d_model), nn.Dropout(dropout))
         self.drop = nn.Dropout(dropout)
 
@@ -53,35 +62,67 @@ class Block(nn.Module):
 class PnFirLM(nn.Module):
     """exp4_wikitext2_lm.py:203-247 (``WikiLM``) with a pn_fir_tau variant."""
 
-    def __init__(self, cfg: LMConfig = LMConfig(), variant: str = "pn_fir_tau_flash"):
+    def __init__(self, cfg: LMConfig = LMConfig(), variant: str = "pn_fir_tau_flash", fused_step_ops: bool = True):
         super().__init__()
         self.cfg = cfg
         self.variant = variant
+        self.fused_step_ops = fused_step_ops
+        norm = LayerNorm if fused_step_ops else nn.LayerNorm
         self.embed = nn.Embedding(cfg.vocab, cfg.d_model)
         self.pos = nn.Embedding(cfg.max_seq, cfg.d_model)
         self.drop = nn.Dropout(cfg.dropout)
         acfg = PnFirConfig(d_model=cfg.d_model, n_heads=cfg.n_heads, p=cfg.p, silence_gamma=cfg.silence_gamma,
                            tau_init=cfg.tau_init, fir_k=cfg.fir_k, dropout=cfg.dropout, causal_mask=True, bias=False)
         cls = _VARIANTS[variant]
-        self.blocks = nn.ModuleList(Block(cfg.d_model, cls(acfg), cfg.dropout, cfg.d_ff) for _ in range(cfg.n_layers))
-        self.ln_f = nn.LayerNorm(cfg.d_model)
+        self.blocks = nn.ModuleList(
+            Block(cfg.d_model, cls(acfg), cfg.dropout, cfg.d_ff, norm) for _ in range(cfg.n_layers))
+        self.ln_f = norm(cfg.d_model)
         self.head = nn.Linear(cfg.d_model, cfg.vocab, bias=False)
         self.head.weight = self.embed.weight
 
-    def forward(self, idx: torch.Tensor, for_loss: bool = False) -> torch.Tensor:
+    def forward(self, idx: torch.Tensor, for_loss: bool = False, targets: torch.Tensor | None = None) -> torch.Tensor:
         """Logits ``[B, N, vocab]``. ``for_loss``: the logits the next-token loss
         scores, ``[B, N-1, vocab_pad]`` for positions 0..N-2, with the vocabulary
         padded to a multiple of 64 (the padded logits are -inf, so they add nothing
         to a softmax): the head GEMM then has 16-byte aligned rows and no slice
-        copy of the logits is needed."""
+        copy of the logits is needed. ``targets`` (``[B, N-1]``, the ids of
+        positions 1..N-1): the mean next-token cross-entropy of positions 0..N-2
+        instead of logits (one kernel pass over the logits with
+        ``fused_step_ops``, else F.cross_entropy)."""
         B, N = idx.shape
         pos = torch.arange(N, device=idx.device).unsqueeze(0)
         h = self.drop(self.embed(idx) + self.pos(pos))
-        for blk in self.blocks:
-            h = blk(h)
-        h = self.ln_f(h)
+        h = self._trunk_fused(h) if self.fused_step_ops else self._trunk(h)
+        if targets is not None:
+            if self.fused_step_ops:
+                return head_cross_entropy(h[:, :-1], self.head.weight, targets)
+            logits = self._padded_logits(h)
+            return nn.functional.cross_entropy(logits.reshape(-1, logits.size(-1)), targets.reshape(-1))
         if not for_loss:
             return self.head(h)
+        return self._padded_logits(h)
+
+    def _trunk(self, h: torch.Tensor) -> torch.Tensor:
+        for blk in self.blocks:
+            h = blk(h)
+        return self.ln_f(h)
+
+    def _trunk_fused(self, h: torch.Tensor) -> torch.Tensor:
+        """The same blocks with every residual add fused into the LayerNorm
+        that follows it (the MLP's add into the next block's ln1, the last one
+        into ln_f) and the MLP on mlp_gelu; returns ln_f's output."""
+        blocks = list(self.blocks)
+        a = blocks[0].ln1(h)
+        for i, blk in enumerate(blocks):
+            att = blk.drop(blk.attn(a))
+            ln2 = blk.ln2
+            h, b = add_layer_norm(h, att, ln2.normalized_shape, ln2.weight, ln2.bias, ln2.eps)
+            f = blk.ffn[3](mlp_gelu(b, blk.ffn[0], blk.ffn[2]))
+            nxt = blocks[i + 1].ln1 if i + 1 < len(blocks) else self.ln_f
+            h, a = add_layer_norm(h, f, nxt.normalized_shape, nxt.weight, nxt.bias, nxt.eps)
+        return a
+
+    def _padded_logits(self, h: torch.Tensor) -> torch.Tensor:
         V = self.cfg.vocab
         Vp = (V + 63) // 64 * 64
         w = F.pad(self.head.weight, (0, 0, 0, Vp - V))
@@ -98,8 +139,7 @@ def lm_loss(model: nn.Module, idx: torch.Tensor) -> torch.Tensor:
     """Next-token cross-entropy of positions 0..N-2 scored on the shifted ids
     (exp4_wikitext2_lm.py:714-719, which slices the logits of all N positions:
     the same loss)."""
-    logits = model(idx, for_loss=True)
-    return nn.functional.cross_entropy(logits.reshape(-1, logits.size(-1)), idx[:, 1:].reshape(-1))
+    return model(idx, targets=idx[:, 1:])
 
 
 def train_step(model: nn.Module, opt: torch.optim.Optimizer, idx: torch.Tensor, clip: float = 1.0) -> torch.Tensor:
@@ -114,6 +154,10 @@ def train_step(model: nn.Module, opt: torch.optim.Optimizer, idx: torch.Tensor, 
     return loss.detach()
 
 
-def make_optimizer(model: nn.Module, lr: float = 3e-4) -> torch.optim.Optimizer:
-    """AdamW(betas=(0.9, 0.95), weight_decay=0.1) as exp4_wikitext2_lm.py:684-689."""
-    return torch.optim.AdamW(model.parameters(), lr=lr, betas=(0.9, 0.95), weight_decay=0.1)
+def make_optimizer(model: nn.Module, lr: float = 3e-4, capturable: bool = False) -> torch.optim.Optimizer:
+    """AdamW(betas=(0.9, 0.95), weight_decay=0.1) as exp4_wikitext2_lm.py:684-689,
+    with PyTorch's single-kernel (fused) implementation of the same update when
+    the parameters are on a CUDA device."""
+    fused = all(p.is_cuda for p in model.parameters())
+    return torch.optim.AdamW(model.parameters(), lr=lr, betas=(0.9, 0.95), weight_decay=0.1, fused=fused,
+                             capturable=capturable)

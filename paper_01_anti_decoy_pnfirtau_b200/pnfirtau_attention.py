@@ -25,7 +25,8 @@ import torch.nn.functional as F
 
 from .pnfirtau_ops import (
     _flash_bnhd,
-    _flash_fir_bnhd,
+    _flash_fir_qkv,
+    _qkv_views,
     fused_fir_applies,
     pn_rows,
     triton_causal_fir,
@@ -197,12 +198,11 @@ class PnFirTauFlashMHA(PnFirTauMHA):
         B, N, _ = x.shape
         scale = 1.0 / math.sqrt(self.head_dim)
         if self.fuse_fir:
-            H, hd = self.n_heads, self.head_dim
-            q_raw, k_raw, v_raw = self.qkv(x).chunk(3, dim=-1)
-            q, k, v = (t.view(B, N, H, hd).transpose(1, 2) for t in (q_raw, k_raw, v_raw))
-            if fused_fir_applies(q, k, v, cfg.fir_k):
-                out = _flash_fir_bnhd(q, k, v, self.score_tau, self.fir_taps, scale, cfg.silence_gamma,
-                                      cfg.causal_mask)
+            H = self.n_heads
+            qkv = self.qkv(x)
+            if fused_fir_applies(*_qkv_views(qkv, H), cfg.fir_k):
+                out = _flash_fir_qkv(qkv, H, self.score_tau, self.fir_taps, scale, cfg.silence_gamma,
+                                     cfg.causal_mask)
                 return self.out(out.transpose(1, 2).reshape(B, N, -1))
         q, k, v = self._qkv_heads(x)
         out = _flash_bnhd(q, k, v, self.score_tau, scale, cfg.silence_gamma, cfg.causal_mask)

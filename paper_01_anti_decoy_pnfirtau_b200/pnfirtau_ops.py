@@ -117,9 +117,15 @@ def _status_ptr(dev: torch.device) -> int:
     return _status_entry(dev).ptr
 
 
+_DEV_MEANING = {
+    _lib.DEV_WAIT_TIMEOUT: "pipeline wait timed out; the outputs of that call are invalid",
+    _lib.DEV_BAD_INDEX: "a cross-entropy target outside [0, vocab) that is not ignore_index; that row's loss is NaN",
+}
+
+
 def _raise(v: int, dev, when: str) -> None:
-    raise RuntimeError(f"pn_fir_tau kernel on {dev} reported device status {v} {when} (pipeline wait timed out; "
-                       "the outputs of that call are invalid)")
+    what = _DEV_MEANING.get(v, "unknown device status")
+    raise RuntimeError(f"pn_fir_tau kernel on {dev} reported device status {v} {when} ({what})")
 
 
 def _check_pending(dev: torch.device) -> None:
@@ -474,6 +480,103 @@ def _fir_view(t: torch.Tensor):
                        "adjacent")
 
 
+def _fir_forward(q, k, v, score_tau, taps, scale, gamma, causal_mask, out_layout, fused_forward, deterministic,
+                 needs_grad: bool):
+    """Forward of flash attention on k~ = causal_fir(k, taps) (see _FlashFirFn).
+    Returns (out, saved tensors, saved arguments) for _fir_backward."""
+    dev = _require_cuda("flash_pn_fir_tau_attention_fir", q, k, v, score_tau, taps)
+    _check_pending(dev)
+    if not (q.dtype == k.dtype == v.dtype):
+        raise RuntimeError(f"flash_pn_fir_tau_attention_fir: q/k/v dtypes differ ({q.dtype}, {k.dtype}, {v.dtype})")
+    B, H, N, D = q.shape
+    if k.shape != q.shape or v.shape != q.shape:
+        raise RuntimeError(f"flash_pn_fir_tau_attention_fir: q {tuple(q.shape)}, k {tuple(k.shape)}, "
+                           f"v {tuple(v.shape)} must match")
+    if taps.numel() != _lib.FIR_FUSED_TAPS:
+        raise RuntimeError(f"flash_pn_fir_tau_attention_fir: {taps.numel()} taps; the fused filter has "
+                           f"{_lib.FIR_FUSED_TAPS}")
+    if out_layout == "bnhd":
+        out = torch.empty((B, N, H, D), device=dev, dtype=q.dtype).transpose(1, 2)
+    else:
+        out = torch.empty((B, H, N, D), device=dev, dtype=q.dtype)
+    stats = torch.empty((2, B, H, N), device=dev, dtype=torch.float32)
+    nmax = torch.empty((2, B, H, N), device=dev, dtype=torch.int32)
+    tau_f32 = score_tau.detach().to(torch.float32).contiguous()
+    taps_f32 = taps.detach().to(torch.float32).contiguous()
+    has_gamma, gamma_val = _gamma_args(gamma)
+    flags = _flash_flags(deterministic)
+    out32 = torch.empty((B, H, N, D), device=dev, dtype=torch.float32) if needs_grad else None
+    L = _lib.lib()
+    if fused_forward:
+        _lib.check(
+            L.pnft_flash_fwd_fir(_ptr(q), _lib.i64x4(q.stride()), _ptr(k), _lib.i64x4(k.stride()),
+                                 _ptr(taps_f32), taps_f32.numel(), _ptr(v), _lib.i64x4(v.stride()),
+                                 _ptr(tau_f32), _ptr(out), _lib.i64x4(out.stride()), _ptr(out32),
+                                 _ptr(stats[0]), _ptr(stats[1]), _ptr(nmax[0]), _ptr(nmax[1]), B, H, N, D,
+                                 float(scale), gamma_val, has_gamma, int(bool(causal_mask)), _dtype_code(q),
+                                 flags, None, _status_ptr(dev), _stream(dev)),
+            "pnft_flash_fwd_fir",
+        )
+    else:
+        (sxb, sxn, sxc), Bf, C = _fir_view(k)
+        # k~ in the layout of k's FIR view, contiguous
+        if C == H * D and (H == 1 or k.stride(1) == D):
+            kt = torch.empty((B, N, H, D), device=dev, dtype=k.dtype).transpose(1, 2)
+            syb, syn = N * H * D, H * D
+        else:
+            kt = torch.empty((B, H, N, D), device=dev, dtype=k.dtype)
+            syb, syn = N * D, D
+        _lib.check(L.pnft_fir_fwd(_ptr(k), sxb, sxn, sxc, _ptr(taps_f32), taps_f32.numel(), _ptr(kt), syb, syn,
+                                  1, Bf, N, C, _dtype_code(k), _stream(dev)), "pnft_fir_fwd")
+        if L.pnft_flash_path(_ptr(q), _lib.i64x4(q.stride()), _ptr(kt), _lib.i64x4(kt.stride()), _ptr(v),
+                             _lib.i64x4(v.stride()), D, _dtype_code(q), flags) != 1:
+            raise RuntimeError("flash_pn_fir_tau_attention_fir: the sm_100a kernels do not serve these inputs")
+        _lib.check(
+            L.pnft_flash_fwd(_ptr(q), _lib.i64x4(q.stride()), _ptr(kt), _lib.i64x4(kt.stride()), _ptr(v),
+                             _lib.i64x4(v.stride()), _ptr(tau_f32), _ptr(out), _lib.i64x4(out.stride()),
+                             _ptr(out32), _ptr(stats[0]), _ptr(stats[1]), _ptr(nmax[0]), _ptr(nmax[1]), B, H, N,
+                             D, float(scale), gamma_val, has_gamma, int(bool(causal_mask)), _dtype_code(q),
+                             flags, None, _status_ptr(dev), _stream(dev)),
+            "pnft_flash_fwd",
+        )
+    saved = (tau_f32, taps_f32, out, out32, stats, nmax)
+    args = (float(scale), gamma_val, has_gamma, int(bool(causal_mask)), flags)
+    return out, saved, args
+
+
+def _fir_backward(q, k, v, saved, args, grad_out, dq, dk, dv, want_dtaps: bool):
+    """Backward of _fir_forward into the caller's dq / dk / dv (any strides the
+    kernels accept: dk with k's adjacent axes). Returns (dtau fp32 scalar,
+    dtaps fp32 or None)."""
+    tau_f32, taps_f32, out, out32, stats, nmax = saved
+    scale, gamma_val, has_gamma, causal, flags = args
+    flags |= _TEST_FLAGS
+    B, H, N, D = q.shape
+    dev = q.device
+    _check_pending(dev)
+    if grad_out.dtype != q.dtype:
+        grad_out = grad_out.to(q.dtype)
+    if grad_out.stride(-1) != 1 or any(s % 8 for s in grad_out.stride()[:3]):
+        grad_out = grad_out.contiguous()
+    dtau = torch.empty((), device=dev, dtype=torch.float32)
+    dtaps = torch.empty(taps_f32.numel(), device=dev, dtype=torch.float32) if want_dtaps else None
+    L = _lib.lib()
+    nbytes = L.pnft_flash_bwd_fir_workspace_size(B, H, N, D, flags)
+    ws = torch.empty(max(nbytes, 1), device=dev, dtype=torch.uint8)
+    _lib.check(
+        L.pnft_flash_bwd_fir(_ptr(q), _lib.i64x4(q.stride()), _ptr(k), _lib.i64x4(k.stride()), _ptr(taps_f32),
+                             taps_f32.numel(), _ptr(v), _lib.i64x4(v.stride()), _ptr(tau_f32), _ptr(out),
+                             _lib.i64x4(out.stride()), _ptr(out32), _ptr(grad_out),
+                             _lib.i64x4(grad_out.stride()), _ptr(stats[0]), _ptr(stats[1]), _ptr(nmax[0]),
+                             _ptr(nmax[1]), _ptr(dq), _lib.i64x4(dq.stride()), _ptr(dk),
+                             _lib.i64x4(dk.stride()), _ptr(dv), _lib.i64x4(dv.stride()), _ptr(dtau),
+                             _ptr(dtaps), _ptr(ws), ws.numel(), B, H, N, D, scale, gamma_val, has_gamma, causal,
+                             _dtype_code(q), flags, _status_ptr(dev), _stream(dev)),
+        "pnft_flash_bwd_fir",
+    )
+    return dtau, dtaps
+
+
 class _FlashFirFn(torch.autograd.Function):
     """Flash attention on the causally filtered keys k~ = causal_fir(k, taps), k
     the raw key projection. Backward: pnft_flash_bwd_fir, which filters its K
@@ -487,80 +590,19 @@ class _FlashFirFn(torch.autograd.Function):
     @staticmethod
     def forward(ctx, q, k, v, score_tau, taps, scale, gamma, causal_mask, out_layout, fused_forward=False,
                 deterministic=None):
-        dev = _require_cuda("flash_pn_fir_tau_attention_fir", q, k, v, score_tau, taps)
-        _check_pending(dev)
-        if not (q.dtype == k.dtype == v.dtype):
-            raise RuntimeError(f"flash_pn_fir_tau_attention_fir: q/k/v dtypes differ ({q.dtype}, {k.dtype}, {v.dtype})")
-        B, H, N, D = q.shape
-        if k.shape != q.shape or v.shape != q.shape:
-            raise RuntimeError(f"flash_pn_fir_tau_attention_fir: q {tuple(q.shape)}, k {tuple(k.shape)}, "
-                               f"v {tuple(v.shape)} must match")
-        if taps.numel() != _lib.FIR_FUSED_TAPS:
-            raise RuntimeError(f"flash_pn_fir_tau_attention_fir: {taps.numel()} taps; the fused filter has "
-                               f"{_lib.FIR_FUSED_TAPS}")
-        if out_layout == "bnhd":
-            out = torch.empty((B, N, H, D), device=dev, dtype=q.dtype).transpose(1, 2)
-        else:
-            out = torch.empty((B, H, N, D), device=dev, dtype=q.dtype)
-        stats = torch.empty((2, B, H, N), device=dev, dtype=torch.float32)
-        nmax = torch.empty((2, B, H, N), device=dev, dtype=torch.int32)
-        tau_f32 = score_tau.detach().to(torch.float32).contiguous()
-        taps_f32 = taps.detach().to(torch.float32).contiguous()
-        has_gamma, gamma_val = _gamma_args(gamma)
-        flags = _flash_flags(deterministic)
-        needs_grad = any(ctx.needs_input_grad[:5])
-        out32 = torch.empty((B, H, N, D), device=dev, dtype=torch.float32) if needs_grad else None
-        L = _lib.lib()
-        if fused_forward:
-            _lib.check(
-                L.pnft_flash_fwd_fir(_ptr(q), _lib.i64x4(q.stride()), _ptr(k), _lib.i64x4(k.stride()),
-                                     _ptr(taps_f32), taps_f32.numel(), _ptr(v), _lib.i64x4(v.stride()),
-                                     _ptr(tau_f32), _ptr(out), _lib.i64x4(out.stride()), _ptr(out32),
-                                     _ptr(stats[0]), _ptr(stats[1]), _ptr(nmax[0]), _ptr(nmax[1]), B, H, N, D,
-                                     float(scale), gamma_val, has_gamma, int(bool(causal_mask)), _dtype_code(q),
-                                     flags, None, _status_ptr(dev), _stream(dev)),
-                "pnft_flash_fwd_fir",
-            )
-        else:
-            (sxb, sxn, sxc), Bf, C = _fir_view(k)
-            # k~ in the layout of k's FIR view, contiguous
-            if C == H * D and (H == 1 or k.stride(1) == D):
-                kt = torch.empty((B, N, H, D), device=dev, dtype=k.dtype).transpose(1, 2)
-                syb, syn = N * H * D, H * D
-            else:
-                kt = torch.empty((B, H, N, D), device=dev, dtype=k.dtype)
-                syb, syn = N * D, D
-            _lib.check(L.pnft_fir_fwd(_ptr(k), sxb, sxn, sxc, _ptr(taps_f32), taps_f32.numel(), _ptr(kt), syb, syn,
-                                      1, Bf, N, C, _dtype_code(k), _stream(dev)), "pnft_fir_fwd")
-            if L.pnft_flash_path(_ptr(q), _lib.i64x4(q.stride()), _ptr(kt), _lib.i64x4(kt.stride()), _ptr(v),
-                                 _lib.i64x4(v.stride()), D, _dtype_code(q), flags) != 1:
-                raise RuntimeError("flash_pn_fir_tau_attention_fir: the sm_100a kernels do not serve these inputs")
-            _lib.check(
-                L.pnft_flash_fwd(_ptr(q), _lib.i64x4(q.stride()), _ptr(kt), _lib.i64x4(kt.stride()), _ptr(v),
-                                 _lib.i64x4(v.stride()), _ptr(tau_f32), _ptr(out), _lib.i64x4(out.stride()),
-                                 _ptr(out32), _ptr(stats[0]), _ptr(stats[1]), _ptr(nmax[0]), _ptr(nmax[1]), B, H, N,
-                                 D, float(scale), gamma_val, has_gamma, int(bool(causal_mask)), _dtype_code(q),
-                                 flags, None, _status_ptr(dev), _stream(dev)),
-                "pnft_flash_fwd",
-            )
-        ctx.save_for_backward(q, k, v, tau_f32, taps_f32, out, out32, stats, nmax)
-        ctx.args = (float(scale), gamma_val, has_gamma, int(bool(causal_mask)), flags)
+        out, saved, args = _fir_forward(q, k, v, score_tau, taps, scale, gamma, causal_mask, out_layout,
+                                        fused_forward, deterministic, any(ctx.needs_input_grad[:5]))
+        ctx.save_for_backward(q, k, v, *saved)
+        ctx.args = args
         ctx.tau_dtype, ctx.tau_shape = score_tau.dtype, score_tau.shape
         ctx.taps_dtype, ctx.taps_shape = taps.dtype, taps.shape
         return out
 
     @staticmethod
     def backward(ctx, grad_out):
-        q, k, v, tau_f32, taps_f32, out, out32, stats, nmax = ctx.saved_tensors
-        scale, gamma_val, has_gamma, causal, flags = ctx.args
-        flags |= _TEST_FLAGS
+        q, k, v, *saved = ctx.saved_tensors
         B, H, N, D = q.shape
         dev = q.device
-        _check_pending(dev)
-        if grad_out.dtype != q.dtype:
-            grad_out = grad_out.to(q.dtype)
-        if grad_out.stride(-1) != 1 or any(s % 8 for s in grad_out.stride()[:3]):
-            grad_out = grad_out.contiguous()
         dq = torch.empty((B, H, N, D), device=dev, dtype=q.dtype)
         # dk with k's adjacent axes: (h, d) for the module's [B,N,H*D] view, else (b, h)
         if H == 1 or k.stride(1) == D:
@@ -568,25 +610,46 @@ class _FlashFirFn(torch.autograd.Function):
         else:
             dk = torch.empty((B, H, N, D), device=dev, dtype=k.dtype)
         dv = torch.empty((B, H, N, D), device=dev, dtype=v.dtype)
-        dtau = torch.empty((), device=dev, dtype=torch.float32)
-        dtaps = torch.empty(taps_f32.numel(), device=dev, dtype=torch.float32) if ctx.needs_input_grad[4] else None
-        L = _lib.lib()
-        nbytes = L.pnft_flash_bwd_fir_workspace_size(B, H, N, D, flags)
-        ws = torch.empty(max(nbytes, 1), device=dev, dtype=torch.uint8)
-        _lib.check(
-            L.pnft_flash_bwd_fir(_ptr(q), _lib.i64x4(q.stride()), _ptr(k), _lib.i64x4(k.stride()), _ptr(taps_f32),
-                                 taps_f32.numel(), _ptr(v), _lib.i64x4(v.stride()), _ptr(tau_f32), _ptr(out),
-                                 _lib.i64x4(out.stride()), _ptr(out32), _ptr(grad_out),
-                                 _lib.i64x4(grad_out.stride()), _ptr(stats[0]), _ptr(stats[1]), _ptr(nmax[0]),
-                                 _ptr(nmax[1]), _ptr(dq), _lib.i64x4(dq.stride()), _ptr(dk),
-                                 _lib.i64x4(dk.stride()), _ptr(dv), _lib.i64x4(dv.stride()), _ptr(dtau),
-                                 _ptr(dtaps), _ptr(ws), ws.numel(), B, H, N, D, scale, gamma_val, has_gamma, causal,
-                                 _dtype_code(q), flags, _status_ptr(dev), _stream(dev)),
-            "pnft_flash_bwd_fir",
-        )
+        dtau, dtaps = _fir_backward(q, k, v, saved, ctx.args, grad_out, dq, dk, dv, ctx.needs_input_grad[4])
         grad_tau = dtau.to(ctx.tau_dtype).reshape(ctx.tau_shape)
         grad_taps = dtaps.to(ctx.taps_dtype).reshape(ctx.taps_shape) if dtaps is not None else None
         return dq, dk, dv, grad_tau, grad_taps, None, None, None, None, None, None
+
+
+def _qkv_views(qkv: torch.Tensor, H: int):
+    """q, k, v as [B,H,N,D] views of the three column blocks of qkv [B,N,3*H*D]."""
+    B, N, C3 = qkv.shape
+    D = C3 // (3 * H)
+    return tuple(t.view(B, N, H, D).transpose(1, 2) for t in qkv.split(H * D, dim=-1))
+
+
+class _FlashFirQkvFn(torch.autograd.Function):
+    """_FlashFirFn on the module's fused projection qkv [B,N,3*H*D] (q, k, v its
+    column blocks). The backward writes dq, dk and dv straight into the column
+    blocks of one d(qkv) tensor, so no gradient concatenation follows it (the
+    backward of ``qkv.chunk(3)``); the result is stored as [B,N,H,D]."""
+
+    @staticmethod
+    def forward(ctx, qkv, H: int, score_tau, taps, scale, gamma, causal_mask, deterministic=None):
+        q, k, v = _qkv_views(qkv, H)
+        out, saved, args = _fir_forward(q, k, v, score_tau, taps, scale, gamma, causal_mask, "bnhd", False,
+                                        deterministic, any(ctx.needs_input_grad[:4]))
+        ctx.save_for_backward(qkv, *saved)
+        ctx.H, ctx.args = H, args
+        ctx.tau_dtype, ctx.tau_shape = score_tau.dtype, score_tau.shape
+        ctx.taps_dtype, ctx.taps_shape = taps.dtype, taps.shape
+        return out
+
+    @staticmethod
+    def backward(ctx, grad_out):
+        qkv, *saved = ctx.saved_tensors
+        q, k, v = _qkv_views(qkv, ctx.H)
+        dqkv = torch.empty_like(qkv, memory_format=torch.contiguous_format)
+        dq, dk, dv = _qkv_views(dqkv, ctx.H)
+        dtau, dtaps = _fir_backward(q, k, v, saved, ctx.args, grad_out, dq, dk, dv, ctx.needs_input_grad[3])
+        grad_tau = dtau.to(ctx.tau_dtype).reshape(ctx.tau_shape)
+        grad_taps = dtaps.to(ctx.taps_dtype).reshape(ctx.taps_shape) if dtaps is not None else None
+        return dqkv, None, grad_tau, grad_taps, None, None, None, None
 
 
 def flash_pn_fir_tau_attention_fir(
@@ -655,9 +718,10 @@ def _flash_bnhd(q, k_tilde, v, score_tau, scale, gamma, causal_mask):
     return _FlashPnFirTauFn.apply(q, k_tilde, v, score_tau, scale, gamma, causal_mask, "bnhd")
 
 
-def _flash_fir_bnhd(q, k, v, score_tau, taps, scale, gamma, causal_mask):
-    """flash_pn_fir_tau_attention_fir with the result stored as [B,N,H,D]."""
-    return _FlashFirFn.apply(q, k, v, score_tau, taps, scale, gamma, causal_mask, "bnhd")
+def _flash_fir_qkv(qkv, H, score_tau, taps, scale, gamma, causal_mask):
+    """flash_pn_fir_tau_attention_fir on the column blocks of qkv [B,N,3*H*D];
+    the result's storage is [B,N,H,D]; one gradient tensor for qkv."""
+    return _FlashFirQkvFn.apply(qkv, H, score_tau, taps, scale, gamma, causal_mask)
 
 
 def fused_fir_applies(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, fir_k: int) -> bool:

@@ -1,0 +1,287 @@
+"""The LM-step kernels (csrc/lm_step.cu via lm_ops) against PyTorch fp32:
+the head's one-pass cross-entropy (loss and logit gradient, padding columns,
+ignore_index, a bad target reported through the status word, the staged and the
+two global-memory variants), the fused head + cross-entropy autograd function,
+LayerNorm forward/backward (vector and scalar paths, bf16 and fp32, affine or
+not, bitwise-reproducible parameter gradients), and the config-4 LM with the
+fused step ops against the same LM with nn.LayerNorm and F.cross_entropy.
+
+Reference composition: experiments/exp4_wikitext2_lm.py:183-259 (Pre-LN
+blocks, tied head) and :714-719 (F.cross_entropy on the logits)."""
+import pytest
+import torch
+import torch.nn.functional as F
+
+from conftest import rel_l2
+from paper_01_anti_decoy_pnfirtau_b200 import _lib
+from paper_01_anti_decoy_pnfirtau_b200.lm import LMConfig, PnFirLM, lm_loss, make_optimizer, train_step
+from paper_01_anti_decoy_pnfirtau_b200.lm_ops import LayerNorm, add_layer_norm, head_cross_entropy, layer_norm, mlp_gelu
+from paper_01_anti_decoy_pnfirtau_b200.pnfirtau_ops import _status_ptr, check_device_status
+
+pytestmark = pytest.mark.gpu
+
+
+def _xent_call(logits, V, t, ignore=-100, scale=1.0):
+    M, ld = logits.shape
+    loss = torch.empty(M, device=logits.device)
+    rc = _lib.lib().pnft_lm_xent(logits.data_ptr(), ld, t.data_ptr(), ignore, loss.data_ptr(), M, V, scale, None,
+                                 _status_ptr(logits.device), torch.cuda.current_stream().cuda_stream)
+    _lib.check(rc, "pnft_lm_xent")
+    return loss
+
+
+# (M, V, ld): staged rows (ld % 8 == 0; more rows per CTA than ring stages, so
+# stages are refilled and their phases wrap), a scalar global row (odd ld), a
+# row too long to stage twice in shared memory (vector global path)
+XENT_CASES = {"staged_lm_vocab": (1000, 33278, 33280), "staged_small": (2000, 1000, 1024),
+              "global_scalar": (19, 517, 519), "global_vec": (5, 70000, 70008)}
+
+
+@pytest.mark.parametrize("case", sorted(XENT_CASES))
+def test_xent_kernel_against_fp32(cuda, case):
+    M, V, ld = XENT_CASES[case]
+    g = torch.Generator(device=cuda).manual_seed(M + V)
+    x = (torch.randn(M, ld, device=cuda, generator=g) * 3).to(torch.bfloat16)
+    t = torch.randint(0, V, (M,), device=cuda, generator=g)
+    t[::7] = -100  # ignored rows
+    t[1] = V - 1   # the last valid column
+    ref_x = x[:, :V].float().requires_grad_(True)
+    per_row = F.cross_entropy(ref_x, t, reduction="none")
+    counted = (t != -100).sum()
+    per_row.sum().backward()
+    buf = x.clone()
+    loss = _xent_call(buf, V, t, scale=1.0)
+    torch.cuda.synchronize()
+    check_device_status(cuda)
+    assert torch.allclose(loss, per_row.detach(), rtol=2e-6, atol=2e-5), (loss - per_row).abs().max()
+    assert float((loss.sum() / counted - per_row.detach().sum() / counted).abs()) < 1e-5
+    grad = buf.float()
+    assert torch.all(grad[:, V:] == 0)
+    assert torch.all(grad[t == -100] == 0)
+    # one bf16 rounding (up to 2^-8 relative) of a value within 2^-11 of the exact
+    # (softmax - onehot): the kernel keeps exp(x - max) as fp16 between its passes
+    assert rel_l2(grad[:, :V], ref_x.grad) < 4e-3
+    err = (grad[:, :V] - ref_x.grad).abs()
+    bound = ref_x.grad.abs() * (2 ** -8 + 2 ** -10) + 1e-7
+    assert torch.all(err <= bound), float((err / bound).max())
+
+
+def test_xent_bad_target_sets_status(cuda):
+    x = torch.randn(4, 64, device=cuda).to(torch.bfloat16)
+    t = torch.tensor([1, 64, 3, -5], device=cuda)  # 64 and -5 are outside [0, 64) and not ignore_index
+    loss = _xent_call(x.clone(), 64, t)
+    with pytest.raises(RuntimeError, match="outside"):
+        check_device_status(cuda)
+    assert torch.isnan(loss[1]) and torch.isnan(loss[3]) and torch.isfinite(loss[0]) and torch.isfinite(loss[2])
+    check_device_status(cuda)  # the word was cleared
+
+
+@pytest.mark.parametrize("V", [33278, 1000])
+def test_head_cross_entropy_matches_autocast_composition(cuda, V):
+    g = torch.Generator(device=cuda).manual_seed(V)
+    h = torch.randn(4, 63, 256, device=cuda, generator=g).requires_grad_(True)
+    w = (torch.randn(V, 256, device=cuda, generator=g) * 0.05).requires_grad_(True)
+    t = torch.randint(0, V, (4, 63), device=cuda, generator=g)
+    t[0, :5] = -100
+    loss = head_cross_entropy(h, w, t)
+    loss.backward()
+    check_device_status(cuda)
+    # reference: the autocast head GEMM (bf16 operands, fp32 accumulation) and an fp32 cross-entropy
+    hr = h.detach().clone().requires_grad_(True)
+    wr = w.detach().clone().requires_grad_(True)
+    logits = hr.to(torch.bfloat16).float() @ wr.to(torch.bfloat16).float().t()
+    ref = F.cross_entropy(logits.reshape(-1, V), t.reshape(-1))
+    ref.backward()
+    assert abs(float(loss) - float(ref)) < 2e-3 * abs(float(ref)), (float(loss), float(ref))
+    assert rel_l2(h.grad, hr.grad) < 1e-2, rel_l2(h.grad, hr.grad)
+    assert rel_l2(w.grad, wr.grad) < 1e-2, rel_l2(w.grad, wr.grad)
+
+
+LN_CASES = {
+    # name: (M, C, x dtype, y dtype, affine)
+    "lm_c256_bf16_out": (16384, 256, torch.float32, torch.bfloat16, True),
+    "c256_f32": (1000, 256, torch.float32, torch.float32, True),
+    "c96_partial_vector": (333, 96, torch.float32, torch.float32, True),
+    "c384": (100, 384, torch.bfloat16, torch.float32, True),
+    "c512_no_affine": (64, 512, torch.float32, torch.float32, False),
+    "c1000_scalar": (77, 1000, torch.float32, torch.bfloat16, True),
+    "c6_scalar": (50, 6, torch.float32, torch.float32, True),
+}
+
+
+@pytest.mark.parametrize("case", sorted(LN_CASES))
+def test_layer_norm_against_fp32(cuda, case):
+    M, C, xdt, ydt, affine = LN_CASES[case]
+    g = torch.Generator(device=cuda).manual_seed(M * 7 + C)
+    x = (torch.randn(M, C, device=cuda, generator=g) * 2 + 0.5).to(xdt).requires_grad_(True)
+    w = (1 + 0.1 * torch.randn(C, device=cuda, generator=g)).requires_grad_(affine) if affine else None
+    b = (0.1 * torch.randn(C, device=cuda, generator=g)).requires_grad_(affine) if affine else None
+    gy = torch.randn(M, C, device=cuda, generator=g).to(ydt)
+    y = layer_norm(x, (C,), w, b, 1e-5, out_dtype=ydt)
+    assert y.dtype == ydt
+    y.backward(gy)
+    xr = x.detach().float().requires_grad_(True)
+    wr = w.detach().clone().requires_grad_(True) if affine else None
+    br = b.detach().clone().requires_grad_(True) if affine else None
+    yr = F.layer_norm(xr, (C,), wr, br, 1e-5)
+    yr.backward(gy.float())
+    # fp32: rounding of the statistics; bf16: at most one bf16 ulp (2^-7 relative) from the rounded reference
+    rtol, atol = (1e-6, 1e-5) if ydt == torch.float32 else (2 ** -7, 1e-4)
+    assert torch.allclose(y.float(), yr.detach().to(ydt).float(), rtol=rtol, atol=atol), (
+        (y.float() - yr).abs().max())
+    tol = 1e-5 if xdt == torch.float32 else 8e-3
+    assert rel_l2(x.grad, xr.grad) < tol, rel_l2(x.grad, xr.grad)
+    if affine:
+        assert rel_l2(w.grad, wr.grad) < 1e-5, rel_l2(w.grad, wr.grad)
+        assert rel_l2(b.grad, br.grad) < 1e-5, rel_l2(b.grad, br.grad)
+        # the parameter gradients are reduced in a fixed order: bitwise equal on a rerun
+        dw1, db1 = w.grad.clone(), b.grad.clone()
+        w.grad = b.grad = None
+        x.grad = None
+        layer_norm(x, (C,), w, b, 1e-5, out_dtype=ydt).backward(gy)
+        assert torch.equal(dw1, w.grad) and torch.equal(db1, b.grad)
+
+
+def test_layernorm_module_is_nn_layernorm(cuda):
+    ln = LayerNorm(256).to(cuda)
+    ref = torch.nn.LayerNorm(256).to(cuda)
+    ref.load_state_dict(ln.state_dict())
+    x = torch.randn(2, 8, 256, device=cuda)
+    assert torch.allclose(ln(x), ref(x), rtol=1e-6, atol=1e-6)
+    with torch.autocast("cuda", dtype=torch.bfloat16):
+        y = ln(x)
+        yr = ref(x)
+    assert y.dtype == torch.bfloat16 and yr.dtype == torch.float32
+    assert torch.equal(y, yr.to(torch.bfloat16)) or rel_l2(y, yr) < 2 ** -8
+
+
+@pytest.mark.parametrize("C", [256, 100])
+def test_add_layer_norm_against_fp32(cuda, C):
+    """s = x + r (fp32 + bf16 branch, as in the LM's residual stream) and LN(s) in
+    one kernel; gradients of x (with the residual path's own gradient of s
+    added), r (bf16), weight, bias. C = 100 takes the scalar path."""
+    g = torch.Generator(device=cuda).manual_seed(C)
+    M = 3000
+    x = torch.randn(M, C, device=cuda, generator=g).requires_grad_(True)
+    r = torch.randn(M, C, device=cuda, generator=g).to(torch.bfloat16).requires_grad_(True)
+    w = (1 + 0.1 * torch.randn(C, device=cuda, generator=g)).requires_grad_(True)
+    b = (0.1 * torch.randn(C, device=cuda, generator=g)).requires_grad_(True)
+    gs = torch.randn(M, C, device=cuda, generator=g)
+    gy = torch.randn(M, C, device=cuda, generator=g).to(torch.bfloat16)
+    s, y = add_layer_norm(x, r, (C,), w, b, 1e-5, out_dtype=torch.bfloat16)
+    assert s.dtype == torch.float32 and y.dtype == torch.bfloat16
+    torch.autograd.backward((s, y), (gs, gy))
+    xr, rr, wr, br = (t.detach().float().clone().requires_grad_(True) for t in (x, r, w, b))
+    sr = xr + rr
+    yr = F.layer_norm(sr, (C,), wr, br, 1e-5)
+    torch.autograd.backward((sr, yr), (gs, gy.float()))
+    assert torch.equal(s, sr.detach())
+    assert torch.allclose(y.float(), yr.detach().to(torch.bfloat16).float(), rtol=2 ** -7, atol=1e-4)
+    assert rel_l2(x.grad, xr.grad) < 1e-5
+    assert r.grad.dtype == torch.bfloat16 and rel_l2(r.grad, rr.grad) < 4e-3
+    assert rel_l2(w.grad, wr.grad) < 1e-5 and rel_l2(b.grad, br.grad) < 1e-5
+
+
+@pytest.mark.parametrize("shape", [(16384, 256, 1024), (300, 64, 200)], ids=["lm_mlp", "ragged_scalar"])
+def test_mlp_gelu_against_pytorch(cuda, shape):
+    """fc2(GELU(fc1(x))) under bf16 autocast: output and every gradient against
+    the fp32 composition (bias gradients and the GELU backward on this library's
+    column-sum kernels; 200 hidden columns take the scalar path)."""
+    M, D, H = shape
+    torch.manual_seed(M)
+    fc1, fc2 = torch.nn.Linear(D, H).to(cuda), torch.nn.Linear(H, D).to(cuda)
+    x = torch.randn(M, D, device=cuda).requires_grad_(True)
+    gy = torch.randn(M, D, device=cuda)
+    with torch.autocast("cuda", dtype=torch.bfloat16):
+        y = mlp_gelu(x, fc1, fc2)
+    assert y.dtype == torch.bfloat16
+    y.backward(gy.to(torch.bfloat16))
+    grads = [x.grad, fc1.weight.grad, fc1.bias.grad, fc2.weight.grad, fc2.bias.grad]
+    ref1, ref2 = torch.nn.Linear(D, H).to(cuda), torch.nn.Linear(H, D).to(cuda)
+    ref1.load_state_dict(fc1.state_dict()), ref2.load_state_dict(fc2.state_dict())
+    xr = x.detach().clone().requires_grad_(True)
+    yr = ref2(F.gelu(ref1(xr)))
+    yr.backward(gy.to(torch.bfloat16).float())
+    assert rel_l2(y, yr) < 1e-2
+    for name, a, b in zip(("x", "w1", "b1", "w2", "b2"), grads,
+                          [xr.grad, ref1.weight.grad, ref1.bias.grad, ref2.weight.grad, ref2.bias.grad]):
+        assert a.dtype == b.dtype and rel_l2(a, b) < 1.5e-2, (name, rel_l2(a, b))
+    # bias gradients are reduced in a fixed order: a rerun is bitwise equal
+    b1, b2 = fc1.bias.grad.clone(), fc2.bias.grad.clone()
+    for prm in (x, *fc1.parameters(), *fc2.parameters()):
+        prm.grad = None
+    with torch.autocast("cuda", dtype=torch.bfloat16):
+        mlp_gelu(x, fc1, fc2).backward(gy.to(torch.bfloat16))
+    assert torch.equal(b1, fc1.bias.grad) and torch.equal(b2, fc2.bias.grad)
+
+
+def test_colsum_and_gelu_bwd_kernels_exact_sums(cuda):
+    """The column sums equal an fp64 sum of the same stored values within fp32
+    rounding; the GELU derivative matches PyTorch's GELU backward on bf16."""
+    L = _lib.lib()
+    st = torch.cuda.current_stream().cuda_stream
+    g = torch.Generator(device=cuda).manual_seed(9)
+    for M, C, dt in ((5000, 1024, torch.bfloat16), (777, 24, torch.float32), (3, 8, torch.bfloat16)):
+        dh = torch.randn(M, C, device=cuda, generator=g).to(dt)
+        a = torch.randn(M, C, device=cuda, generator=g).to(dt) * 2
+        nb = L.pnft_colsum_workspace_size(M, C)
+        ws = torch.empty(max(nb, 1), dtype=torch.uint8, device=cuda)
+        out = torch.empty(C, device=cuda)
+        _lib.check(L.pnft_colsum(dh.data_ptr(), C, out.data_ptr(), ws.data_ptr(), nb, M, C,
+                                 _lib.DTYPE_BF16 if dt == torch.bfloat16 else _lib.DTYPE_F32, st), "colsum")
+        ref = dh.double().sum(0)
+        assert torch.allclose(out.double(), ref, rtol=1e-5, atol=1e-4 * M ** 0.5)
+        da = torch.empty_like(dh)
+        _lib.check(L.pnft_gelu_bwd_colsum(dh.data_ptr(), C, a.data_ptr(), C, da.data_ptr(), C, out.data_ptr(),
+                                          ws.data_ptr(), nb, M, C,
+                                          _lib.DTYPE_BF16 if dt == torch.bfloat16 else _lib.DTYPE_F32, st), "gelu")
+        ar = a.detach().float().requires_grad_(True)
+        F.gelu(ar).backward(dh.float())
+        tol = 2 ** -7 if dt == torch.bfloat16 else 1e-6
+        assert torch.allclose(da.float(), ar.grad.to(dt).float(), rtol=tol, atol=1e-6)
+        assert torch.allclose(out.double(), da.double().sum(0), rtol=1e-5, atol=1e-4 * M ** 0.5)
+
+
+def _lm_pair(cuda, N=128, B=4):
+    cfg = LMConfig(max_seq=N)
+    torch.manual_seed(3)
+    fused = PnFirLM(cfg, fused_step_ops=True).to(cuda)
+    plain = PnFirLM(cfg, fused_step_ops=False).to(cuda)
+    plain.load_state_dict(fused.state_dict())
+    g = torch.Generator(device=cuda).manual_seed(5)
+    idx = torch.randint(0, cfg.vocab, (B, N), device=cuda, generator=g)
+    return cfg, fused, plain, idx
+
+
+def test_lm_fused_step_ops_match_pytorch_composition(cuda):
+    """Config-4 model (D256 H4 L6 V33278) at a shorter sequence: loss and every
+    parameter gradient of one bf16-autocast step, fused ops vs nn.LayerNorm +
+    F.cross_entropy on the same weights."""
+    cfg, fused, plain, idx = _lm_pair(cuda)
+    assert list(fused.state_dict()) == list(plain.state_dict())
+    losses = []
+    for m in (fused, plain):
+        with torch.autocast("cuda", dtype=torch.bfloat16):
+            loss = lm_loss(m, idx)
+        loss.backward()
+        losses.append(float(loss))
+    check_device_status(cuda)
+    assert abs(losses[0] - losses[1]) < 2e-3 * abs(losses[1]), losses
+    pf, pp = dict(fused.named_parameters()), dict(plain.named_parameters())
+    for name in pf:
+        assert rel_l2(pf[name].grad, pp[name].grad) < 2e-2, (name, rel_l2(pf[name].grad, pp[name].grad))
+
+
+def test_lm_training_steps_track_pytorch_composition(cuda):
+    """Three AdamW steps (fused AdamW for the fused model, the default foreach
+    AdamW for the other): the loss trajectories stay together."""
+    cfg, fused, plain, idx = _lm_pair(cuda)
+    opt_f = make_optimizer(fused)
+    opt_p = torch.optim.AdamW(plain.parameters(), lr=3e-4, betas=(0.9, 0.95), weight_decay=0.1)
+    assert opt_f.defaults.get("fused")
+    lf = [float(train_step(fused, opt_f, idx)) for _ in range(3)]
+    lp = [float(train_step(plain, opt_p, idx)) for _ in range(3)]
+    check_device_status(cuda)
+    assert lf[-1] < lf[0] and lp[-1] < lp[0]
+    for a, b in zip(lf, lp):
+        assert abs(a - b) < 5e-3 * abs(b), (lf, lp)
