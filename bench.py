@@ -832,92 +832,62 @@ def bench_fir(args, dist_: Dist, dev, iters: int = 20) -> dict:
 
 
 def bench_lm(args, dist_: Dist, dev) -> dict:
-    """Config 4: 6-layer LM training step, bf16 autocast, AdamW, DDP at N > 1."""
-    from paper_01_anti_decoy_pnfirtau_b200.lm import LMConfig, PnFirLM, make_optimizer, train_step
+    """Config 4: 6-layer LM training step, bf16 autocast, AdamW, data parallel
+    over NCCL at N > 1. Headline: the step captured in one CUDA graph
+    (lm.GraphedTrainStep: forward, backward, one NCCL gradient average, clip,
+    fused AdamW). Beside it the same step run eagerly (DDP at N > 1), which
+    is bound by the host's per-op launch overhead."""
+    import torch.distributed as dist
+
+    from paper_01_anti_decoy_pnfirtau_b200.lm import GraphedTrainStep, LMConfig, PnFirLM, make_optimizer, train_step
 
     cfg = LMConfig()
-    torch.manual_seed(args.seed)
-    model = PnFirLM(cfg).to(dev)
-    nparams = model.param_count()
-    if dist_.active:
-        model = torch.nn.parallel.DistributedDataParallel(model, device_ids=[dev.index])
-    opt = make_optimizer(model)
     B, N = 32, cfg.max_seq
     g = torch.Generator(device=dev).manual_seed(args.seed + 17 * dist_.rank)
     batches = [torch.randint(0, cfg.vocab, (B, N), generator=g, device=dev) for _ in range(4)]
-    for i in range(3):
-        train_step(model, opt, batches[i % 4])
-    torch.cuda.synchronize()
     s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    dist_.barrier()
-    torch.cuda.synchronize()
-    s.record()
-    loss = None
-    for i in range(args.lm_steps):
-        loss = train_step(model, opt, batches[i % 4])
-    e.record()
-    torch.cuda.synchronize()
-    ms = dist_.max(s.elapsed_time(e), dev)
-    ms_step = ms / args.lm_steps
-    res = {"tokens_per_s": round(dist_.world * B * N / (ms_step / 1e3), 1), "ms_per_step": round(ms_step, 3),
-           "steps": args.lm_steps, "global_batch": B * dist_.world, "seq_len": N, "params": nparams,
-           "loss": round(float(loss), 4), "model": "6-layer Pre-LN pn_fir_tau LM, D256 H4 MLP4x V33278, bf16 autocast, AdamW",
-           "step_ops": "library LayerNorm and one-pass head cross-entropy kernels, fused AdamW",
-           "parallelism": f"ddp{dist_.world}" if dist_.world > 1 else "single GPU"}
-    if not dist_.active:
-        try:
-            res.update(bench_lm_graph(args, dev, cfg, batches))
-        except Exception as exc:  # report, keep the eager number
-            res["graph"] = f"capture failed: {type(exc).__name__}: {exc}"[:200]
-    return res
 
-
-def bench_lm_graph(args, dev, cfg, batches) -> dict:
-    """The same training step captured once in a CUDA graph and replayed (the
-    reference's exp4c technique for the launch-bound 6-layer stack): loss,
-    backward, clip_grad_norm_ and AdamW(capturable=True) in one graph; each step
-    copies its batch into the captured input. Single GPU (DDP stays eager)."""
-    from paper_01_anti_decoy_pnfirtau_b200.lm import PnFirLM, lm_loss, make_optimizer
+    def timed(run_step) -> tuple[float, torch.Tensor]:
+        for i in range(3):
+            run_step(batches[i % 4])
+        torch.cuda.synchronize()
+        dist_.barrier()
+        torch.cuda.synchronize()
+        s.record()
+        loss = None
+        for i in range(args.lm_steps):
+            loss = run_step(batches[i % 4])
+        e.record()
+        torch.cuda.synchronize()
+        return dist_.max(s.elapsed_time(e), dev) / args.lm_steps, loss
 
     torch.manual_seed(args.seed)
     model = PnFirLM(cfg).to(dev)
+    nparams = model.param_count()
     opt = make_optimizer(model, capturable=True)
-    static_idx = batches[0].clone()
-
-    def step():
-        with torch.autocast(device_type="cuda", dtype=torch.bfloat16, cache_enabled=False):
-            loss = lm_loss(model, static_idx)
-        loss.backward()
-        torch.nn.utils.clip_grad_norm_(model.parameters(), 1.0)
-        opt.step()
-        return loss.detach()
-
-    side = torch.cuda.Stream(dev)
-    side.wait_stream(torch.cuda.current_stream(dev))
-    with torch.cuda.stream(side):
-        for _ in range(3):
-            opt.zero_grad(set_to_none=True)
-            step()
-    torch.cuda.current_stream(dev).wait_stream(side)
-    graph = torch.cuda.CUDAGraph()
-    opt.zero_grad(set_to_none=True)
-    with torch.cuda.graph(graph):
-        static_loss = step()
-    for i in range(3):
-        static_idx.copy_(batches[i % len(batches)])
-        graph.replay()
+    graphed = GraphedTrainStep(model, opt, batches[0], group=dist.group.WORLD if dist_.active else None)
+    ms_g, loss_g = timed(graphed.step)
+    loss_g = float(loss_g)
+    graphed.close()
+    del graphed, opt, model
     torch.cuda.synchronize()
-    s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    s.record()
-    for i in range(args.lm_steps):
-        static_idx.copy_(batches[i % len(batches)])
-        graph.replay()
-    e.record()
-    torch.cuda.synchronize()
-    ms_step = s.elapsed_time(e) / args.lm_steps
-    B, N = static_idx.shape
-    return {"tokens_per_s_graph": round(B * N / (ms_step / 1e3), 1), "ms_per_step_graph": round(ms_step, 3),
-            "loss_graph": round(float(static_loss), 4)}
+
+    torch.manual_seed(args.seed)
+    model = PnFirLM(cfg).to(dev)
+    if dist_.active:
+        model = torch.nn.parallel.DistributedDataParallel(model, device_ids=[dev.index])
+    opt = make_optimizer(model)
+    ms_e, loss_e = timed(lambda idx: train_step(model, opt, idx))
+    tok = dist_.world * B * N
+    return {"tokens_per_s": round(tok / (ms_g / 1e3), 1), "ms_per_step": round(ms_g, 3), "loss": round(loss_g, 4),
+            "tokens_per_s_eager": round(tok / (ms_e / 1e3), 1), "ms_per_step_eager": round(ms_e, 3),
+            "loss_eager": round(float(loss_e), 4), "steps": args.lm_steps, "global_batch": B * dist_.world,
+            "seq_len": N, "params": nparams,
+            "model": "6-layer Pre-LN pn_fir_tau LM, D256 H4 MLP4x V33278, bf16 autocast, AdamW",
+            "step": "one CUDA graph per step: forward, backward, NCCL gradient average (N > 1), clip, fused AdamW; "
+                    "eager: the same ops launched one by one (DDP at N > 1)",
+            "step_ops": "library LayerNorm, MLP-backward and one-pass head cross-entropy kernels, fused AdamW",
+            "parallelism": f"dp{dist_.world}" if dist_.world > 1 else "single GPU"}
 
 
 # ---------------------------------------------------------------------------

@@ -364,12 +364,30 @@ PNFT_API size_t pnft_colsum_workspace_size(int64_t M, int64_t C);
 /* Backward of the MLP's exact (erf) GELU fused with the first Linear's bias
  * gradient: da[r, c] = dh[r, c] * GELU'(a[r, c]) (written in `dtype`), and
  * db[c] = sum over rows of da[r, c] as stored (fp32, fixed order). a is the
- * GELU input. workspace: pnft_colsum_workspace_size(M, C) bytes.
+ * GELU input. workspace: pnft_colsum_workspace_size(M, C) bytes. table: as
+ * pnft_gelu_fwd (GELU' of bfloat16 a; NULL: computed per CTA).
  * Replaces: nn.GELU's backward and grad_output.sum(0) of the first nn.Linear
  * (same call sites). */
+/* Floats of the GELU lookup table (GELU and GELU' of every bfloat16 a with
+ * |a| in [2^-16, 16)), built by pnft_gelu_table. */
+#define PNFT_GELU_TABLE_FLOATS 10240
+
+/* Builds the GELU lookup table (PNFT_GELU_TABLE_FLOATS fp32, 16-byte aligned)
+ * that pnft_gelu_fwd / pnft_gelu_bwd_colsum copy into shared memory. */
+PNFT_API int pnft_gelu_table(float* table, void* stream);
+
+/* y = GELU(a) = a * Phi(a) (the exact, erf form of nn.GELU()), rows of C
+ * elements with row strides sa / sy; float32 or bfloat16, arithmetic in fp32.
+ * bfloat16 rows look GELU up in `table` (pnft_gelu_table's output; NULL: every
+ * CTA computes its own copy, same values). Values outside the table's range
+ * use the formula.
+ * Replaces: nn.GELU's forward in the MLP (experiments/exp4_wikitext2_lm.py:183-200). */
+PNFT_API int pnft_gelu_fwd(const void* a, int64_t sa, void* y, int64_t sy, int64_t M, int64_t C, int dtype,
+                  const float* table, void* stream);
+
 PNFT_API int pnft_gelu_bwd_colsum(const void* dh, int64_t sdh, const void* a, int64_t sa, void* da, int64_t sda,
                          float* db, void* workspace, size_t workspace_bytes, int64_t M, int64_t C, int dtype,
-                         void* stream);
+                         const float* table, void* stream);
 
 #ifdef __cplusplus
 }

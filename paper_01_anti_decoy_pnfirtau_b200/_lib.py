@@ -19,6 +19,7 @@ SILENCE_PEAK, SILENCE_MASS_RELU, SILENCE_MASS_POW = 0, 1, 2
 FLASH_FORCE_GENERIC, FLASH_DETERMINISTIC, FLASH_PREFER_SM100 = 0x1, 0x2, 0x4
 FLASH_TEST_STALL = 0x100  # test-only: the tcgen05 kernels take their timeout path
 FIR_FUSED_TAPS = 7  # PNFT_FIR_FUSED_TAPS
+GELU_TABLE_FLOATS = 10240  # PNFT_GELU_TABLE_FLOATS
 
 _I64x4 = c_int64 * 4
 _P = c_void_p
@@ -101,8 +102,10 @@ SIGNATURES: dict[str, tuple] = {
     ),
     "pnft_colsum": (c_int, [_P, c_int64, _P, _P, c_size_t, c_int64, c_int64, c_int, _P]),
     "pnft_colsum_workspace_size": (c_size_t, [c_int64, c_int64]),
+    "pnft_gelu_table": (c_int, [_P, _P]),
+    "pnft_gelu_fwd": (c_int, [_P, c_int64, _P, c_int64, c_int64, c_int64, c_int, _P, _P]),
     "pnft_gelu_bwd_colsum": (
-        c_int, [_P, c_int64, _P, c_int64, _P, c_int64, _P, _P, c_size_t, c_int64, c_int64, c_int, _P]),
+        c_int, [_P, c_int64, _P, c_int64, _P, c_int64, _P, _P, c_size_t, c_int64, c_int64, c_int, _P, _P]),
 }
 
 _lock = threading.Lock()

@@ -782,10 +782,59 @@ int ln_bwd_entry(const LnBwdArgs& a, int dy_dtype, int x_dtype, float* dgamma, f
 // Linear-layer bias gradients: column sums, optionally fused with the GELU backward
 // =====================================================================================
 
-// exact (erf) GELU derivative: Phi(a) + a * phi(a)
+// exact (erf) GELU and its derivative Phi(a) + a * phi(a)
+__device__ __forceinline__ float gelu_exact(float a) {
+  constexpr float kInvSqrt2 = 0.70710678118654752f;
+  return 0.5f * a * (1.f + erff(a * kInvSqrt2));
+}
 __device__ __forceinline__ float gelu_grad(float a) {
   constexpr float kInvSqrt2 = 0.70710678118654752f, kInvSqrt2Pi = 0.39894228040143268f;
   return 0.5f * (1.f + erff(a * kInvSqrt2)) + a * kInvSqrt2Pi * expf(-0.5f * a * a);
+}
+
+// For bf16 inputs GELU and GELU' depend only on the 16-bit pattern of a. A CTA
+// tabulates them (the same fp32 formulas) in shared memory for |a| in
+// [2^-16, 16), 2 signs x 20 binades x 128 mantissas, and looks elements up
+// there; the rare |a| outside the range take the formula.
+constexpr int kGeluE0 = 111;  // biased exponent of 2^-16
+constexpr int kGeluNE = 20;   // binades up to 2^4
+constexpr int kGeluN = 2 * kGeluNE * 128;
+
+__device__ __forceinline__ float gelu_table_arg(int i) {
+  const uint32_t sign = (uint32_t)i / (kGeluNE * 128), rem = (uint32_t)i % (kGeluNE * 128);
+  return __uint_as_float(((sign << 15) | ((kGeluE0 + rem / 128) << 7) | (rem % 128)) << 16);
+}
+
+// The CTA's shared-memory table: copied from `src` (built once per device by
+// pnft_gelu_table) when given, else computed here.
+template <bool GRAD>
+__device__ __forceinline__ void gelu_table_init(float* tbl, const float* src) {
+  if (src) {
+    const float4* s4 = reinterpret_cast<const float4*>(src + (GRAD ? kGeluN : 0));
+    for (int i = threadIdx.x; i < kGeluN / 4; i += blockDim.x) reinterpret_cast<float4*>(tbl)[i] = __ldg(s4 + i);
+  } else {
+    for (int i = threadIdx.x; i < kGeluN; i += blockDim.x) {
+      const float a = gelu_table_arg(i);
+      tbl[i] = GRAD ? gelu_grad(a) : gelu_exact(a);
+    }
+  }
+}
+
+__global__ void gelu_table_kernel(float* out) {
+  const int i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i < kGeluN) {
+    const float a = gelu_table_arg(i);
+    out[i] = gelu_exact(a);
+    out[kGeluN + i] = gelu_grad(a);
+  }
+}
+
+template <bool GRAD>
+__device__ __forceinline__ float gelu_lookup(const float* tbl, uint32_t bits16) {
+  const uint32_t de = ((bits16 >> 7) & 0xFFu) - kGeluE0;
+  if (de < (uint32_t)kGeluNE) return tbl[((bits16 >> 15) * kGeluNE + de) * 128 + (bits16 & 0x7Fu)];
+  const float a = __uint_as_float(bits16 << 16);
+  return GRAD ? gelu_grad(a) : gelu_exact(a);
 }
 
 struct ColArgs {
@@ -796,6 +845,7 @@ struct ColArgs {
   void* da;       // g * gelu'(a) (written when a is given)
   int64_t sda;
   float* part;    // [C][nblk]
+  const float* table;  // pnft_gelu_table output, or null
   int64_t M;
   int C;
   int64_t rows_per_blk;
@@ -809,6 +859,12 @@ struct ColArgs {
 template <typename T, int VW>
 __global__ void __launch_bounds__(LT) colsum_kernel(ColArgs p) {
   __shared__ float red[LT * VW];
+  constexpr bool kTable = VW == 8;  // bf16 vectors: GELU' from the table
+  __shared__ float gtab[kTable ? kGeluN : 1];
+  if (kTable && p.a) {
+    gelu_table_init<true>(gtab, p.table);
+    __syncthreads();
+  }
   const T* g = static_cast<const T*>(p.g);
   const T* av = static_cast<const T*>(p.a);
   T* da = static_cast<T*>(p.da);
@@ -831,14 +887,15 @@ __global__ void __launch_bounds__(LT) colsum_kernel(ColArgs p) {
           f[0] = to_f32(g[row * p.sg + j]);
         }
         if (av) {
-          float x[VW];
           if constexpr (VW == 8) {
-            unpack8(*reinterpret_cast<const uint4*>(av + row * p.sa + (int64_t)j * 8), x);
-          } else {
-            x[0] = to_f32(av[row * p.sa + j]);
-          }
+            const uint4 u = *reinterpret_cast<const uint4*>(av + row * p.sa + (int64_t)j * 8);
+            const uint32_t w[4] = {u.x, u.y, u.z, u.w};
 #pragma unroll
-          for (int k = 0; k < VW; ++k) f[k] = (float)from_f32<T>(f[k] * gelu_grad(x[k]));  // the stored value
+            for (int k = 0; k < 8; ++k)  // the stored (rounded) value is what gets summed
+              f[k] = (float)from_f32<T>(f[k] * gelu_lookup<true>(gtab, k & 1 ? w[k / 2] >> 16 : w[k / 2] & 0xFFFFu));
+          } else {
+            f[0] = (float)from_f32<T>(f[0] * gelu_grad(to_f32(av[row * p.sa + j])));
+          }
           if constexpr (VW == 8) {
             uint4 o;
             o.x = sm100::pack_bf16x2(f[0], f[1]);
@@ -891,6 +948,48 @@ int col_entry(ColArgs p, float* out, int dtype, cudaStream_t st) {
     return colsum_launch<__nv_bfloat16, 8>(p, out, st);
   if (dtype == PNFT_DTYPE_BF16) return colsum_launch<__nv_bfloat16, 1>(p, out, st);
   return colsum_launch<float, 1>(p, out, st);
+}
+
+// y = GELU(a) (exact erf form), rows of C elements with row strides sa / sy.
+// bf16 with 16-byte vectors: table lookups; otherwise the formula per element.
+template <typename T, bool VEC>
+__global__ void __launch_bounds__(LT) gelu_fwd_kernel(const T* a, int64_t sa, T* y, int64_t sy, int64_t M, int C,
+                                                     const float* table) {
+  __shared__ float gtab[VEC ? kGeluN : 1];
+  if constexpr (VEC) {
+    gelu_table_init<false>(gtab, table);
+    __syncthreads();
+    const int vpr = C / 8;
+    const int64_t n = M * vpr;
+    for (int64_t i = (int64_t)blockIdx.x * LT + threadIdx.x; i < n; i += (int64_t)gridDim.x * LT) {
+      const int64_t row = i / vpr;
+      const int j = (int)(i - row * vpr);
+      const uint4 u = *reinterpret_cast<const uint4*>(a + row * sa + (int64_t)j * 8);
+      const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+      uint32_t o[4];
+#pragma unroll
+      for (int k = 0; k < 4; ++k)
+        o[k] = sm100::pack_bf16x2(gelu_lookup<false>(gtab, w[k] & 0xFFFFu), gelu_lookup<false>(gtab, w[k] >> 16));
+      *reinterpret_cast<uint4*>(y + row * sy + (int64_t)j * 8) = make_uint4(o[0], o[1], o[2], o[3]);
+    }
+  } else {
+    const int64_t n = M * C;
+    for (int64_t i = (int64_t)blockIdx.x * LT + threadIdx.x; i < n; i += (int64_t)gridDim.x * LT) {
+      const int64_t row = i / C;
+      const int c = (int)(i - row * C);
+      y[row * sy + c] = from_f32<T>(gelu_exact(to_f32(a[row * sa + c])));
+    }
+  }
+}
+
+template <typename T, bool VEC>
+int gelu_fwd_launch(const void* a, int64_t sa, void* y, int64_t sy, int64_t M, int64_t C, const float* table,
+                    cudaStream_t st) {
+  static const int per_sm = resident_per_sm(gelu_fwd_kernel<T, VEC>, 0);
+  const int64_t items = VEC ? M * (C / 8) : M * C;
+  const int grid = (int)std::max<int64_t>(1, std::min<int64_t>((items + LT - 1) / LT, (int64_t)per_sm * device_sms()));
+  gelu_fwd_kernel<T, VEC><<<grid, LT, 0, st>>>(static_cast<const T*>(a), sa, static_cast<T*>(y), sy, M, (int)C, table);
+  return check_launch("gelu fwd");
 }
 
 }  // namespace
@@ -1024,17 +1123,41 @@ extern "C" int pnft_colsum(const void* g, int64_t sg, float* out, void* workspac
   if (int rc = col_check("colsum", g, sg, out, workspace, workspace_bytes, M, C, dtype)) return rc;
   cudaStream_t st = as_stream(stream);
   if (M == 0) return cudaMemsetAsync(out, 0, sizeof(float) * C, st) == cudaSuccess ? PNFT_OK : check_launch("colsum", 0);
-  ColArgs p{g, sg, nullptr, 0, nullptr, 0, static_cast<float*>(workspace), M, (int)C, 0};
+  ColArgs p{g, sg, nullptr, 0, nullptr, 0, static_cast<float*>(workspace), nullptr, M, (int)C, 0};
   return col_entry(p, out, dtype, st);
 }
 
 extern "C" int pnft_gelu_bwd_colsum(const void* dh, int64_t sdh, const void* a, int64_t sa, void* da, int64_t sda,
                                     float* db, void* workspace, size_t workspace_bytes, int64_t M, int64_t C,
-                                    int dtype, void* stream) {
+                                    int dtype, const float* table, void* stream) {
   if (int rc = col_check("gelu_bwd_colsum", dh, sdh, db, workspace, workspace_bytes, M, C, dtype)) return rc;
   if (M > 0 && (!a || !da || sa < C || sda < C)) return fail(PNFT_EINVAL, "gelu_bwd_colsum: bad a / da");
   cudaStream_t st = as_stream(stream);
   if (M == 0) return cudaMemsetAsync(db, 0, sizeof(float) * C, st) == cudaSuccess ? PNFT_OK : check_launch("gelu_bwd_colsum", 0);
-  ColArgs p{dh, sdh, a, sa, da, sda, static_cast<float*>(workspace), M, (int)C, 0};
+  if (table && reinterpret_cast<uintptr_t>(table) % 16) return fail(PNFT_EINVAL, "gelu_bwd_colsum: table not 16-byte aligned");
+  ColArgs p{dh, sdh, a, sa, da, sda, static_cast<float*>(workspace), table, M, (int)C, 0};
   return col_entry(p, db, dtype, st);
+}
+
+extern "C" int pnft_gelu_table(float* table, void* stream) {
+  if (!table) return fail(PNFT_EINVAL, "gelu table: null pointer");
+  if (reinterpret_cast<uintptr_t>(table) % 16) return fail(PNFT_EINVAL, "gelu table: not 16-byte aligned");
+  gelu_table_kernel<<<(kGeluN + 255) / 256, 256, 0, as_stream(stream)>>>(table);
+  return check_launch("gelu table");
+}
+
+extern "C" int pnft_gelu_fwd(const void* a, int64_t sa, void* y, int64_t sy, int64_t M, int64_t C, int dtype,
+                             const float* table, void* stream) {
+  if (M < 0 || C <= 0 || C > (1 << 24)) return fail(PNFT_EINVAL, "gelu fwd: bad shape M=%lld C=%lld", (long long)M, (long long)C);
+  if (!ln_dtype_ok(dtype)) return fail(PNFT_EUNSUPPORTED, "gelu fwd: float32 or bfloat16 expected");
+  if (M == 0) return PNFT_OK;
+  if (!a || !y) return fail(PNFT_EINVAL, "gelu fwd: null pointer");
+  if (sa < C || sy < C) return fail(PNFT_EINVAL, "gelu fwd: row strides must be >= C");
+  cudaStream_t st = as_stream(stream);
+  if (dtype == PNFT_DTYPE_BF16) {
+    if (C % 8 == 0 && sa % 8 == 0 && sy % 8 == 0 && aligned16(a) && aligned16(y))
+      return gelu_fwd_launch<__nv_bfloat16, true>(a, sa, y, sy, M, C, table, st);
+    return gelu_fwd_launch<__nv_bfloat16, false>(a, sa, y, sy, M, C, table, st);
+  }
+  return gelu_fwd_launch<float, false>(a, sa, y, sy, M, C, table, st);
 }

@@ -161,3 +161,89 @@ def make_optimizer(model: nn.Module, lr: float = 3e-4, capturable: bool = False)
     fused = all(p.is_cuda for p in model.parameters())
     return torch.optim.AdamW(model.parameters(), lr=lr, betas=(0.9, 0.95), weight_decay=0.1, fused=fused,
                              capturable=capturable)
+
+
+class GraphedTrainStep:
+    """``train_step`` captured once in a CUDA graph and replayed (the technique
+    of the reference's exp4c, experiments/exp4c_cuda_graphs.py, applied to the
+    whole training step): bf16-autocast loss, backward, the gradient average
+    over a data-parallel group, clip_grad_norm_ and the optimizer step run as
+    one graph launch; ``step(idx)`` copies the batch into the captured input.
+
+    Data parallelism without DDP's hooks: after the backward every gradient is
+    gathered into one flat fp32 buffer, averaged across ``group`` by one NCCL
+    all-reduce inside the graph, and copied back. The ranks' weights start
+    equal (rank 0's are broadcast at construction).
+
+    ``opt`` must be capturable (``make_optimizer(model, capturable=True)``).
+    Construction runs ``warmup`` steps on ``example_idx`` (a side stream; the
+    optimizer creates its state and NCCL its communicator there), captures a
+    step, and then restores the parameters and the optimizer state, so it
+    leaves the model as it found it. The graph's NCCL call must be released
+    (``close()``) before the process group is destroyed."""
+
+    def __init__(self, model: nn.Module, opt: torch.optim.Optimizer, example_idx: torch.Tensor, group=None,
+                 clip: float = 1.0, warmup: int = 3):
+        import torch.distributed as dist
+
+        self.model, self.opt, self.clip, self.group = model, opt, clip, group
+        self.world = dist.get_world_size(group) if group is not None else 1
+        self.params = [p for p in model.parameters() if p.requires_grad]
+        dev = self.params[0].device
+        if self.world > 1:
+            src = dist.get_global_rank(group, 0)
+            with torch.no_grad():
+                for p in self.params:
+                    dist.broadcast(p, src=src, group=group)
+        self.sizes = [p.numel() for p in self.params]
+        self.flat = torch.empty(sum(self.sizes), dtype=torch.float32, device=dev) if self.world > 1 else None
+        self.idx = example_idx.detach().clone()
+        saved_p = [p.detach().clone() for p in self.params]
+        saved_s = {id(p): {k: (v.clone() if torch.is_tensor(v) else v) for k, v in opt.state[p].items()}
+                   for p in self.params if p in opt.state}
+        side = torch.cuda.Stream(dev)
+        side.wait_stream(torch.cuda.current_stream(dev))
+        with torch.cuda.stream(side):
+            for _ in range(warmup):
+                opt.zero_grad(set_to_none=True)
+                self._step()
+        torch.cuda.current_stream(dev).wait_stream(side)
+        self.graph = torch.cuda.CUDAGraph()
+        opt.zero_grad(set_to_none=True)
+        with torch.cuda.graph(self.graph):
+            self.loss = self._step()
+        torch.cuda.synchronize(dev)
+        # back to the state before construction
+        with torch.no_grad():
+            for p, s in zip(self.params, saved_p):
+                p.copy_(s)
+            for p in self.params:
+                st = opt.state.get(p, {})
+                old = saved_s.get(id(p))
+                for k, v in st.items():
+                    if torch.is_tensor(v):
+                        v.copy_(old[k]) if old is not None and k in old else v.zero_()
+
+    def _step(self) -> torch.Tensor:
+        import torch.distributed as dist
+
+        with torch.autocast(device_type="cuda", dtype=torch.bfloat16, cache_enabled=False):
+            loss = lm_loss(self.model, self.idx)
+        loss.backward()
+        if self.world > 1:
+            grads = [p.grad for p in self.params]
+            torch.cat([g.reshape(-1) for g in grads], out=self.flat)
+            dist.all_reduce(self.flat, op=dist.ReduceOp.AVG, group=self.group)
+            torch._foreach_copy_(grads, [t.view_as(g) for t, g in zip(self.flat.split(self.sizes), grads)])
+        torch.nn.utils.clip_grad_norm_(self.params, self.clip)
+        self.opt.step()
+        return loss.detach()
+
+    def step(self, idx: torch.Tensor) -> torch.Tensor:
+        """One replayed training step on ``idx``; returns the loss tensor (no host sync)."""
+        self.idx.copy_(idx)
+        self.graph.replay()
+        return self.loss
+
+    def close(self) -> None:
+        self.graph = None

@@ -14,8 +14,10 @@ language-model experiments (experiments/exp4_wikitext2_lm.py:183-259, loss at
 - ``add_layer_norm(x, r, ...)``: ``s = x + r`` and ``LayerNorm(s)`` in one
   pass; its backward adds the residual path's gradient of ``s`` and writes the
   branch's gradient directly in the branch's dtype.
-- ``mlp_gelu(x, fc1, fc2)``: ``fc2(GELU(fc1(x)))`` with the autocast GEMMs;
-  the backward fuses the GELU derivative with ``fc1``'s bias gradient, sums
+- ``mlp_gelu(x, fc1, fc2)``: ``fc2(GELU(fc1(x)))`` with the autocast GEMMs
+  and this library's GELU (bf16: a per-CTA shared-memory table of the exact
+  GELU over the bf16 bit patterns); the backward fuses the GELU derivative
+  (tabulated the same way) with ``fc1``'s bias gradient, sums
   ``fc2``'s bias gradient with the same column-sum kernel (both fp32, fixed
   order) and produces the weight gradients from fp32-output GEMMs.
 - ``head_cross_entropy``: ``F.cross_entropy(h @ W.T, targets)`` (mean over
@@ -219,6 +221,22 @@ def add_layer_norm(x: torch.Tensor, r: torch.Tensor, normalized_shape, weight: t
     return _AddLayerNormFn.apply(xd, rd, weight, bias, C, eps, out_dtype or _autocast_dtype(x))
 
 
+_GELU_TABLES: dict[int, torch.Tensor] = {}
+
+
+def _gelu_table(dev: torch.device) -> torch.Tensor | None:
+    """The device's GELU lookup table (pnft_gelu_table), built at the first call
+    made outside CUDA-graph capture; during a capture that comes first the
+    kernels build their own per-CTA copies (None)."""
+    idx = dev.index if dev.index is not None else torch.cuda.current_device()
+    t = _GELU_TABLES.get(idx)
+    if t is None and not torch.cuda.is_current_stream_capturing():
+        t = torch.empty(_lib.GELU_TABLE_FLOATS, dtype=torch.float32, device=dev)
+        _lib.check(_lib.lib().pnft_gelu_table(t.data_ptr(), _stream(dev)), "pnft_gelu_table")
+        _GELU_TABLES[idx] = t
+    return t
+
+
 def _colsum_ws(M: int, C: int, dev: torch.device):
     nbytes = _lib.lib().pnft_colsum_workspace_size(M, C)
     return torch.empty(max(nbytes, 1), dtype=torch.uint8, device=dev), nbytes
@@ -237,7 +255,10 @@ class _MlpGeluFn(torch.autograd.Function):
         x2 = x2 if x2.stride(-1) == 1 else x2.contiguous()
         w1c, w2c = w1.to(dt), w2.to(dt)
         a0 = torch.addmm(b1.to(dt), x2, w1c.t()) if b1 is not None else torch.mm(x2, w1c.t())
-        a1 = F.gelu(a0)
+        a1 = torch.empty_like(a0)
+        _lib.check(_lib.lib().pnft_gelu_fwd(a0.data_ptr(), a0.stride(0), a1.data_ptr(), a1.stride(0), a0.shape[0],
+                                            a0.shape[1], _ln_code(dt, "mlp_gelu"), _ptr(_gelu_table(dev)),
+                                            _stream(dev)), "pnft_gelu_fwd")
         out = torch.addmm(b2.to(dt), a1, w2c.t()) if b2 is not None else torch.mm(a1, w2c.t())
         ctx.save_for_backward(x2, w1c, w2c, a0, a1)
         ctx.x_shape, ctx.x_dtype, ctx.dev = x.shape, x.dtype, dev
@@ -266,7 +287,8 @@ class _MlpGeluFn(torch.autograd.Function):
         ws, nb = _colsum_ws(M, H, dev)
         _lib.check(L.pnft_gelu_bwd_colsum(da1.data_ptr(), da1.stride(0), a0.data_ptr(), a0.stride(0), da0.data_ptr(),
                                           da0.stride(0), db1.data_ptr(), ws.data_ptr(), nb, M, H,
-                                          _ln_code(dt, "mlp_gelu"), st), "pnft_gelu_bwd_colsum")
+                                          _ln_code(dt, "mlp_gelu"), _ptr(_gelu_table(dev)), st),
+                   "pnft_gelu_bwd_colsum")
         if ctx.needs_input_grad[1]:
             dw1 = _mm_f32(da0.t(), x2)
         if ctx.needs_input_grad[0]:

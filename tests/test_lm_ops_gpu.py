@@ -21,6 +21,10 @@ from paper_01_anti_decoy_pnfirtau_b200.pnfirtau_ops import _status_ptr, check_de
 pytestmark = pytest.mark.gpu
 
 
+def _ptr(t):
+    return None if t is None else t.data_ptr()
+
+
 def _xent_call(logits, V, t, ignore=-100, scale=1.0):
     M, ld = logits.shape
     loss = torch.empty(M, device=logits.device)
@@ -232,14 +236,53 @@ def test_colsum_and_gelu_bwd_kernels_exact_sums(cuda):
         ref = dh.double().sum(0)
         assert torch.allclose(out.double(), ref, rtol=1e-5, atol=1e-4 * M ** 0.5)
         da = torch.empty_like(dh)
-        _lib.check(L.pnft_gelu_bwd_colsum(dh.data_ptr(), C, a.data_ptr(), C, da.data_ptr(), C, out.data_ptr(),
-                                          ws.data_ptr(), nb, M, C,
-                                          _lib.DTYPE_BF16 if dt == torch.bfloat16 else _lib.DTYPE_F32, st), "gelu")
+        tab = torch.empty(_lib.GELU_TABLE_FLOATS, device=cuda)
+        _lib.check(L.pnft_gelu_table(tab.data_ptr(), st), "gelu table")
+        runs = []
+        for table in (None, tab):  # per-CTA tables and the device table give the same values
+            _lib.check(L.pnft_gelu_bwd_colsum(dh.data_ptr(), C, a.data_ptr(), C, da.data_ptr(), C, out.data_ptr(),
+                                              ws.data_ptr(), nb, M, C,
+                                              _lib.DTYPE_BF16 if dt == torch.bfloat16 else _lib.DTYPE_F32,
+                                              _ptr(table), st), "gelu")
+            runs.append((da.clone(), out.clone()))
+        assert torch.equal(runs[0][0], runs[1][0]) and torch.equal(runs[0][1], runs[1][1])
         ar = a.detach().float().requires_grad_(True)
         F.gelu(ar).backward(dh.float())
         tol = 2 ** -7 if dt == torch.bfloat16 else 1e-6
         assert torch.allclose(da.float(), ar.grad.to(dt).float(), rtol=tol, atol=1e-6)
         assert torch.allclose(out.double(), da.double().sum(0), rtol=1e-5, atol=1e-4 * M ** 0.5)
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float32])
+def test_gelu_fwd_against_pytorch(cuda, dtype):
+    """pnft_gelu_fwd against F.gelu (exact erf form): bf16 through the
+    per-CTA table (every binade it covers, and values outside it: tiny, zero,
+    |a| >= 16), fp32 and a ragged width through the formula."""
+    L = _lib.lib()
+    st = torch.cuda.current_stream().cuda_stream
+    g = torch.Generator(device=cuda).manual_seed(4)
+    code = _lib.DTYPE_BF16 if dtype == torch.bfloat16 else _lib.DTYPE_F32
+    tab = torch.empty(_lib.GELU_TABLE_FLOATS, device=cuda)
+    _lib.check(L.pnft_gelu_table(tab.data_ptr(), st), "gelu table")
+    ys = []
+    for M, C in ((4096, 1024), (37, 20)):
+        a = torch.randn(M, C, device=cuda, generator=g) * torch.exp2(torch.randint(-20, 6, (M, C), device=cuda,
+                                                                                    generator=g).float())
+        a[0, :8] = torch.tensor([0.0, -0.0, 1e-30, -3e-7, 16.0, -16.0, 40.0, -40.0])
+        a = a.to(dtype)
+        y = torch.empty_like(a)
+        for table in (None, tab):  # per-CTA tables and the device table give the same values
+            _lib.check(L.pnft_gelu_fwd(a.data_ptr(), C, y.data_ptr(), C, M, C, code, _ptr(table), st), "gelu")
+            ys.append(y.clone())
+        assert torch.equal(ys[0], ys[1])
+        ys.clear()
+        ref = F.gelu(a.float())
+        if dtype == torch.bfloat16:
+            # the fp32 result rounded to bf16: equal, or one ulp off where the fp32 values round apart
+            assert torch.allclose(y.float(), ref.to(dtype).float(), rtol=2 ** -7, atol=1e-30)
+            assert (y.float() == ref.to(dtype).float()).float().mean() > 0.995
+        else:
+            assert torch.allclose(y, ref, rtol=2e-6, atol=1e-30)
 
 
 def _lm_pair(cuda, N=128, B=4):
