@@ -70,6 +70,10 @@ def parse_args():
     ap.add_argument("--no-lm", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-fir", action="store_true")
+    ap.add_argument("--no-lm-kernels", action="store_true", help="skip timing the LM step's kernels alone")
+    ap.add_argument("--lm-kernels-only", action="store_true",
+                    help="only the LM step's kernels, one call each then timed (the profiling command)")
+    ap.add_argument("--lm-kernel-rows", type=int, default=16352, help="logit rows of the cross-entropy timing")
     ap.add_argument("--no-sweep", action="store_true", help="skip the config-3 tau sweep")
     ap.add_argument("--no-c5", action="store_true", help="skip the config-5 measurement")
     ap.add_argument("--no-triton", action="store_true",
@@ -512,6 +516,8 @@ def bench_ours(args, dist_: Dist) -> dict:
         result["lm"] = bench_lm(args, dist_, dev)
     if not args.no_fir:
         result["fir"] = bench_fir(args, dist_, dev)
+    if not args.no_lm_kernels:
+        result["lm_kernels"] = bench_lm_kernels(args, dev)
     if dist_.rank == 0 and dist_.world == 1 and not args.no_cpu:
         tf, cores, n, el, kind, what = cpu_oracle_sample(w, args.cpu_seconds, args.seed)
         result["cpu_baseline"] = {"value": round(tf, 6), "unit": "TFLOP/s", "cores": cores, "kind": kind,
@@ -749,6 +755,89 @@ def bench_e2e(args, dist_: Dist, w: dict, dev, flops: float, P) -> dict:
                    "H2D / compute / D2H on three streams"}
 
 
+def bench_lm_kernels(args, dev, iters: int = 10) -> dict:
+    """The LM step's own kernels (csrc/lm_step.cu) alone at config 4's shapes:
+    the head cross-entropy over `--lm-kernel-rows` x 33280 bf16 logits (one
+    pass: logits read, gradient written), the residual add + LayerNorm forward
+    and backward over [16384, 256], and the MLP's GELU forward and GELU backward
+    + bias gradient over [16384, 1024]. Each entry point is called once first
+    (the order an ncu capture sees), then timed with CUDA events; three operand
+    sets rotate so every pass reads more than L2 holds. GB/s counts the
+    algorithmic bytes (each operand read or written once)."""
+    from paper_01_anti_decoy_pnfirtau_b200 import _lib
+
+    L = _lib.lib()
+    st = torch.cuda.current_stream(dev).cuda_stream
+    g = torch.Generator(device=dev).manual_seed(args.seed + 7)
+    BF, F32 = _lib.DTYPE_BF16, _lib.DTYPE_F32
+    M1, V, ld = args.lm_kernel_rows, 33278, 33280
+    M, C, H = 16384, 256, 1024
+    logits = (torch.randn(M1, ld, generator=g, device=dev) * 3).to(torch.bfloat16)
+    tgt = torch.randint(0, V, (M1,), generator=g, device=dev)
+    row_loss = torch.empty(M1, device=dev)
+    gtab = torch.empty(_lib.GELU_TABLE_FLOATS, device=dev)
+    _lib.check(L.pnft_gelu_table(gtab.data_ptr(), st), "pnft_gelu_table")
+    lnb = L.pnft_layernorm_bwd_workspace_size(M, C)
+    cb = L.pnft_colsum_workspace_size(M, H)
+    w, b = torch.ones(C, device=dev), torch.zeros(C, device=dev)
+    dw, db, db1 = torch.empty(C, device=dev), torch.empty(C, device=dev), torch.empty(H, device=dev)
+    sets = []
+    for _ in range(3):
+        o = {"x": torch.randn(M, C, generator=g, device=dev),
+             "r": torch.randn(M, C, generator=g, device=dev).to(torch.bfloat16),
+             "s": torch.empty(M, C, device=dev), "y": torch.empty(M, C, device=dev, dtype=torch.bfloat16),
+             "mean": torch.empty(M, device=dev), "rstd": torch.empty(M, device=dev),
+             "gy": torch.randn(M, C, generator=g, device=dev).to(torch.bfloat16),
+             "gs": torch.randn(M, C, generator=g, device=dev), "dx": torch.empty(M, C, device=dev),
+             "dr": torch.empty(M, C, device=dev, dtype=torch.bfloat16),
+             "lnws": torch.empty(lnb, dtype=torch.uint8, device=dev),
+             "dh": torch.randn(M, H, generator=g, device=dev).to(torch.bfloat16),
+             "a0": torch.randn(M, H, generator=g, device=dev).to(torch.bfloat16),
+             "da": torch.empty(M, H, device=dev, dtype=torch.bfloat16),
+             "cws": torch.empty(cb, dtype=torch.uint8, device=dev)}
+        sets.append(o)
+    calls = {
+        "head_xent": (lambda o: L.pnft_lm_xent(logits.data_ptr(), ld, tgt.data_ptr(), -100, row_loss.data_ptr(),
+                                               M1, V, 1.0, None, None, st), 2 * M1 * ld * 2,
+                      f"[{M1}, {ld}] bf16 logits -> loss + gradient in place"),
+        "add_layernorm_fwd": (lambda o: L.pnft_add_layernorm_fwd(
+            o["x"].data_ptr(), C, o["r"].data_ptr(), C, BF, o["s"].data_ptr(), C, w.data_ptr(), b.data_ptr(), 1e-5,
+            o["y"].data_ptr(), C, o["mean"].data_ptr(), o["rstd"].data_ptr(), M, C, F32, BF, st),
+            M * C * (4 + 2 + 4 + 2), f"[{M}, {C}]: x f32 + r bf16 -> s f32, y bf16"),
+        "add_layernorm_bwd": (lambda o: L.pnft_add_layernorm_bwd(
+            o["gy"].data_ptr(), C, o["gs"].data_ptr(), C, o["s"].data_ptr(), C, w.data_ptr(), o["mean"].data_ptr(),
+            o["rstd"].data_ptr(), o["dx"].data_ptr(), C, o["dr"].data_ptr(), C, BF, dw.data_ptr(), db.data_ptr(),
+            o["lnws"].data_ptr(), lnb, M, C, BF, F32, st),
+            M * C * (2 + 4 + 4 + 4 + 2), f"[{M}, {C}]: dy bf16, s f32, gs f32 -> dx f32, dr bf16, dgamma, dbeta"),
+        "gelu_bwd_colsum": (lambda o: L.pnft_gelu_bwd_colsum(
+            o["dh"].data_ptr(), H, o["a0"].data_ptr(), H, o["da"].data_ptr(), H, db1.data_ptr(), o["cws"].data_ptr(),
+            cb, M, H, BF, gtab.data_ptr(), st), M * H * 6, f"[{M}, {H}] bf16: dh, a -> da, bias gradient"),
+        "gelu_fwd": (lambda o: L.pnft_gelu_fwd(o["a0"].data_ptr(), H, o["da"].data_ptr(), H, M, H, BF,
+                                              gtab.data_ptr(), st), M * H * 4, f"[{M}, {H}] bf16"),
+    }
+    for name, (fn, _, _) in calls.items():
+        _lib.check(fn(sets[0]), name)
+    torch.cuda.synchronize()
+    peak = measured_peaks().get("hbm_gbs")
+    res = {}
+    s_, e_ = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    for name, (fn, nbytes, what) in calls.items():
+        for i in range(3):
+            fn(sets[i % 3])
+        s_.record()
+        for i in range(iters):
+            fn(sets[i % 3])
+        e_.record()
+        torch.cuda.synchronize()
+        us = s_.elapsed_time(e_) / iters * 1e3
+        gbs = nbytes / us / 1e3
+        res[name] = {"us": round(us, 2), "GB/s": round(gbs, 1), "frac_of_hbm": round(gbs / peak, 3) if peak else None,
+                     "what": what}
+    res["note"] = ("each kernel alone, CUDA events, operands rotated over three sets (the cross-entropy's logits "
+                   "exceed L2 on their own); the same kernels inside the LM step: profiles/lm_step_kernels.md")
+    return res
+
+
 def bench_fir(args, dist_: Dist, dev, iters: int = 20) -> dict:
     """Standalone causal FIR (triton_causal_fir, 7 Gaussian taps, bf16) as achieved
     HBM GB/s: bytes = one read of x + one write of y per pass (the 6-row halo
@@ -939,6 +1028,11 @@ def main():
         res = bench_reference(args, dist_)
         if res is not None:
             print(json.dumps(res), file=out, flush=True)
+        return
+    if args.lm_kernels_only:
+        dev = torch.device("cuda", dist_.local_rank)
+        torch.cuda.set_device(dev)
+        print(json.dumps({"lm_kernels": bench_lm_kernels(args, dev)}), file=out, flush=True)
         return
     res = bench_ours(args, dist_)
     if dist_.rank == 0:

@@ -49,6 +49,9 @@ def test_bench_json_contract_gpu():
     assert e2e["h2d_bytes_per_step"] == 4 * 8 * 8 * 4096 * 64 * 2 and e2e["d2h_bytes_per_step"] == 4 * 8 * 8 * 4096 * 64 * 2 + 4
     assert d["gpu_launches"] > 0 and "sm_mhz" in d["clocks"] and "reasons" in d["clocks"]
     assert d["fir"]["c5_k_8x16384x2048"]["GB/s"] > 0 and d["fir"]["lm_k_32x512x256"]["device_GB/s"] > 0
+    lk = d["lm_kernels"]
+    for k in ("head_xent", "add_layernorm_fwd", "add_layernorm_bwd", "gelu_bwd_colsum", "gelu_fwd"):
+        assert lk[k]["us"] > 0 and 0 < lk[k]["frac_of_hbm"] < 1.2, (k, lk[k])
     assert rf["traffic"] > 1e8 and "profiles/" in rf["traffic_source"]
     # config 3's tau sweep: silence only at +0.5, where about half the causal tiles skip
     sw = d["tau_sweep"]
@@ -58,6 +61,18 @@ def test_bench_json_contract_gpu():
     assert d["deterministic"]["value"] > 0
     c5 = d["c5"]
     assert c5["heads_per_rank"] == 128 and c5["value"] > 0 and c5["roofline"]["frac"] > 0
+
+
+@pytest.mark.gpu
+def test_bench_lm_section_gpu():
+    """Config 4's LM step in the bench line: the graph-captured step (headline)
+    and the eager one, same losses from the same weights and batches."""
+    d = _run_bench(["--steps", "3", "--warmup", "3", "--no-e2e", "--no-fir", "--no-sweep", "--no-c5", "--no-cpu",
+                    "--no-triton", "--no-lm-kernels", "--lm-steps", "2"], timeout=900)
+    lm = d["lm"]
+    assert lm["tokens_per_s"] > 0 and lm["tokens_per_s_eager"] > 0 and lm["params"] == 13383174
+    assert lm["global_batch"] == 32 and lm["seq_len"] == 512
+    assert abs(lm["loss"] - lm["loss_eager"]) < 1e-2 * abs(lm["loss_eager"])
 
 
 @pytest.mark.gpu
