@@ -763,7 +763,10 @@ def bench_lm_kernels(args, dev, iters: int = 10) -> dict:
     + bias gradient over [16384, 1024]. Each entry point is called once first
     (the order an ncu capture sees), then timed with CUDA events; three operand
     sets rotate so every pass reads more than L2 holds. GB/s counts the
-    algorithmic bytes (each operand read or written once)."""
+    algorithmic bytes (each operand read or written once). The timed loop
+    launches back to back from the host; the weight-gradient GEMMs are timed
+    from a replayed CUDA graph of the same calls (their host-side setup, two
+    tensor-map encodes per call, would otherwise be timed)."""
     from paper_01_anti_decoy_pnfirtau_b200 import _lib
 
     L = _lib.lib()
@@ -781,6 +784,9 @@ def bench_lm_kernels(args, dev, iters: int = 10) -> dict:
     cb = L.pnft_colsum_workspace_size(M, H)
     w, b = torch.ones(C, device=dev), torch.zeros(C, device=dev)
     dw, db, db1 = torch.empty(C, device=dev), torch.empty(C, device=dev), torch.empty(H, device=dev)
+    wg1, wg2 = torch.empty(H, C, device=dev), torch.empty(C, C, device=dev)
+    wgb = max(L.pnft_gemm_at_b_workspace_size(M, H, C), L.pnft_gemm_at_b_workspace_size(M, C, C))
+    wgws = torch.empty(max(wgb, 16), dtype=torch.uint8, device=dev)
     sets = []
     for _ in range(3):
         o = {"x": torch.randn(M, C, generator=g, device=dev),
@@ -797,42 +803,72 @@ def bench_lm_kernels(args, dev, iters: int = 10) -> dict:
              "cws": torch.empty(cb, dtype=torch.uint8, device=dev)}
         sets.append(o)
     calls = {
-        "head_xent": (lambda o: L.pnft_lm_xent(logits.data_ptr(), ld, tgt.data_ptr(), -100, row_loss.data_ptr(),
+        "head_xent": (lambda o, st: L.pnft_lm_xent(logits.data_ptr(), ld, tgt.data_ptr(), -100, row_loss.data_ptr(),
                                                M1, V, 1.0, None, None, st), 2 * M1 * ld * 2,
                       f"[{M1}, {ld}] bf16 logits -> loss + gradient in place"),
-        "add_layernorm_fwd": (lambda o: L.pnft_add_layernorm_fwd(
+        "add_layernorm_fwd": (lambda o, st: L.pnft_add_layernorm_fwd(
             o["x"].data_ptr(), C, o["r"].data_ptr(), C, BF, o["s"].data_ptr(), C, w.data_ptr(), b.data_ptr(), 1e-5,
             o["y"].data_ptr(), C, o["mean"].data_ptr(), o["rstd"].data_ptr(), M, C, F32, BF, st),
             M * C * (4 + 2 + 4 + 2), f"[{M}, {C}]: x f32 + r bf16 -> s f32, y bf16"),
-        "add_layernorm_bwd": (lambda o: L.pnft_add_layernorm_bwd(
+        "add_layernorm_bwd": (lambda o, st: L.pnft_add_layernorm_bwd(
             o["gy"].data_ptr(), C, o["gs"].data_ptr(), C, o["s"].data_ptr(), C, w.data_ptr(), o["mean"].data_ptr(),
             o["rstd"].data_ptr(), o["dx"].data_ptr(), C, o["dr"].data_ptr(), C, BF, dw.data_ptr(), db.data_ptr(),
             o["lnws"].data_ptr(), lnb, M, C, BF, F32, st),
             M * C * (2 + 4 + 4 + 4 + 2), f"[{M}, {C}]: dy bf16, s f32, gs f32 -> dx f32, dr bf16, dgamma, dbeta"),
-        "gelu_bwd_colsum": (lambda o: L.pnft_gelu_bwd_colsum(
+        "gelu_bwd_colsum": (lambda o, st: L.pnft_gelu_bwd_colsum(
             o["dh"].data_ptr(), H, o["a0"].data_ptr(), H, o["da"].data_ptr(), H, db1.data_ptr(), o["cws"].data_ptr(),
             cb, M, H, BF, gtab.data_ptr(), st), M * H * 6, f"[{M}, {H}] bf16: dh, a -> da, bias gradient"),
-        "gelu_fwd": (lambda o: L.pnft_gelu_fwd(o["a0"].data_ptr(), H, o["da"].data_ptr(), H, M, H, BF,
+        "gelu_fwd": (lambda o, st: L.pnft_gelu_fwd(o["a0"].data_ptr(), H, o["da"].data_ptr(), H, M, H, BF,
                                               gtab.data_ptr(), st), M * H * 4, f"[{M}, {H}] bf16"),
+        # weight gradients dW = dY^T X of the MLP's first layer ([1024, 256] over 16384 tokens) and of the
+        # attention's output projection ([256, 256])
+        "weight_grad_fc1": (lambda o, st: L.pnft_gemm_at_b(o["da"].data_ptr(), H, o["gy"].data_ptr(), C,
+                                                       wg1.data_ptr(), C, wgws.data_ptr(), wgb, M, H, C, BF, None,
+                                                       st), (M * H + M * C) * 2 + H * C * 4,
+                            f"[{M}, {H}]^T x [{M}, {C}] bf16 -> [{H}, {C}] fp32, split-K tcgen05"),
+        "weight_grad_out": (lambda o, st: L.pnft_gemm_at_b(o["gy"].data_ptr(), C, o["r"].data_ptr(), C,
+                                                       wg2.data_ptr(), C, wgws.data_ptr(), wgb, M, C, C, BF, None,
+                                                       st), (M * C + M * C) * 2 + C * C * 4,
+                            f"[{M}, {C}]^T x [{M}, {C}] bf16 -> [{C}, {C}] fp32, split-K tcgen05"),
     }
     for name, (fn, _, _) in calls.items():
-        _lib.check(fn(sets[0]), name)
+        _lib.check(fn(sets[0], st), name)
     torch.cuda.synchronize()
     peak = measured_peaks().get("hbm_gbs")
     res = {}
     s_, e_ = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     for name, (fn, nbytes, what) in calls.items():
         for i in range(3):
-            fn(sets[i % 3])
-        s_.record()
-        for i in range(iters):
-            fn(sets[i % 3])
-        e_.record()
-        torch.cuda.synchronize()
+            fn(sets[i % 3], st)
+        if name.startswith("weight_grad"):
+            # device time from a replayed graph of the calls (their host-side setup is not timed)
+            side = torch.cuda.Stream(dev)
+            side.wait_stream(torch.cuda.current_stream(dev))
+            graph = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(graph, stream=side):
+                for i in range(iters):
+                    _lib.check(fn(sets[i % 3], side.cuda_stream), name)
+            torch.cuda.current_stream(dev).wait_stream(side)
+            graph.replay()
+            torch.cuda.synchronize()
+            s_.record()
+            graph.replay()
+            e_.record()
+            torch.cuda.synchronize()
+            del graph
+        else:
+            s_.record()
+            for i in range(iters):
+                fn(sets[i % 3], st)
+            e_.record()
+            torch.cuda.synchronize()
         us = s_.elapsed_time(e_) / iters * 1e3
         gbs = nbytes / us / 1e3
         res[name] = {"us": round(us, 2), "GB/s": round(gbs, 1), "frac_of_hbm": round(gbs / peak, 3) if peak else None,
                      "what": what}
+        if name.startswith("weight_grad"):
+            mm = H if name.endswith("fc1") else C
+            res[name]["TFLOP/s"] = round(2 * M * mm * C / us / 1e6, 1)
     res["note"] = ("each kernel alone, CUDA events, operands rotated over three sets (the cross-entropy's logits "
                    "exceed L2 on their own); the same kernels inside the LM step: profiles/lm_step_kernels.md")
     return res

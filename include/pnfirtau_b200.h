@@ -368,6 +368,22 @@ PNFT_API size_t pnft_colsum_workspace_size(int64_t M, int64_t C);
  * pnft_gelu_fwd (GELU' of bfloat16 a; NULL: computed per CTA).
  * Replaces: nn.GELU's backward and grad_output.sum(0) of the first nn.Linear
  * (same call sites). */
+/* Weight gradient of a Linear layer: C[M x N] (fp32, row stride ldc) = A^T B,
+ * A [K x M] and B [K x N] bfloat16 rows (row strides lda / ldb, multiples of 8;
+ * M and N multiples of 8; 16-byte aligned bases), i.e. dW = dY^T X with K the
+ * token count. tcgen05 MMAs with the K reduction split over the SMs; the splits'
+ * fp32 partials (workspace: pnft_gemm_at_b_workspace_size(K, M, N) bytes,
+ * 16-byte aligned; 0 bytes when one split suffices) are added in a fixed order.
+ * sm_100 devices only (PNFT_EUNSUPPORTED elsewhere). status: as the flash entry
+ * points (bounded pipeline waits).
+ * Replaces: the weight-gradient GEMM of nn.Linear's backward in the Pre-LN
+ * blocks (experiments/exp4_wikitext2_lm.py:183-200). */
+PNFT_API int pnft_gemm_at_b(const void* a, int64_t lda, const void* b, int64_t ldb, float* c, int64_t ldc,
+                   void* workspace, size_t workspace_bytes, int64_t K, int64_t M, int64_t N, int dtype,
+                   int32_t* status, void* stream);
+
+PNFT_API size_t pnft_gemm_at_b_workspace_size(int64_t K, int64_t M, int64_t N);
+
 /* Floats of the GELU lookup table (GELU and GELU' of every bfloat16 a with
  * |a| in [2^-16, 16)), built by pnft_gelu_table. */
 #define PNFT_GELU_TABLE_FLOATS 10240

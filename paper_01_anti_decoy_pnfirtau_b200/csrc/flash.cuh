@@ -125,6 +125,10 @@ int head_group(int64_t BH, int64_t head_bytes);
 int tma_map_bhnd(CUtensorMap* m, const void* base, const int64_t* s, int64_t B, int64_t H, int64_t N, int64_t D,
                  int rows);
 bool tma_ok_bhnd(const void* ptr, const int64_t* s);
+// 2-D bf16 map over `rows` rows of `cols` elements (row stride in elements, a
+// multiple of 8; base 16-byte aligned): boxes of 64 columns x box_rows rows,
+// 128-byte swizzled, out-of-range elements read as zero.
+int tma_map_rows(CUtensorMap* m, const void* base, int64_t cols, int64_t rows, int64_t row_stride, int box_rows);
 bool device_is_sm100();
 
 }  // namespace pnft

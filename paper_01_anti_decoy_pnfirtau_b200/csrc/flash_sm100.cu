@@ -617,6 +617,20 @@ int tma_map_bhnd(CUtensorMap* m, const void* base, const int64_t* s, int64_t B, 
   return PNFT_OK;
 }
 
+int tma_map_rows(CUtensorMap* m, const void* base, int64_t cols, int64_t rows, int64_t row_stride, int box_rows) {
+  EncodeTiledFn enc = encode_fn();
+  if (!enc) return fail(PNFT_ECUDA, "cuTensorMapEncodeTiled unavailable from the driver");
+  const cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
+  const cuuint64_t strides[1] = {(cuuint64_t)row_stride * 2};
+  const cuuint32_t box[2] = {64, (cuuint32_t)box_rows};
+  const cuuint32_t estr[2] = {1, 1};
+  const CUresult r = enc(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims, strides, box, estr,
+                         CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                         CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return fail(PNFT_ECUDA, "cuTensorMapEncodeTiled failed (%d)", (int)r);
+  return PNFT_OK;
+}
+
 bool tma_ok_bhnd(const void* ptr, const int64_t* s) {
   if ((reinterpret_cast<uintptr_t>(ptr) & 15) != 0) return false;
   if (s[3] != 1) return false;

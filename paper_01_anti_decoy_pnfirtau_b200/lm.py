@@ -9,8 +9,9 @@ x + ffn(ln2 x)) -> ln_f -> head tied to the embedding.
 With ``fused_step_ops`` (default) the step's non-attention work runs on this
 library's kernels (lm_ops): each residual add fused with the LayerNorm after
 it (output written in the autocast dtype), the MLP's GELU backward fused with
-its bias gradients, and the head's loss and logit gradient in one pass over the
-logits. With ``fused_step_ops=False`` the blocks are nn.LayerNorm, nn.Linear,
+its bias gradients, the weight gradients of the projections and the MLP from a
+split-K tcgen05 GEMM, and the head's loss and logit gradient in one pass over
+the logits. With ``fused_step_ops=False`` the blocks are nn.LayerNorm, nn.Linear,
 nn.GELU and F.cross_entropy. Parameters and state_dict keys are the same either
 way.
 """
@@ -22,7 +23,7 @@ import torch
 import torch.nn as nn
 import torch.nn.functional as F
 
-from .lm_ops import LayerNorm, add_layer_norm, head_cross_entropy, mlp_gelu
+from .lm_ops import LayerNorm, Linear, add_layer_norm, head_cross_entropy, mlp_gelu
 from .pnfirtau_attention import PnFirConfig, PnFirTauFlashMHA, PnFirTauMHA, PnFirTauTritonMHA
 
 _VARIANTS = {"pn_fir_tau": PnFirTauMHA, "pn_fir_tau_triton": PnFirTauTritonMHA, "pn_fir_tau_flash": PnFirTauFlashMHA}
@@ -77,6 +78,11 @@ class PnFirLM(nn.Module):
         self.blocks = nn.ModuleList(
             Block(cfg.d_model, cls(acfg), cfg.dropout, cfg.d_ff, norm) for _ in range(cfg.n_layers))
         self.ln_f = norm(cfg.d_model)
+        if fused_step_ops:
+            # the attention's projections with the library's weight-gradient GEMM (same parameters)
+            for blk in self.blocks:
+                for name in ("qkv", "out"):
+                    setattr(blk.attn, name, Linear.sharing(getattr(blk.attn, name)))
         self.head = nn.Linear(cfg.d_model, cfg.vocab, bias=False)
         self.head.weight = self.embed.weight
 

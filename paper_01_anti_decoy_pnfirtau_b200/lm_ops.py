@@ -20,6 +20,9 @@ language-model experiments (experiments/exp4_wikitext2_lm.py:183-259, loss at
   (tabulated the same way) with ``fc1``'s bias gradient, sums
   ``fc2``'s bias gradient with the same column-sum kernel (both fp32, fixed
   order) and produces the weight gradients from fp32-output GEMMs.
+- ``Linear``: ``nn.Linear`` whose weight gradient comes from a split-K
+  tcgen05 GEMM (the few, long reductions of dW = dY^T X over 16K tokens leave a
+  library GEMM with too few CTAs); ``mlp_gelu`` uses the same kernel.
 - ``head_cross_entropy``: ``F.cross_entropy(h @ W.T, targets)`` (mean over
   the rows whose target is not ``ignore_index``) with the bf16 head GEMM of
   autocast, and the loss and the logit gradient produced by one kernel pass over
@@ -246,6 +249,36 @@ def _mm_f32(a: torch.Tensor, b: torch.Tensor) -> torch.Tensor:
     return torch.mm(a, b) if a.dtype == torch.float32 else torch.mm(a, b, out_dtype=torch.float32)
 
 
+_SM100: dict[int, bool] = {}
+
+
+def _is_sm100(dev: torch.device) -> bool:
+    idx = dev.index if dev.index is not None else torch.cuda.current_device()
+    if idx not in _SM100:
+        _SM100[idx] = torch.cuda.get_device_capability(idx) == (10, 0)
+    return _SM100[idx]
+
+
+def _weight_grad(dy: torch.Tensor, x: torch.Tensor) -> torch.Tensor:
+    """dW = dy^T x in fp32 (dy [K, M], x [K, N]: a Linear layer's weight gradient
+    over K tokens): the split-K tcgen05 kernel (pnft_gemm_at_b) for bf16 rows it
+    serves, else a library GEMM with fp32 output."""
+    K, M = dy.shape
+    N = x.shape[1]
+    dev = dy.device
+    if (dy.dtype == x.dtype == torch.bfloat16 and _is_sm100(dev) and M % 8 == 0 and N % 8 == 0
+            and dy.stride(1) == 1 and x.stride(1) == 1 and dy.stride(0) % 8 == 0 and x.stride(0) % 8 == 0
+            and dy.data_ptr() % 16 == 0 and x.data_ptr() % 16 == 0):
+        out = torch.empty((M, N), dtype=torch.float32, device=dev)
+        nbytes = _lib.lib().pnft_gemm_at_b_workspace_size(K, M, N)
+        ws = torch.empty(max(nbytes, 16), dtype=torch.uint8, device=dev)
+        _lib.check(_lib.lib().pnft_gemm_at_b(dy.data_ptr(), dy.stride(0), x.data_ptr(), x.stride(0), out.data_ptr(), N,
+                                             ws.data_ptr(), nbytes, K, M, N, _lib.DTYPE_BF16, _status_ptr(dev),
+                                             _stream(dev)), "pnft_gemm_at_b")
+        return out
+    return _mm_f32(dy.t(), x)
+
+
 class _MlpGeluFn(torch.autograd.Function):
     @staticmethod
     def forward(ctx, x, w1, b1, w2, b2, dt: torch.dtype):
@@ -275,7 +308,7 @@ class _MlpGeluFn(torch.autograd.Function):
         st = _stream(dev)
         dw1 = db1 = dw2 = db2 = dx = None
         if ctx.needs_input_grad[3]:
-            dw2 = _mm_f32(g2.t(), a1)
+            dw2 = _weight_grad(g2, a1)
         if ctx.needs_input_grad[4]:
             db2 = torch.empty(Dout, dtype=torch.float32, device=dev)
             ws, nb = _colsum_ws(M, Dout, dev)
@@ -290,7 +323,7 @@ class _MlpGeluFn(torch.autograd.Function):
                                           _ln_code(dt, "mlp_gelu"), _ptr(_gelu_table(dev)), st),
                    "pnft_gelu_bwd_colsum")
         if ctx.needs_input_grad[1]:
-            dw1 = _mm_f32(da0.t(), x2)
+            dw1 = _weight_grad(da0, x2)
         if ctx.needs_input_grad[0]:
             dx = torch.mm(da0, w1c).to(ctx.x_dtype).view(ctx.x_shape)
         pw1, pb1, pw2, pb2 = ctx.p_dtypes
@@ -306,6 +339,63 @@ def mlp_gelu(x: torch.Tensor, fc1: nn.Linear, fc2: nn.Linear) -> torch.Tensor:
     if dt not in _LN_DTYPES:
         dt = torch.float32
     return _MlpGeluFn.apply(x, fc1.weight, fc1.bias, fc2.weight, fc2.bias, dt)
+
+
+class _LinearFn(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, x, weight, bias, dt: torch.dtype):
+        _require_cuda("Linear", x, weight)
+        D = x.shape[-1]
+        x2 = x.reshape(-1, D).to(dt)
+        x2 = x2 if x2.stride(-1) == 1 else x2.contiguous()
+        w = weight.to(dt)
+        y = torch.addmm(bias.to(dt), x2, w.t()) if bias is not None else torch.mm(x2, w.t())
+        ctx.save_for_backward(x2, w)
+        ctx.x_shape, ctx.x_dtype = x.shape, x.dtype
+        ctx.p_dtypes = (weight.dtype, None if bias is None else bias.dtype)
+        return y.view(*x.shape[:-1], y.shape[-1])
+
+    @staticmethod
+    def backward(ctx, g):
+        x2, w = ctx.saved_tensors
+        dt, dev = x2.dtype, x2.device
+        Dout = w.shape[0]
+        g2 = _rows(g, Dout, dt, like=dt)
+        dx = dw = db = None
+        if ctx.needs_input_grad[0]:
+            dx = torch.mm(g2, w).to(ctx.x_dtype).view(ctx.x_shape)
+        if ctx.needs_input_grad[1]:
+            dw = _weight_grad(g2, x2).to(ctx.p_dtypes[0])
+        if ctx.needs_input_grad[2]:
+            db = torch.empty(Dout, dtype=torch.float32, device=dev)
+            ws, nb = _colsum_ws(g2.shape[0], Dout, dev)
+            _lib.check(_lib.lib().pnft_colsum(g2.data_ptr(), g2.stride(0), db.data_ptr(), ws.data_ptr(), nb,
+                                              g2.shape[0], Dout, _ln_code(dt, "Linear"), _stream(dev)), "pnft_colsum")
+            db = db.to(ctx.p_dtypes[1])
+        return dx, dw, db, None
+
+
+class Linear(nn.Linear):
+    """``nn.Linear`` (same parameters and state_dict keys) whose forward is the
+    autocast GEMM and whose backward computes the weight gradient with the
+    split-K tcgen05 kernel (``pnft_gemm_at_b``, fp32) and the bias gradient
+    with the fixed-order column sum. ``Linear.sharing(lin)`` wraps an existing
+    layer's parameters without re-initialising anything."""
+
+    def forward(self, x: torch.Tensor) -> torch.Tensor:
+        dt = _autocast_dtype(x)
+        if dt not in _LN_DTYPES:
+            dt = torch.float32
+        return _LinearFn.apply(x, self.weight, self.bias, dt)
+
+    @classmethod
+    def sharing(cls, lin: nn.Linear) -> "Linear":
+        new = torch.nn.utils.skip_init(cls, lin.in_features, lin.out_features, bias=lin.bias is not None,
+                                       device=lin.weight.device, dtype=lin.weight.dtype)
+        new.weight = lin.weight
+        if lin.bias is not None:
+            new.bias = lin.bias
+        return new
 
 
 class _HeadXentFn(torch.autograd.Function):

@@ -15,7 +15,8 @@ import torch.nn.functional as F
 from conftest import rel_l2
 from paper_01_anti_decoy_pnfirtau_b200 import _lib
 from paper_01_anti_decoy_pnfirtau_b200.lm import LMConfig, PnFirLM, lm_loss, make_optimizer, train_step
-from paper_01_anti_decoy_pnfirtau_b200.lm_ops import LayerNorm, add_layer_norm, head_cross_entropy, layer_norm, mlp_gelu
+from paper_01_anti_decoy_pnfirtau_b200.lm_ops import (LayerNorm, Linear, add_layer_norm, head_cross_entropy, layer_norm,
+                                                     mlp_gelu)
 from paper_01_anti_decoy_pnfirtau_b200.pnfirtau_ops import _status_ptr, check_device_status
 
 pytestmark = pytest.mark.gpu
@@ -283,6 +284,63 @@ def test_gelu_fwd_against_pytorch(cuda, dtype):
             assert (y.float() == ref.to(dtype).float()).float().mean() > 0.995
         else:
             assert torch.allclose(y, ref, rtol=2e-6, atol=1e-30)
+
+
+GEMM_CASES = {
+    # name: (K, M, N, lda pad, ldb pad)
+    "lm_fc2": (16384, 256, 1024, 0, 0),
+    "lm_qkv": (16384, 768, 256, 0, 0),
+    "lm_out": (16384, 256, 256, 0, 0),
+    "ragged": (5000, 136, 72, 0, 0),
+    "one_split": (300, 128, 128, 0, 0),
+    "strided": (4096, 64, 192, 16, 8),
+}
+
+
+@pytest.mark.parametrize("case", sorted(GEMM_CASES))
+def test_gemm_at_b_against_fp32(cuda, case):
+    """pnft_gemm_at_b (split-K tcgen05, weight gradients) against an fp32
+    product of the same bf16 operands; a rerun is bitwise equal."""
+    K, M, N, pa, pb = GEMM_CASES[case]
+    L = _lib.lib()
+    st = torch.cuda.current_stream().cuda_stream
+    g = torch.Generator(device=cuda).manual_seed(K + M + N)
+    a = torch.randn(K, M + pa, device=cuda, generator=g).to(torch.bfloat16)[:, :M]
+    b = torch.randn(K, N + pb, device=cuda, generator=g).to(torch.bfloat16)[:, :N]
+    nbytes = L.pnft_gemm_at_b_workspace_size(K, M, N)
+    ws = torch.empty(max(nbytes, 16), dtype=torch.uint8, device=cuda)
+    outs = []
+    for _ in range(2):
+        c = torch.full((M, N), float("nan"), device=cuda)
+        _lib.check(L.pnft_gemm_at_b(a.data_ptr(), a.stride(0), b.data_ptr(), b.stride(0), c.data_ptr(), N,
+                                    ws.data_ptr(), nbytes, K, M, N, _lib.DTYPE_BF16, _status_ptr(cuda), st),
+                   "pnft_gemm_at_b")
+        outs.append(c)
+    check_device_status(cuda)
+    ref = a.float().t() @ b.float()
+    assert torch.isfinite(outs[0]).all()
+    assert (outs[0] - ref).abs().max() <= 1e-5 * ref.abs().max() + 1e-6 * K ** 0.5, float((outs[0] - ref).abs().max())
+    assert torch.equal(outs[0], outs[1])
+
+
+def test_linear_module_matches_nn_linear(cuda):
+    """lm_ops.Linear (weight gradient from pnft_gemm_at_b, bias gradient from the
+    column sum) against nn.Linear under bf16 autocast on the same parameters."""
+    torch.manual_seed(2)
+    ref = torch.nn.Linear(256, 768).to(cuda)
+    lin = Linear.sharing(torch.nn.Linear(256, 768).to(cuda))
+    lin.load_state_dict(ref.state_dict())
+    x = torch.randn(32, 512, 256, device=cuda)
+    xa, xb = x.clone().requires_grad_(True), x.clone().requires_grad_(True)
+    gy = torch.randn(32, 512, 768, device=cuda).to(torch.bfloat16)
+    with torch.autocast("cuda", dtype=torch.bfloat16):
+        ya, yb = lin(xa), ref(xb)
+    assert ya.dtype == yb.dtype == torch.bfloat16 and torch.equal(ya, yb)
+    ya.backward(gy)
+    yb.backward(gy)
+    assert rel_l2(xa.grad, xb.grad) < 1e-2
+    # the library's gradients are fp32 sums of the bf16 products; autocast's are rounded to bf16
+    assert rel_l2(lin.weight.grad, ref.weight.grad) < 5e-3 and rel_l2(lin.bias.grad, ref.bias.grad) < 5e-3
 
 
 def _lm_pair(cuda, N=128, B=4):
