@@ -410,9 +410,9 @@ __global__ void __launch_bounds__(LT) ln_fwd_kernel(LnFwdArgs a) {
   const int64_t nwarp = (int64_t)gridDim.x * LWARPS;
   const int C = a.C;
   const float invC = 1.f / (float)C;
-  const TX* x = static_cast<const TX*>(a.x);
-  TY* y = static_cast<TY*>(a.y);
-  TX* sum = static_cast<TX*>(a.s);
+  const TX* __restrict__ x = static_cast<const TX*>(a.x);
+  TY* __restrict__ y = static_cast<TY*>(a.y);
+  TX* __restrict__ sum = static_cast<TX*>(a.s);
   if constexpr (VPL > 0) {
     float g[VPL][4], b[VPL][4];
 #pragma unroll
@@ -516,10 +516,10 @@ __global__ void __launch_bounds__(LT, 2) ln_bwd_kernel(LnBwdArgs a) {
   const int64_t nwarp = (int64_t)gridDim.x * LWARPS;
   const int C = a.C;
   const float invC = 1.f / (float)C;
-  const TDY* dy = static_cast<const TDY*>(a.dy);
-  const TX* x = static_cast<const TX*>(a.x);
-  const TX* gs = static_cast<const TX*>(a.gs);
-  TX* dx = static_cast<TX*>(a.dx);
+  const TDY* __restrict__ dy = static_cast<const TDY*>(a.dy);
+  const TX* __restrict__ x = static_cast<const TX*>(a.x);
+  const TX* __restrict__ gs = static_cast<const TX*>(a.gs);
+  TX* __restrict__ dx = static_cast<TX*>(a.dx);
   if constexpr (VPL > 0) {
     float g[VPL][4], dg[VPL][4], db[VPL][4];
 #pragma unroll
@@ -829,12 +829,21 @@ __global__ void gelu_table_kernel(float* out) {
   }
 }
 
+// Table index of a bf16 bit pattern: sign-major, then binade, then mantissa, i.e.
+// (bits & 0x7FFF) - (kGeluE0 << 7) + sign * kGeluNE * 128 over a contiguous range.
+// Outside the table GELU has closed forms to fp32 precision: for |a| >= 16,
+// Phi(a) is 1 or 0 and a*phi(a) underflows (GELU = a or -0, GELU' = 1 or 0;
+// NaN and -inf give NaN like the erf formula); for |a| < 2^-16, Phi(a) =
+// 0.5 + a*phi(0) and phi(a) = phi(0) to within a relative a^2 (GELU =
+// 0.5a + phi(0)a^2, GELU' = 0.5 + 2 phi(0) a).
 template <bool GRAD>
 __device__ __forceinline__ float gelu_lookup(const float* tbl, uint32_t bits16) {
-  const uint32_t de = ((bits16 >> 7) & 0xFFu) - kGeluE0;
-  if (de < (uint32_t)kGeluNE) return tbl[((bits16 >> 15) * kGeluNE + de) * 128 + (bits16 & 0x7Fu)];
+  constexpr float kPhi0 = 0.39894228040143268f;  // 1/sqrt(2 pi)
+  const uint32_t mag = bits16 & 0x7FFFu, off = mag - ((uint32_t)kGeluE0 << 7);
+  if (off < (uint32_t)(kGeluNE * 128)) return tbl[off + (bits16 >> 15) * (kGeluNE * 128)];
   const float a = __uint_as_float(bits16 << 16);
-  return GRAD ? gelu_grad(a) : gelu_exact(a);
+  if (mag >= (uint32_t)(kGeluE0 + kGeluNE) << 7) return GRAD ? (a >= 0.f ? 1.f : a * 0.f) : (a >= 0.f ? a : a * 0.f);
+  return GRAD ? fmaf(a, 2.f * kPhi0, 0.5f) : fmaf(kPhi0 * a, a, 0.5f * a);
 }
 
 struct ColArgs {
@@ -865,9 +874,10 @@ __global__ void __launch_bounds__(LT) colsum_kernel(ColArgs p) {
     gelu_table_init<true>(gtab, p.table);
     __syncthreads();
   }
-  const T* g = static_cast<const T*>(p.g);
-  const T* av = static_cast<const T*>(p.a);
-  T* da = static_cast<T*>(p.da);
+  // distinct buffers: the next rows' loads may move above this row's stores
+  const T* __restrict__ g = static_cast<const T*>(p.g);
+  const T* __restrict__ av = static_cast<const T*>(p.a);
+  T* __restrict__ da = static_cast<T*>(p.da);
   const int vpr = p.C / VW;                 // column vectors per row
   const int jn = vpr < LT ? vpr : LT;       // vectors processed side by side
   const int par = LT / jn;                  // row lanes
@@ -879,6 +889,7 @@ __global__ void __launch_bounds__(LT) colsum_kernel(ColArgs p) {
 #pragma unroll
     for (int k = 0; k < VW; ++k) acc[k] = 0.f;
     if (trp < par && j < vpr) {
+#pragma unroll 4
       for (int64_t row = r0 + trp; row < r1; row += par) {
         float f[VW];
         if constexpr (VW == 8) {
@@ -890,20 +901,18 @@ __global__ void __launch_bounds__(LT) colsum_kernel(ColArgs p) {
           if constexpr (VW == 8) {
             const uint4 u = *reinterpret_cast<const uint4*>(av + row * p.sa + (int64_t)j * 8);
             const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+            uint32_t o[4];
 #pragma unroll
-            for (int k = 0; k < 8; ++k)  // the stored (rounded) value is what gets summed
-              f[k] = (float)from_f32<T>(f[k] * gelu_lookup<true>(gtab, k & 1 ? w[k / 2] >> 16 : w[k / 2] & 0xFFFFu));
+            for (int k = 0; k < 4; ++k) {
+              o[k] = sm100::pack_bf16x2(f[2 * k] * gelu_lookup<true>(gtab, w[k] & 0xFFFFu),
+                                        f[2 * k + 1] * gelu_lookup<true>(gtab, w[k] >> 16));
+              // the stored (rounded) values are what gets summed
+              f[2 * k] = __uint_as_float(o[k] << 16);
+              f[2 * k + 1] = __uint_as_float(o[k] & 0xffff0000u);
+            }
+            *reinterpret_cast<uint4*>(da + row * p.sda + (int64_t)j * 8) = make_uint4(o[0], o[1], o[2], o[3]);
           } else {
             f[0] = (float)from_f32<T>(f[0] * gelu_grad(to_f32(av[row * p.sa + j])));
-          }
-          if constexpr (VW == 8) {
-            uint4 o;
-            o.x = sm100::pack_bf16x2(f[0], f[1]);
-            o.y = sm100::pack_bf16x2(f[2], f[3]);
-            o.z = sm100::pack_bf16x2(f[4], f[5]);
-            o.w = sm100::pack_bf16x2(f[6], f[7]);
-            *reinterpret_cast<uint4*>(da + row * p.sda + (int64_t)j * 8) = o;
-          } else {
             da[row * p.sda + j] = from_f32<T>(f[0]);
           }
         }
@@ -953,24 +962,29 @@ int col_entry(ColArgs p, float* out, int dtype, cudaStream_t st) {
 // y = GELU(a) (exact erf form), rows of C elements with row strides sa / sy.
 // bf16 with 16-byte vectors: table lookups; otherwise the formula per element.
 template <typename T, bool VEC>
-__global__ void __launch_bounds__(LT) gelu_fwd_kernel(const T* a, int64_t sa, T* y, int64_t sy, int64_t M, int C,
-                                                     const float* table) {
+__global__ void __launch_bounds__(LT) gelu_fwd_kernel(const T* __restrict__ a, int64_t sa, T* __restrict__ y, int64_t sy,
+                                                     int64_t M, int C, const float* __restrict__ table) {
   __shared__ float gtab[VEC ? kGeluN : 1];
   if constexpr (VEC) {
     gelu_table_init<false>(gtab, table);
     __syncthreads();
+    // thread -> fixed column vector j of its rows (no index division in the loop)
     const int vpr = C / 8;
-    const int64_t n = M * vpr;
-    for (int64_t i = (int64_t)blockIdx.x * LT + threadIdx.x; i < n; i += (int64_t)gridDim.x * LT) {
-      const int64_t row = i / vpr;
-      const int j = (int)(i - row * vpr);
-      const uint4 u = *reinterpret_cast<const uint4*>(a + row * sa + (int64_t)j * 8);
-      const uint32_t w[4] = {u.x, u.y, u.z, u.w};
-      uint32_t o[4];
+    const int jn = vpr < LT ? vpr : LT, par = LT / jn;
+    const int tj = threadIdx.x % jn, trp = threadIdx.x / jn;
+    if (trp < par) {
+      for (int j = tj; j < vpr; j += jn) {
+#pragma unroll 4
+        for (int64_t row = (int64_t)blockIdx.x * par + trp; row < M; row += (int64_t)gridDim.x * par) {
+          const uint4 u = *reinterpret_cast<const uint4*>(a + row * sa + (int64_t)j * 8);
+          const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+          uint32_t o[4];
 #pragma unroll
-      for (int k = 0; k < 4; ++k)
-        o[k] = sm100::pack_bf16x2(gelu_lookup<false>(gtab, w[k] & 0xFFFFu), gelu_lookup<false>(gtab, w[k] >> 16));
-      *reinterpret_cast<uint4*>(y + row * sy + (int64_t)j * 8) = make_uint4(o[0], o[1], o[2], o[3]);
+          for (int k = 0; k < 4; ++k)
+            o[k] = sm100::pack_bf16x2(gelu_lookup<false>(gtab, w[k] & 0xFFFFu), gelu_lookup<false>(gtab, w[k] >> 16));
+          *reinterpret_cast<uint4*>(y + row * sy + (int64_t)j * 8) = make_uint4(o[0], o[1], o[2], o[3]);
+        }
+      }
     }
   } else {
     const int64_t n = M * C;
@@ -986,8 +1000,10 @@ template <typename T, bool VEC>
 int gelu_fwd_launch(const void* a, int64_t sa, void* y, int64_t sy, int64_t M, int64_t C, const float* table,
                     cudaStream_t st) {
   static const int per_sm = resident_per_sm(gelu_fwd_kernel<T, VEC>, 0);
-  const int64_t items = VEC ? M * (C / 8) : M * C;
-  const int grid = (int)std::max<int64_t>(1, std::min<int64_t>((items + LT - 1) / LT, (int64_t)per_sm * device_sms()));
+  // vector path: a CTA covers LT / (C/8) rows per pass (at least one); scalar path: LT elements
+  const int64_t rows_per_pass = VEC ? std::max<int64_t>(1, LT / std::max<int64_t>(1, C / 8)) : 1;
+  const int64_t items = VEC ? (M + rows_per_pass - 1) / rows_per_pass : (M * C + LT - 1) / LT;
+  const int grid = (int)std::max<int64_t>(1, std::min<int64_t>(items, (int64_t)per_sm * device_sms()));
   gelu_fwd_kernel<T, VEC><<<grid, LT, 0, st>>>(static_cast<const T*>(a), sa, static_cast<T*>(y), sy, M, (int)C, table);
   return check_launch("gelu fwd");
 }
