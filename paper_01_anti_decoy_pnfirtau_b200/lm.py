@@ -203,6 +203,11 @@ class GraphedTrainStep:
                     dist.broadcast(p, src=src, group=group)
         self.sizes = [p.numel() for p in self.params]
         self.flat = torch.empty(sum(self.sizes), dtype=torch.float32, device=dev) if self.world > 1 else None
+        # per-parameter views of the flat buffer: gradients are gathered into it and
+        # scattered back with multi-tensor copies (torch.cat of the 77 gradients runs the
+        # 34 MB embedding gradient on few blocks: 179 us against ~15 us)
+        self.flat_views = ([t.view_as(p) for t, p in zip(self.flat.split(self.sizes), self.params)]
+                           if self.world > 1 else None)
         self.idx = example_idx.detach().clone()
         saved_p = [p.detach().clone() for p in self.params]
         saved_s = {id(p): {k: (v.clone() if torch.is_tensor(v) else v) for k, v in opt.state[p].items()}
@@ -238,9 +243,9 @@ class GraphedTrainStep:
         loss.backward()
         if self.world > 1:
             grads = [p.grad for p in self.params]
-            torch.cat([g.reshape(-1) for g in grads], out=self.flat)
+            torch._foreach_copy_(self.flat_views, grads)
             dist.all_reduce(self.flat, op=dist.ReduceOp.AVG, group=self.group)
-            torch._foreach_copy_(grads, [t.view_as(g) for t, g in zip(self.flat.split(self.sizes), grads)])
+            torch._foreach_copy_(grads, self.flat_views)
         torch.nn.utils.clip_grad_norm_(self.params, self.clip)
         self.opt.step()
         return loss.detach()
