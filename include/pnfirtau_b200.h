@@ -243,9 +243,9 @@ PNFT_API size_t pnft_flash_bwd_workspace_size(int64_t B, int64_t H, int64_t N, i
  * its 8 preceding rows (zeros before the sequence start) and filtered in shared
  * memory into k~ = causal_fir(k, taps), bit-identical to pnft_fir_fwd, before the
  * QK^T MMA. taps: device fp32[PNFT_FIR_FUSED_TAPS], index 6 = lag 0. The other
- * arguments as pnft_flash_fwd. Served by the sm_100a kernels only (bf16, head dim
- * 64/128, 16-byte aligned rows with unit head-dim stride); other inputs return
- * PNFT_EUNSUPPORTED.
+ * arguments as pnft_flash_fwd. Served by the sm_100a kernels only (bf16, head dims
+ * that are multiples of 16 up to 128, 16-byte aligned rows with unit head-dim
+ * stride); other inputs return PNFT_EUNSUPPORTED.
  * Replaces: triton_causal_fir(k) followed by flash_pn_fir_tau_attention in
  * PnFirTauFlashMHA.forward (src/pnfirtau_attention.py:285-316,
  * src/triton_pnfirtau.py:685-691, 971-983). */

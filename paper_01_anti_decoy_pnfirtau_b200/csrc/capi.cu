@@ -92,7 +92,7 @@ static int fill_common(FlashArgs& a, const void* q, const int64_t* sq, const voi
   if (!sq || !sk || !sv) return fail(PNFT_EINVAL, "flash: null stride array");
   a.q = q; a.k = k; a.v = v; a.tau = tau;
   for (int i = 0; i < 4; ++i) { a.sq[i] = sq[i]; a.sk[i] = sk[i]; a.sv[i] = sv[i]; }
-  a.B = B; a.H = H; a.N = N; a.D = D; a.scale = scale; a.gamma = gamma; a.has_gamma = has_gamma;
+  a.B = B; a.H = H; a.N = N; a.D = D; a.acc_d = acc_width(D); a.scale = scale; a.gamma = gamma; a.has_gamma = has_gamma;
   a.causal = causal; a.dtype = dtype; a.flags = flags; a.status = status;
   return PNFT_OK;
 }
@@ -133,7 +133,7 @@ static int flash_fwd_entry(const void* q, const int64_t* sq, const void* k, cons
   cudaStream_t st = as_stream(stream);
   if (use_sm100(a)) return flash_fwd_sm100(a, st);
   if (fir_taps)
-    return fail(PNFT_EUNSUPPORTED, "flash fwd: the fused FIR runs on the sm_100a kernels only (bf16, head dim 64/128, "
+    return fail(PNFT_EUNSUPPORTED, "flash fwd: the fused FIR runs on the sm_100a kernels only (bf16, head dims multiples of 16 up to 128, "
                                    "16-byte aligned rows with unit head-dim stride)");
   return flash_fwd_generic(a, st);
 }

@@ -35,7 +35,8 @@ struct FlashArgs {
   float scale, gamma;
   int has_gamma, causal, dtype, flags;
   // bwd workspace carve-up
-  float* dq_acc;       // fp32 [B,H,N,D] contiguous
+  float* dq_acc;       // fp32 [B,H,N,acc_d] contiguous
+  int64_t acc_d;       // row stride of dq_acc: acc_width(D)
   // per-row backward coefficients (see below): record of row n of head bh at
   // r = bh * rec_rows(N) + n; the padding rows past N hold silent-row records
   float4* coefP;       // rows 2j, 2j+1 interleaved: {c1_0, c1_1, -D_0, -D_1}
@@ -83,6 +84,14 @@ struct BwdWorkspace {
   size_t off_dq, off_coef, off_live, off_part, off_sem, total;
 };
 BwdWorkspace bwd_workspace_layout(int64_t B, int64_t H, int64_t N, int64_t D);
+// Row width of the fp32 dQ accumulator: the sm_100a kernels compute head dims that
+// are multiples of 16 below 64 (or between 64 and 128) zero-padded to 64 (128), and
+// add whole padded rows into it; every kernel family uses the same layout.
+inline int64_t acc_width(int64_t D) {
+  if (D > 0 && D % 16 == 0 && D < 64) return 64;
+  if (D > 64 && D % 16 == 0 && D < 128) return 128;
+  return D;
+}
 
 int flash_fwd_generic(const FlashArgs& a, cudaStream_t st);
 int flash_bwd_generic(const FlashArgs& a, cudaStream_t st);
@@ -90,7 +99,7 @@ int flash_bwd_generic(const FlashArgs& a, cudaStream_t st);
 int flash_bwd_prep(const FlashArgs& a, cudaStream_t st);
 int flash_bwd_finish(const FlashArgs& a, cudaStream_t st);
 
-// sm_100a tcgen05/TMA kernels (bf16, D in {64,128}).
+// sm_100a tcgen05/TMA kernels (bf16, D a multiple of 16 up to 128; computed as 64 or 128).
 bool flash_sm100_supported(const FlashArgs& a);
 int flash_fwd_sm100(const FlashArgs& a, cudaStream_t st);
 int flash_bwd_sm100(const FlashArgs& a, cudaStream_t st);

@@ -211,8 +211,8 @@ __global__ void __launch_bounds__(256) flash_bwd_prep_kernel(FlashArgs a) {
                    (a.sdo[1] % 8) == 0 && (a.sdo[0] % 8) == 0 && (reinterpret_cast<uintptr_t>(a.dout) & 15) == 0 &&
                    (reinterpret_cast<uintptr_t>(a.out32) & 15) == 0;
   {  // this block's rows of the fp32 dQ accumulator start at zero (the backward adds into them)
-    const int64_t n0 = (int64_t)blockIdx.x * 64, cnt = (min((int64_t)64, a.N - n0)) * a.D;
-    float* z = a.dq_acc + (bh * a.N + n0) * a.D;
+    const int64_t n0 = (int64_t)blockIdx.x * 64, cnt = (min((int64_t)64, a.N - n0)) * a.acc_d;
+    float* z = a.dq_acc + (bh * a.N + n0) * a.acc_d;
     if ((reinterpret_cast<uintptr_t>(z) & 15) == 0 && (cnt & 3) == 0) {
       for (int64_t i = threadIdx.x; i < cnt / 4; i += blockDim.x) reinterpret_cast<float4*>(z)[i] = make_float4(0.f, 0.f, 0.f, 0.f);
     } else {
@@ -338,7 +338,7 @@ __global__ void __launch_bounds__(GTHREADS) flash_bwd_generic_kernel(FlashArgs a
   const T* K = static_cast<const T*>(a.k) + b * a.sk[0] + h * a.sk[1];
   const T* V = static_cast<const T*>(a.v) + b * a.sv[0] + h * a.sv[1];
   const T* dO = static_cast<const T*>(a.dout) + b * a.sdo[0] + h * a.sdo[1];
-  float* dQa = a.dq_acc + bh * N * a.D;
+  float* dQa = a.dq_acc + bh * N * a.acc_d;
   load_tile<T, DP>(sK, K, a.sk[2], a.sk[3], k0, N, D);
   load_tile<T, DP>(sV, V, a.sv[2], a.sv[3], k0, N, D);
   const float tau = __ldg(a.tau);
@@ -481,7 +481,7 @@ __global__ void __launch_bounds__(GTHREADS) flash_bwd_generic_kernel(FlashArgs a
         for (int jj = 0; jj < NJ; ++jj) {
           const int64_t row = q0 + rg + 16 * ii;
           const int e = cg + 16 * jj;
-          old[ii][jj] = (row < N && e < D) ? __ldcg(dQa + row * a.D + e) : 0.f;
+          old[ii][jj] = (row < N && e < D) ? __ldcg(dQa + row * a.acc_d + e) : 0.f;
         }
 #pragma unroll
       for (int ii = 0; ii < 4; ++ii)
@@ -489,7 +489,7 @@ __global__ void __launch_bounds__(GTHREADS) flash_bwd_generic_kernel(FlashArgs a
         for (int jj = 0; jj < NJ; ++jj) {
           const int64_t row = q0 + rg + 16 * ii;
           const int e = cg + 16 * jj;
-          if (row < N && e < D) __stcg(dQa + row * a.D + e, old[ii][jj] + dq[ii][jj]);
+          if (row < N && e < D) __stcg(dQa + row * a.acc_d + e, old[ii][jj] + dq[ii][jj]);
         }
       det_turn_pass(q0);
     } else {
@@ -500,7 +500,7 @@ __global__ void __launch_bounds__(GTHREADS) flash_bwd_generic_kernel(FlashArgs a
 #pragma unroll
         for (int jj = 0; jj < NJ; ++jj) {
           const int e = cg + 16 * jj;
-          if (e < D) atomicAdd(dQa + row * a.D + e, dq[ii][jj]);
+          if (e < D) atomicAdd(dQa + row * a.acc_d + e, dq[ii][jj]);
         }
       }
     }
@@ -587,7 +587,7 @@ __global__ void __launch_bounds__(256) dq_cast_kernel(FlashArgs a) {
          i += (int64_t)gridDim.x * blockDim.x) {
       const int64_t row = i / per_row, c = (i - row * per_row) * 8;
       const int64_t n = row % a.N, bh = row / a.N, b = bh / a.H, h = bh % a.H;
-      const float4* src = reinterpret_cast<const float4*>(a.dq_acc + row * a.D + c);
+      const float4* src = reinterpret_cast<const float4*>(a.dq_acc + row * a.acc_d + c);
       float4 f0 = src[0], f1 = src[1];
       f0.x *= fs; f0.y *= fs; f0.z *= fs; f0.w *= fs;
       f1.x *= fs; f1.y *= fs; f1.z *= fs; f1.w *= fs;
@@ -608,7 +608,7 @@ __global__ void __launch_bounds__(256) dq_cast_kernel(FlashArgs a) {
   const int64_t total = a.B * a.H * a.N * a.D;
   for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
     const int64_t e = i % a.D, n = (i / a.D) % a.N, bh = i / (a.D * a.N), b = bh / a.H, h = bh % a.H;
-    dq[b * a.sdq[0] + h * a.sdq[1] + n * a.sdq[2] + e * a.sdq[3]] = from_f32<T>(fs * a.dq_acc[i]);
+    dq[b * a.sdq[0] + h * a.sdq[1] + n * a.sdq[2] + e * a.sdq[3]] = from_f32<T>(fs * a.dq_acc[(bh * a.N + n) * a.acc_d + e]);
   }
 }
 
@@ -625,7 +625,7 @@ BwdWorkspace bwd_workspace_layout(int64_t B, int64_t H, int64_t N, int64_t D) {
   const size_t rows = (size_t)(B * H * N), recs = (size_t)(B * H * rec_rows(N));
   const size_t ntiles64 = (size_t)(B * H) * (size_t)((N + GB - 1) / GB);
   w.off_dq = 0;
-  w.off_coef = up(rows * (size_t)D * sizeof(float));
+  w.off_coef = up(rows * (size_t)acc_width(D) * sizeof(float));
   // coefP (two floats per row), tiev, argv, pcmpv: recs records each
   w.off_live = w.off_coef + up(recs * (sizeof(float2) + sizeof(float) + sizeof(int32_t) + sizeof(float)));
   w.off_part = w.off_live + up(ntiles64 * sizeof(int32_t));

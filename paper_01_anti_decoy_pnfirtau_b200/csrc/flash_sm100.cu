@@ -1,5 +1,7 @@
 // sm_100a flash pn_fir_tau kernels: TMA -> shared memory, tcgen05 MMAs with
-// TMEM accumulators, warp-specialised pipelines. bf16 inputs, head dim 64/128.
+// TMEM accumulators, warp-specialised pipelines. bf16 inputs, head dim 64/128 (smaller
+// head dims that are multiples of 16 run zero-padded: the TMA loads fill the missing
+// head dims with zeros and the epilogue stores only the real ones).
 //
 // Forward, one CTA per (128 query rows, b*h), 192 threads, two CTAs per SM (each
 // holds 256 of the 512 TMEM columns; the two CTAs' tile phases are independent,
@@ -135,6 +137,7 @@ struct FwdParams {
   const float* tau;
   int32_t* status;
   int H, N, nq, nk;
+  int dreal;  // the operands' head dim: D when D is 64 / 128, else zero-padded to D by the TMA loads
   float scale, gamma;
   int has_gamma, causal;
   int stall;  // PNFT_FLASH_TEST_STALL: the elementwise warps first wait on B_STALL
@@ -528,12 +531,13 @@ __global__ void __launch_bounds__(f_threads<FIR>(), FIR ? 1 : 2) flash_fwd_sm100
 #pragma unroll
     for (int cb = 0; cb < D / NQW; cb += 16) {  // group g writes head dims [g*D/NQW, (g+1)*D/NQW)
       const int d0 = g * (D / NQW) + cb;
+      if (d0 >= p.dreal) break;  // zero-padded head dims: computed, never stored (warp-uniform)
       uint32_t r[16];
       if (o_written) {
         tmem_load16(tmem + lane_off + TM_O + (uint32_t)d0, r);
       }
       if (row < p.N && o_ok && p.out32) {
-        float4* o32 = reinterpret_cast<float4*>(p.out32 + ((int64_t)bh * p.N + row) * D + d0);
+        float4* o32 = reinterpret_cast<float4*>(p.out32 + ((int64_t)bh * p.N + row) * p.dreal + d0);
 #pragma unroll
         for (int v = 0; v < 4; ++v) {
           float4 f;
@@ -662,7 +666,9 @@ bool device_is_sm100() {
 // test u == peak needs the forward's S recomputed by the same arithmetic.
 bool flash_sm100_supported(const FlashArgs& a) {
   if (a.dtype != PNFT_DTYPE_BF16) return false;
-  if (a.D != 64 && a.D != 128) return false;
+  // head dims that are multiples of 16 up to 128; below 64 (or between 64 and 128) the
+  // TMA loads zero-fill the operands to 64 (128) head dims, which changes no product
+  if (a.D < 16 || a.D > 128 || a.D % 16 != 0) return false;
   if (a.N < 1 || a.N > (int64_t)1 << 30) return false;
   if (!tma_ok_bhnd(a.q, a.sq) || !tma_ok_bhnd(a.k, a.sk) || !tma_ok_bhnd(a.v, a.sv)) return false;
   return device_is_sm100();
@@ -687,6 +693,7 @@ int flash_fwd_sm100(const FlashArgs& a, cudaStream_t st) {
   p.status = a.status;
   p.H = (int)a.H;
   p.N = (int)a.N;
+  p.dreal = (int)a.D;
   p.nq = (int)((a.N + FM - 1) / FM);
   p.nk = (int)((a.N + FN - 1) / FN);
   p.scale = a.scale;
@@ -708,10 +715,10 @@ int flash_fwd_sm100(const FlashArgs& a, cudaStream_t st) {
     rc = tma_map_bhnd(&p.tkr, a.k, a.sk, a.B, a.H, a.N, a.D, RAW_ROWS);
     if (rc) return rc;
     p.taps = a.fir_taps;
-    if (a.D == 64) return launch(flash_fwd_sm100_kernel<64, true>, FwdLayout<64>::SMEM_FIR);
+    if (a.D <= 64) return launch(flash_fwd_sm100_kernel<64, true>, FwdLayout<64>::SMEM_FIR);
     return launch(flash_fwd_sm100_kernel<128, true>, FwdLayout<128>::SMEM_FIR);
   }
-  if (a.D == 64) return launch(flash_fwd_sm100_kernel<64, false>, FwdLayout<64>::SMEM);
+  if (a.D <= 64) return launch(flash_fwd_sm100_kernel<64, false>, FwdLayout<64>::SMEM);
   return launch(flash_fwd_sm100_kernel<128, false>, FwdLayout<128>::SMEM);
 }
 

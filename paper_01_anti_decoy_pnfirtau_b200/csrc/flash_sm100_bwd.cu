@@ -1,4 +1,5 @@
-// sm_100a backward of flash pn_fir_tau (bf16, head dim 64/128).
+// sm_100a backward of flash pn_fir_tau (bf16, head dim 64/128; smaller head dims that
+// are multiples of 16 zero-padded to them, as in the forward).
 //
 // One CTA per (128 keys, b*h), KV-parallel over the 64-query tiles at or below
 // the causal diagonal whose rows are not all silent (per-tile flags from the
@@ -154,6 +155,7 @@ struct BwdParams {
   const float* tau;
   int32_t* status;
   int H, N, nq64, nkt;
+  int dreal;  // the operands' head dim (zero-padded to D by the TMA loads when smaller)
   float scale;
   int causal;
   int stall;  // PNFT_FLASH_TEST_STALL: the elementwise warps first wait on C_STALL
@@ -614,6 +616,7 @@ __global__ void __launch_bounds__(B_THREADS, 1) flash_bwd_sm100_kernel(const __g
 #pragma unroll
       for (int cb = 0; cb < D / NEW; cb += 16) {
         const int d0 = hh * (D / NEW) + cb;
+        if (d0 >= p.dreal) break;  // zero-padded head dims: never stored (warp-uniform)
         uint32_t r[16];
         if (have) {
           tmem_load16(tmem + lane_off + tcol + (uint32_t)d0, r);
@@ -862,6 +865,7 @@ int flash_bwd_sm100(const FlashArgs& a0, cudaStream_t st) {
   p.status = a.status;
   p.H = (int)a.H;
   p.N = (int)a.N;
+  p.dreal = (int)a.D;
   p.nq64 = (int)((a.N + BM - 1) / BM);
   p.nkt = nkt;
   p.scale = a.scale;
@@ -881,10 +885,10 @@ int flash_bwd_sm100(const FlashArgs& a0, cudaStream_t st) {
     return check_launch("flash bwd sm100");
   };
   if (a.fir_taps)
-    rc = a.D == 64 ? launch(flash_bwd_sm100_kernel<64, true>, BwdLayout<64>::SMEM)
+    rc = a.D <= 64 ? launch(flash_bwd_sm100_kernel<64, true>, BwdLayout<64>::SMEM)
                    : launch(flash_bwd_sm100_kernel<128, true>, BwdLayout<128>::SMEM);
   else
-    rc = a.D == 64 ? launch(flash_bwd_sm100_kernel<64, false>, BwdLayout<64>::SMEM)
+    rc = a.D <= 64 ? launch(flash_bwd_sm100_kernel<64, false>, BwdLayout<64>::SMEM)
                    : launch(flash_bwd_sm100_kernel<128, false>, BwdLayout<128>::SMEM);
   if (rc) return rc;
   return flash_bwd_finish(a, st);

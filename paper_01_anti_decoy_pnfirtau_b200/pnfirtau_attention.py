@@ -180,7 +180,7 @@ class PnFirTauFlashMHA(PnFirTauMHA):
 
     ``fuse_fir`` (default) routes the keys' causal filter through
     flash_pn_fir_tau_attention_fir where that path serves the inputs (7 taps,
-    bf16, head dim 64/128): the backward filters its key tile inside the
+    bf16, head dims that are multiples of 16 up to 128): the backward filters its key tile inside the
     attention kernel (no filtered-key tensor is kept for it, no separate
     filter backward node) and the forward runs one filter pass before the
     attention kernel. The results equal the unfused path's (the tile filter is

@@ -672,7 +672,7 @@ def flash_pn_fir_tau_attention_fir(
     tile per CTA); the forward does with ``fused_forward=True``, and otherwise
     runs one standalone filter pass, which is faster there because every query
     tile re-reads the key tiles. ``k`` is the raw key projection ``[B, H, N, D]``
-    (bf16, head dim 64/128; sm_100a kernels only). Gradients reach ``k`` and, when
+    (bf16, head dims that are multiples of 16 up to 128; sm_100a kernels only). Gradients reach ``k`` and, when
     it requires grad, ``taps``. ``deterministic`` as in flash_pn_fir_tau_attention.
     Composition replaced: src/pnfirtau_attention.py:285-316."""
     if scale is None:
@@ -726,6 +726,6 @@ def _flash_fir_qkv(qkv, H, score_tau, taps, scale, gamma, causal_mask):
 
 def fused_fir_applies(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, fir_k: int) -> bool:
     """Whether flash_pn_fir_tau_attention_fir serves these inputs (7 taps, bf16,
-    head dim 64/128, the sm_100a kernels)."""
+    head dims that are multiples of 16 up to 128, the sm_100a kernels)."""
     return (fir_k == _lib.FIR_FUSED_TAPS and q.is_cuda and q.dtype == torch.bfloat16
-            and q.shape[-1] in (64, 128) and flash_kernel_path(q, k, v) == "sm100")
+            and q.shape[-1] % 16 == 0 and 16 <= q.shape[-1] <= 128 and flash_kernel_path(q, k, v) == "sm100")

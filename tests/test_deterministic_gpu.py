@@ -64,7 +64,9 @@ CASES = {
     "sm100_noncausal": (1, 2, 384, 64, torch.bfloat16, 0.3, 0.0, False, False, "sm100"),
     "sm100_fused_fir": (2, 2, 520, 64, torch.bfloat16, 0.0, 0.0, True, True, "sm100"),
     "generic_fp32": (1, 2, 300, 64, torch.float32, 0.1, 0.0, False, True, "generic"),
-    "generic_bf16_d32": (2, 1, 257, 32, torch.bfloat16, 0.0, 0.0, False, True, "generic"),
+    "generic_bf16_d24": (2, 1, 257, 24, torch.bfloat16, 0.0, 0.0, False, True, "generic"),
+    "sm100_d32_padded": (2, 2, 384, 32, torch.bfloat16, 0.2, 0.3, False, True, "sm100"),
+    "sm100_d16_fused_fir": (1, 2, 300, 16, torch.bfloat16, 0.0, 0.0, True, True, "sm100"),
 }
 
 

@@ -43,7 +43,7 @@ def _run(q, k, v, do, tau, taps, fused, fused_forward=False):
 
 
 @pytest.mark.parametrize("fused_forward", [False, True])
-@pytest.mark.parametrize("D", [64, 128])
+@pytest.mark.parametrize("D", [16, 32, 64, 128])
 @pytest.mark.parametrize("N,tau", [(128, 0.0), (300, -0.2), (520, 0.3), (70, 0.1)])
 def test_fused_fir_matches_unfused(cuda, D, N, tau, fused_forward):
     q, k, v = _module_layout(2, 2, N, D, 11 + N + D, cuda)
@@ -60,7 +60,7 @@ def test_fused_fir_matches_unfused(cuda, D, N, tau, fused_forward):
     assert rel_l2(fu[5], un[5]) < 1e-5, ("dtaps", rel_l2(fu[5], un[5]))
 
 
-@pytest.mark.parametrize("D", [64, 128])
+@pytest.mark.parametrize("D", [16, 64, 128])
 def test_fused_fir_vs_oracle(cuda, D):
     B, H, N = 2, 2, 256
     q, k, v = _module_layout(B, H, N, D, 5 + D, cuda)
