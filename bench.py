@@ -21,7 +21,9 @@ Multi-GPU: every rank runs its own config-3-sized shard of batch x heads
 (weak scaling, no collective on the operator's data path); the shared tau
 gradient is summed across ranks with one fp64 all-reduce per backward on a side
 stream (TauGradReducer: no step waits for the other ranks; the sum is collected
-at the end of the timed region), and the LM uses DDP over NCCL.
+at the end of the timed region). The LM is data parallel: its headline step is
+captured in one CUDA graph per rank with the gradient average (one NCCL
+all-reduce) inside it; the eager comparison uses DDP.
 ``--impl reference`` times the reference's eager algorithm on the host cores
 on rank 0 only.
 """

@@ -7,16 +7,23 @@
 //    staged into shared memory by a 1-D bulk copy (cp.async.bulk, a ring of up
 //    to three rows per CTA, one persistent CTA per SM), reduced there (max,
 //    then one exponential per element, kept in fp16 beside its sum), and
-//    overwritten in place in HBM by scale * (softmax - onehot). HBM traffic is one read and one write of the
-//    logits, against the eager path's logit copies, log-softmax output and its
-//    backward re-reads.
+//    overwritten in place in HBM by scale * (softmax - onehot). HBM traffic is
+//    one read and one write of the logits, against the eager path's logit
+//    copies, log-softmax output and its backward re-reads.
 //
-//  * layernorm_fwd / layernorm_bwd: nn.LayerNorm of the Pre-LN blocks
-//    (exp4_wikitext2_lm.py:183-200). One warp per row with the row held in
-//    registers; the forward writes the normalised row directly in the type of
-//    the GEMM that consumes it (bf16 under autocast) and keeps mean and 1/std;
-//    the backward gives dx and per-CTA partial sums of dgamma / dbeta, which a
-//    second kernel adds in a fixed order (bitwise reproducible).
+//  * (add_)layernorm_fwd / _bwd: nn.LayerNorm of the Pre-LN blocks
+//    (exp4_wikitext2_lm.py:183-200), optionally fused with the residual add
+//    before it. One warp per row with the row held in registers; the forward
+//    writes the normalised row directly in the type of the GEMM that consumes
+//    it (bf16 under autocast) and keeps mean and 1/std; the backward gives dx
+//    (plus the residual path's gradient, and the branch's gradient in its own
+//    type) and per-CTA partial sums of dgamma / dbeta, which a second kernel
+//    adds in a fixed order (bitwise reproducible).
+//
+//  * colsum / gelu_bwd_colsum / gelu_fwd: the MLP's bias gradients as
+//    fixed-order column sums, the GELU backward fused with the first of them,
+//    and the GELU forward; bf16 GELU and GELU' come from a per-device table over
+//    the bf16 bit patterns (pnft_gelu_table) copied into shared memory.
 #include <math.h>
 
 #include <algorithm>
