@@ -82,7 +82,7 @@ def parse_args():
                     help="reference arm: skip timing the reference's Triton kernels on the GPU")
     ap.add_argument("--sweep-steps", type=int, default=10)
     ap.add_argument("--c5-steps", type=int, default=4)
-    ap.add_argument("--e2e-chunks", type=int, default=8,
+    ap.add_argument("--e2e-chunks", type=int, default=4,
                     help="pipeline chunks of the e2e step (whole heads each; 1 = one call per step)")
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--cpu-seconds", type=float, default=12.0)
@@ -666,12 +666,17 @@ def bench_e2e(args, dist_: Dist, w: dict, dev, flops: float, P) -> dict:
     """Same op through the public API with pinned host inputs and host outputs:
     every step copies q,k,v,dO host->device and out,dq,dk,dv,dtau device->host.
 
-    The step is pipelined over chunks of whole heads (--e2e-chunks, default 8: one
-    batch element each for config 3; one call of the public API per chunk), as a caller streaming host data would run it: the
-    host->device copies of chunk i+1, the attention fwd+bwd of chunk i and the
-    device->host copies of chunk i-1 run on three streams, so the two PCIe
-    directions and the kernels overlap. Every byte of the serial version is still
-    copied every step; dtau is the sum over chunks (all-reduced over ranks)."""
+    The step is pipelined over chunks of whole heads (--e2e-chunks, default 4: two
+    batch elements each for config 3; one call of the public API per chunk; each
+    call and its copies cost ~0.4 ms of host time, so 8 chunks are host-bound), as a
+    caller streaming host data would run it: the host->device copies of chunk i+1,
+    the attention fwd+bwd of chunk i and the device->host copies of chunk i-1 run
+    on three streams, so the two PCIe directions and the kernels overlap, and so do
+    consecutive steps (step s+1's first uploads start once step s's compute has
+    read those device buffers, not after its last download; the timed region ends
+    when the last step's results are in host memory). Every byte of the serial
+    version is still copied every step; dtau is the sum over chunks (all-reduced
+    over ranks). `host_link` times the same copies alone."""
     from paper_01_anti_decoy_pnfirtau_b200.pnfirtau_ops import flash_pn_fir_tau_attention
 
     hq, hk, hv, hdo = (t.detach().cpu().pin_memory() for t in make_inputs(w, args.seed + 7, dev))
@@ -695,10 +700,6 @@ def bench_e2e(args, dist_: Dist, w: dict, dev, flops: float, P) -> dict:
     done_cmp = [None] * nchunk  # compute of chunk i finished reading its device inputs (previous step)
 
     def step():
-        main = torch.cuda.current_stream(dev)
-        start = torch.cuda.Event()
-        start.record(main)
-        s_in.wait_event(start)
         total = None
         for i, (b0, b1, h0, h1) in enumerate(bounds):
             sl = (slice(b0, b1), slice(h0, h1))
@@ -733,8 +734,8 @@ def bench_e2e(args, dist_: Dist, w: dict, dev, flops: float, P) -> dict:
             s_out.wait_event(fin)
             summed = reducer.result() if dist_.world > 1 else total  # s_out waits for the all-reduce
             htau.copy_(summed, non_blocking=True)
-        main.wait_stream(s_out)
 
+    main = torch.cuda.current_stream(dev)
     for _ in range(max(2, min(args.warmup, 3))):
         step()
     torch.cuda.synchronize()
@@ -742,19 +743,66 @@ def bench_e2e(args, dist_: Dist, w: dict, dev, flops: float, P) -> dict:
     s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     dist_.barrier()
     torch.cuda.synchronize()
-    s.record()
+    s.record(main)
+    for st_ in (s_in, s_cmp, s_out):
+        st_.wait_event(s)
     for _ in range(steps):
         step()
-    e.record()
+    for st_ in (s_in, s_cmp, s_out):
+        main.wait_stream(st_)
+    e.record(main)
     torch.cuda.synchronize()
     ms = dist_.max(s.elapsed_time(e), dev)
     h2d = sum(t.numel() * t.element_size() for t in (hq, hk, hv, hdo))
     d2h = sum(t.numel() * t.element_size() for t in outs) + htau.element_size()
+    link = _host_link_floor(dist_, dev, (hq, hk, hv, hdo), (gq_, gk_, gv_, gdo_), outs)
+    per_step = ms / steps
     return {"value": round(dist_.world * flops * steps / (ms / 1e3) / 1e12, 3), "unit": "TFLOP/s",
-            "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h, "ms_per_step": round(ms / steps, 4),
+            "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h, "ms_per_step": round(per_step, 4),
             "steps": steps, "chunks": nchunk,
             "api": "flash_pn_fir_tau_attention + torch.autograd.grad per batch chunk, pinned host buffers, "
-                   "H2D / compute / D2H on three streams"}
+                   "H2D / compute / D2H on three streams",
+            "host_link": dict(link, frac=round(link["both_ms"] / per_step, 3))}
+
+
+def _host_link_floor(dist_: Dist, dev, hin, din, hout, reps: int = 3) -> dict:
+    """The copies of one e2e step alone: every input host->device and every output
+    device->host, first one direction at a time, then both at once on two streams
+    (the floor of a step whose copies overlap its kernels perfectly). Pinned host
+    buffers, one copy call per tensor, max over ranks (all ranks copy at once, as
+    in the step, so they share the host's memory and PCIe switches)."""
+    s_in, s_out = torch.cuda.Stream(dev), torch.cuda.Stream(dev)
+
+    def run(h2d: bool, d2h: bool) -> float:
+        torch.cuda.synchronize()
+        dist_.barrier()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        main = torch.cuda.current_stream(dev)
+        a.record(main)
+        s_in.wait_event(a)
+        s_out.wait_event(a)
+        for _ in range(reps):
+            if h2d:
+                with torch.cuda.stream(s_in):
+                    for d, h in zip(din, hin):
+                        d.copy_(h, non_blocking=True)
+            if d2h:
+                with torch.cuda.stream(s_out):
+                    for h, d in zip(hout, din):
+                        h.copy_(d, non_blocking=True)
+        main.wait_stream(s_in)
+        main.wait_stream(s_out)
+        b.record(main)
+        torch.cuda.synchronize()
+        return dist_.max(a.elapsed_time(b), dev) / reps
+
+    run(True, True)  # warm-up
+    nin = sum(t.numel() * t.element_size() for t in hin)
+    nout = sum(t.numel() * t.element_size() for t in hout)
+    t_in, t_out, t_both = run(True, False), run(False, True), run(True, True)
+    return {"h2d_ms": round(t_in, 4), "d2h_ms": round(t_out, 4), "both_ms": round(t_both, 4),
+            "h2d_gbs": round(nin / t_in / 1e6, 1), "d2h_gbs": round(nout / t_out / 1e6, 1),
+            "note": "the step's copies alone (no kernels); frac = both_ms / e2e ms_per_step"}
 
 
 def bench_lm_kernels(args, dev, iters: int = 10) -> dict:
