@@ -47,6 +47,10 @@ def test_bench_json_contract_gpu():
     assert rf["bound"] in ("hbm", "tensor") and rf["peak"] > 0 and 0 < rf["frac"] == pytest.approx(rf["achieved"] / rf["peak"], rel=1e-2)
     e2e = d["e2e"]
     assert e2e["h2d_bytes_per_step"] == 4 * 8 * 8 * 4096 * 64 * 2 and e2e["d2h_bytes_per_step"] == 4 * 8 * 8 * 4096 * 64 * 2 + 4
+    # the host link's own floor: the step's copies alone, and the e2e step no faster than them
+    hl = e2e["host_link"]
+    assert hl["h2d_gbs"] > 0 and hl["d2h_gbs"] > 0 and hl["both_ms"] > 0
+    assert hl["frac"] == pytest.approx(hl["both_ms"] / e2e["ms_per_step"], rel=1e-2) and hl["frac"] < 1.2
     assert d["gpu_launches"] > 0 and "sm_mhz" in d["clocks"] and "reasons" in d["clocks"]
     assert d["fir"]["c5_k_8x16384x2048"]["GB/s"] > 0 and d["fir"]["lm_k_32x512x256"]["device_GB/s"] > 0
     lk = d["lm_kernels"]
