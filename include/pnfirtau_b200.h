@@ -405,6 +405,14 @@ PNFT_API int pnft_gelu_bwd_colsum(const void* dh, int64_t sdh, const void* a, in
                          float* db, void* workspace, size_t workspace_bytes, int64_t M, int64_t C, int dtype,
                          const float* table, void* stream);
 
+/* bfloat16 copies of `count` fp32 tensors in one launch. `table` (device
+ * memory, int64 rows of {src address, dst address, element count}) names each
+ * tensor; dst[e] = src[e] rounded to nearest even for e < count of that row.
+ * max_n: the largest element count (sizes the grid).
+ * Replaces: the per-GEMM weight / bias casts of bf16 autocast in the LM step
+ * (torch.autocast around experiments/exp4_wikitext2_lm.py:712-729). */
+PNFT_API int pnft_cast_bf16(const int64_t* table, int count, int64_t max_n, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

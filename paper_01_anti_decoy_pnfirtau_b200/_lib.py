@@ -107,6 +107,7 @@ SIGNATURES: dict[str, tuple] = {
         c_int, [_P, c_int64, _P, c_int64, _P, c_int64, _P, c_size_t, c_int64, c_int64, c_int64, c_int, _P, _P]),
     "pnft_gemm_at_b_workspace_size": (c_size_t, [c_int64, c_int64, c_int64]),
     "pnft_gelu_fwd": (c_int, [_P, c_int64, _P, c_int64, c_int64, c_int64, c_int, _P, _P]),
+    "pnft_cast_bf16": (c_int, [_P, c_int, c_int64, _P]),
     "pnft_gelu_bwd_colsum": (
         c_int, [_P, c_int64, _P, c_int64, _P, c_int64, _P, _P, c_size_t, c_int64, c_int64, c_int, _P, _P]),
 }

@@ -1015,10 +1015,51 @@ int gelu_fwd_launch(const void* a, int64_t sa, void* y, int64_t sy, int64_t M, i
   return check_launch("gelu fwd");
 }
 
+// ---------------------------------------------------------------- bf16 copies of parameters
+// Tensor i of the table (rows of {src, dst, n}): dst[e] = bf16(src[e]) for e < n,
+// round to nearest even (the cast autocast does per GEMM). blockIdx.y = tensor,
+// grid-stride over its elements 8 at a time (two 16-byte loads, one 16-byte
+// store) when both pointers are 16-byte aligned.
+__global__ void __launch_bounds__(256) cast_bf16_multi_kernel(const int64_t* __restrict__ table) {
+  const int64_t* row = table + 3 * blockIdx.y;
+  const float* src = reinterpret_cast<const float*>(row[0]);
+  __nv_bfloat16* dst = reinterpret_cast<__nv_bfloat16*>(row[1]);
+  const int64_t n = row[2];
+  const int64_t step = (int64_t)gridDim.x * 256;
+  if (((reinterpret_cast<uintptr_t>(src) | reinterpret_cast<uintptr_t>(dst)) & 15) == 0) {
+    const int64_t n8 = n / 8;
+    for (int64_t v = (int64_t)blockIdx.x * 256 + threadIdx.x; v < n8; v += step) {
+      const float4 a = __ldcs(reinterpret_cast<const float4*>(src) + 2 * v);
+      const float4 b = __ldcs(reinterpret_cast<const float4*>(src) + 2 * v + 1);
+      uint4 w;
+      w.x = sm100::pack_bf16x2(a.x, a.y);
+      w.y = sm100::pack_bf16x2(a.z, a.w);
+      w.z = sm100::pack_bf16x2(b.x, b.y);
+      w.w = sm100::pack_bf16x2(b.z, b.w);
+      reinterpret_cast<uint4*>(dst)[v] = w;
+    }
+    for (int64_t e = 8 * n8 + (int64_t)blockIdx.x * 256 + threadIdx.x; e < n; e += step)
+      dst[e] = __float2bfloat16_rn(src[e]);
+  } else {
+    for (int64_t e = (int64_t)blockIdx.x * 256 + threadIdx.x; e < n; e += step) dst[e] = __float2bfloat16_rn(src[e]);
+  }
+}
+
 }  // namespace
 }  // namespace pnft
 
 using namespace pnft;
+
+extern "C" int pnft_cast_bf16(const int64_t* table, int count, int64_t max_n, void* stream) {
+  if (count < 0 || count > 65535 || max_n < 0) return fail(PNFT_EINVAL, "cast bf16: bad count %d / max_n %lld", count, (long long)max_n);
+  if (count == 0 || max_n == 0) return PNFT_OK;
+  if (!table) return fail(PNFT_EINVAL, "cast bf16: null table");
+  // enough blocks for the largest tensor to keep every SM busy; smaller ones exit early
+  const int64_t want = (max_n + 8 * 256 - 1) / (8 * 256);
+  const int gx = (int)std::max<int64_t>(1, std::min<int64_t>(want, (int64_t)device_sms() * 8));
+  cast_bf16_multi_kernel<<<dim3((unsigned)gx, (unsigned)count), 256, 0, as_stream(stream)>>>(table);
+  return check_launch("cast bf16");
+}
 
 extern "C" int pnft_lm_xent(void* logits, int64_t ld, const int64_t* targets, int64_t ignore_index,
                             float* row_loss, int64_t M, int64_t V, float grad_scale, const float* grad_scale_dev,

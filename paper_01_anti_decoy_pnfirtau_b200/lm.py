@@ -23,7 +23,7 @@ import torch
 import torch.nn as nn
 import torch.nn.functional as F
 
-from .lm_ops import LayerNorm, Linear, add_layer_norm, head_cross_entropy, mlp_gelu
+from .lm_ops import Bf16Casts, LayerNorm, Linear, add_layer_norm, head_cross_entropy, mlp_gelu
 from .pnfirtau_attention import PnFirConfig, PnFirTauFlashMHA, PnFirTauMHA, PnFirTauTritonMHA
 
 _VARIANTS = {"pn_fir_tau": PnFirTauMHA, "pn_fir_tau_triton": PnFirTauTritonMHA, "pn_fir_tau_flash": PnFirTauFlashMHA}
@@ -85,6 +85,7 @@ class PnFirLM(nn.Module):
                     setattr(blk.attn, name, Linear.sharing(getattr(blk.attn, name)))
         self.head = nn.Linear(cfg.d_model, cfg.vocab, bias=False)
         self.head.weight = self.embed.weight
+        self._casts: Bf16Casts | None = None  # bf16 copies of the GEMM parameters (_step_casts)
 
     def forward(self, idx: torch.Tensor, for_loss: bool = False, targets: torch.Tensor | None = None) -> torch.Tensor:
         """Logits ``[B, N, vocab]``. ``for_loss``: the logits the next-token loss
@@ -98,10 +99,11 @@ class PnFirLM(nn.Module):
         B, N = idx.shape
         pos = torch.arange(N, device=idx.device).unsqueeze(0)
         h = self.drop(self.embed(idx) + self.pos(pos))
-        h = self._trunk_fused(h) if self.fused_step_ops else self._trunk(h)
+        casts = self._step_casts(idx.device)
+        h = self._trunk_fused(h, casts) if self.fused_step_ops else self._trunk(h)
         if targets is not None:
             if self.fused_step_ops:
-                return head_cross_entropy(h[:, :-1], self.head.weight, targets)
+                return head_cross_entropy(h[:, :-1], self.head.weight, targets, casts=casts)
             logits = self._padded_logits(h)
             return nn.functional.cross_entropy(logits.reshape(-1, logits.size(-1)), targets.reshape(-1))
         if not for_loss:
@@ -113,7 +115,32 @@ class PnFirLM(nn.Module):
             h = blk(h)
         return self.ln_f(h)
 
-    def _trunk_fused(self, h: torch.Tensor) -> torch.Tensor:
+    def _step_casts(self, dev: torch.device) -> Bf16Casts | None:
+        """With the fused step ops under bf16 CUDA autocast: the bf16 copies of
+        every GEMM weight and bias (the head's padded to a multiple of 64 rows),
+        refreshed by one kernel launch, which the GEMMs of this forward and its
+        backward use instead of one cast per GEMM. None otherwise."""
+        if not (self.fused_step_ops and dev.type == "cuda" and torch.is_autocast_enabled("cuda")
+                and torch.get_autocast_dtype("cuda") == torch.bfloat16):
+            return None
+        if self._casts is None:
+            lins = [lin for blk in self.blocks for lin in (blk.attn.qkv, blk.attn.out)]
+            params = [t for lin in lins for t in (lin.weight, lin.bias)]
+            params += [t for blk in self.blocks for t in (blk.ffn[0].weight, blk.ffn[0].bias, blk.ffn[2].weight,
+                                                          blk.ffn[2].bias)]
+            params.append(self.head.weight)
+            if torch.cuda.is_current_stream_capturing() or any(
+                    t is not None and (t.dtype != torch.float32 or not t.is_contiguous() or t.device != dev)
+                    for t in params):
+                return None
+            vp = (self.cfg.vocab + 63) // 64 * 64
+            self._casts = Bf16Casts(params, padded={id(self.head.weight): vp})
+            for lin in lins:
+                lin.casts = self._casts
+        self._casts.refresh()
+        return self._casts
+
+    def _trunk_fused(self, h: torch.Tensor, casts: Bf16Casts | None = None) -> torch.Tensor:
         """The same blocks with every residual add fused into the LayerNorm
         that follows it (the MLP's add into the next block's ln1, the last one
         into ln_f) and the MLP on mlp_gelu; returns ln_f's output."""
@@ -123,7 +150,7 @@ class PnFirLM(nn.Module):
             att = blk.drop(blk.attn(a))
             ln2 = blk.ln2
             h, b = add_layer_norm(h, att, ln2.normalized_shape, ln2.weight, ln2.bias, ln2.eps)
-            f = blk.ffn[3](mlp_gelu(b, blk.ffn[0], blk.ffn[2]))
+            f = blk.ffn[3](mlp_gelu(b, blk.ffn[0], blk.ffn[2], casts))
             nxt = blocks[i + 1].ln1 if i + 1 < len(blocks) else self.ln_f
             h, a = add_layer_norm(h, f, nxt.normalized_shape, nxt.weight, nxt.bias, nxt.eps)
         return a

@@ -28,6 +28,9 @@ language-model experiments (experiments/exp4_wikitext2_lm.py:183-259, loss at
   autocast, and the loss and the logit gradient produced by one kernel pass over
   the logits, in place. The backward is two GEMMs on that gradient; the
   gradients of ``h`` and ``W`` are accumulated in fp32.
+- ``Bf16Casts``: bf16 copies of a model's fp32 GEMM parameters made by one
+  kernel launch per step (instead of one cast per GEMM), which ``Linear``,
+  ``mlp_gelu`` and ``head_cross_entropy`` use while they are current.
 
 CUDA only, like the attention operators; a CPU tensor raises.
 """
@@ -279,20 +282,101 @@ def _weight_grad(dy: torch.Tensor, x: torch.Tensor) -> torch.Tensor:
     return _mm_f32(dy.t(), x)
 
 
+def _cast(t: torch.Tensor | None, dt: torch.dtype) -> torch.Tensor | None:
+    return None if t is None else t.to(dt)
+
+
+class Bf16Casts:
+    """bfloat16 copies of fp32 CUDA parameters, all refreshed by one kernel
+    launch (``pnft_cast_bf16``), for the bf16 GEMMs of a training step: the LM
+    refreshes them once at the start of each forward instead of casting every
+    weight and bias per GEMM (the values are the same: round to nearest even).
+
+    A copy is handed out only while its parameter still has the storage and the
+    version counter seen at the last ``refresh()`` (an in-place update such as
+    an optimizer step makes it stale until the next refresh). ``padded``: rows
+    to pad a 2-D parameter to (its copy's extra rows stay zero), as the LM head's
+    GEMM wants. The device table of addresses is written outside CUDA graph
+    capture (the first refresh); a refresh inside a capture records only the
+    kernel launch."""
+
+    def __init__(self, params, padded: dict | None = None):
+        self.params = [p for p in params if p is not None]
+        if not self.params:
+            raise ValueError("Bf16Casts: no parameters")
+        dev = self.params[0].device
+        for t in self.params:
+            if t.device != dev or t.dtype != torch.float32 or not t.is_contiguous():
+                raise ValueError("Bf16Casts: contiguous fp32 parameters on one CUDA device expected")
+        self.device = dev
+        self.index = {id(t): i for i, t in enumerate(self.params)}
+        self.copies, self.full = [], {}
+        for t in self.params:
+            rows = (padded or {}).get(id(t))
+            if rows:
+                full = torch.zeros((rows, t.shape[1]), dtype=torch.bfloat16, device=dev)
+                self.full[id(t)] = full
+                self.copies.append(full[: t.shape[0]])
+            else:
+                self.copies.append(torch.empty(t.shape, dtype=torch.bfloat16, device=dev))
+        self._ptrs: list[int] | None = None
+        self._table: torch.Tensor | None = None
+        self._seen: list[tuple[int, int]] = []
+
+    def refresh(self) -> None:
+        ptrs = [t.data_ptr() for t in self.params]
+        if ptrs != self._ptrs:
+            if torch.cuda.is_current_stream_capturing():
+                raise RuntimeError("Bf16Casts: parameters moved during CUDA graph capture")
+            rows = [[t.data_ptr(), c.data_ptr(), t.numel()] for t, c in zip(self.params, self.copies)]
+            self._table = torch.tensor(rows, dtype=torch.int64).to(self.device)
+            self._ptrs = ptrs
+        n = max(t.numel() for t in self.params)
+        _lib.check(_lib.lib().pnft_cast_bf16(self._table.data_ptr(), len(self.params), n, _stream(self.device)),
+                   "pnft_cast_bf16")
+        self._seen = [(t.data_ptr(), t._version) for t in self.params]
+
+    def _current(self, t: torch.Tensor) -> int:
+        i = self.index.get(id(t), -1)
+        if i < 0 or not self._seen or self._seen[i] != (t.data_ptr(), t._version):
+            return -1
+        return i
+
+    def lookup(self, *params):
+        """The current copies of ``params`` (None entries stay None), or None if
+        any of them has no current copy."""
+        out = []
+        for t in params:
+            if t is None:
+                out.append(None)
+                continue
+            i = self._current(t)
+            if i < 0:
+                return None
+            out.append(self.copies[i])
+        return tuple(out)
+
+    def padded(self, t: torch.Tensor) -> torch.Tensor | None:
+        """The zero-padded current copy of ``t`` (a parameter given ``padded``
+        rows), or None."""
+        return self.full.get(id(t)) if self._current(t) >= 0 else None
+
+
 class _MlpGeluFn(torch.autograd.Function):
     @staticmethod
-    def forward(ctx, x, w1, b1, w2, b2, dt: torch.dtype):
+    def forward(ctx, x, w1, b1, w2, b2, dt: torch.dtype, pre=None):
         dev = _require_cuda("mlp_gelu", x, w1, w2)
         D = x.shape[-1]
         x2 = x.reshape(-1, D).to(dt)
         x2 = x2 if x2.stride(-1) == 1 else x2.contiguous()
-        w1c, w2c = w1.to(dt), w2.to(dt)
-        a0 = torch.addmm(b1.to(dt), x2, w1c.t()) if b1 is not None else torch.mm(x2, w1c.t())
+        # pre: the parameters already cast to dt (Bf16Casts), else cast here
+        w1c, b1c, w2c, b2c = pre if pre is not None else (_cast(w1, dt), _cast(b1, dt), _cast(w2, dt), _cast(b2, dt))
+        a0 = torch.addmm(b1c, x2, w1c.t()) if b1 is not None else torch.mm(x2, w1c.t())
         a1 = torch.empty_like(a0)
         _lib.check(_lib.lib().pnft_gelu_fwd(a0.data_ptr(), a0.stride(0), a1.data_ptr(), a1.stride(0), a0.shape[0],
                                             a0.shape[1], _ln_code(dt, "mlp_gelu"), _ptr(_gelu_table(dev)),
                                             _stream(dev)), "pnft_gelu_fwd")
-        out = torch.addmm(b2.to(dt), a1, w2c.t()) if b2 is not None else torch.mm(a1, w2c.t())
+        out = torch.addmm(b2c, a1, w2c.t()) if b2 is not None else torch.mm(a1, w2c.t())
         ctx.save_for_backward(x2, w1c, w2c, a0, a1)
         ctx.x_shape, ctx.x_dtype, ctx.dev = x.shape, x.dtype, dev
         ctx.p_dtypes = tuple(None if t is None else t.dtype for t in (w1, b1, w2, b2))
@@ -329,27 +413,30 @@ class _MlpGeluFn(torch.autograd.Function):
         pw1, pb1, pw2, pb2 = ctx.p_dtypes
         cast = lambda t, d: None if t is None else t.to(d)  # noqa: E731
         return (dx, cast(dw1, pw1), cast(db1, pb1) if ctx.needs_input_grad[2] else None, cast(dw2, pw2),
-                cast(db2, pb2), None)
+                cast(db2, pb2), None, None)
 
 
-def mlp_gelu(x: torch.Tensor, fc1: nn.Linear, fc2: nn.Linear) -> torch.Tensor:
+def mlp_gelu(x: torch.Tensor, fc1: nn.Linear, fc2: nn.Linear, casts: "Bf16Casts | None" = None) -> torch.Tensor:
     """``fc2(GELU(fc1(x)))`` (exact GELU) computed in the CUDA autocast dtype when
-    autocast is on (else in ``x.dtype``); see the module docstring."""
+    autocast is on (else in ``x.dtype``); see the module docstring. ``casts``: a
+    ``Bf16Casts`` holding current bf16 copies of the layers' parameters (used
+    when the dtype is bf16 and every copy is current)."""
     dt = _autocast_dtype(x)
     if dt not in _LN_DTYPES:
         dt = torch.float32
-    return _MlpGeluFn.apply(x, fc1.weight, fc1.bias, fc2.weight, fc2.bias, dt)
+    pre = casts.lookup(fc1.weight, fc1.bias, fc2.weight, fc2.bias) if casts is not None and dt == torch.bfloat16 else None
+    return _MlpGeluFn.apply(x, fc1.weight, fc1.bias, fc2.weight, fc2.bias, dt, pre)
 
 
 class _LinearFn(torch.autograd.Function):
     @staticmethod
-    def forward(ctx, x, weight, bias, dt: torch.dtype):
+    def forward(ctx, x, weight, bias, dt: torch.dtype, pre=None):
         _require_cuda("Linear", x, weight)
         D = x.shape[-1]
         x2 = x.reshape(-1, D).to(dt)
         x2 = x2 if x2.stride(-1) == 1 else x2.contiguous()
-        w = weight.to(dt)
-        y = torch.addmm(bias.to(dt), x2, w.t()) if bias is not None else torch.mm(x2, w.t())
+        w, b = pre if pre is not None else (weight.to(dt), _cast(bias, dt))  # pre: cast by Bf16Casts
+        y = torch.addmm(b, x2, w.t()) if bias is not None else torch.mm(x2, w.t())
         ctx.save_for_backward(x2, w)
         ctx.x_shape, ctx.x_dtype = x.shape, x.dtype
         ctx.p_dtypes = (weight.dtype, None if bias is None else bias.dtype)
@@ -372,7 +459,7 @@ class _LinearFn(torch.autograd.Function):
             _lib.check(_lib.lib().pnft_colsum(g2.data_ptr(), g2.stride(0), db.data_ptr(), ws.data_ptr(), nb,
                                               g2.shape[0], Dout, _ln_code(dt, "Linear"), _stream(dev)), "pnft_colsum")
             db = db.to(ctx.p_dtypes[1])
-        return dx, dw, db, None
+        return dx, dw, db, None, None
 
 
 class Linear(nn.Linear):
@@ -380,13 +467,19 @@ class Linear(nn.Linear):
     autocast GEMM and whose backward computes the weight gradient with the
     split-K tcgen05 kernel (``pnft_gemm_at_b``, fp32) and the bias gradient
     with the fixed-order column sum. ``Linear.sharing(lin)`` wraps an existing
-    layer's parameters without re-initialising anything."""
+    layer's parameters without re-initialising anything. ``casts`` (plain
+    attribute, default None): a ``Bf16Casts`` whose current bf16 copies of the
+    parameters the bf16 GEMM uses instead of casting them per call."""
+
+    casts: "Bf16Casts | None" = None
 
     def forward(self, x: torch.Tensor) -> torch.Tensor:
         dt = _autocast_dtype(x)
         if dt not in _LN_DTYPES:
             dt = torch.float32
-        return _LinearFn.apply(x, self.weight, self.bias, dt)
+        c = self.casts
+        pre = c.lookup(self.weight, self.bias) if c is not None and dt == torch.bfloat16 else None
+        return _LinearFn.apply(x, self.weight, self.bias, dt, pre)
 
     @classmethod
     def sharing(cls, lin: nn.Linear) -> "Linear":
@@ -400,7 +493,7 @@ class Linear(nn.Linear):
 
 class _HeadXentFn(torch.autograd.Function):
     @staticmethod
-    def forward(ctx, h, weight, targets, ignore_index: int):
+    def forward(ctx, h, weight, targets, ignore_index: int, wpad=None):
         dev = _require_cuda("head_cross_entropy", h, weight, targets)
         _check_pending(dev)
         D = h.shape[-1]
@@ -411,9 +504,12 @@ class _HeadXentFn(torch.autograd.Function):
         M = hb.shape[0]
         if t.numel() != M:
             raise RuntimeError(f"head_cross_entropy: {M} rows but {t.numel()} targets")
-        wp = torch.empty((Vp, D), dtype=torch.bfloat16, device=dev)
-        wp[:V].copy_(weight.detach())
-        wp[V:].zero_()
+        if wpad is not None:  # [Vp, D] bf16: the weight's current copy, zero rows past V
+            wp = wpad
+        else:
+            wp = torch.empty((Vp, D), dtype=torch.bfloat16, device=dev)
+            wp[:V].copy_(weight.detach())
+            wp[V:].zero_()
         logits = torch.mm(hb, wp.t())  # [M, Vp] bf16, fp32 accumulation (the autocast head GEMM)
         counted = (t != ignore_index).sum(dtype=torch.float32)
         inv = torch.reciprocal(counted)
@@ -433,15 +529,18 @@ class _HeadXentFn(torch.autograd.Function):
             dh = (torch.mm(g, wp, out_dtype=torch.float32) * go).to(ctx.h_dtype).view(ctx.h_shape)
         if ctx.needs_input_grad[1]:
             dw = (torch.mm(g.t(), hb, out_dtype=torch.float32)[: ctx.V] * go).to(ctx.w_dtype)
-        return dh, dw, None, None
+        return dh, dw, None, None, None
 
 
 def head_cross_entropy(h: torch.Tensor, weight: torch.Tensor, targets: torch.Tensor,
-                       ignore_index: int = -100) -> torch.Tensor:
+                       ignore_index: int = -100, *, casts: "Bf16Casts | None" = None) -> torch.Tensor:
     """Mean next-token cross-entropy of ``h @ weight.T`` against ``targets``
     (``F.cross_entropy`` semantics: rows whose target is ``ignore_index`` are
     left out of the mean). ``h``: ``[..., D]``; ``weight``: ``[V, D]`` (the LM
     head, tied to the embedding in the reference's model); ``targets``: the
     matching ``[...]`` int64 ids. The head GEMM runs in bf16 with fp32
-    accumulation (as under bf16 autocast) and the loss is fp32."""
-    return _HeadXentFn.apply(h, weight, targets, ignore_index)
+    accumulation (as under bf16 autocast) and the loss is fp32. ``casts``
+    (keyword only): a ``Bf16Casts`` holding a current bf16 copy of ``weight``
+    padded to a multiple of 64 rows, used instead of casting it here."""
+    wpad = casts.padded(weight) if casts is not None else None
+    return _HeadXentFn.apply(h, weight, targets, ignore_index, wpad)

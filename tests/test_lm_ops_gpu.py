@@ -343,6 +343,57 @@ def test_linear_module_matches_nn_linear(cuda):
     assert rel_l2(lin.weight.grad, ref.weight.grad) < 5e-3 and rel_l2(lin.bias.grad, ref.bias.grad) < 5e-3
 
 
+def test_bf16_casts_match_per_tensor_casts(cuda):
+    """pnft_cast_bf16 through Bf16Casts: every copy bitwise equal to .to(bf16)
+    (16-byte aligned tensors, unaligned views, lengths that are not multiples of
+    8, one element), the padded copy's extra rows zero, copies withheld once a
+    parameter changes in place and handed out again after the next refresh."""
+    from paper_01_anti_decoy_pnfirtau_b200.lm_ops import Bf16Casts
+
+    g = torch.Generator(device=cuda).manual_seed(11)
+    flat = torch.randn(50000, device=cuda, generator=g) * 100
+    ts = [torch.randn(1000, 256, device=cuda, generator=g), flat[1:1 + 1001], flat[2000:2000 + 8 * 37],
+          flat[3003:3004], torch.randn(33278, 16, device=cuda, generator=g)]
+    casts = Bf16Casts(ts, padded={id(ts[4]): 33280})
+    casts.refresh()
+    got = casts.lookup(*ts)
+    assert got is not None
+    for t, c in zip(ts, got):
+        assert c.dtype == torch.bfloat16 and torch.equal(c, t.to(torch.bfloat16))
+    pad = casts.padded(ts[4])
+    assert pad.shape == (33280, 16) and torch.all(pad[33278:] == 0) and torch.equal(pad[:33278], got[4])
+    assert casts.padded(ts[0]) is None  # no padded rows for it: lookup() only
+    ts[0].add_(1.0)  # in place: a new version
+    assert casts.lookup(ts[0]) is None and casts.lookup(ts[1]) is not None
+    casts.refresh()
+    assert torch.equal(casts.lookup(ts[0])[0], ts[0].to(torch.bfloat16))
+    assert casts.lookup(torch.zeros(3, device=cuda)) is None  # not one of its parameters
+
+
+def test_lm_step_casts_change_nothing(cuda):
+    """The LM's one-launch bf16 copies of its GEMM parameters give the same loss,
+    bit for bit, as casting every weight per GEMM, and the same gradients up to
+    the attention's dQ accumulation order (atomic adds across key tiles)."""
+    cfg = LMConfig(max_seq=128)
+    torch.manual_seed(3)
+    a = PnFirLM(cfg).to(cuda)
+    b = PnFirLM(cfg).to(cuda)
+    b.load_state_dict(a.state_dict())
+    b._step_casts = lambda dev: None  # per-GEMM casts
+    idx = torch.randint(0, cfg.vocab, (2, 128), device=cuda, generator=torch.Generator(device=cuda).manual_seed(4))
+    out = []
+    for m in (a, b):
+        with torch.autocast("cuda", dtype=torch.bfloat16):
+            loss = lm_loss(m, idx)
+        loss.backward()
+        out.append((loss.detach(), {n: p.grad for n, p in m.named_parameters()}))
+    check_device_status(cuda)
+    assert a._casts is not None and b._casts is None
+    assert torch.equal(out[0][0], out[1][0])
+    for n in out[0][1]:
+        assert rel_l2(out[0][1][n], out[1][1][n]) < 1e-4, (n, rel_l2(out[0][1][n], out[1][1][n]))
+
+
 def _lm_pair(cuda, N=128, B=4):
     cfg = LMConfig(max_seq=N)
     torch.manual_seed(3)
