@@ -770,8 +770,10 @@ def _host_link_floor(dist_: Dist, dev, hin, din, hout, reps: int = 3) -> dict:
     device->host, first one direction at a time, then both at once on two streams
     (the floor of a step whose copies overlap its kernels perfectly). Pinned host
     buffers, one copy call per tensor, max over ranks (all ranks copy at once, as
-    in the step, so they share the host's memory and PCIe switches)."""
+    in the step, so they share the host's memory and PCIe switches). The downloads
+    read their own device buffers, not the ones being uploaded."""
     s_in, s_out = torch.cuda.Stream(dev), torch.cuda.Stream(dev)
+    dsrc = [torch.zeros_like(h, device=dev) for h in hout]
 
     def run(h2d: bool, d2h: bool) -> float:
         torch.cuda.synchronize()
@@ -788,7 +790,7 @@ def _host_link_floor(dist_: Dist, dev, hin, din, hout, reps: int = 3) -> dict:
                         d.copy_(h, non_blocking=True)
             if d2h:
                 with torch.cuda.stream(s_out):
-                    for h, d in zip(hout, din):
+                    for h, d in zip(hout, dsrc):
                         h.copy_(d, non_blocking=True)
         main.wait_stream(s_in)
         main.wait_stream(s_out)
