@@ -101,6 +101,7 @@ class Dist:
         self.rank = int(os.environ.get("RANK", "0"))
         self.local_rank = int(os.environ.get("LOCAL_RANK", "0"))
         self.active = self.world > 1
+        self.tau_group = None  # NCCL group of the per-backward tau all-reduce (init)
 
     def init(self, backend: str):
         if self.active:
@@ -115,6 +116,15 @@ class Dist:
                 opts.is_high_priority_stream = True
             dist.init_process_group(backend, timeout=timedelta(seconds=180), pg_options=opts,
                                     device_id=torch.device("cuda", self.local_rank) if backend == "nccl" else None)
+            if backend == "nccl":
+                # the 8-byte tau all-reduce of every backward on its own communicator
+                # whose kernel takes one CTA: it runs beside the next step's
+                # attention kernels and takes one SM slot from them, not several
+                topts = dist.ProcessGroupNCCL.Options()
+                topts.is_high_priority_stream = True
+                topts.config.min_ctas = 1
+                topts.config.max_ctas = 1
+                self.tau_group = dist.new_group(backend="nccl", pg_options=topts)
 
     def barrier(self):
         if self.active:
@@ -426,7 +436,7 @@ def bench_ours(args, dist_: Dist) -> dict:
     # tau's gradient: this rank's partial is summed over the ranks in fp64 on a side
     # stream (TauGradReducer), so no step waits for the other ranks; the sum is
     # collected once, by the consumer of tau's gradient, at the end of the timed region
-    reducer = TauGradReducer()
+    reducer = TauGradReducer(dist_.tau_group)
 
     def step(evs=None):
         if evs is not None:
@@ -586,7 +596,7 @@ def bench_tau_sweep(args, dist_: Dist, w: dict, dev) -> dict:
     out = {}
     for tau0 in (-0.5, 0.0, 0.5):
         tau = torch.tensor(tau0, device=dev, requires_grad=True)
-        ms, fwd, bwd = _time_fwd_bwd(q, k, v, do, tau, args.sweep_steps, 3, TauGradReducer())
+        ms, fwd, bwd = _time_fwd_bwd(q, k, v, do, tau, args.sweep_steps, 3, TauGradReducer(dist_.tau_group))
         ms = dist_.max(ms, dev)
         _, M, _, _, live = flash_pn_fir_tau_forward_stats(q, k, v, tau.detach())
         ncausal = float(causal.sum()) * B * H
@@ -621,7 +631,7 @@ def bench_deterministic(args, dist_: Dist, w: dict, dev) -> dict:
     q, k, v, do = make_inputs(w, args.seed + 1000 * dist_.rank, dev)
     tau = torch.tensor(args.tau, device=dev, requires_grad=True)
     attn = functools.partial(flash_pn_fir_tau_attention, deterministic=True)
-    ms, fwd, bwd = _time_fwd_bwd(q, k, v, do, tau, args.sweep_steps, 3, TauGradReducer(), attention=attn)
+    ms, fwd, bwd = _time_fwd_bwd(q, k, v, do, tau, args.sweep_steps, 3, TauGradReducer(dist_.tau_group), attention=attn)
     ms = dist_.max(ms, dev)
     return {"ms_per_step": round(ms / args.sweep_steps, 4),
             "value": round(dist_.world * flops_fwd_bwd(w) * args.sweep_steps / (ms / 1e3) / 1e12, 2),
@@ -641,7 +651,7 @@ def bench_c5(args, dist_: Dist, dev) -> dict:
     ws = dict(w, B=1, H=hi - lo)
     q, k, v, do = make_inputs(ws, args.seed + 50 + lo, dev)
     tau = torch.tensor(0.0, device=dev, requires_grad=True)
-    ms, fwd, bwd = _time_fwd_bwd(q, k, v, do, tau, args.c5_steps, 2, TauGradReducer())
+    ms, fwd, bwd = _time_fwd_bwd(q, k, v, do, tau, args.c5_steps, 2, TauGradReducer(dist_.tau_group))
     ms = dist_.max(ms, dev)
     total = flops_fwd_bwd(w)
     mine = flops_fwd_bwd(ws)
@@ -696,7 +706,7 @@ def bench_e2e(args, dist_: Dist, w: dict, dev, flops: float, P) -> dict:
     s_in, s_cmp, s_out = torch.cuda.Stream(dev), torch.cuda.Stream(dev), torch.cuda.Stream(dev)
     from paper_01_anti_decoy_pnfirtau_b200 import TauGradReducer
 
-    reducer = TauGradReducer()
+    reducer = TauGradReducer(dist_.tau_group)
     done_cmp = [None] * nchunk  # compute of chunk i finished reading its device inputs (previous step)
 
     def step():

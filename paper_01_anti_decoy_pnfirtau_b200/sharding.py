@@ -67,7 +67,10 @@ class TauGradReducer:
     (which adds the sum to ``tau.grad``), as data-parallel training finalises its
     gradient buckets before the optimizer step. Every rank must push the same
     number of times, in the same order (one collective per backward).
-    On CPU tensors (``gloo``) the all-reduce runs inline.
+    On CPU tensors (``gloo``) the all-reduce runs inline. ``group`` may be a
+    communicator of its own whose kernels take one CTA (NCCL options
+    ``min_ctas = max_ctas = 1``): the 8-byte collective then runs beside the
+    next step's kernels without queueing behind them.
     """
 
     def __init__(self, group=None):
