@@ -124,7 +124,7 @@ class Dist:
                 topts.is_high_priority_stream = True
                 topts.config.min_ctas = 1
                 topts.config.max_ctas = 1
-                self.tau_group = dist.new_group(backend="nccl", pg_options=topts)
+                self.tau_group = dist.new_group(backend="nccl", pg_options=topts, timeout=timedelta(seconds=180))
 
     def barrier(self):
         if self.active:
