@@ -37,6 +37,7 @@ struct FlashArgs {
   // bwd workspace carve-up
   float* dq_acc;       // fp32 [B,H,N,acc_d] contiguous
   int64_t acc_d;       // row stride of dq_acc: acc_width(D)
+  int acc_swz;         // rows of dq_acc hold their 16-byte chunks in acc_chunk order (the d=64 tcgen05 backward)
   // per-row backward coefficients (see below): record of row n of head bh at
   // r = bh * rec_rows(N) + n; the padding rows past N hold silent-row records
   float4* coefP;       // rows 2j, 2j+1 interleaved: {c1_0, c1_1, -D_0, -D_1}
@@ -78,6 +79,11 @@ __device__ __forceinline__ RowCoef load_row_coef(const float4* coefP, const floa
 // so every tile's records start 256-byte aligned and a tile load never reads
 // past its head.
 __host__ __device__ __forceinline__ int64_t rec_rows(int64_t N) { return (N + 63) / 64 * 64; }
+
+// Swizzled dQ accumulator rows (acc_swz, 64 floats per row): the 16-byte chunk c of
+// row n sits at chunk c ^ (n & 15). A drain thread then stores a whole row of one
+// query as 16-byte stores while the 32 rows of a warp fall in distinct bank groups.
+__host__ __device__ __forceinline__ int acc_chunk(int c, int64_t n) { return c ^ (int)(n & 15); }
 
 // Workspace layout shared by both kernel families (256-byte aligned sections).
 struct BwdWorkspace {

@@ -562,8 +562,10 @@ __global__ void __launch_bounds__(256) dq_cast_rows_kernel(FlashArgs a) {
   if (n >= a.N) return;
   constexpr int D = 8 << SH;
   const int c = (int)(li & ((1u << SH) - 1)) * 8;
-  const float4* src = reinterpret_cast<const float4*>(a.dq_acc + ((int64_t)bh * a.N + n) * D + c);
-  float4 f0 = __ldcs(src), f1 = __ldcs(src + 1);
+  const float4* row4 = reinterpret_cast<const float4*>(a.dq_acc + ((int64_t)bh * a.N + n) * D);
+  const int c4 = c >> 2;  // 16-byte chunks c4, c4 + 1 of the row (swizzled: D == 64 only)
+  float4 f0 = __ldcs(row4 + (a.acc_swz ? acc_chunk(c4, n) : c4));
+  float4 f1 = __ldcs(row4 + (a.acc_swz ? acc_chunk(c4 + 1, n) : c4 + 1));
   const float fs = a.dq_scale;
   uint4 w;
   w.x = pack2<T>(fs * f0.x, fs * f0.y);
@@ -587,8 +589,9 @@ __global__ void __launch_bounds__(256) dq_cast_kernel(FlashArgs a) {
          i += (int64_t)gridDim.x * blockDim.x) {
       const int64_t row = i / per_row, c = (i - row * per_row) * 8;
       const int64_t n = row % a.N, bh = row / a.N, b = bh / a.H, h = bh % a.H;
-      const float4* src = reinterpret_cast<const float4*>(a.dq_acc + row * a.acc_d + c);
-      float4 f0 = src[0], f1 = src[1];
+      const float4* row4 = reinterpret_cast<const float4*>(a.dq_acc + row * a.acc_d);
+      const int c4 = (int)(c >> 2);
+      float4 f0 = row4[a.acc_swz ? acc_chunk(c4, n) : c4], f1 = row4[a.acc_swz ? acc_chunk(c4 + 1, n) : c4 + 1];
       f0.x *= fs; f0.y *= fs; f0.z *= fs; f0.w *= fs;
       f1.x *= fs; f1.y *= fs; f1.z *= fs; f1.w *= fs;
       T* dst = dq + b * a.sdq[0] + h * a.sdq[1] + n * a.sdq[2] + c;
@@ -608,7 +611,8 @@ __global__ void __launch_bounds__(256) dq_cast_kernel(FlashArgs a) {
   const int64_t total = a.B * a.H * a.N * a.D;
   for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
     const int64_t e = i % a.D, n = (i / a.D) % a.N, bh = i / (a.D * a.N), b = bh / a.H, h = bh % a.H;
-    dq[b * a.sdq[0] + h * a.sdq[1] + n * a.sdq[2] + e * a.sdq[3]] = from_f32<T>(fs * a.dq_acc[(bh * a.N + n) * a.acc_d + e]);
+    const int64_t ep = a.acc_swz ? (int64_t)((acc_chunk((int)(e >> 2), n) << 2) | (int)(e & 3)) : e;
+    dq[b * a.sdq[0] + h * a.sdq[1] + n * a.sdq[2] + e * a.sdq[3]] = from_f32<T>(fs * a.dq_acc[(bh * a.N + n) * a.acc_d + ep]);
   }
 }
 

@@ -13,7 +13,9 @@
 //                then for tile t-1 (overlapping tile t's elementwise work):
 //                  dV += P^T dO   (TS: P^T bf16 from TMEM)
 //                  dK += dS^T Q   (SS: dS^T bf16 from shared memory)
-//                  dQ^T = K^T dS^T (SS, M = head dims), into TMEM
+//                  dQ of a pair of query tiles = dS K (SS, M = 128 queries,
+//                  N = head dims; D=64), or dQ^T = K^T dS^T per tile (SS,
+//                  M = head dims; D=128), into TMEM
 //   warps 4-11   elementwise, thread = TMEM lane = key; warpgroup g owns query
 //                columns [32g, 32g+32). Each thread pulls its whole S/dP slice
 //                into registers and releases TMEM at once, then computes
@@ -25,14 +27,15 @@
 //                on tiles that cross the diagonal or a sequence end; the gate
 //                term is one patched entry per row (value tests only on tiles
 //                holding a row with several maxima).
-//   warps 12-15  dQ drain: TMEM -> fp32 staging tile in smem -> one
+//   warps 12-15  dQ drain: TMEM -> fp32 staging tile in smem (D=64: each
+//                thread one query row, 16-byte stores in acc_chunk order) -> one
 //                cp.reduce.async.bulk add into the fp32 dQ accumulator (in
 //                deterministic mode: a read-modify-write of the tile once the
 //                lower key tiles of the head have added theirs, so the fp32
 //                additions happen in key order on every run).
 // Finally the elementwise warps write dK, dV (bf16) from TMEM.
-// TMEM columns: S [0,64) dP [64,128) P^T x2 [128,192) dV [192,192+D)
-//               dK [192+D,192+2D) dQ^T (x2 for D=64) [192+2D, 512).
+// TMEM columns: see BwdLayout (D=64: S/dP x2 [0,256), dV, dK, dQ of a tile pair
+//               [384,448); D=128: S/dP [0,128), P^T x2, dV, dK, dQ^T [448,512)).
 // Semantics: src/triton_pnfirtau.py:445-621 with the per-row terms of
 // flash_bwd_prep (RowCoef). S is recomputed by the tensor core exactly as in
 // the tcgen05 forward, so u == peak finds the forward's maxima.
@@ -84,8 +87,8 @@ struct BwdLayout {
   static constexpr int KBYTES = BN * D * 2;
   static constexpr int QBYTES = BM * D * 2;
   static constexpr int NDQ = D == 64 ? 2 : 1;   // dQ buffers in TMEM
-  // D=64: dQ^T of two consecutive tiles in one MMA sequence (N = 128 queries from two
-  // adjacent dS tiles), accumulated in the NDQ * 64 columns as one buffer
+  // D=64: dQ of two consecutive tiles in one MMA sequence (M = 128 queries from two
+  // adjacent dS tiles, N = 64 head dims)
   static constexpr bool DQ_PAIR = D == 64;
   static constexpr int NSTG = D == 64 ? 2 : 1;  // dQ staging tiles in smem
   static constexpr int STG_BYTES = BM * D * 4;
@@ -114,7 +117,8 @@ struct BwdLayout {
   // TMEM. D=64: two S/dP buffers [128b, 128b+128) (S at +0, dP at +64); a warp
   // writes the packed P^T of each 16-query group over the first 8 of that group's S
   // columns (its own columns) once they are in registers, so buffer b is free again once dV of its tile has been issued
-  // (MMAs of one thread run in order). dV [256,320) dK [320,384) dQ^T x2 [384,512).
+  // (MMAs of one thread run in order). dV [256,320) dK [320,384) dQ of a tile pair
+  // [384,448).
   // D=128: one S/dP buffer [0,128), P^T x2 [128,192), dV [192,320), dK [320,448),
   // dQ^T [448,512).
   static constexpr int NSB = D == 64 ? 2 : 1;
@@ -339,7 +343,9 @@ __global__ void __launch_bounds__(B_THREADS, 1) flash_bwd_sm100_kernel(const __g
     constexpr uint32_t ID_S = idesc_f16(BN, BM, 1, 0, 0);   // S^T, dP^T: K-major A and B
     constexpr uint32_t ID_G = idesc_f16(BN, D, 1, 0, 1);    // dV (A in TMEM), dK (A K-major); B MN-major
     constexpr uint32_t ID_DQ = idesc_f16(D, BM, 1, 1, 1);   // dQ^T: M = head dims
-    constexpr uint32_t ID_DQ2 = idesc_f16(D, 2 * BM, 1, 1, 1);  // dQ^T of a tile pair (N = 128)
+    // dQ of a tile pair, not transposed: M = the pair's 128 queries (A = dS, queries
+    // contiguous in the dS^T tiles), N = head dims (B = K, head dims contiguous)
+    constexpr uint32_t ID_DQ2 = idesc_f16(2 * BM, D, 1, 1, 1);
     // Descriptors of k-step 0; a k-step moves +32 B inside a 128-byte K-major row
     // (+2 in descriptor units, +GROUP bytes across 64-column groups) or +16 rows
     // (2048 B, +128) of an MN-major tile.
@@ -385,18 +391,18 @@ __global__ void __launch_bounds__(B_THREADS, 1) flash_bwd_sm100_kernel(const __g
       __syncwarp();
       return true;
     };
-    // dQ^T of tiles u and u+1 (u even; `two` false for a last tile alone): the
-    // dS tiles u % NDS and u % NDS + 1 are adjacent, one 64-query atom apart, so the
-    // MN-major descriptor of tile u spans both (its atom stride is the dS tile size)
+    // dQ of tiles u and u+1 (u even; `two` false for a last tile alone, whose partner
+    // rows the drain ignores): the dS tiles u % NDS and u % NDS + 1 are adjacent, one
+    // 64-query atom apart, so the MN-major descriptor of tile u spans both (its atom
+    // stride is the dS tile size). TMEM lane = query of the pair, column = head dim.
     auto dq_pair = [&](int u, bool two) -> bool {
       const int ds = u % L::NDS;
       if (!warp_wait(bar(C_DQEMPTY), ((u >> 1) & 1) ^ 1, ab)) return false;
       tc_fence_after();
       if (elect_one()) {
-        const uint32_t id = two ? ID_DQ2 : ID_DQ;
 #pragma unroll
         for (int kk = 0; kk < BN / 16; ++kk)
-          mma_ss(tmem + L::TM_DQ, dKmn + kk * 128, dSmn + ds * DSSTEP + kk * 128, id, kk > 0);
+          mma_ss(tmem + L::TM_DQ, dSmn + ds * DSSTEP + kk * 128, dKmn + kk * 128, ID_DQ2, kk > 0);
         mma_commit(bar(C_DQFULL));
         mma_commit(bar(C_PDSEMPTY + ds));
         if (two) mma_commit(bar(C_PDSEMPTY + ds + 1));
@@ -722,11 +728,12 @@ __global__ void __launch_bounds__(B_THREADS, 1) flash_bwd_sm100_kernel(const __g
     LiveTiles lt(live, i_first, p.nq64, p.det != 0);
     bool mt;
     if constexpr (L::DQ_PAIR) {
-      // tile pairs: dQ^T columns [0,64) = tile A's queries, [64,128) = tile B's;
-      // head dim 16*wq + l in lane l < 16 of quadrant wq (M=64 layout)
-      static_assert(L::NSTG == 2, "one staging tile per tile of a pair");
-      const bool holds = lane < 16;
-      const int d = 16 * wq + lane;
+      // tile pairs: TMEM lane = query of the pair (quadrants 0-1: tile A, 2-3: tile
+      // B), columns = head dims; each thread stores its query's row of 64 head dims
+      // as 16 chunks of 16 bytes into the row-major staging tile (chunks swizzled by
+      // acc_chunk, the accumulator's own order)
+      static_assert(L::NSTG == 2 && D == 64, "one staging tile per tile of a pair, rows of 64 head dims");
+      const int tsel = wq >> 1, ql = 32 * (wq & 1) + lane;  // tile of the pair, row in that tile
       for (int pr = 0;; ++pr) {
         const int ia = lt.next(&mt);
         if (ia < 0) break;
@@ -736,15 +743,17 @@ __global__ void __launch_bounds__(B_THREADS, 1) flash_bwd_sm100_kernel(const __g
         if (leader) bulk_wait_read<0>();  // the previous pair's reduces have read both staging tiles
         named_bar_sync(4, 128);
         if (!dead) tc_fence_after();
+        float* stg = reinterpret_cast<float*>(smem + L::OFF_STG + tsel * L::STG_BYTES);  // [64 q][D]
 #pragma unroll
-        for (int h4 = 0; h4 < 4; ++h4) {  // 32 query columns at a time
-          if (h4 >= 2 && !two) break;
+        for (int h = 0; h < 2; ++h) {  // head dims [32h, 32h + 32)
           uint32_t r[32];
-          if (!dead) tmem_load32(tmem + lane_off + L::TM_DQ + 32u * h4, r);
-          float* stg = reinterpret_cast<float*>(smem + L::OFF_STG + (h4 >> 1) * L::STG_BYTES);  // [64 q][D]
-          if (holds && !dead) {
+          if (!dead) tmem_load32(tmem + lane_off + L::TM_DQ + 32u * h, r);
+          if (!dead && (tsel == 0 || two)) {
 #pragma unroll
-            for (int q = 0; q < 32; ++q) stg[(32 * (h4 & 1) + q) * D + d] = __uint_as_float(r[q]);
+            for (int v = 0; v < 8; ++v)
+              reinterpret_cast<float4*>(stg + ql * D)[acc_chunk(8 * h + v, ql)] =
+                  make_float4(__uint_as_float(r[4 * v]), __uint_as_float(r[4 * v + 1]), __uint_as_float(r[4 * v + 2]),
+                              __uint_as_float(r[4 * v + 3]));
           }
         }
         if (!dead) {
@@ -832,6 +841,7 @@ int flash_bwd_sm100(const FlashArgs& a0, cudaStream_t st) {
   const int nkt = (int)((a.N + BN - 1) / BN);
   a.n_dtau_part = a.B * a.H * nkt;
   a.dq_scale = 10.f * a.scale;  // the kernel accumulates dS' = dS / (10 scale) into dQ
+  a.acc_swz = a.D <= 64 ? 1 : 0;  // d = 64 kernel: tile-pair dQ rows stored in acc_chunk order
   int rc = flash_bwd_prep(a, st);
   if (rc) return rc;
   BwdParams p;
